@@ -1,0 +1,236 @@
+// lmx.cu -- kernels' host launchers and the op-level C ABI (include/lmx.h).
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "lmx_internal.h"
+#include "norm_argmax.cuh"
+#include "qmm.cuh"
+
+// Device error word: bounded waits that give up record a code here.
+__device__ unsigned g_lmx_kernel_error;
+
+namespace lmx {
+
+namespace {
+thread_local std::string t_last_error;
+
+struct DevInfo {
+  bool init = false;
+  int sms = 0;
+  unsigned* err = nullptr;
+};
+DevInfo g_dev[64];
+std::mutex g_dev_mu;
+
+DevInfo& dev() {
+  int d = 0;
+  cudaGetDevice(&d);
+  DevInfo& di = g_dev[d & 63];
+  if (!di.init) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!di.init) {
+      cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d);
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_lmx_kernel_error) == cudaSuccess) di.err = (unsigned*)p;
+      di.init = true;
+    }
+  }
+  return di;
+}
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return LMX_OK;
+  return set_error(LMX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int device_sms() { return dev().sms; }
+unsigned* device_error_word() { return dev().err; }
+
+// ---------------------------------------------------------------------------
+// K1 launcher
+// ---------------------------------------------------------------------------
+template <int BITS, int MT, int RB>
+static int launch_qmv_t(const QmmArgs& a, cudaStream_t st) {
+  constexpr int V = RB * MT, SEGB = 32 * 16 * BITS / 8, NW = kQmmThreads / 32;
+  const int nseg = (a.K + 511) / 512;
+  const int csize = nseg <= NW ? 1 : (nseg + NW - 1) / NW;
+  if (csize > 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d exceeds 32768", a.K);
+  const int rs = csize == 1 ? NW / nseg : 1;
+  const int items = a.mode == QMM_SWIGLU ? 2 * a.N : a.N;
+  const int nbatch = (items + RB - 1) / RB;
+  const size_t stage = (size_t)NW * RB * SEGB;
+  int nst = (int)((160 * 1024) / stage);
+  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
+  const size_t smem = nst * stage + (size_t)NW * nst * 8 + 2 * NW * V * 4 + kQmmMaxNormRows * 4;
+  static bool attr_set[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (!attr_set[d & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(qmv_kernel<BITS, MT, RB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                        "qmm: set smem");
+    if (rc) return rc;
+    if (csize > 1)
+      cudaFuncSetAttribute(qmv_kernel<BITS, MT, RB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    attr_set[d & 63] = true;
+  }
+  int nclusters = (nbatch + rs - 1) / rs;
+  const int max_clusters = device_sms() / csize;
+  if (nclusters > max_clusters) nclusters = max_clusters;
+  if (nclusters < 1) nclusters = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nclusters * csize);
+  cfg.blockDim = dim3(kQmmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (csize > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, a, nst), "qmm: launch");
+}
+
+template <int BITS>
+static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
+  if (a.M <= 1) return launch_qmv_t<BITS, 1, 8>(a, st);
+  if (a.M <= 2) return launch_qmv_t<BITS, 2, 8>(a, st);
+  if (a.M <= 4) return launch_qmv_t<BITS, 4, 8>(a, st);
+  return launch_qmv_t<BITS, 8, 4>(a, st);
+}
+
+int launch_qmm(const QmmCall& c, cudaStream_t st) {
+  if (c.M == 0 || c.N == 0) return LMX_OK;
+  if (c.M < 0 || c.N < 0 || c.K <= 0 || c.K % 64)
+    return set_error(LMX_ERR_INVALID, "qmm: bad shape M=%d N=%d K=%d", c.M, c.N, c.K);
+  if (c.bits != 4 && c.bits != 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: bits=%d", c.bits);
+  if (c.norm_w && c.M > kQmmMaxNormRows)
+    return set_error(LMX_ERR_INVALID, "qmm: fused norm needs M <= %d", kQmmMaxNormRows);
+  if (!c.x || !c.y || ((uintptr_t)c.x & 15))
+    return set_error(LMX_ERR_INVALID, "qmm: x must be a 16-byte aligned device pointer");
+  QmmArgs a;
+  a.x = c.x;
+  a.norm_w = c.norm_w;
+  a.eps = c.eps;
+  a.nmat = c.nmat;
+  for (int i = 0; i < 3; ++i) {
+    a.mat[i].w = c.mat[i].w;
+    a.mat[i].s = c.mat[i].s;
+    a.mat[i].b = c.mat[i].b;
+    a.mat[i].rows = c.mat[i].rows;
+    if (i < c.nmat && (!c.mat[i].w || ((uintptr_t)c.mat[i].w & 15) || !c.mat[i].s || !c.mat[i].b))
+      return set_error(LMX_ERR_INVALID, "qmm: weight %d must be 16-byte aligned", i);
+  }
+  a.N = c.N;
+  a.y = c.y;
+  a.ldy = c.ldy;
+  a.res = c.res;
+  a.M = c.M;
+  a.K = c.K;
+  a.mode = c.mode;
+  a.err = device_error_word();
+  return c.bits == 4 ? launch_qmv_bits<4>(a, st) : launch_qmv_bits<8>(a, st);
+}
+
+int launch_rms_norm(const bf16_t* x, const bf16_t* w, bf16_t* y, int rows, int dim, float eps,
+                    cudaStream_t st) {
+  if (rows == 0) return LMX_OK;
+  if (!x || !w || !y || rows < 0 || dim <= 0)
+    return set_error(LMX_ERR_INVALID, "rms_norm: bad arguments");
+  return cuda_check(lmx_launch(rms_norm_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, true, x, w, y,
+                               rows, dim, eps),
+                    "rms_norm: launch");
+}
+
+int launch_argmax(const bf16_t* logits, int rows, int V, int32_t* out, cudaStream_t st) {
+  if (rows == 0) return LMX_OK;
+  if (!logits || !out || rows < 0 || V <= 0) return set_error(LMX_ERR_INVALID, "argmax: bad arguments");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows * kArgmaxCluster);
+  cfg.blockDim = dim3(512);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kArgmaxCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_check(cudaLaunchKernelEx(&cfg, argmax_kernel, logits, V, out), "argmax: launch");
+}
+
+}  // namespace lmx
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+using namespace lmx;
+
+extern "C" const char* lmx_last_error(void) { return t_last_error.c_str(); }
+extern "C" const char* lmx_version(void) { return "lmx-b200 0.1"; }
+
+extern "C" int lmx_device_error(unsigned* code, int clear) {
+  unsigned v = 0;
+  int rc = cuda_check(cudaMemcpyFromSymbol(&v, g_lmx_kernel_error, sizeof(v)), "device_error");
+  if (rc) return rc;
+  if (code) *code = v;
+  if (clear && v) {
+    unsigned z = 0;
+    rc = cuda_check(cudaMemcpyToSymbol(g_lmx_kernel_error, &z, sizeof(z)), "device_error");
+  }
+  return rc;
+}
+
+extern "C" int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
+                                    const void* biases, void* y, int M, int N, int K, int group_size,
+                                    int bits, void* stream) {
+  if (group_size != 64)
+    return set_error(LMX_ERR_UNSUPPORTED, "quantized_matmul: group_size %d (only 64)", group_size);
+  QmmCall c;
+  c.x = (const bf16_t*)x;
+  c.mat[0].w = w;
+  c.mat[0].s = (const bf16_t*)scales;
+  c.mat[0].b = (const bf16_t*)biases;
+  c.mat[0].rows = N;
+  c.nmat = 1;
+  c.N = N;
+  c.y = (bf16_t*)y;
+  c.ldy = N;
+  c.M = M;
+  c.K = K;
+  c.bits = bits;
+  return launch_qmm(c, (cudaStream_t)stream);
+}
+
+extern "C" int lmx_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
+                            void* stream) {
+  return launch_rms_norm((const bf16_t*)x, (const bf16_t*)w, (bf16_t*)y, rows, dim, eps,
+                         (cudaStream_t)stream);
+}
+
+extern "C" int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream) {
+  return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
+}

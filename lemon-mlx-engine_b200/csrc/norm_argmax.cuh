@@ -1,0 +1,97 @@
+// norm_argmax.cuh -- standalone RMSNorm and the cluster argmax.
+#pragma once
+#include <cooperative_groups.h>
+
+#include "lmx_common.cuh"
+namespace cg = cooperative_groups;
+
+namespace lmx {
+
+// RMSNorm (mx::fast::rms_norm, e.g. src/llm/models/qwen3.cpp:78,145), one warp
+// per row.  Canonical order: lane partials p_l = fma chain of x_i^2 over
+// i = l, l+32, ..., butterfly (16,8,4,2,1), r = 1/sqrt(ss/dim + eps),
+// y = bf16((x*r)*w).  Bit-identical to the prologue fused into qmv_kernel.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const bf16_t* x, const bf16_t* w, bf16_t* y,
+                                                       int rows, int dim, float eps) {
+  grid_wait();
+  grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bf16_t* xr = x + (size_t)row * dim;
+  float p = 0.0f;
+  for (int i = lane; i < dim; i += 32) {
+    float v = bf2f(xr[i]);
+    p = __fmaf_rn(v, v, p);
+  }
+  p = warp_sum_xor(p, 16, 1);
+  const float f = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)dim), eps)));
+  bf16_t* yr = y + (size_t)row * dim;
+  for (int i = lane; i < dim; i += 32) yr[i] = f2bf(__fmul_rn(__fmul_rn(bf2f(xr[i]), f), bf2f(w[i])));
+}
+
+// (value, index) max with the lowest index winning ties; NaN never wins.
+LMX_DEV bool am_better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+LMX_DEV void am_warp(float& bv, int& bi) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+}
+
+// Block-level argmax of a slice; returns the result in thread 0.
+LMX_DEV void am_block(float& bv, int& bi, float* sv, int* si) {
+  am_warp(bv, bi);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+    am_warp(bv, bi);
+  }
+}
+
+// argmax over V per row: a cluster of kArgmaxCluster CTAs per row, each
+// reducing a contiguous slice; rank 0 combines the partials through DSMEM
+// (no global scratch).
+static constexpr int kArgmaxCluster = 8;
+__global__ void __launch_bounds__(512) argmax_kernel(const bf16_t* logits, int V, int32_t* out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ float cv;
+  __shared__ int ci;
+  grid_wait();
+  grid_launch_dependents();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+  const int row = blockIdx.x / cs;
+  const int chunk = (V + cs - 1) / cs;
+  const int j0 = rank * chunk, j1 = min(V, j0 + chunk);
+  const bf16_t* l = logits + (size_t)row * V;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    float v = bf2f(l[j]);
+    if (v == v && am_better(v, j, bv, bi)) { bv = v; bi = j; }
+  }
+  am_block(bv, bi, sv, si);
+  if (threadIdx.x == 0) { cv = bv; ci = bi; }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    float rv = cv;
+    int ri = ci;
+    for (int r = 1; r < cs; ++r) {
+      float ov = *cluster.map_shared_rank(&cv, r);
+      int oi = *cluster.map_shared_rank(&ci, r);
+      if (am_better(ov, oi, rv, ri)) { rv = ov; ri = oi; }
+    }
+    out[row] = ri == 0x7fffffff ? 0 : ri;
+  }
+  cluster.sync();
+}
+
+}  // namespace lmx

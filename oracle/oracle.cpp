@@ -1,0 +1,1000 @@
+// oracle.cpp -- CPU restatement of the reference's speculative-decode hot path.
+//
+// TEST INFRASTRUCTURE ONLY (see oracle.h for the scope, the pinned/unpinned
+// split and the rule that nothing in the product may use this file).
+//
+// Build: oracle/Makefile (g++ -O3 -fopenmp -ffp-contract=off).  Contraction is
+// off so every fp32 multiply/add below is its own IEEE operation; every fused
+// multiply-add is written as std::fma, exactly where the CUDA kernels use
+// __fmaf_rn, so both sides execute the same operations in the same order.
+#include "oracle.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef unsigned __int128 u128;
+
+// ---------------------------------------------------------------------------
+// scalar numerics
+// ---------------------------------------------------------------------------
+static inline float bf2f(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+static inline uint16_t f2bf(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // quiet NaN
+  u += 0x7fffu + ((u >> 16) & 1u);                                              // RNE
+  return (uint16_t)(u >> 16);
+}
+static inline float u2f(uint32_t u) {
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+extern "C" float orc_bf16_to_f32(uint16_t h) { return bf2f(h); }
+extern "C" uint16_t orc_f32_to_bf16(float x) { return f2bf(x); }
+
+// exp(x): Cody-Waite reduction x = n*ln2 + r (ln2 split hi/lo, hi with 16
+// significant bits so n*ln2_hi is exact), e^r by the degree-7 Taylor
+// polynomial in Horner form, then an exact scaling by 2^n.  Domain clamps:
+// x > 88 -> +inf, x < -87 -> 0.  Every operation is a single IEEE fp32
+// operation so the CUDA kernels reproduce the result bit for bit.
+extern "C" float orc_exp(float x) {
+  if (x != x) return x;
+  if (x > 88.0f) return INFINITY;
+  if (x < -87.0f) return 0.0f;
+  const float kLog2e = 0x1.715476p+0f;
+  const float kLn2Hi = 0x1.62e4p-1f;
+  const float kLn2Lo = 0x1.7f7d1cp-20f;
+  float n = std::rint(x * kLog2e);
+  float r = std::fma(-n, kLn2Hi, x);
+  r = std::fma(-n, kLn2Lo, r);
+  float p = 0x1.a01a02p-13f;            // 1/5040
+  p = std::fma(p, r, 0x1.6c16c2p-10f);  // 1/720
+  p = std::fma(p, r, 0x1.111112p-7f);   // 1/120
+  p = std::fma(p, r, 0x1.555556p-5f);   // 1/24
+  p = std::fma(p, r, 0x1.555556p-3f);   // 1/6
+  p = std::fma(p, r, 0.5f);
+  p = std::fma(p, r, 1.0f);
+  p = std::fma(p, r, 1.0f);
+  int ni = (int)n;
+  return p * u2f((uint32_t)(ni + 127) << 23);
+}
+
+static inline float sigmoid_f(float g) { return 1.0f / (1.0f + orc_exp(-g)); }
+
+// ---------------------------------------------------------------------------
+// Philox4x32-10 (Salmon et al., SC'11) and the synthetic-data generators
+// ---------------------------------------------------------------------------
+static inline void philox10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int i = 0; i < 10; ++i) {
+    uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+    uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+    uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    uint32_t n1 = (uint32_t)p1;
+    uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    uint32_t n3 = (uint32_t)p0;
+    c[0] = n0; c[1] = n1; c[2] = n2; c[3] = n3;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+extern "C" void orc_philox(uint64_t seed, const uint32_t ctr_in[4], uint32_t out[4]) {
+  uint32_t c[4] = {ctr_in[0], ctr_in[1], ctr_in[2], ctr_in[3]};
+  philox10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  std::memcpy(out, c, 16);
+}
+
+// Element e of tensor `tid`: counter (e_lo, e_hi, tid, 0x243F6A88).
+static inline void gen_block(uint64_t seed, uint32_t tid, uint64_t e, uint32_t out[4]) {
+  out[0] = (uint32_t)e;
+  out[1] = (uint32_t)(e >> 32);
+  out[2] = tid;
+  out[3] = 0x243F6A88u;
+  philox10(out, (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+extern "C" float orc_normal_scale(float std_dev) {
+  return (float)((double)std_dev * std::sqrt(3.0) / 4194304.0);
+}
+
+// Irwin-Hall(4) of 22-bit uniforms: S in [0, 2^24), z = S - 2^23 is exact in
+// fp32, w = bf16(z * C) with C = std*sqrt(3)/2^22 (variance of the sum of four
+// U(0,1) is 1/3).
+static inline uint16_t normal_bf16(uint64_t seed, uint32_t tid, uint64_t e, float C) {
+  uint32_t r[4];
+  gen_block(seed, tid, e, r);
+  int32_t S = (int32_t)((r[0] >> 10) + (r[1] >> 10) + (r[2] >> 10) + (r[3] >> 10));
+  float z = (float)(S - (1 << 23));
+  return f2bf(z * C);
+}
+
+extern "C" void orc_gen_normal_bf16(uint64_t seed, uint32_t tid, float std_dev, int64_t n,
+                                    uint16_t* out) {
+  const float C = orc_normal_scale(std_dev);
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < n; ++e) out[e] = normal_bf16(seed, tid, (uint64_t)e, C);
+}
+
+extern "C" void orc_gen_words(uint64_t seed, uint32_t tid, int64_t n_words, uint32_t* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (n_words + 3) / 4; ++i) {
+    uint32_t r[4];
+    gen_block(seed, tid, (uint64_t)i, r);
+    for (int j = 0; j < 4 && 4 * i + j < n_words; ++j) out[4 * i + j] = r[j];
+  }
+}
+
+extern "C" void orc_gen_tokens(uint64_t seed, uint32_t tid, int64_t n, int vocab, int32_t* out) {
+  for (int64_t e = 0; e < n; ++e) {
+    uint32_t r[4];
+    gen_block(seed, tid, (uint64_t)e, r);
+    out[e] = (int32_t)(((uint64_t)r[0] * (uint64_t)vocab) >> 32);
+  }
+}
+
+// Uniform draws for sampling: counter (seq, step, slot, stream), key seed^golden.
+extern "C" uint32_t orc_uniform24(uint64_t seed, uint32_t seq, uint32_t step, uint32_t slot,
+                                  uint32_t stream) {
+  uint32_t c[4] = {seq, step, slot, stream};
+  uint64_t k = seed ^ 0x9E3779B97F4A7C15ull;
+  philox10(c, (uint32_t)k, (uint32_t)(k >> 32));
+  return c[0] >> 8;
+}
+
+// ---------------------------------------------------------------------------
+// Affine group quantization.  Packing (pinned by the reference's
+// debug_layer0_reference.py:53-82): value j of a row sits in word j/(32/bits)
+// at bit offset (j % (32/bits))*bits, LSB first; w = q*scale + bias.
+// The quantize rule (MLX's is unpinned): scale = bf16((max-min)/(2^bits-1)),
+// bias = bf16(min), q = clamp(rint((w - bias)/scale)).  A constant group gets
+// scale 1.  Dequantized value: bf16(fma(scale, q, bias)).
+// ---------------------------------------------------------------------------
+static inline void quantize_group(const uint16_t* w, int n, int bits, uint32_t* words,
+                                  uint16_t* s_out, uint16_t* b_out) {
+  float mn = bf2f(w[0]), mx = bf2f(w[0]);
+  for (int j = 1; j < n; ++j) {
+    float v = bf2f(w[j]);
+    mn = std::min(mn, v);
+    mx = std::max(mx, v);
+  }
+  const int nb = (1 << bits) - 1;
+  uint16_t sb = f2bf((mx - mn) / (float)nb);
+  float sc = bf2f(sb);
+  if (sc == 0.0f) { sb = f2bf(1.0f); sc = 1.0f; }
+  uint16_t bb = f2bf(mn);
+  float bi = bf2f(bb);
+  const int per = 32 / bits;
+  for (int j = 0; j < n / per; ++j) words[j] = 0;
+  for (int j = 0; j < n; ++j) {
+    float qf = std::rint((bf2f(w[j]) - bi) / sc);
+    int q = (int)qf;
+    q = q < 0 ? 0 : (q > nb ? nb : q);
+    words[j / per] |= (uint32_t)q << ((j % per) * bits);
+  }
+  *s_out = sb;
+  *b_out = bb;
+}
+
+static inline int qcode(const uint32_t* row_words, int j, int bits) {
+  const int per = 32 / bits;
+  return (int)((row_words[j / per] >> ((j % per) * bits)) & ((1u << bits) - 1u));
+}
+
+extern "C" int orc_quantize(const uint16_t* w, int N, int K, int group, int bits, uint32_t* wq,
+                            uint16_t* scales, uint16_t* biases) {
+  if ((bits != 4 && bits != 8) || group <= 0 || K % group || group % (32 / bits)) return 1;
+  const int G = K / group, KW = K * bits / 32;
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n)
+    for (int g = 0; g < G; ++g)
+      quantize_group(w + (size_t)n * K + (size_t)g * group, group, bits,
+                     wq + (size_t)n * KW + (size_t)g * group * bits / 32,
+                     scales + (size_t)n * G + g, biases + (size_t)n * G + g);
+  return 0;
+}
+
+extern "C" int orc_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
+                              int N, int K, int group, int bits, uint16_t* out) {
+  if ((bits != 4 && bits != 8) || group <= 0 || K % group) return 1;
+  const int G = K / group, KW = K * bits / 32;
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n)
+    for (int k = 0; k < K; ++k) {
+      float s = bf2f(scales[(size_t)n * G + k / group]);
+      float b = bf2f(biases[(size_t)n * G + k / group]);
+      out[(size_t)n * K + k] = f2bf(std::fma(s, (float)qcode(wq + (size_t)n * KW, k, bits), b));
+    }
+  return 0;
+}
+
+extern "C" int orc_gen_sweep_weights(uint64_t seed, uint32_t tid, int N, int K, int bits,
+                                     uint32_t* wq, uint16_t* scales, uint16_t* biases) {
+  if ((bits != 4 && bits != 8) || K % 64) return 1;
+  orc_gen_words(seed, tid, (int64_t)N * K * bits / 32, wq);
+  const int64_t G = (int64_t)N * (K / 64);
+  const float C = orc_normal_scale(0.02f);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < G; ++i) {
+    uint16_t z = normal_bf16(seed, tid + 1, (uint64_t)i, C);
+    uint16_t s = f2bf(std::fabs(bf2f(z)) / 7.5f);
+    scales[i] = s;
+    biases[i] = f2bf(-8.0f * bf2f(s));
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// quantized_matmul  y[M,N] = x[M,K] . dequant(W[N,K])^T
+// (reference call site: include/mlx-lm/common/quantized_linear.h:82-85).
+// Uses MLX's affine identity  sum_j x_j (s q_j + b) = s sum_j q_j x_j + b sum_j x_j.
+// Canonical fp32 order (group size 64, any bits, independent of M):
+//   quarter c (16 consecutive k):  Q_c = fma chain over j ascending from 0
+//                                  X_c = add chain over j ascending from 0
+//   group g:   d_g  = (Q_4g + Q_4g+1) + (Q_4g+2 + Q_4g+3);   xs_g likewise from X
+//              e_g  = fma(s_g, d_g, b_g * xs_g)
+//   segment (8 groups, missing groups = 0):
+//              t = ((e0+e1)+(e2+e3)) + ((e4+e5)+(e6+e7))
+//   row total: segments added left to right;  y = bf16(total)
+// ---------------------------------------------------------------------------
+static void qmm_block8(const float* xf, const float* xsum, int M, int K, const uint32_t* wq,
+                       const uint16_t* sc, const uint16_t* bi, int n0, int nr, int N,
+                       int bits, uint16_t* y) {
+  const int KW = K * bits / 32, G = K / 64, NSEG = (G + 7) / 8;
+  std::vector<float> qv((size_t)K * 8, 0.0f);
+  float s8[8], b8[8];
+  for (int r = 0; r < nr; ++r) {
+    const uint32_t* row = wq + (size_t)(n0 + r) * KW;
+    for (int k = 0; k < K; ++k) qv[(size_t)k * 8 + r] = (float)qcode(row, k, bits);
+  }
+  for (int m = 0; m < M; ++m) {
+    const float* xr = xf + (size_t)m * K;
+    float tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int seg = 0; seg < NSEG; ++seg) {
+      float e[8][8];
+      for (int gi = 0; gi < 8; ++gi) {
+        const int g = seg * 8 + gi;
+        if (g >= G) {
+          for (int r = 0; r < 8; ++r) e[gi][r] = 0.0f;
+          continue;
+        }
+        float Q[4][8];
+        for (int c = 0; c < 4; ++c) {
+          for (int r = 0; r < 8; ++r) Q[c][r] = 0.0f;
+          for (int j = 0; j < 16; ++j) {
+            const int k = 64 * g + 16 * c + j;
+            const float xv = xr[k];
+            const float* qk = &qv[(size_t)k * 8];
+            for (int r = 0; r < 8; ++r) Q[c][r] = std::fma(qk[r], xv, Q[c][r]);
+          }
+        }
+        for (int r = 0; r < 8; ++r) {
+          s8[r] = r < nr ? bf2f(sc[(size_t)(n0 + r) * G + g]) : 0.0f;
+          b8[r] = r < nr ? bf2f(bi[(size_t)(n0 + r) * G + g]) : 0.0f;
+        }
+        const float xs = xsum[(size_t)m * G + g];
+        for (int r = 0; r < 8; ++r) {
+          float d = (Q[0][r] + Q[1][r]) + (Q[2][r] + Q[3][r]);
+          e[gi][r] = std::fma(s8[r], d, b8[r] * xs);
+        }
+      }
+      for (int r = 0; r < 8; ++r) {
+        float t = ((e[0][r] + e[1][r]) + (e[2][r] + e[3][r])) +
+                  ((e[4][r] + e[5][r]) + (e[6][r] + e[7][r]));
+        tot[r] = seg == 0 ? t : tot[r] + t;
+      }
+    }
+    for (int r = 0; r < nr; ++r) y[(size_t)m * N + n0 + r] = f2bf(tot[r]);
+  }
+}
+
+extern "C" int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* scales,
+                       const uint16_t* biases, uint16_t* y, int M, int N, int K, int group,
+                       int bits) {
+  if (group != 64 || (bits != 4 && bits != 8) || K % 64 || M < 0 || N < 0) return 1;
+  if (M == 0 || N == 0) return 0;
+  const int G = K / 64;
+  std::vector<float> xf((size_t)M * K), xsum((size_t)M * G);
+  for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf2f(x[i]);
+  for (int m = 0; m < M; ++m)
+    for (int g = 0; g < G; ++g) {
+      float X[4];
+      for (int c = 0; c < 4; ++c) {
+        float a = 0.0f;
+        for (int j = 0; j < 16; ++j) a = a + xf[(size_t)m * K + 64 * g + 16 * c + j];
+        X[c] = a;
+      }
+      xsum[(size_t)m * G + g] = (X[0] + X[1]) + (X[2] + X[3]);
+    }
+  const int nblk = (N + 7) / 8;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int n0 = blk * 8, nr = std::min(8, N - n0);
+    qmm_block8(xf.data(), xsum.data(), M, K, wq, scales, biases, n0, nr, N, bits, y);
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// rms_norm (mx::fast::rms_norm; formula debug_numerical_trace.py:103-108)
+//   p_l = fma chain of x_i^2 over i = l, l+32, ... (l = 0..31), from 0
+//   butterfly: for off in 16,8,4,2,1: p_l = p_l + p_(l^off);  ss = p_0
+//   r = 1 / sqrt(ss / dim + eps);   y_i = bf16((x_i * r) * w_i)
+// ---------------------------------------------------------------------------
+static float rms_factor(const float* xr, int dim, float eps) {
+  float p[32];
+  for (int l = 0; l < 32; ++l) {
+    float a = 0.0f;
+    for (int i = l; i < dim; i += 32) a = std::fma(xr[i], xr[i], a);
+    p[l] = a;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    float q[32];
+    for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+    std::memcpy(p, q, sizeof(p));
+  }
+  return 1.0f / std::sqrt(p[0] / (float)dim + eps);
+}
+
+extern "C" void orc_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int dim,
+                             float eps) {
+#pragma omp parallel for schedule(static) if (rows > 64)
+  for (int r = 0; r < rows; ++r) {
+    std::vector<float> xr(dim);
+    for (int i = 0; i < dim; ++i) xr[i] = bf2f(x[(size_t)r * dim + i]);
+    const float f = rms_factor(xr.data(), dim, eps);
+    for (int i = 0; i < dim; ++i) y[(size_t)r * dim + i] = f2bf((xr[i] * f) * bf2f(w[i]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE, NeoX half-split (traditional = false), examples/test_device_rope.cpp:15-46:
+//   inv_freq_i = base^(-2i/dims); theta = pos * inv_freq_i  (double, then fp32
+//   cos/sin table);  rx1 = x1*c - x2*s;  rx2 = x2*c + x1*s  (products rounded
+//   separately, one bf16 rounding at the end)
+// ---------------------------------------------------------------------------
+extern "C" void orc_rope_table(int max_pos, int dims, float base, float* cos_t, float* sin_t) {
+  const int half = dims / 2;
+  for (int p = 0; p < max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      double inv = std::pow((double)base, -2.0 * (double)i / (double)dims);
+      double th = (double)p * inv;
+      cos_t[(size_t)p * half + i] = (float)std::cos(th);
+      sin_t[(size_t)p * half + i] = (float)std::sin(th);
+    }
+}
+
+extern "C" void orc_rope(uint16_t* x, const int32_t* pos, int rows, int heads, int dim,
+                         const float* cos_t, const float* sin_t) {
+  const int half = dim / 2;
+  for (int r = 0; r < rows; ++r)
+    for (int h = 0; h < heads; ++h) {
+      uint16_t* v = x + ((size_t)r * heads + h) * dim;
+      const float* c = cos_t + (size_t)pos[r] * half;
+      const float* s = sin_t + (size_t)pos[r] * half;
+      for (int i = 0; i < half; ++i) {
+        float a = bf2f(v[i]), b = bf2f(v[i + half]);
+        float t1 = a * c[i], t2 = b * s[i], t3 = b * c[i], t4 = a * s[i];
+        v[i] = f2bf(t1 - t2);
+        v[i + half] = f2bf(t3 + t4);
+      }
+    }
+}
+
+// swiglu (include/mlx-lm/common/activations.h:24-33): silu(g) * u with every
+// MLX op materialised in bf16: sg = bf16(sigmoid(g)), a = bf16(g*sg), y = bf16(a*u).
+static inline uint16_t swiglu1(uint16_t g, uint16_t u) {
+  float gf = bf2f(g);
+  float sg = bf2f(f2bf(sigmoid_f(gf)));
+  float a = bf2f(f2bf(gf * sg));
+  return f2bf(a * bf2f(u));
+}
+extern "C" void orc_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = swiglu1(g[i], u[i]);
+}
+extern "C" void orc_add(const uint16_t* a, const uint16_t* b, uint16_t* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = f2bf(bf2f(a[i]) + bf2f(b[i]));
+}
+
+// argmax over the last axis, first maximum wins (NaN never wins).
+extern "C" void orc_argmax(const uint16_t* logits, int rows, int V, int32_t* out) {
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t* l = logits + (size_t)r * V;
+    int best = 0;
+    float bv = -INFINITY;
+    bool any = false;
+    for (int j = 0; j < V; ++j) {
+      float v = bf2f(l[j]);
+      if (v != v) continue;
+      if (!any || v > bv) { bv = v; best = j; any = true; }
+    }
+    out[r] = best;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SDPA for decode / verify (mx::fast::scaled_dot_product_attention with the
+// [T, offset+T] causal mask of src/common/kv_cache.cpp:15-30).  Canonical order:
+//   qs_d = q_d * scale;  keys are taken in splits of 128 (split s = keys
+//   [128s, 128s+128) clipped to the row's visible range 0..offset+t):
+//     score_j = fma chain over d ascending from 0
+//     m_s = max score;  p_j = exp(score_j - m_s)
+//     l_s = add chain of p_j over j ascending from 0
+//     o_s[d] = fma chain of p_j * v_j[d] over j ascending from 0
+//   combine over splits ascending: M = max m_s, w_s = exp(m_s - M),
+//     L = fma(w_s, l_s, L), O[d] = fma(w_s, o_s[d], O[d]) from 0
+//   out[d] = bf16(O[d] / L)
+// ---------------------------------------------------------------------------
+static const int kSdpaSplit = 128;
+
+extern "C" void orc_sdpa(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                         int T, int Hq, int Hkv, int D, int cap, int offset, float scale) {
+  const int G = Hq / Hkv;
+#pragma omp parallel for collapse(2) schedule(dynamic) if (T * Hq > 8)
+  for (int t = 0; t < T; ++t)
+    for (int h = 0; h < Hq; ++h) {
+      const int kvh = h / G, L = offset + t + 1, nsp = (L + kSdpaSplit - 1) / kSdpaSplit;
+      const uint16_t* kb = k + (size_t)kvh * cap * D;
+      const uint16_t* vb = v + (size_t)kvh * cap * D;
+      std::vector<float> qs(D), ms(nsp), ls(nsp), os((size_t)nsp * D), sc(kSdpaSplit);
+      for (int d = 0; d < D; ++d) qs[d] = bf2f(q[((size_t)t * Hq + h) * D + d]) * scale;
+      for (int s = 0; s < nsp; ++s) {
+        const int j0 = s * kSdpaSplit, j1 = std::min(L, j0 + kSdpaSplit);
+        float m = -INFINITY;
+        for (int j = j0; j < j1; ++j) {
+          float a = 0.0f;
+          for (int d = 0; d < D; ++d) a = std::fma(qs[d], bf2f(kb[(size_t)j * D + d]), a);
+          sc[j - j0] = a;
+          m = std::max(m, a);
+        }
+        float l = 0.0f;
+        for (int j = j0; j < j1; ++j) {
+          sc[j - j0] = orc_exp(sc[j - j0] - m);
+          l = l + sc[j - j0];
+        }
+        for (int d = 0; d < D; ++d) {
+          float o = 0.0f;
+          for (int j = j0; j < j1; ++j) o = std::fma(sc[j - j0], bf2f(vb[(size_t)j * D + d]), o);
+          os[(size_t)s * D + d] = o;
+        }
+        ms[s] = m;
+        ls[s] = l;
+      }
+      float M = -INFINITY;
+      for (int s = 0; s < nsp; ++s) M = std::max(M, ms[s]);
+      float Lt = 0.0f;
+      std::vector<float> O(D, 0.0f);
+      for (int s = 0; s < nsp; ++s) {
+        const float w = orc_exp(ms[s] - M);
+        Lt = std::fma(w, ls[s], Lt);
+        for (int d = 0; d < D; ++d) O[d] = std::fma(w, os[(size_t)s * D + d], O[d]);
+      }
+      for (int d = 0; d < D; ++d) out[((size_t)t * Hq + h) * D + d] = f2bf(O[d] / Lt);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Sampling in exact integer arithmetic (the reference's categorical sampler,
+// src/common/generate.cpp:83-120, draws Gumbel noise from MLX's RNG, which is
+// not reproducible; both sides here consume the same caller-supplied 24-bit
+// uniforms instead, and every decision is an exact integer comparison, so the
+// result does not depend on any summation order).
+//   w_j   = rint(exp((l_j - max l) * (1/T)) * 2^32)            (uint64)
+//   top-p: keep the smallest prefix of tokens ordered by (w desc, index asc)
+//          whose mass satisfies 2^24 * kept >= rint(top_p * 2^24) * Z
+//   draw:  smallest index t with 2^24 * cumsum_t(kept w) > u24 * Z_kept
+// Speculative acceptance (Leviathan et al. 2023; Chen et al. 2023):
+//   accept d  iff  u24 * q(d) * Zp < 2^24 * p(d) * Zq
+//   on the first rejection draw from r_j = max(0, p_j Zq - q_j Zp);
+//   after K acceptances draw the bonus token from p_K.
+// ---------------------------------------------------------------------------
+struct Dist {
+  std::vector<uint64_t> w;
+  std::vector<uint8_t> keep;
+  uint64_t Z = 0;
+};
+
+static void make_dist(const uint16_t* l, int V, float temperature, float top_p, Dist& d) {
+  float mx = -INFINITY;
+  for (int j = 0; j < V; ++j) {
+    float v = bf2f(l[j]);
+    if (v == v && v > mx) mx = v;
+  }
+  const float inv_t = 1.0f / temperature;
+  d.w.assign(V, 0);
+  d.keep.assign(V, 0);
+  uint64_t Z = 0;
+  for (int j = 0; j < V; ++j) {
+    float v = bf2f(l[j]);
+    if (v != v) continue;
+    float e = orc_exp((v - mx) * inv_t);
+    d.w[j] = (uint64_t)std::llrint(e * 4294967296.0f);
+    Z += d.w[j];
+  }
+  if (!(top_p > 0.0f && top_p < 1.0f)) {
+    std::fill(d.keep.begin(), d.keep.end(), 1);
+    d.Z = Z;
+    return;
+  }
+  const uint64_t P24 = (uint64_t)std::llrint(top_p * 16777216.0f);
+  std::vector<int> order(V);
+  for (int j = 0; j < V; ++j) order[j] = j;
+  std::sort(order.begin(), order.end(), [&](int a, int b) {
+    return d.w[a] != d.w[b] ? d.w[a] > d.w[b] : a < b;
+  });
+  uint64_t cum = 0;
+  for (int i = 0; i < V; ++i) {
+    d.keep[order[i]] = 1;
+    cum += d.w[order[i]];
+    if (((u128)cum << 24) >= (u128)P24 * Z) break;
+  }
+  d.Z = cum;
+}
+
+static int draw_dist(const Dist& d, uint32_t u24) {
+  const u128 target = (u128)u24 * d.Z;
+  u128 cum = 0;
+  int last = 0;
+  for (size_t j = 0; j < d.w.size(); ++j) {
+    if (!d.keep[j] || d.w[j] == 0) continue;
+    cum += d.w[j];
+    last = (int)j;
+    if ((cum << 24) > target) return (int)j;
+  }
+  return last;
+}
+
+extern "C" int orc_sample(const uint16_t* logits, int V, float temperature, float top_p,
+                          uint32_t u24) {
+  if (temperature <= 0.0f) {
+    int32_t t;
+    orc_argmax(logits, 1, V, &t);
+    return t;
+  }
+  Dist d;
+  make_dist(logits, V, temperature, top_p, d);
+  return draw_dist(d, u24);
+}
+
+extern "C" int orc_accept_greedy(const uint16_t* target_logits, const int32_t* drafts, int K,
+                                 int V, int32_t* out_tokens) {
+  std::vector<int32_t> pred(K + 1);
+  orc_argmax(target_logits, K + 1, V, pred.data());
+  int acc = 0;
+  while (acc < K && pred[acc] == drafts[acc]) {
+    out_tokens[acc] = drafts[acc];
+    ++acc;
+  }
+  out_tokens[acc] = pred[acc];
+  return acc;
+}
+
+extern "C" int orc_accept_stochastic(const uint16_t* target_logits, const uint16_t* draft_logits,
+                                     const int32_t* drafts, int K, int V, float temperature,
+                                     float top_p, const uint32_t* u_accept, uint32_t u_final,
+                                     int32_t* out_tokens) {
+  if (temperature <= 0.0f) return orc_accept_greedy(target_logits, drafts, K, V, out_tokens);
+  Dist p, q;
+  for (int i = 0; i < K; ++i) {
+    make_dist(target_logits + (size_t)i * V, V, temperature, top_p, p);
+    make_dist(draft_logits + (size_t)i * V, V, temperature, top_p, q);
+    const int d = drafts[i];
+    const uint64_t pd = p.keep[d] ? p.w[d] : 0, qd = q.keep[d] ? q.w[d] : 0;
+    if ((u128)u_accept[i] * qd * p.Z < ((u128)pd * q.Z << 24)) {
+      out_tokens[i] = d;
+      continue;
+    }
+    // residual max(0, p - q), drawn by inverse CDF in index order
+    std::vector<u128> r(V);
+    u128 R = 0;
+    for (int j = 0; j < V; ++j) {
+      u128 a = p.keep[j] ? (u128)p.w[j] * q.Z : 0, b = q.keep[j] ? (u128)q.w[j] * p.Z : 0;
+      r[j] = a > b ? a - b : 0;
+      R += r[j];
+    }
+    if (R == 0) {
+      out_tokens[i] = draw_dist(p, u_final);
+      return i;
+    }
+    const u128 target = (u128)u_final * R;
+    u128 cum = 0;
+    int pick = 0;
+    for (int j = 0; j < V; ++j) {
+      if (r[j] == 0) continue;
+      cum += r[j];
+      pick = j;
+      if ((cum << 24) > target) break;
+    }
+    out_tokens[i] = pick;
+    return i;
+  }
+  make_dist(target_logits + (size_t)K * V, V, temperature, top_p, p);
+  out_tokens[K] = draw_dist(p, u_final);
+  return K;
+}
+
+// ---------------------------------------------------------------------------
+// Model (Qwen3 / Llama decoder, src/llm/models/qwen3.cpp:69-220,
+// src/llm/models/llama.cpp:203-469) with synthetic weights:
+// linear and embedding weights N(0,0.02) (Irwin-Hall) in bf16, quantized with
+// the rule above; norm weights are ones (the reference's initialisers,
+// qwen3.cpp:51-52,129-131,159).  Tensor ids: embed 1, lm_head 2,
+// layer l kind k -> (l+1)*16 + k.
+// ---------------------------------------------------------------------------
+namespace {
+struct QW {
+  int N = 0, K = 0;
+  std::vector<uint32_t> w;
+  std::vector<uint16_t> s, b;
+};
+struct Layer {
+  QW w[7];  // q k v o gate up down
+  std::vector<uint16_t> in_norm, post_norm, q_norm, k_norm;
+};
+struct Model {
+  orc_model_cfg c;
+  int bits, group;
+  std::vector<Layer> L;
+  QW embed, lm_head;
+  std::vector<uint16_t> final_norm;
+  int max_pos = 16384;
+  std::vector<float> cos_t, sin_t;
+  const QW& head() const { return c.tied ? embed : lm_head; }
+};
+struct Cache {
+  int L, B, cap, Hk, D, bits;
+  std::vector<std::vector<uint16_t>> k, v;             // bf16 [B][Hk][cap][D]
+  std::vector<std::vector<uint32_t>> kq, vq;           // packed [B][Hk][cap][D*bits/32]
+  std::vector<std::vector<uint16_t>> ks, kb, vs, vb;   // [B][Hk][cap][D/64]
+  std::vector<int> len;
+};
+
+void gen_qw(QW& q, uint64_t seed, uint32_t tid, int N, int K, int bits, int group) {
+  q.N = N;
+  q.K = K;
+  std::vector<uint16_t> tmp((size_t)N * K);
+  orc_gen_normal_bf16(seed, tid, 0.02f, (int64_t)tmp.size(), tmp.data());
+  q.w.resize((size_t)N * K * bits / 32);
+  q.s.resize((size_t)N * (K / group));
+  q.b.resize(q.s.size());
+  orc_quantize(tmp.data(), N, K, group, bits, q.w.data(), q.s.data(), q.b.data());
+}
+
+void qmm(const Model& m, const QW& w, const uint16_t* x, uint16_t* y, int M) {
+  orc_qmm(x, w.w.data(), w.s.data(), w.b.data(), y, M, w.N, w.K, m.group, m.bits);
+}
+}  // namespace
+
+extern "C" void* orc_model_create(const orc_model_cfg* cfg, uint64_t seed) {
+  if (cfg->group != 64 || (cfg->bits != 4 && cfg->bits != 8)) return nullptr;
+  Model* m = new Model();
+  m->c = *cfg;
+  m->bits = cfg->bits;
+  m->group = cfg->group;
+  const int H = cfg->hidden, D = cfg->head_dim, I = cfg->inter;
+  const int NQ = cfg->heads * D, NK = cfg->kv_heads * D;
+  m->L.resize(cfg->layers);
+  for (int l = 0; l < cfg->layers; ++l) {
+    Layer& L = m->L[l];
+    const int shp[7][2] = {{NQ, H}, {NK, H}, {NK, H}, {H, NQ}, {I, H}, {I, H}, {H, I}};
+    for (int k = 0; k < 7; ++k)
+      gen_qw(L.w[k], seed, (uint32_t)((l + 1) * 16 + k), shp[k][0], shp[k][1], m->bits, m->group);
+    L.in_norm.assign(H, f2bf(1.0f));
+    L.post_norm.assign(H, f2bf(1.0f));
+    L.q_norm.assign(D, f2bf(1.0f));
+    L.k_norm.assign(D, f2bf(1.0f));
+  }
+  gen_qw(m->embed, seed, 1, cfg->vocab, H, m->bits, m->group);
+  if (!cfg->tied) gen_qw(m->lm_head, seed, 2, cfg->vocab, H, m->bits, m->group);
+  m->final_norm.assign(H, f2bf(1.0f));
+  m->cos_t.resize((size_t)m->max_pos * D / 2);
+  m->sin_t.resize(m->cos_t.size());
+  orc_rope_table(m->max_pos, D, cfg->rope_theta, m->cos_t.data(), m->sin_t.data());
+  return m;
+}
+
+extern "C" void orc_model_free(void* m) { delete (Model*)m; }
+
+extern "C" int orc_model_weight(void* mp, int layer, int kind, uint32_t* wq, uint16_t* s,
+                                uint16_t* b) {
+  Model& m = *(Model*)mp;
+  const QW* q = nullptr;
+  if (kind == 7) q = &m.embed;
+  else if (kind == 8) q = &m.head();
+  else if (layer >= 0 && layer < (int)m.L.size() && kind >= 0 && kind < 7) q = &m.L[layer].w[kind];
+  if (!q) return 1;
+  std::memcpy(wq, q->w.data(), q->w.size() * 4);
+  std::memcpy(s, q->s.data(), q->s.size() * 2);
+  std::memcpy(b, q->b.data(), q->b.size() * 2);
+  return 0;
+}
+
+extern "C" void* orc_cache_create(void* mp, int n_layers, int batch, int capacity, int kv_bits) {
+  Model& m = *(Model*)mp;
+  if (kv_bits != 16 && kv_bits != 4 && kv_bits != 8) return nullptr;
+  Cache* c = new Cache();
+  c->L = n_layers;
+  c->B = batch;
+  c->cap = capacity;
+  c->Hk = m.c.kv_heads;
+  c->D = m.c.head_dim;
+  c->bits = kv_bits;
+  c->len.assign(batch, 0);
+  const size_t rows = (size_t)batch * c->Hk * capacity;
+  for (int l = 0; l < n_layers; ++l) {
+    if (kv_bits == 16) {
+      c->k.emplace_back(rows * c->D, 0);
+      c->v.emplace_back(rows * c->D, 0);
+    } else {
+      c->kq.emplace_back(rows * c->D * kv_bits / 32, 0);
+      c->vq.emplace_back(rows * c->D * kv_bits / 32, 0);
+      for (auto* a : {&c->ks, &c->kb, &c->vs, &c->vb}) a->emplace_back(rows * (c->D / 64), 0);
+    }
+  }
+  return c;
+}
+extern "C" void orc_cache_free(void* c) { delete (Cache*)c; }
+extern "C" int orc_cache_len(void* c, int b) { return ((Cache*)c)->len[b]; }
+extern "C" void orc_cache_set_position(void* cp, int b, int pos) {
+  Cache& c = *(Cache*)cp;
+  if (pos < c.len[b]) c.len[b] = pos;  // rows past pos are dead (kv_cache.cpp:135-142)
+}
+
+// Forward T tokens per sequence through layers [0, n_layers), then the final
+// norm and lm_head (for every position, or only each sequence's last one).
+static int forward_impl(Model& m, Cache& c, int n_layers, const int32_t* tokens, int B, int T,
+                        uint16_t* logits, bool last_only) {
+  const orc_model_cfg& cf = m.c;
+  const int H = cf.hidden, D = cf.head_dim, Hq = cf.heads, Hk = cf.kv_heads, R = B * T;
+  const int NQ = Hq * D, NK = Hk * D, I = cf.inter, G = H / 64;
+  if (n_layers > c.L || B != c.B) return 1;
+  for (int b = 0; b < B; ++b)
+    if (c.len[b] + T > c.cap || c.len[b] + T > m.max_pos) return 2;
+  std::vector<uint16_t> h((size_t)R * H), xn((size_t)R * H), q((size_t)R * NQ), k((size_t)R * NK),
+      v((size_t)R * NK), o((size_t)R * NQ), a((size_t)R * H), g((size_t)R * I), u((size_t)R * I);
+  // embedding lookup = dequantized row of the packed table
+  for (int r = 0; r < R; ++r) {
+    const int tok = tokens[r];
+    const uint32_t* row = m.embed.w.data() + (size_t)tok * H * m.bits / 32;
+    for (int i = 0; i < H; ++i) {
+      float s = bf2f(m.embed.s[(size_t)tok * G + i / 64]), bb = bf2f(m.embed.b[(size_t)tok * G + i / 64]);
+      h[(size_t)r * H + i] = f2bf(std::fma(s, (float)qcode(row, i, m.bits), bb));
+    }
+  }
+  std::vector<int32_t> pos(R);
+  for (int b = 0; b < B; ++b)
+    for (int t = 0; t < T; ++t) pos[b * T + t] = c.len[b] + t;
+  const float scale = (float)(1.0 / std::sqrt((double)D));
+  for (int l = 0; l < n_layers; ++l) {
+    Layer& L = m.L[l];
+    orc_rms_norm(h.data(), L.in_norm.data(), xn.data(), R, H, cf.eps);
+    qmm(m, L.w[0], xn.data(), q.data(), R);
+    qmm(m, L.w[1], xn.data(), k.data(), R);
+    qmm(m, L.w[2], xn.data(), v.data(), R);
+    if (cf.qk_norm) {
+      orc_rms_norm(q.data(), L.q_norm.data(), q.data(), R * Hq, D, cf.eps);
+      orc_rms_norm(k.data(), L.k_norm.data(), k.data(), R * Hk, D, cf.eps);
+    }
+    orc_rope(q.data(), pos.data(), R, Hq, D, m.cos_t.data(), m.sin_t.data());
+    orc_rope(k.data(), pos.data(), R, Hk, D, m.cos_t.data(), m.sin_t.data());
+    // KV append at each sequence's offset (quantize on append for 4/8-bit)
+    for (int b = 0; b < B; ++b)
+      for (int t = 0; t < T; ++t)
+        for (int hk = 0; hk < Hk; ++hk) {
+          const size_t row = ((size_t)b * Hk + hk) * c.cap + (size_t)(c.len[b] + t);
+          const uint16_t* ks = &k[((size_t)(b * T + t) * Hk + hk) * D];
+          const uint16_t* vs = &v[((size_t)(b * T + t) * Hk + hk) * D];
+          if (c.bits == 16) {
+            std::memcpy(&c.k[l][row * D], ks, D * 2);
+            std::memcpy(&c.v[l][row * D], vs, D * 2);
+          } else {
+            const int WPR = D * c.bits / 32, gpr = D / 64;
+            for (int gi = 0; gi < gpr; ++gi) {
+              quantize_group(ks + 64 * gi, 64, c.bits, &c.kq[l][row * WPR + gi * 64 * c.bits / 32],
+                             &c.ks[l][row * gpr + gi], &c.kb[l][row * gpr + gi]);
+              quantize_group(vs + 64 * gi, 64, c.bits, &c.vq[l][row * WPR + gi * 64 * c.bits / 32],
+                             &c.vs[l][row * gpr + gi], &c.vb[l][row * gpr + gi]);
+            }
+          }
+        }
+    for (int b = 0; b < B; ++b) {
+      const uint16_t* kb;
+      const uint16_t* vb;
+      std::vector<uint16_t> kd, vd;
+      const size_t base = (size_t)b * Hk * c.cap;
+      if (c.bits == 16) {
+        kb = &c.k[l][base * D];
+        vb = &c.v[l][base * D];
+      } else {  // the reference dequantizes the whole cache (kv_cache.cpp:271-298)
+        const int WPR = D * c.bits / 32, gpr = D / 64;
+        kd.assign((size_t)Hk * c.cap * D, 0);
+        vd.assign(kd.size(), 0);
+        for (int hk = 0; hk < Hk; ++hk)
+          for (int j = 0; j < c.len[b] + T; ++j) {
+            const size_t row = base + (size_t)hk * c.cap + j;
+            for (int d = 0; d < D; ++d) {
+              const int gi = d / 64;
+              kd[((size_t)hk * c.cap + j) * D + d] = f2bf(std::fma(bf2f(c.ks[l][row * gpr + gi]),
+                  (float)qcode(&c.kq[l][row * WPR], d, c.bits), bf2f(c.kb[l][row * gpr + gi])));
+              vd[((size_t)hk * c.cap + j) * D + d] = f2bf(std::fma(bf2f(c.vs[l][row * gpr + gi]),
+                  (float)qcode(&c.vq[l][row * WPR], d, c.bits), bf2f(c.vb[l][row * gpr + gi])));
+            }
+          }
+        kb = kd.data();
+        vb = vd.data();
+      }
+      orc_sdpa(&q[(size_t)b * T * NQ], kb, vb, &o[(size_t)b * T * NQ], T, Hq, Hk, D, c.cap,
+               c.len[b], scale);
+    }
+    qmm(m, L.w[3], o.data(), a.data(), R);
+    orc_add(h.data(), a.data(), h.data(), (int64_t)R * H);
+    orc_rms_norm(h.data(), L.post_norm.data(), xn.data(), R, H, cf.eps);
+    qmm(m, L.w[4], xn.data(), g.data(), R);
+    qmm(m, L.w[5], xn.data(), u.data(), R);
+    orc_swiglu(g.data(), u.data(), g.data(), (int64_t)R * I);
+    qmm(m, L.w[6], g.data(), a.data(), R);
+    orc_add(h.data(), a.data(), h.data(), (int64_t)R * H);
+  }
+  for (int b = 0; b < B; ++b) c.len[b] += T;
+  if (!logits) return 0;
+  if (last_only) {
+    std::vector<uint16_t> hl((size_t)B * H);
+    for (int b = 0; b < B; ++b)
+      std::memcpy(&hl[(size_t)b * H], &h[((size_t)b * T + T - 1) * H], H * 2);
+    orc_rms_norm(hl.data(), m.final_norm.data(), hl.data(), B, H, cf.eps);
+    qmm(m, m.head(), hl.data(), logits, B);
+  } else {
+    orc_rms_norm(h.data(), m.final_norm.data(), xn.data(), R, H, cf.eps);
+    qmm(m, m.head(), xn.data(), logits, R);
+  }
+  return 0;
+}
+
+extern "C" int orc_forward(void* model, void* cache, int n_layers, const int32_t* tokens, int B,
+                           int T, uint16_t* logits) {
+  return forward_impl(*(Model*)model, *(Cache*)cache, n_layers, tokens, B, T, logits, false);
+}
+
+// Speculative decode (src/common/generate.cpp:669-933 generalised to a draft
+// model).  Per step and sequence, with p = target length and y = the token at
+// position p (already decided, emitted first -- "d0"):
+//   draft forward over [x_(p-1), y] (re-writes position p-1 so a fully
+//   accepted previous step needs no catch-up), then K-1 single-token forwards;
+//   each draft token is argmax (greedy) or a draw from q (uniform stream 0);
+//   verify: target forward over [y, d1..dK] (K+1 tokens);
+//   accept: greedy prefix match, or rejection sampling (streams 1 and 2);
+//   emit y, d1..d_acc; the next y is the correction / bonus token;
+//   rollback: target length p+acc+1, draft length p+acc.
+extern "C" int orc_spec_generate(void* target, void* draft, const int32_t* prompts, int B, int P,
+                                 const orc_spec_params* prm, int kv_bits, int32_t* out,
+                                 int64_t* stats) {
+  Model& tm = *(Model*)target;
+  Model& dm = draft ? *(Model*)draft : tm;
+  const int dl = draft ? dm.c.layers : prm->draft_layers;
+  const int K = prm->K, V = tm.c.vocab, MT = prm->max_tokens;
+  const bool greedy = !(prm->temperature > 0.0f);
+  if (K < 1 || dl < 1 || dl > dm.c.layers || P < 2 || dm.c.vocab != V) return 1;
+  const int cap = P + MT + K + 8;
+  std::unique_ptr<Cache> tc((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, kv_bits));
+  std::unique_ptr<Cache> dc((Cache*)orc_cache_create(&dm, dl, B, cap, kv_bits));
+  if (!tc || !dc) return 1;
+  std::vector<uint16_t> lg((size_t)B * V);
+  int rc = forward_impl(tm, *tc, tm.c.layers, prompts, B, P, lg.data(), true);
+  if (rc) return rc;
+  std::vector<int32_t> y(B), last(B), pp((size_t)B * (P - 1));
+  for (int b = 0; b < B; ++b) {
+    y[b] = greedy ? orc_sample(&lg[(size_t)b * V], V, 0.0f, 1.0f, 0)
+                  : orc_sample(&lg[(size_t)b * V], V, prm->temperature, prm->top_p,
+                               orc_uniform24(prm->seed, b, 0, 0, 3));
+    last[b] = prompts[(size_t)b * P + P - 1];
+    std::memcpy(&pp[(size_t)b * (P - 1)], &prompts[(size_t)b * P], (P - 1) * 4);
+  }
+  rc = forward_impl(dm, *dc, dl, pp.data(), B, P - 1, nullptr, true);
+  if (rc) return rc;
+  std::vector<int> emitted(B, 0);
+  std::vector<int32_t> d((size_t)B * K), tok2((size_t)B * 2), vt((size_t)B * (K + 1)),
+      outt(K + 1);
+  std::vector<uint16_t> qlog((size_t)B * K * V), tlog((size_t)B * (K + 1) * V);
+  int64_t steps = 0, proposed = 0, accepted = 0;
+  for (uint32_t step = 1;; ++step) {
+    bool any = false;
+    for (int b = 0; b < B; ++b) any |= emitted[b] < MT;
+    if (!any) break;
+    for (int b = 0; b < B; ++b) {
+      tok2[2 * b] = last[b];
+      tok2[2 * b + 1] = y[b];
+    }
+    for (int i = 0; i < K; ++i) {
+      if (i == 0) rc = forward_impl(dm, *dc, dl, tok2.data(), B, 2, lg.data(), true);
+      else {
+        std::vector<int32_t> t1(B);
+        for (int b = 0; b < B; ++b) t1[b] = d[(size_t)b * K + i - 1];
+        rc = forward_impl(dm, *dc, dl, t1.data(), B, 1, lg.data(), true);
+      }
+      if (rc) return rc;
+      for (int b = 0; b < B; ++b) {
+        std::memcpy(&qlog[((size_t)b * K + i) * V], &lg[(size_t)b * V], (size_t)V * 2);
+        d[(size_t)b * K + i] =
+            greedy ? orc_sample(&lg[(size_t)b * V], V, 0.0f, 1.0f, 0)
+                   : orc_sample(&lg[(size_t)b * V], V, prm->temperature, prm->top_p,
+                                orc_uniform24(prm->seed, b, step, i, 0));
+      }
+    }
+    for (int b = 0; b < B; ++b) {
+      vt[(size_t)b * (K + 1)] = y[b];
+      for (int i = 0; i < K; ++i) vt[(size_t)b * (K + 1) + 1 + i] = d[(size_t)b * K + i];
+    }
+    std::vector<int> p0(B);
+    for (int b = 0; b < B; ++b) p0[b] = tc->len[b];
+    rc = forward_impl(tm, *tc, tm.c.layers, vt.data(), B, K + 1, tlog.data(), false);
+    if (rc) return rc;
+    for (int b = 0; b < B; ++b) {
+      int acc;
+      if (greedy) {
+        acc = orc_accept_greedy(&tlog[(size_t)b * (K + 1) * V], &d[(size_t)b * K], K, V, outt.data());
+      } else {
+        std::vector<uint32_t> ua(K);
+        for (int i = 0; i < K; ++i) ua[i] = orc_uniform24(prm->seed, b, step, i, 1);
+        acc = orc_accept_stochastic(&tlog[(size_t)b * (K + 1) * V], &qlog[(size_t)b * K * V],
+                                    &d[(size_t)b * K], K, V, prm->temperature, prm->top_p,
+                                    ua.data(), orc_uniform24(prm->seed, b, step, 0, 2), outt.data());
+      }
+      if (emitted[b] >= MT) {  // finished: recompute the same step, never advance
+        tc->len[b] = p0[b];
+        dc->len[b] = p0[b] - 1;
+        continue;
+      }
+      out[(size_t)b * MT + emitted[b]++] = y[b];
+      for (int i = 0; i < acc; ++i)
+        if (emitted[b] < MT) out[(size_t)b * MT + emitted[b]++] = outt[i];
+      last[b] = acc > 0 ? outt[acc - 1] : y[b];
+      y[b] = outt[acc];
+      tc->len[b] = p0[b] + acc + 1;
+      dc->len[b] = p0[b] + acc;
+      accepted += acc;
+      proposed += K;
+    }
+    steps += 1;
+  }
+  if (stats) {
+    stats[0] = steps;
+    stats[1] = proposed;
+    stats[2] = accepted;
+  }
+  return 0;
+}
+
+extern "C" int orc_generate(void* target, const int32_t* prompts, int B, int P, int max_tokens,
+                            int kv_bits, int32_t* out) {
+  Model& tm = *(Model*)target;
+  const int V = tm.c.vocab;
+  std::unique_ptr<Cache> tc((Cache*)orc_cache_create(&tm, tm.c.layers, B, P + max_tokens + 8, kv_bits));
+  if (!tc) return 1;
+  std::vector<uint16_t> lg((size_t)B * V);
+  int rc = forward_impl(tm, *tc, tm.c.layers, prompts, B, P, lg.data(), true);
+  if (rc) return rc;
+  std::vector<int32_t> y(B);
+  orc_argmax(lg.data(), B, V, y.data());
+  for (int i = 0; i < max_tokens; ++i) {
+    for (int b = 0; b < B; ++b) out[(size_t)b * max_tokens + i] = y[b];
+    if (i + 1 == max_tokens) break;
+    rc = forward_impl(tm, *tc, tm.c.layers, y.data(), B, 1, lg.data(), true);
+    if (rc) return rc;
+    orc_argmax(lg.data(), B, V, y.data());
+  }
+  return 0;
+}
