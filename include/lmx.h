@@ -64,6 +64,83 @@ int lmx_device_error(unsigned* code, int clear);
  * src/common/generate.cpp:43,801).  logits [rows, V] bf16 -> out [rows] int32. */
 int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream);
 
+
+/* ---------------------------------------------------------------------------
+ * Models.  Replaces the ModelContext function table of a loaded Qwen3 /
+ * Llama model (include/mlx-lm/common/model_container.h:20-51; graphs
+ * src/llm/models/qwen3.cpp:69-220, llama.cpp:203-469).  Weights are synthetic
+ * and seeded: linear / embedding weights N(0,0.02) (Irwin-Hall of Philox
+ * draws) in bf16, affine-quantized (group 64) on the device; norms are ones.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  int hidden, layers, inter, heads, kv_heads, head_dim, vocab;
+  float rope_theta, eps;
+  int qk_norm;     /* Qwen3 q/k RMSNorm (1) or none (Llama, 0)           */
+  int tied;        /* lm_head shares the packed embedding                 */
+  int bits;        /* 4 or 8                                              */
+  int group_size;  /* 64                                                  */
+} lmx_model_config;
+
+int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model);
+/* A model that runs only the first n_layers of `model` (shares its weights,
+ * embedding, final norm and lm_head): the self-draft of the speculative
+ * configs.  Free it with lmx_model_free before freeing `model`. */
+int lmx_model_view(void* model, int n_layers, void** view);
+int lmx_model_free(void* model);
+/* Copy one packed weight to host memory (kind: 0 q,1 k,2 v,3 o,4 gate,5 up,
+ * 6 down,7 embed,8 lm_head). */
+int lmx_model_weight(void* model, int layer, int kind, void* w_host, void* s_host, void* b_host);
+
+/* ---------------------------------------------------------------------------
+ * KV cache: KVCacheSimple / QuantizedKVCache (src/common/kv_cache.cpp:34-142,
+ * :243-377).  kv_bits 16 (bf16), 8 or 4 (affine group 64, quantized on
+ * append, dequantized inside SDPA).  Rows are preallocated to `capacity`.
+ * ------------------------------------------------------------------------- */
+int lmx_cache_create(void* model, int n_layers, int batch, int capacity, int kv_bits,
+                     int max_tokens_per_forward, void** cache);
+int lmx_cache_free(void* cache);
+/* KVCacheSimple::set_position (kv_cache.cpp:135-142): roll sequence `seq`
+ * back to `pos` rows (no-op if pos >= its length). */
+int lmx_cache_set_position(void* cache, int seq, int pos);
+int lmx_cache_len(void* cache, int seq, int* len);
+/* ModelContext::call_fn for a [B, T] token block (host ints): runs the first
+ * n_layers, appends K/V at each sequence's length, writes logits [B, T, V]
+ * bf16 to logits_host (may be NULL) and advances the lengths. */
+int lmx_forward(void* model, void* cache, int n_layers, const int32_t* tokens_host, int B, int T,
+                void* logits_host);
+
+/* ---------------------------------------------------------------------------
+ * Speculative decoding: TokenIterator::mtp_speculative_step / next()
+ * (src/common/generate.cpp:669-933, :968-1045) generalised to a draft model.
+ * Per step and sequence: the draft proposes d1..dK, the target verifies
+ * [d0, d1..dK] in one K+1-token pass, the accepted prefix d0..d_acc is
+ * emitted (d0 first, as the reference's emission contract), the correction /
+ * bonus token becomes the next d0 and both caches roll back.  All
+ * bookkeeping runs on the device; one step is replayed as a CUDA graph.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  int batch;        /* independent sequences decoded together            */
+  int K;            /* draft tokens per step (reference n_draft_tokens-1) */
+  int max_tokens;   /* tokens emitted per sequence                       */
+  int prompt_len;
+  int kv_bits;      /* 16, 8 or 4                                        */
+  float temperature;/* 0 = greedy (ArgMaxSampler)                        */
+  float top_p;
+  uint64_t seed;    /* uniform draws of the stochastic path              */
+} lmx_spec_config;
+
+/* draft may be NULL (self-draft: the first draft_layers of target). */
+int lmx_spec_create(void* target, void* draft, int draft_layers, const lmx_spec_config* cfg,
+                    void** spec);
+int lmx_spec_prefill(void* spec, const int32_t* prompts_host /* [batch, prompt_len] */);
+/* Decode until every sequence has emitted max_tokens; *seconds = device time
+ * of the decode loop (prefill excluded). */
+int lmx_spec_decode(void* spec, int use_graph, double* seconds);
+/* out_host [batch, max_tokens]; stats_host[4] = steps, drafts proposed,
+ * drafts accepted, tokens emitted (summed over sequences). */
+int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_host);
+int lmx_spec_free(void* spec);
+
 #ifdef __cplusplus
 }
 #endif

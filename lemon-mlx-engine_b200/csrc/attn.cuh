@@ -1,0 +1,324 @@
+// attn.cuh -- K4 (q/k RMSNorm + RoPE + KV-cache append / quantize) and
+// K2 (split-K decode / verify SDPA over a bf16 or 4/8-bit affine KV cache).
+//
+// Reference: Qwen3Attention::operator() (src/llm/models/qwen3.cpp:69-99):
+// q/k rms_norm per head, NeoX rope at the cache offset, cache->update
+// (KVCacheSimple::update_impl src/common/kv_cache.cpp:34-110, or
+// QuantizedKVCache::update_impl :271-298 which quantizes on append and
+// dequantizes the whole cache for SDPA), then
+// mx::fast::scaled_dot_product_attention with the [T, offset+T] causal mask
+// (src/common/kv_cache.cpp:15-30).  Here the dequantize is fused into the
+// SDPA tile loads and the append into the norm/rope kernel.
+#pragma once
+#include "lmx_common.cuh"
+
+namespace lmx {
+
+static constexpr int kHeadDim = 128;
+static constexpr int kSplit = 128;   // keys per SDPA split (canonical constant)
+static constexpr int kRowTile = 32;  // query rows per SDPA block
+
+struct KvDesc {
+  int B, Hk, cap, bits;        // bits: 16 (bf16) or 4 / 8 (affine, group 64)
+  bf16_t* k;                   // bf16: [B][Hk][cap][D]
+  bf16_t* v;
+  uint32_t* kq;                // quantized: [B][Hk][cap][D*bits/32]
+  uint32_t* vq;
+  bf16_t *ks, *kb, *vs, *vb;   // [B][Hk][cap][D/64]
+  int* len;                    // [B] valid rows per sequence (device)
+};
+
+// ---------------------------------------------------------------------------
+// K4: one warp per (token row, head).  Lane l holds d = l, l+32, l+64, l+96,
+// i.e. both halves of the rope pairs (l, l+64) and (l+32, l+96).
+// RMSNorm canonical order as in norm_argmax.cuh (32 lane partials, butterfly).
+// Quantize rule (per group of 64): scale = bf16((max-min)/(2^bits-1)) (1 if
+// zero), bias = bf16(min), q = clamp(rint((x - bias)/scale)).
+// ---------------------------------------------------------------------------
+struct PrepArgs {
+  const bf16_t* qkv;      // [R, ldq]: q heads, k heads, v heads
+  int ldq;
+  int R, T, Hq, Hk;
+  const bf16_t* qn;       // q_norm weight [D] or null (no q/k norm)
+  const bf16_t* kn;
+  float eps;
+  const float* cos_t;     // [max_pos][D/2]
+  const float* sin_t;
+  int max_pos;
+  bf16_t* q_out;          // [R, Hq*D]
+  KvDesc kv;
+  unsigned* err;
+};
+
+LMX_DEV void quant_pack_group(const float* vals /*smem [64]*/, int bits, uint32_t* words,
+                              bf16_t* s_out, bf16_t* b_out, int lane, float mn, float mx) {
+  const int nb = (1 << bits) - 1;
+  bf16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), (float)nb));
+  float sc = bf2f(sb);
+  if (sc == 0.0f) { sb = f2bf(1.0f); sc = 1.0f; }
+  bf16_t bb = f2bf(mn);
+  const float bi = bf2f(bb);
+  const int per = 32 / bits, nwords = 64 / per;
+  if (lane < nwords) {
+    uint32_t w = 0;
+    for (int j = 0; j < per; ++j) {
+      int q = (int)rintf(__fdiv_rn(__fsub_rn(vals[lane * per + j], bi), sc));
+      q = q < 0 ? 0 : (q > nb ? nb : q);
+      w |= (uint32_t)q << (j * bits);
+    }
+    words[lane] = w;
+  }
+  if (lane == 0) { *s_out = sb; *b_out = bb; }
+}
+
+__global__ void __launch_bounds__(256) attn_prep_kernel(PrepArgs a) {
+  __shared__ float stage[8][kHeadDim];
+  grid_wait();
+  grid_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nh = a.Hq + 2 * a.Hk;
+  const int task = blockIdx.x * 8 + warp;
+  if (task >= a.R * nh) return;
+  const int r = task / nh, h = task % nh;
+  const int b = r / a.T, t = r % a.T;
+  const int pos = a.kv.len[b] + t;
+  if (pos >= a.kv.cap || pos >= a.max_pos) {
+    if (lane == 0 && a.err) atomicExch(a.err, 0x41u);
+    return;
+  }
+  const bf16_t* src = a.qkv + (size_t)r * a.ldq + (size_t)h * kHeadDim;
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = bf2f(src[lane + 32 * i]);
+  const bool is_q = h < a.Hq, is_k = !is_q && h < a.Hq + a.Hk;
+  if (is_q || is_k) {
+    const bf16_t* nw = is_q ? a.qn : a.kn;
+    if (nw) {
+      float p = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p = __fmaf_rn(x[i], x[i], p);
+      p = warp_sum_xor(p, 16, 1);
+      const float f = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)kHeadDim), a.eps)));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = bf2f(f2bf(__fmul_rn(__fmul_rn(x[i], f), bf2f(nw[lane + 32 * i]))));
+    }
+    // NeoX rope: pairs (d, d+64)
+    const float* ct = a.cos_t + (size_t)pos * (kHeadDim / 2);
+    const float* st = a.sin_t + (size_t)pos * (kHeadDim / 2);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int d = lane + 32 * i;
+      const float c = ct[d], s = st[d];
+      const float u = x[i], w = x[i + 2];
+      x[i] = bf2f(f2bf(__fsub_rn(__fmul_rn(u, c), __fmul_rn(w, s))));
+      x[i + 2] = bf2f(f2bf(__fadd_rn(__fmul_rn(w, c), __fmul_rn(u, s))));
+    }
+  }
+  if (is_q) {
+    bf16_t* dst = a.q_out + (size_t)r * a.Hq * kHeadDim + (size_t)h * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f2bf(x[i]);
+    return;
+  }
+  const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hk;
+  const size_t row = ((size_t)b * a.kv.Hk + hk) * a.kv.cap + pos;
+  if (a.kv.bits == 16) {
+    bf16_t* dst = (is_k ? a.kv.k : a.kv.v) + row * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f2bf(x[i]);
+    return;
+  }
+  // quantize two groups of 64 (group 0 = d < 64 -> x[0], x[1]; group 1 -> x[2], x[3])
+  float* sv = stage[warp];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sv[lane + 32 * i] = x[i];
+  __syncwarp();
+  const int bits = a.kv.bits, wpr = kHeadDim * bits / 32;
+  uint32_t* words = (is_k ? a.kv.kq : a.kv.vq) + row * wpr;
+  bf16_t* so = (is_k ? a.kv.ks : a.kv.vs) + row * 2;
+  bf16_t* bo = (is_k ? a.kv.kb : a.kv.vb) + row * 2;
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    float mn = fminf(x[2 * gi], x[2 * gi + 1]), mx = fmaxf(x[2 * gi], x[2 * gi + 1]);
+    for (int off = 16; off >= 1; off >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+    quant_pack_group(sv + 64 * gi, bits, words + gi * (64 * bits / 32), so + gi, bo + gi, lane, mn, mx);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K2: split-K SDPA.  Grid (nsplit_max * row_tiles, Hk, B); 256 threads.
+// Query rows of one (b, kv head): r = t*G + g (head kvh*G + g), tiled by 32.
+// Canonical order (identical to oracle orc_sdpa):
+//   qs = q * scale; score = fma chain over d ascending from 0
+//   m_s = max over visible keys of the split; p = exp(score - m_s)
+//   l_s = butterfly of 32 lane partials (lane l: keys j0+l+32k ascending)
+//   o_s[d] = fma chain of p_j v_j[d] over the split's keys ascending from 0
+//   combine (last block of the tile, splits ascending):
+//     M = max m_s, w = exp(m_s - M), L = fma(w, l_s, L), O = fma(w, o_s, O)
+//   out = bf16(O / L)
+// Scratch (caller-owned): partials [B][Hk][tiles][nsplit][32][130] floats and
+// counters [B][Hk][tiles] (zero at rest; the combining block resets its own).
+// ---------------------------------------------------------------------------
+struct SdpaArgs {
+  const bf16_t* q;        // [B*T, Hq*D] roped queries
+  KvDesc kv;
+  int T, Hq;
+  float scale;
+  int nsplit;             // splits per row tile in the grid (>= ceil(max len / 128))
+  int tiles;
+  float* part;            // scratch partials
+  unsigned* counters;     // scratch counters
+  bf16_t* out;            // [B*T, Hq*D]
+};
+
+static constexpr int kPartStride = kHeadDim + 2;  // m, l, o[128]
+
+LMX_DEV float kv_elem(const KvDesc& kv, bool is_k, size_t row, int d) {
+  if (kv.bits == 16) return bf2f((is_k ? kv.k : kv.v)[row * kHeadDim + d]);
+  const int bits = kv.bits, per = 32 / bits;
+  const uint32_t w = (is_k ? kv.kq : kv.vq)[row * (kHeadDim * bits / 32) + d / per];
+  const int q = (int)((w >> ((d % per) * bits)) & ((1u << bits) - 1u));
+  const float s = bf2f((is_k ? kv.ks : kv.vs)[row * 2 + d / 64]);
+  const float b = bf2f((is_k ? kv.kb : kv.vb)[row * 2 + d / 64]);
+  return bf2f(f2bf(__fmaf_rn(s, (float)q, b)));
+}
+
+__global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  bf16_t* Kt = reinterpret_cast<bf16_t*>(smem);                 // [D][kSplit] (transposed)
+  bf16_t* Vs = Kt + kHeadDim * kSplit;                           // [kSplit][D]
+  float* Qs = reinterpret_cast<float*>(Vs + kSplit * kHeadDim);  // [32][D]
+  float* S = Qs + kRowTile * kHeadDim;                           // [32][kSplit]
+  __shared__ bool is_last;
+
+  grid_wait();
+  grid_launch_dependents();
+  const int split = blockIdx.x % a.nsplit, tile = blockIdx.x / a.nsplit;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int G = a.Hq / a.kv.Hk, rows = G * a.T;
+  const int r0 = tile * kRowTile, nr = min(kRowTile, rows - r0);
+  if (nr <= 0) return;
+  const int off = a.kv.len[b];
+  const int t_last = (r0 + nr - 1) / G;
+  const int jmax = off + t_last + 1;  // keys visible to the tile's last row
+  const int tile_splits = (jmax + kSplit - 1) / kSplit;
+  if (split >= tile_splits) return;
+  const int j0 = split * kSplit, jn = min(kSplit, jmax - j0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t kvrow0 = ((size_t)b * a.kv.Hk + kvh) * a.kv.cap + j0;
+
+  // stage K (transposed), V and the scaled queries
+  for (int e = tid; e < kSplit * kHeadDim; e += 256) {
+    const int j = e / kHeadDim, d = e % kHeadDim;
+    float kv_k = 0.0f, kv_v = 0.0f;
+    if (j < jn) {
+      kv_k = kv_elem(a.kv, true, kvrow0 + j, d);
+      kv_v = kv_elem(a.kv, false, kvrow0 + j, d);
+    }
+    Kt[d * kSplit + j] = f2bf(kv_k);
+    Vs[j * kHeadDim + d] = f2bf(kv_v);
+  }
+  for (int e = tid; e < kRowTile * kHeadDim; e += 256) {
+    const int rr = e / kHeadDim, d = e % kHeadDim;
+    float qv = 0.0f;
+    if (rr < nr) {
+      const int r = r0 + rr, t = r / G, g = r % G;
+      qv = __fmul_rn(bf2f(a.q[((size_t)b * a.T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + g) * kHeadDim + d]),
+                     a.scale);
+    }
+    Qs[e] = qv;
+  }
+  __syncthreads();
+
+  // scores: thread (key j, row parity)
+  {
+    const int j = tid & (kSplit - 1), rp = tid >> 7;
+    for (int rr = rp; rr < nr; rr += 2) {
+      const float* qr = Qs + rr * kHeadDim;
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int d = 0; d < kHeadDim; ++d) acc = __fmaf_rn(qr[d], bf2f(Kt[d * kSplit + j]), acc);
+      S[rr * kSplit + j] = acc;
+    }
+  }
+  __syncthreads();
+
+  // softmax statistics per row: one warp per row
+  float* part_base = a.part + ((((size_t)b * a.kv.Hk + kvh) * a.tiles + tile) * a.nsplit + split) *
+                                  (size_t)kRowTile * kPartStride;
+  for (int rr = warp; rr < nr; rr += 8) {
+    const int t = (r0 + rr) / G;
+    const int vis = min(jn, off + t + 1 - j0);  // visible keys of this row in the split (may be <= 0)
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kSplit / 32; ++k) {
+      const int j = lane + 32 * k;
+      if (j < vis) m = fmaxf(m, S[rr * kSplit + j]);
+    }
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float lp = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kSplit / 32; ++k) {
+      const int j = lane + 32 * k;
+      float p = 0.0f;
+      if (j < vis) p = exp_c(__fsub_rn(S[rr * kSplit + j], m));
+      S[rr * kSplit + j] = p;
+      lp = __fadd_rn(lp, p);
+    }
+    lp = warp_sum_xor(lp, 16, 1);
+    if (lane == 0) {
+      part_base[rr * kPartStride + 0] = m;
+      part_base[rr * kPartStride + 1] = lp;
+    }
+  }
+  __syncthreads();
+
+  // o[d] = sum_j p_j v_j[d] : thread (d, row parity), chain over the split's keys
+  {
+    const int d = tid & (kHeadDim - 1), rp = tid >> 7;
+    for (int rr = rp; rr < nr; rr += 2) {
+      const float* pr = S + rr * kSplit;
+      float acc = 0.0f;
+      for (int j = 0; j < jn; ++j) acc = __fmaf_rn(pr[j], bf2f(Vs[j * kHeadDim + d]), acc);
+      part_base[rr * kPartStride + 2 + d] = acc;
+    }
+  }
+
+  // last block of this (b, kvh, tile) combines
+  __threadfence();
+  __syncthreads();
+  unsigned* ctr = a.counters + ((size_t)b * a.kv.Hk + kvh) * a.tiles + tile;
+  if (tid == 0) {
+    unsigned prev = atomicAdd(ctr, 1u);
+    is_last = prev + 1 == (unsigned)tile_splits;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float* pbase = a.part + (((size_t)b * a.kv.Hk + kvh) * a.tiles + tile) * a.nsplit *
+                                    (size_t)kRowTile * kPartStride;
+  for (int e = tid; e < nr * kHeadDim; e += 256) {
+    const int rr = e / kHeadDim, d = e % kHeadDim;
+    float M = -INFINITY;
+    for (int s = 0; s < tile_splits; ++s) M = fmaxf(M, pbase[((size_t)s * kRowTile + rr) * kPartStride]);
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < tile_splits; ++s) {
+      const float* ps = pbase + ((size_t)s * kRowTile + rr) * kPartStride;
+      const float w = exp_c(__fsub_rn(ps[0], M));
+      L = __fmaf_rn(w, ps[1], L);
+      O = __fmaf_rn(w, ps[2 + d], O);
+    }
+    const int r = r0 + rr, t = r / G, g = r % G;
+    a.out[((size_t)b * a.T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + g) * kHeadDim + d] =
+        f2bf(__fdiv_rn(O, L));
+  }
+  if (tid == 0) *ctr = 0u;
+}
+
+static constexpr size_t kSdpaSmem = (size_t)kHeadDim * kSplit * 2 * 2 +
+                                    (size_t)kRowTile * kHeadDim * 4 + (size_t)kRowTile * kSplit * 4;
+
+}  // namespace lmx

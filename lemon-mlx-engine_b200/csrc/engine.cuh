@@ -1,0 +1,785 @@
+// engine.cuh -- the C++ host side of the speculative-decode path: model
+// weights, KV caches, the verify / draft forward graph and the speculative
+// loop.  It mirrors the reference's TokenIterator contract
+// (src/common/generate.cpp:669-933, :968-1045): d0 is emitted first, then the
+// accepted drafts; the next d0 is the correction / bonus token; the target
+// cache is rolled back to p+acc+1.  Everything per step stays on the device
+// and one step is captured as a CUDA graph.
+#pragma once
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "lmx_internal.h"
+
+namespace lmx {
+
+// ---------------------------------------------------------------------------
+// launchers of the attention / engine kernels
+// ---------------------------------------------------------------------------
+static int launch_attn_prep(const PrepArgs& a, cudaStream_t st) {
+  const int tasks = a.R * (a.Hq + 2 * a.Hk);
+  if (tasks == 0) return LMX_OK;
+  return cuda_check(lmx_launch(attn_prep_kernel, dim3((tasks + 7) / 8), dim3(256), 0, st, true, a),
+                    "attn_prep: launch");
+}
+
+static int launch_sdpa(const SdpaArgs& a, int B, cudaStream_t st) {
+  static bool attr_set[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (!attr_set[d & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(sdpa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kSdpaSmem),
+                        "sdpa: set smem");
+    if (rc) return rc;
+    attr_set[d & 63] = true;
+  }
+  return cuda_check(lmx_launch(sdpa_split_kernel, dim3(a.nsplit * a.tiles, a.kv.Hk, B), dim3(256), kSdpaSmem,
+                               st, true, a),
+                    "sdpa: launch");
+}
+
+static int launch_cluster_rows(void (*kern)(const bf16_t*, int, SpecState, int, int), int rows,
+                               const bf16_t* logits, int V, const SpecState& s, int i, int adv,
+                               cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows * kArgmaxCluster);
+  cfg.blockDim = dim3(512);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kArgmaxCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kern, logits, V, s, i, adv), "draft_argmax: launch");
+}
+
+// ---------------------------------------------------------------------------
+// device memory arena (setup-time allocations only)
+// ---------------------------------------------------------------------------
+struct DevBuf {
+  void* p = nullptr;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { if (p) cudaFree(p); }
+};
+
+struct Arena {
+  std::vector<std::unique_ptr<DevBuf>> bufs;
+  template <typename T>
+  int alloc(T** out, size_t count, bool zero = true) {
+    auto b = std::make_unique<DevBuf>();
+    const size_t bytes = count * sizeof(T) > 0 ? count * sizeof(T) : 16;
+    if (cudaMalloc(&b->p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(LMX_ERR_OOM, "cudaMalloc(%zu) failed", bytes);
+    }
+    if (zero && cudaMemset(b->p, 0, bytes) != cudaSuccess) return cuda_check(cudaGetLastError(), "memset");
+    *out = (T*)b->p;
+    bufs.push_back(std::move(b));
+    return LMX_OK;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct QWeight {
+  uint32_t* w = nullptr;
+  bf16_t* s = nullptr;
+  bf16_t* b = nullptr;
+  int N = 0, K = 0;
+  QMat mat() const {
+    QMat m;
+    m.w = w;
+    m.s = s;
+    m.b = b;
+    m.rows = N;
+    return m;
+  }
+};
+
+struct Layer {
+  QWeight w[7];  // q k v o gate up down
+  bf16_t *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct Model {
+  lmx_model_config c;
+  int n_layers = 0;  // layers this (possibly view) model runs
+  std::vector<Layer> L;
+  QWeight embed, lm_head;
+  bf16_t* final_norm = nullptr;
+  float *cos_t = nullptr, *sin_t = nullptr;
+  int max_pos = 16384;
+  std::shared_ptr<Arena> arena;  // shared by views
+  const QWeight& head() const { return c.tied ? embed : lm_head; }
+};
+
+static int gen_qweight(Arena& ar, QWeight& q, uint64_t seed, uint32_t tid, int N, int K, int bits,
+                       cudaStream_t st) {
+  q.N = N;
+  q.K = K;
+  int rc = ar.alloc(&q.w, (size_t)N * K * bits / 32, false);
+  if (!rc) rc = ar.alloc(&q.s, (size_t)N * (K / 64), false);
+  if (!rc) rc = ar.alloc(&q.b, (size_t)N * (K / 64), false);
+  if (rc) return rc;
+  const float C = (float)((double)0.02f * std::sqrt(3.0) / 4194304.0);
+  const int64_t groups = (int64_t)N * (K / 64);
+  gen_qweight_kernel<<<(unsigned)((groups + 127) / 128), 128, 0, st>>>(seed, tid, N, K, bits, C, q.w, q.s, q.b);
+  return cuda_check(cudaGetLastError(), "gen_qweight");
+}
+
+static int fill_ones(Arena& ar, bf16_t** p, int n, cudaStream_t st) {
+  int rc = ar.alloc(p, n, false);
+  if (rc) return rc;
+  fill_bf16_kernel<<<(n + 255) / 256, 256, 0, st>>>(*p, n, (bf16_t)0x3F80);
+  return cuda_check(cudaGetLastError(), "fill");
+}
+
+static int model_create(const lmx_model_config& c, uint64_t seed, Model** out) {
+  if (c.group_size != 64 || (c.bits != 4 && c.bits != 8) || c.head_dim != kHeadDim ||
+      c.hidden % 512 || c.heads % c.kv_heads || c.layers < 1 || c.vocab < 1)
+    return set_error(LMX_ERR_UNSUPPORTED, "model config not supported (head_dim 128, group 64, 4/8-bit)");
+  auto m = std::make_unique<Model>();
+  m->c = c;
+  m->n_layers = c.layers;
+  m->arena = std::make_shared<Arena>();
+  Arena& ar = *m->arena;
+  const int H = c.hidden, D = c.head_dim, I = c.inter, NQ = c.heads * D, NK = c.kv_heads * D;
+  cudaStream_t st = 0;
+  m->L.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const int shp[7][2] = {{NQ, H}, {NK, H}, {NK, H}, {H, NQ}, {I, H}, {I, H}, {H, I}};
+    for (int k = 0; k < 7; ++k) {
+      int rc = gen_qweight(ar, m->L[l].w[k], seed, (uint32_t)((l + 1) * 16 + k), shp[k][0], shp[k][1], c.bits, st);
+      if (rc) return rc;
+    }
+    int rc = fill_ones(ar, &m->L[l].in_norm, H, st);
+    if (!rc) rc = fill_ones(ar, &m->L[l].post_norm, H, st);
+    if (!rc) rc = fill_ones(ar, &m->L[l].q_norm, D, st);
+    if (!rc) rc = fill_ones(ar, &m->L[l].k_norm, D, st);
+    if (rc) return rc;
+  }
+  int rc = gen_qweight(ar, m->embed, seed, 1, c.vocab, H, c.bits, st);
+  if (!rc && !c.tied) rc = gen_qweight(ar, m->lm_head, seed, 2, c.vocab, H, c.bits, st);
+  if (!rc) rc = fill_ones(ar, &m->final_norm, H, st);
+  if (rc) return rc;
+  // RoPE table: inv_freq_i = base^(-2i/D), theta = pos*inv_freq (double), fp32 cos/sin
+  std::vector<float> ct((size_t)m->max_pos * D / 2), stt(ct.size());
+  for (int p = 0; p < m->max_pos; ++p)
+    for (int i = 0; i < D / 2; ++i) {
+      const double th = (double)p * std::pow((double)c.rope_theta, -2.0 * (double)i / (double)D);
+      ct[(size_t)p * D / 2 + i] = (float)std::cos(th);
+      stt[(size_t)p * D / 2 + i] = (float)std::sin(th);
+    }
+  rc = ar.alloc(&m->cos_t, ct.size(), false);
+  if (!rc) rc = ar.alloc(&m->sin_t, stt.size(), false);
+  if (rc) return rc;
+  rc = cuda_check(cudaMemcpy(m->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice), "rope table");
+  if (!rc) rc = cuda_check(cudaMemcpy(m->sin_t, stt.data(), stt.size() * 4, cudaMemcpyHostToDevice), "rope table");
+  if (!rc) rc = cuda_check(cudaDeviceSynchronize(), "model init");
+  if (rc) return rc;
+  *out = m.release();
+  return LMX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// KV cache (KVCacheSimple / QuantizedKVCache, src/common/kv_cache.cpp):
+// preallocated to `capacity` rows; lengths live on the device.
+// ---------------------------------------------------------------------------
+struct Cache {
+  int n_layers = 0, B = 0, cap = 0, bits = 16, Hk = 0;
+  std::vector<KvDesc> kv;
+  int* len = nullptr;
+  Arena ar;
+};
+
+static int cache_create(const Model& m, int n_layers, int B, int cap, int bits, Cache** out) {
+  if (bits != 16 && bits != 4 && bits != 8) return set_error(LMX_ERR_UNSUPPORTED, "kv_bits %d", bits);
+  if (n_layers < 1 || n_layers > m.n_layers || B < 1 || cap < 1 || cap > m.max_pos)
+    return set_error(LMX_ERR_INVALID, "cache: bad arguments");
+  auto c = std::make_unique<Cache>();
+  c->n_layers = n_layers;
+  c->B = B;
+  c->cap = cap;
+  c->bits = bits;
+  c->Hk = m.c.kv_heads;
+  int rc = c->ar.alloc(&c->len, B);
+  if (rc) return rc;
+  const size_t rows = (size_t)B * c->Hk * cap;
+  c->kv.resize(n_layers);
+  for (int l = 0; l < n_layers; ++l) {
+    KvDesc& d = c->kv[l];
+    std::memset(&d, 0, sizeof(d));
+    d.B = B;
+    d.Hk = c->Hk;
+    d.cap = cap;
+    d.bits = bits;
+    d.len = c->len;
+    if (bits == 16) {
+      rc = c->ar.alloc(&d.k, rows * kHeadDim);
+      if (!rc) rc = c->ar.alloc(&d.v, rows * kHeadDim);
+    } else {
+      rc = c->ar.alloc(&d.kq, rows * kHeadDim * bits / 32);
+      if (!rc) rc = c->ar.alloc(&d.vq, rows * kHeadDim * bits / 32);
+      if (!rc) rc = c->ar.alloc(&d.ks, rows * 2);
+      if (!rc) rc = c->ar.alloc(&d.kb, rows * 2);
+      if (!rc) rc = c->ar.alloc(&d.vs, rows * 2);
+      if (!rc) rc = c->ar.alloc(&d.vb, rows * 2);
+    }
+    if (rc) return rc;
+  }
+  *out = c.release();
+  return LMX_OK;
+}
+
+}  // namespace lmx
+
+namespace lmx {
+
+// ---------------------------------------------------------------------------
+// activation workspace (sized at setup for the largest forward)
+// ---------------------------------------------------------------------------
+static constexpr int kPrefillChunk = 32;
+
+struct Workspace {
+  int Rmax = 0, tiles = 0, splits = 0, B = 0, Hk = 0;
+  bf16_t *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *o = nullptr, *act = nullptr,
+         *logits = nullptr;
+  float* part = nullptr;
+  unsigned* counters = nullptr;
+  Arena ar;
+};
+
+static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_rows, Workspace& ws) {
+  const lmx_model_config& c = m.c;
+  const int R = B * Tmax, NQ = c.heads * kHeadDim, NK = c.kv_heads * kHeadDim;
+  const int G = c.heads / c.kv_heads;
+  ws.Rmax = R;
+  ws.B = B;
+  ws.Hk = c.kv_heads;
+  ws.tiles = (G * Tmax + kRowTile - 1) / kRowTile;
+  ws.splits = (cap + kSplit - 1) / kSplit;
+  int rc = ws.ar.alloc(&ws.h, (size_t)R * c.hidden);
+  if (!rc) rc = ws.ar.alloc(&ws.xn, (size_t)R * (c.hidden > c.inter ? c.hidden : c.inter));
+  if (!rc) rc = ws.ar.alloc(&ws.qkv, (size_t)R * (NQ + 2 * NK));
+  if (!rc) rc = ws.ar.alloc(&ws.q, (size_t)R * NQ);
+  if (!rc) rc = ws.ar.alloc(&ws.o, (size_t)R * NQ);
+  if (!rc) rc = ws.ar.alloc(&ws.act, (size_t)R * c.inter);
+  if (!rc) rc = ws.ar.alloc(&ws.logits, (size_t)logit_rows * c.vocab);
+  if (!rc)
+    rc = ws.ar.alloc(&ws.part, (size_t)B * c.kv_heads * ws.tiles * ws.splits * kRowTile * kPartStride, false);
+  if (!rc) rc = ws.ar.alloc(&ws.counters, (size_t)B * c.kv_heads * ws.tiles);
+  return rc;
+}
+
+// One forward of T tokens per sequence through layers [0, n_layers) of m,
+// appending K/V at each sequence's device-side cache length (the caller
+// advances the lengths).  Per layer: qkv GEMV (+fused RMSNorm) -> q/k norm,
+// RoPE, KV append -> SDPA -> o_proj GEMV (+residual) -> gate|up GEMV
+// (+RMSNorm, SwiGLU) -> down GEMV (+residual); then the final norm and the
+// lm_head for every row or only each sequence's last row.
+static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, int tok_ld, int tok_off,
+                   int B, int T, Workspace& ws, bf16_t* logits, bool last_only, cudaStream_t st) {
+  const lmx_model_config& cf = m.c;
+  const int H = cf.hidden, I = cf.inter, Hq = cf.heads, Hk = cf.kv_heads;
+  const int NQ = Hq * kHeadDim, NK = Hk * kHeadDim, G = Hq / Hk, R = B * T;
+  if (R > ws.Rmax || B != c.B || n_layers > c.n_layers || n_layers > m.n_layers)
+    return set_error(LMX_ERR_INVALID, "forward: shape exceeds workspace");
+  const int tiles = (G * T + kRowTile - 1) / kRowTile, splits = (c.cap + kSplit - 1) / kSplit;
+  if (tiles > ws.tiles || splits > ws.splits || B > ws.B || Hk != ws.Hk)
+    return set_error(LMX_ERR_INVALID, "forward: attention scratch too small");
+  const bool fuse = R <= kQmmMaxNormRows;
+  int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
+                                 (const uint32_t*)m.embed.w, (const bf16_t*)m.embed.s,
+                                 (const bf16_t*)m.embed.b, H, cf.bits, ws.h, R),
+                      "embed");
+  if (rc) return rc;
+  const float scale = (float)(1.0 / std::sqrt((double)kHeadDim));
+  for (int l = 0; l < n_layers && !rc; ++l) {
+    const Layer& L = m.L[l];
+    QmmCall qc;
+    if (fuse) {
+      qc.x = ws.h;
+      qc.norm_w = L.in_norm;
+    } else {
+      rc = launch_rms_norm(ws.h, L.in_norm, ws.xn, R, H, cf.eps, st);
+      qc.x = ws.xn;
+    }
+    qc.eps = cf.eps;
+    qc.mat[0] = L.w[0].mat();
+    qc.mat[1] = L.w[1].mat();
+    qc.mat[2] = L.w[2].mat();
+    qc.nmat = 3;
+    qc.N = NQ + 2 * NK;
+    qc.y = ws.qkv;
+    qc.ldy = qc.N;
+    qc.M = R;
+    qc.K = H;
+    qc.bits = cf.bits;
+    if (!rc) rc = launch_qmm(qc, st);
+
+    PrepArgs pa;
+    pa.qkv = ws.qkv;
+    pa.ldq = NQ + 2 * NK;
+    pa.R = R;
+    pa.T = T;
+    pa.Hq = Hq;
+    pa.Hk = Hk;
+    pa.qn = cf.qk_norm ? L.q_norm : nullptr;
+    pa.kn = cf.qk_norm ? L.k_norm : nullptr;
+    pa.eps = cf.eps;
+    pa.cos_t = m.cos_t;
+    pa.sin_t = m.sin_t;
+    pa.max_pos = m.max_pos;
+    pa.q_out = ws.q;
+    pa.kv = c.kv[l];
+    pa.err = device_error_word();
+    if (!rc) rc = launch_attn_prep(pa, st);
+
+    SdpaArgs sa;
+    sa.q = ws.q;
+    sa.kv = c.kv[l];
+    sa.T = T;
+    sa.Hq = Hq;
+    sa.scale = scale;
+    sa.nsplit = splits;
+    sa.tiles = tiles;
+    sa.part = ws.part;
+    sa.counters = ws.counters;
+    sa.out = ws.o;
+    if (!rc) rc = launch_sdpa(sa, B, st);
+
+    QmmCall oc;
+    oc.x = ws.o;
+    oc.mat[0] = L.w[3].mat();
+    oc.N = H;
+    oc.y = ws.h;
+    oc.ldy = H;
+    oc.res = ws.h;
+    oc.M = R;
+    oc.K = NQ;
+    oc.bits = cf.bits;
+    oc.mode = kResid;
+    if (!rc) rc = launch_qmm(oc, st);
+
+    QmmCall gc;
+    if (fuse) {
+      gc.x = ws.h;
+      gc.norm_w = L.post_norm;
+    } else {
+      if (!rc) rc = launch_rms_norm(ws.h, L.post_norm, ws.xn, R, H, cf.eps, st);
+      gc.x = ws.xn;
+    }
+    gc.eps = cf.eps;
+    gc.mat[0] = L.w[4].mat();
+    gc.mat[1] = L.w[5].mat();
+    gc.nmat = 2;
+    gc.N = I;
+    gc.y = ws.act;
+    gc.ldy = I;
+    gc.M = R;
+    gc.K = H;
+    gc.bits = cf.bits;
+    gc.mode = kSwiglu;
+    if (!rc) rc = launch_qmm(gc, st);
+
+    QmmCall dc;
+    dc.x = ws.act;
+    dc.mat[0] = L.w[6].mat();
+    dc.N = H;
+    dc.y = ws.h;
+    dc.ldy = H;
+    dc.res = ws.h;
+    dc.M = R;
+    dc.K = I;
+    dc.bits = cf.bits;
+    dc.mode = kResid;
+    if (!rc) rc = launch_qmm(dc, st);
+  }
+  if (rc || !logits) return rc;
+  QmmCall hc;
+  const int M = last_only ? B : R;
+  const bf16_t* src = ws.h;
+  if (M > kQmmMaxNormRows) {
+    rc = launch_rms_norm(ws.h, m.final_norm, ws.xn, R, H, cf.eps, st);
+    if (rc) return rc;
+    src = ws.xn;
+  } else {
+    hc.norm_w = m.final_norm;
+  }
+  hc.x = last_only ? src + (size_t)(T - 1) * H : src;
+  hc.ldx = last_only ? T * H : H;
+  hc.eps = cf.eps;
+  hc.mat[0] = m.head().mat();
+  hc.N = cf.vocab;
+  hc.y = logits;
+  hc.ldy = cf.vocab;
+  hc.M = M;
+  hc.K = H;
+  hc.bits = cf.bits;
+  return launch_qmm(hc, st);
+}
+
+static int add_len(int* len, int B, int n, cudaStream_t st) {
+  return cuda_check(lmx_launch(add_len_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, len, B, n),
+                    "add_len");
+}
+
+// Forward a [B, T] token block in chunks (prefill), advancing the lengths.
+static int forward_chunked(const Model& m, Cache& c, int n_layers, const int32_t* tok, int ld, int T, int B,
+                           Workspace& ws, bf16_t* last_logits, cudaStream_t st) {
+  int rc = LMX_OK;
+  for (int t0 = 0; t0 < T && !rc; t0 += kPrefillChunk) {
+    const int tn = T - t0 < kPrefillChunk ? T - t0 : kPrefillChunk;
+    const bool last = t0 + tn >= T;
+    rc = forward(m, c, n_layers, tok, ld, t0, B, tn, ws, last ? last_logits : nullptr, true, st);
+    if (!rc) rc = add_len(c.len, B, tn, st);
+  }
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// speculative decoder
+// ---------------------------------------------------------------------------
+struct Spec {
+  Model* tm = nullptr;
+  Model* dm = nullptr;
+  int dl = 0;
+  lmx_spec_config cfg;
+  std::unique_ptr<Cache> tc, dc;
+  Workspace ws;
+  SpecState s;
+  int32_t *prompts = nullptr, *yprefill = nullptr;
+  Arena ar;
+  cudaStream_t st = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  bool prefilled = false;
+  ~Spec() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
+static int spec_step(Spec& sp) {
+  const int B = sp.cfg.batch, K = sp.cfg.K, V = sp.tm->c.vocab;
+  cudaStream_t st = sp.st;
+  int rc = LMX_OK;
+  for (int i = 0; i < K && !rc; ++i) {
+    if (i == 0)
+      rc = forward(*sp.dm, *sp.dc, sp.dl, sp.s.tok2, 2, 0, B, 2, sp.ws, sp.ws.logits, true, st);
+    else
+      rc = forward(*sp.dm, *sp.dc, sp.dl, sp.s.drafts, K, i - 1, B, 1, sp.ws, sp.ws.logits, true, st);
+    if (!rc) rc = launch_cluster_rows(draft_argmax_kernel, B, sp.ws.logits, V, sp.s, i, i == 0 ? 2 : 1, st);
+  }
+  if (!rc) rc = forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
+  if (!rc) rc = launch_argmax(sp.ws.logits, B * (K + 1), V, sp.s.pred, st);
+  if (!rc)
+    rc = cuda_check(lmx_launch(accept_greedy_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s),
+                    "accept");
+  return rc;
+}
+
+}  // namespace lmx
+
+namespace lmx {
+
+static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
+  if (cfg.batch < 1 || cfg.K < 1 || cfg.max_tokens < 1 || cfg.prompt_len < 2)
+    return set_error(LMX_ERR_INVALID, "spec: bad config");
+  if (cfg.temperature > 0.0f)
+    return set_error(LMX_ERR_UNSUPPORTED, "spec: stochastic acceptance not built yet");
+  if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
+    return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
+  auto sp = std::make_unique<Spec>();
+  sp->tm = tm;
+  sp->dm = dm;
+  sp->dl = dl;
+  sp->cfg = cfg;
+  const int B = cfg.batch, K = cfg.K, P = cfg.prompt_len;
+  const int cap = P + cfg.max_tokens + K + 8;
+  Cache *tc = nullptr, *dc = nullptr;
+  int rc = cache_create(*tm, tm->n_layers, B, cap, cfg.kv_bits, &tc);
+  if (rc) return rc;
+  sp->tc.reset(tc);
+  rc = cache_create(*dm, dl, B, cap, cfg.kv_bits, &dc);
+  if (rc) return rc;
+  sp->dc.reset(dc);
+  // one workspace serves both models (sized by the larger of each dimension)
+  lmx_model_config big = tm->c;
+  big.hidden = std::max(tm->c.hidden, dm->c.hidden);
+  big.inter = std::max(tm->c.inter, dm->c.inter);
+  big.heads = std::max(tm->c.heads, dm->c.heads);
+  big.kv_heads = std::max(tm->c.kv_heads, dm->c.kv_heads);
+  Model shape;
+  shape.c = big;
+  const int Tmax = std::max(K + 1, kPrefillChunk);
+  if (tm->c.kv_heads != dm->c.kv_heads || tm->c.heads / tm->c.kv_heads != dm->c.heads / dm->c.kv_heads)
+    return set_error(LMX_ERR_UNSUPPORTED, "spec: draft and target must share the GQA layout");
+  rc = workspace_create(shape, B, Tmax, cap, B * (K + 1), sp->ws);
+  if (rc) return rc;
+  SpecState& s = sp->s;
+  s.B = B;
+  s.K = K;
+  s.max_tokens = cfg.max_tokens;
+  rc = sp->ar.alloc(&s.tok2, (size_t)2 * B);
+  if (!rc) rc = sp->ar.alloc(&s.drafts, (size_t)B * K);
+  if (!rc) rc = sp->ar.alloc(&s.vt, (size_t)B * (K + 1));
+  if (!rc) rc = sp->ar.alloc(&s.pred, (size_t)B * (K + 1));
+  if (!rc) rc = sp->ar.alloc(&s.emitted, (size_t)B);
+  if (!rc) rc = sp->ar.alloc(&s.accepted, (size_t)B);
+  if (!rc) rc = sp->ar.alloc(&s.steps, (size_t)B);
+  if (!rc) rc = sp->ar.alloc(&s.out, (size_t)B * cfg.max_tokens);
+  if (!rc) rc = sp->ar.alloc(&sp->prompts, (size_t)B * P);
+  if (!rc) rc = sp->ar.alloc(&sp->yprefill, (size_t)B);
+  if (rc) return rc;
+  s.tlen = sp->tc->len;
+  s.dlen = sp->dc->len;
+  if (!rc) rc = cuda_check(cudaStreamCreateWithFlags(&sp->st, cudaStreamNonBlocking), "stream");
+  if (rc) return rc;
+  *out = sp.release();
+  return LMX_OK;
+}
+
+// Prefill (TokenIterator::prepare, src/common/generate.cpp:508-549): the
+// target runs the prompt and its argmax at the last position is d0 of the
+// first step; the draft runs prompt[0, P-1) (its first step re-runs P-1).
+static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
+  const int B = sp.cfg.batch, P = sp.cfg.prompt_len;
+  cudaStream_t st = sp.st;
+  int rc = cuda_check(cudaMemcpyAsync(sp.prompts, prompts_host, (size_t)B * P * 4, cudaMemcpyHostToDevice, st),
+                      "prompts");
+  if (!rc) rc = cuda_check(cudaMemsetAsync(sp.tc->len, 0, B * 4, st), "len");
+  if (!rc) rc = cuda_check(cudaMemsetAsync(sp.dc->len, 0, B * 4, st), "len");
+  if (!rc) rc = forward_chunked(*sp.tm, *sp.tc, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
+  if (!rc) rc = launch_argmax(sp.ws.logits, B, sp.tm->c.vocab, sp.yprefill, st);
+  if (!rc) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
+  if (!rc)
+    rc = cuda_check(lmx_launch(prefill_done_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
+                               (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill),
+                    "prefill_done");
+  if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "prefill");
+  if (!rc) sp.prefilled = true;
+  return rc;
+}
+
+// Decode until every sequence has max_tokens: one captured graph per step.
+static int spec_decode(Spec& sp, int use_graph, double* seconds) {
+  if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "spec: decode before prefill");
+  cudaStream_t st = sp.st;
+  int rc = LMX_OK;
+  if (use_graph && !sp.exec) {
+    rc = cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "capture begin");
+    if (rc) return rc;
+    int rc2 = spec_step(sp);
+    cudaGraph_t g = nullptr;
+    rc = cuda_check(cudaStreamEndCapture(st, &g), "capture end");
+    if (rc2) {
+      if (g) cudaGraphDestroy(g);
+      return rc2;
+    }
+    if (rc) return rc;
+    sp.graph = g;
+    rc = cuda_check(cudaGraphInstantiate(&sp.exec, g, 0), "graph instantiate");
+    if (rc) return rc;
+  }
+  const int B = sp.cfg.batch, MT = sp.cfg.max_tokens;
+  std::vector<int> em(B);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, st);
+  const int check_every = 4;
+  for (int it = 0; it < MT + 1 && !rc; it += check_every) {
+    for (int k = 0; k < check_every && !rc; ++k)
+      rc = use_graph ? cuda_check(cudaGraphLaunch(sp.exec, st), "graph launch") : spec_step(sp);
+    if (rc) break;
+    rc = cuda_check(cudaMemcpyAsync(em.data(), sp.s.emitted, B * 4, cudaMemcpyDeviceToHost, st), "emitted");
+    if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "decode step");
+    bool all = true;
+    for (int b = 0; b < B; ++b) all = all && em[b] >= MT;
+    if (all) break;
+  }
+  cudaEventRecord(e1, st);
+  cudaEventSynchronize(e1);
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (seconds) *seconds = ms * 1e-3;
+  if (!rc) {
+    unsigned code = 0;
+    cudaMemcpyFromSymbol(&code, g_lmx_kernel_error, sizeof(code));
+    if (code) rc = set_error(LMX_ERR_CUDA, "kernel reported error 0x%x", code);
+  }
+  return rc;
+}
+
+}  // namespace lmx
+
+// ---------------------------------------------------------------------------
+// C ABI: models, caches, forward, speculative generation
+// ---------------------------------------------------------------------------
+using namespace lmx;
+
+extern "C" int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model) {
+  if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create: null argument");
+  Model* m = nullptr;
+  int rc = model_create(*cfg, seed, &m);
+  if (!rc) *model = m;
+  return rc;
+}
+
+extern "C" int lmx_model_view(void* model, int n_layers, void** view) {
+  Model* m = (Model*)model;
+  if (!m || !view || n_layers < 1 || n_layers > m->n_layers)
+    return set_error(LMX_ERR_INVALID, "model_view: bad arguments");
+  Model* v = new Model(*m);
+  v->n_layers = n_layers;
+  *view = v;
+  return LMX_OK;
+}
+
+extern "C" int lmx_model_free(void* model) {
+  delete (Model*)model;
+  return LMX_OK;
+}
+
+extern "C" int lmx_model_weight(void* model, int layer, int kind, void* w_host, void* s_host,
+                                void* b_host) {
+  Model* m = (Model*)model;
+  if (!m) return set_error(LMX_ERR_INVALID, "model_weight: null model");
+  const QWeight* q = nullptr;
+  if (kind == 7) q = &m->embed;
+  else if (kind == 8) q = &m->head();
+  else if (layer >= 0 && layer < (int)m->L.size() && kind >= 0 && kind < 7) q = &m->L[layer].w[kind];
+  if (!q) return set_error(LMX_ERR_INVALID, "model_weight: bad layer/kind");
+  const size_t nw = (size_t)q->N * q->K * m->c.bits / 32, ng = (size_t)q->N * (q->K / 64);
+  int rc = cuda_check(cudaMemcpy(w_host, q->w, nw * 4, cudaMemcpyDeviceToHost), "copy w");
+  if (!rc) rc = cuda_check(cudaMemcpy(s_host, q->s, ng * 2, cudaMemcpyDeviceToHost), "copy s");
+  if (!rc) rc = cuda_check(cudaMemcpy(b_host, q->b, ng * 2, cudaMemcpyDeviceToHost), "copy b");
+  return rc;
+}
+
+struct CacheHandle {
+  Cache* c = nullptr;
+  Workspace ws;
+  int Tmax = 0;
+  ~CacheHandle() { delete c; }
+};
+
+extern "C" int lmx_cache_create(void* model, int n_layers, int batch, int capacity, int kv_bits,
+                                int max_tokens_per_forward, void** cache) {
+  Model* m = (Model*)model;
+  if (!m || !cache || max_tokens_per_forward < 1) return set_error(LMX_ERR_INVALID, "cache_create: bad arguments");
+  auto h = std::make_unique<CacheHandle>();
+  int rc = cache_create(*m, n_layers, batch, capacity, kv_bits, &h->c);
+  if (!rc) rc = workspace_create(*m, batch, max_tokens_per_forward, capacity, batch * max_tokens_per_forward, h->ws);
+  if (rc) return rc;
+  h->Tmax = max_tokens_per_forward;
+  *cache = h.release();
+  return LMX_OK;
+}
+
+extern "C" int lmx_cache_free(void* cache) {
+  delete (CacheHandle*)cache;
+  return LMX_OK;
+}
+
+// KVCache::set_position (src/common/kv_cache.cpp:135-142): rows past pos are dropped.
+extern "C" int lmx_cache_set_position(void* cache, int seq, int pos) {
+  CacheHandle* h = (CacheHandle*)cache;
+  if (!h || seq < 0 || seq >= h->c->B) return set_error(LMX_ERR_INVALID, "set_position: bad sequence");
+  int cur = 0;
+  int rc = cuda_check(cudaMemcpy(&cur, h->c->len + seq, 4, cudaMemcpyDeviceToHost), "len");
+  if (!rc && pos < cur) rc = cuda_check(cudaMemcpy(h->c->len + seq, &pos, 4, cudaMemcpyHostToDevice), "len");
+  return rc;
+}
+
+extern "C" int lmx_cache_len(void* cache, int seq, int* len) {
+  CacheHandle* h = (CacheHandle*)cache;
+  if (!h || !len || seq < 0 || seq >= h->c->B) return set_error(LMX_ERR_INVALID, "cache_len: bad arguments");
+  return cuda_check(cudaMemcpy(len, h->c->len + seq, 4, cudaMemcpyDeviceToHost), "len");
+}
+
+// One forward of tokens [B, T] (host) through the first n_layers; logits
+// [B, T, V] bf16 copied to logits_host (may be NULL).  Advances the lengths.
+extern "C" int lmx_forward(void* model, void* cache, int n_layers, const int32_t* tokens_host, int B, int T,
+                           void* logits_host) {
+  Model* m = (Model*)model;
+  CacheHandle* h = (CacheHandle*)cache;
+  if (!m || !h || !tokens_host || T < 1 || T > h->Tmax || B != h->c->B)
+    return set_error(LMX_ERR_INVALID, "forward: bad arguments");
+  int32_t* tok = nullptr;
+  Arena ar;
+  int rc = ar.alloc(&tok, (size_t)B * T);
+  if (!rc) rc = cuda_check(cudaMemcpy(tok, tokens_host, (size_t)B * T * 4, cudaMemcpyHostToDevice), "tokens");
+  if (!rc) rc = forward(*m, *h->c, n_layers, tok, T, 0, B, T, h->ws, logits_host ? h->ws.logits : nullptr, false, 0);
+  if (!rc) rc = add_len(h->c->len, B, T, 0);
+  if (!rc) rc = cuda_check(cudaDeviceSynchronize(), "forward");
+  if (!rc && logits_host)
+    rc = cuda_check(cudaMemcpy(logits_host, h->ws.logits, (size_t)B * T * m->c.vocab * 2, cudaMemcpyDeviceToHost),
+                    "logits");
+  return rc;
+}
+
+extern "C" int lmx_spec_create(void* target, void* draft, int draft_layers, const lmx_spec_config* cfg,
+                               void** spec) {
+  Model* tm = (Model*)target;
+  Model* dm = draft ? (Model*)draft : tm;
+  if (!tm || !cfg || !spec) return set_error(LMX_ERR_INVALID, "spec_create: null argument");
+  const int dl = draft_layers > 0 ? draft_layers : dm->n_layers;
+  if (dl > dm->n_layers) return set_error(LMX_ERR_INVALID, "spec_create: draft_layers > draft layers");
+  Spec* sp = nullptr;
+  int rc = spec_create(tm, dm, dl, *cfg, &sp);
+  if (!rc) *spec = sp;
+  return rc;
+}
+
+extern "C" int lmx_spec_prefill(void* spec, const int32_t* prompts_host) {
+  if (!spec || !prompts_host) return set_error(LMX_ERR_INVALID, "spec_prefill: null argument");
+  return spec_prefill(*(Spec*)spec, prompts_host);
+}
+
+extern "C" int lmx_spec_decode(void* spec, int use_graph, double* seconds) {
+  if (!spec) return set_error(LMX_ERR_INVALID, "spec_decode: null argument");
+  return spec_decode(*(Spec*)spec, use_graph, seconds);
+}
+
+extern "C" int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_host) {
+  Spec* sp = (Spec*)spec;
+  if (!sp) return set_error(LMX_ERR_INVALID, "spec_result: null argument");
+  const int B = sp->cfg.batch;
+  int rc = LMX_OK;
+  if (out_host)
+    rc = cuda_check(cudaMemcpy(out_host, sp->s.out, (size_t)B * sp->cfg.max_tokens * 4, cudaMemcpyDeviceToHost),
+                    "out");
+  if (!rc && stats_host) {
+    std::vector<int> steps(B), acc(B), em(B);
+    rc = cuda_check(cudaMemcpy(steps.data(), sp->s.steps, B * 4, cudaMemcpyDeviceToHost), "stats");
+    if (!rc) rc = cuda_check(cudaMemcpy(acc.data(), sp->s.accepted, B * 4, cudaMemcpyDeviceToHost), "stats");
+    if (!rc) rc = cuda_check(cudaMemcpy(em.data(), sp->s.emitted, B * 4, cudaMemcpyDeviceToHost), "stats");
+    int64_t st = 0, ac = 0, e = 0;
+    for (int b = 0; b < B; ++b) { st += steps[b]; ac += acc[b]; e += em[b]; }
+    stats_host[0] = st;
+    stats_host[1] = st * sp->cfg.K;
+    stats_host[2] = ac;
+    stats_host[3] = e;
+  }
+  return rc;
+}
+
+extern "C" int lmx_spec_free(void* spec) {
+  delete (Spec*)spec;
+  return LMX_OK;
+}

@@ -1,0 +1,208 @@
+// engine_kernels.cuh -- small kernels of the speculative loop: synthetic
+// weights, embedding lookup, draft-token selection and greedy acceptance with
+// all bookkeeping kept on the device (so a whole step replays as one graph).
+#pragma once
+#include <cooperative_groups.h>
+
+#include "lmx_common.cuh"
+#include "norm_argmax.cuh"
+namespace cg = cooperative_groups;
+
+namespace lmx {
+
+// ---------------------------------------------------------------------------
+// Synthetic weights, bit-identical to the oracle's orc_gen_normal_bf16 +
+// orc_quantize: element e of tensor tid is Irwin-Hall(4) of 22-bit Philox
+// uniforms (counter (e_lo, e_hi, tid, 0x243F6A88)), bf16(z * C); each group of
+// 64 is quantized with scale = bf16((max-min)/(2^bits-1)), bias = bf16(min).
+// One thread per group.
+// ---------------------------------------------------------------------------
+LMX_DEV bf16_t gen_normal(uint64_t seed, uint32_t tid, uint64_t e, float C) {
+  uint32_t c[4] = {(uint32_t)e, (uint32_t)(e >> 32), tid, 0x243F6A88u};
+  philox10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  int32_t S = (int32_t)((c[0] >> 10) + (c[1] >> 10) + (c[2] >> 10) + (c[3] >> 10));
+  return f2bf(__fmul_rn((float)(S - (1 << 23)), C));
+}
+
+__global__ void gen_qweight_kernel(uint64_t seed, uint32_t tid, int N, int K, int bits, float C,
+                                   uint32_t* wq, bf16_t* scales, bf16_t* biases) {
+  const int G = K / 64;
+  const int64_t grp = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (grp >= (int64_t)N * G) return;
+  const int n = (int)(grp / G), g = (int)(grp % G);
+  const uint64_t e0 = (uint64_t)n * K + (uint64_t)g * 64;
+  float v[64];
+  float mn = 0.0f, mx = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < 64; ++j) {
+    v[j] = bf2f(gen_normal(seed, tid, e0 + j, C));
+    mn = j == 0 ? v[j] : fminf(mn, v[j]);
+    mx = j == 0 ? v[j] : fmaxf(mx, v[j]);
+  }
+  const int nb = (1 << bits) - 1;
+  bf16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), (float)nb));
+  float sc = bf2f(sb);
+  if (sc == 0.0f) { sb = f2bf(1.0f); sc = 1.0f; }
+  const bf16_t bb = f2bf(mn);
+  const float bi = bf2f(bb);
+  const int per = 32 / bits;
+  uint32_t* wout = wq + (size_t)n * (K * bits / 32) + (size_t)g * (64 * bits / 32);
+  for (int w = 0; w < 64 / per; ++w) {
+    uint32_t word = 0;
+    for (int j = 0; j < per; ++j) {
+      int q = (int)rintf(__fdiv_rn(__fsub_rn(v[w * per + j], bi), sc));
+      q = q < 0 ? 0 : (q > nb ? nb : q);
+      word |= (uint32_t)q << (j * bits);
+    }
+    wout[w] = word;
+  }
+  scales[grp] = sb;
+  biases[grp] = bb;
+}
+
+__global__ void fill_bf16_kernel(bf16_t* p, int64_t n, bf16_t v) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Embedding lookup from the packed (tied) table: h = bf16(fma(s, q, b)).
+// Token of row r: tok[(r / T) * ld + off + r % T].
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const int32_t* tok, int T, int ld, int off, const uint32_t* wq,
+                             const bf16_t* s, const bf16_t* b, int H, int bits, bf16_t* h, int R) {
+  grid_wait();
+  grid_launch_dependents();
+  const int r = blockIdx.x;
+  if (r >= R) return;
+  const int t = tok[(r / T) * ld + off + r % T];
+  const int per = 32 / bits, G = H / 64;
+  const uint32_t* row = wq + (size_t)t * (H * bits / 32);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const int q = (int)((row[i / per] >> ((i % per) * bits)) & ((1u << bits) - 1u));
+    h[(size_t)r * H + i] =
+        f2bf(__fmaf_rn(bf2f(s[(size_t)t * G + i / 64]), (float)q, bf2f(b[(size_t)t * G + i / 64])));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Device-side state of the speculative loop (one entry per sequence).
+// ---------------------------------------------------------------------------
+struct SpecState {
+  int B, K, max_tokens;
+  int32_t* tok2;     // [B][2]: token at position p-1, token y at position p
+  int32_t* drafts;   // [B][K]
+  int32_t* vt;       // [B][K+1]: verify input y, d1..dK
+  int32_t* pred;     // [B][K+1]: target argmax of the verify pass
+  int* tlen;         // [B] target cache length (= p)
+  int* dlen;         // [B] draft cache length
+  int* emitted;      // [B]
+  int* accepted;     // [B] accepted drafts (sum)
+  int* steps;        // [B] speculative steps taken while unfinished
+  int32_t* out;      // [B][max_tokens]
+};
+
+// Greedy draft token i of every sequence: cluster argmax of the draft logits
+// (rows [B][V]), then rank 0 records d_{i+1}, advances the draft length by the
+// forward's token count and, after the last draft, assembles the verify input.
+__global__ void __launch_bounds__(512) draft_argmax_kernel(const bf16_t* logits, int V, SpecState s,
+                                                          int i, int adv) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ float cv;
+  __shared__ int ci;
+  grid_wait();
+  grid_launch_dependents();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+  const int b = blockIdx.x / cs;
+  const int chunk = (V + cs - 1) / cs;
+  const int j0 = rank * chunk, j1 = min(V, j0 + chunk);
+  const bf16_t* l = logits + (size_t)b * V;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    float v = bf2f(l[j]);
+    if (v == v && am_better(v, j, bv, bi)) { bv = v; bi = j; }
+  }
+  am_block(bv, bi, sv, si);
+  if (threadIdx.x == 0) { cv = bv; ci = bi; }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    float rv = cv;
+    int ri = ci;
+    for (int r = 1; r < cs; ++r) {
+      float ov = *cluster.map_shared_rank(&cv, r);
+      int oi = *cluster.map_shared_rank(&ci, r);
+      if (am_better(ov, oi, rv, ri)) { rv = ov; ri = oi; }
+    }
+    const int tok = ri == 0x7fffffff ? 0 : ri;
+    s.drafts[b * s.K + i] = tok;
+    const bool done = s.emitted[b] >= s.max_tokens;
+    if (!done) s.dlen[b] += adv;
+    if (i == s.K - 1) {
+      s.vt[b * (s.K + 1)] = s.tok2[2 * b + 1];
+      for (int k = 0; k < s.K; ++k) s.vt[b * (s.K + 1) + 1 + k] = s.drafts[b * s.K + k];
+    }
+  }
+  cluster.sync();
+}
+
+// Greedy acceptance (src/common/generate.cpp:800-823) and commit/rollback
+// (:850-888): accept while pred[i] == d_{i+1}; emit y, d1..d_acc; the next y
+// is the correction or bonus token; target length p+acc+1, draft length p+acc.
+// Finished sequences are frozen (nothing emitted, lengths unchanged).
+__global__ void accept_greedy_kernel(SpecState s) {
+  grid_wait();
+  grid_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= s.B) return;
+  const int K = s.K;
+  const int p = s.tlen[b];
+  if (s.emitted[b] >= s.max_tokens) {
+    s.dlen[b] = p - 1;
+    return;
+  }
+  const int32_t* pr = s.pred + b * (K + 1);
+  const int32_t* d = s.drafts + b * K;
+  int acc = 0;
+  while (acc < K && pr[acc] == d[acc]) ++acc;
+  const int y = s.tok2[2 * b + 1];
+  int e = s.emitted[b];
+  int32_t* o = s.out + (size_t)b * s.max_tokens;
+  if (e < s.max_tokens) o[e++] = y;
+  for (int k = 0; k < acc; ++k)
+    if (e < s.max_tokens) o[e++] = d[k];
+  s.emitted[b] = e;
+  s.accepted[b] += acc;
+  s.steps[b] += 1;
+  s.tok2[2 * b] = acc > 0 ? d[acc - 1] : y;
+  s.tok2[2 * b + 1] = pr[acc];
+  s.tlen[b] = p + acc + 1;
+  s.dlen[b] = p + acc;
+}
+
+// Prefill bookkeeping: y = argmax of the last prompt position (already in
+// pred[b*(K+1)]), tok2 = (prompt[P-1], y), lengths P and P-1.
+__global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, const int32_t* y) {
+  grid_wait();
+  grid_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= s.B) return;
+  s.tok2[2 * b] = prompts[(size_t)b * P + P - 1];
+  s.tok2[2 * b + 1] = y[b];
+  s.tlen[b] = P;
+  s.dlen[b] = P - 1;
+  s.emitted[b] = 0;
+  s.accepted[b] = 0;
+  s.steps[b] = 0;
+}
+
+__global__ void add_len_kernel(int* len, int B, int n) {
+  grid_wait();
+  grid_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) len[b] += n;
+}
+
+}  // namespace lmx

@@ -7,6 +7,8 @@
 #include "lmx_internal.h"
 #include "norm_argmax.cuh"
 #include "qmm.cuh"
+#include "attn.cuh"
+#include "engine_kernels.cuh"
 
 // Device error word: bounded waits that give up record a code here.
 __device__ unsigned g_lmx_kernel_error;
@@ -62,19 +64,59 @@ unsigned* device_error_word() { return dev().err; }
 // ---------------------------------------------------------------------------
 // K1 launcher
 // ---------------------------------------------------------------------------
+// Plan the K1 launch: warps per row, segments per warp, ring depth and the
+// shared-memory layout (must match qmv_kernel).
+struct QmvShape {
+  QmvPlan p;
+  int csize, RB;
+  size_t smem;
+};
+
+static int qmv_plan(int K, int MT, int bits, QmvShape& out) {
+  constexpr int NW = kQmmThreads / 32;
+  const int SEGB = 64 * bits;
+  const int nseg = (K + 511) / 512, G = K / 64, KWB = K * bits / 8;
+  const int spw_reg = MT >= 8 ? 1 : 8 / MT;
+  const int spw_smem = bits == 4 ? 8 : 4;
+  const int spw_cap = spw_reg < spw_smem ? spw_reg : spw_smem;
+  const int Wt = (nseg + spw_cap - 1) / spw_cap;
+  QmvPlan& p = out.p;
+  if (Wt <= NW) {
+    out.csize = 1;
+    p.W = Wt;
+    p.SPW = (nseg + p.W - 1) / p.W;
+    p.rs = NW / p.W;
+  } else {
+    out.csize = (Wt + NW - 1) / NW;
+    p.W = NW;
+    p.SPW = (nseg + NW * out.csize - 1) / (NW * out.csize);
+    p.rs = 1;
+  }
+  if (out.csize > 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d too large for M=%d", K, MT);
+  p.full_rows = out.csize == 1 && p.W == 1;
+  p.sb_bulk = (G % 8) == 0;
+  p.RP = p.full_rows ? KWB : p.SPW * SEGB;
+  p.SP = p.sb_bulk ? (p.full_rows ? G * 2 : p.SPW * 16) : 0;
+  int RB = MT == 1 ? 16 : (MT == 8 ? 4 : 8);
+  while (RB > 4 && RB * (p.RP + 2 * p.SP) > 12 * 1024) RB /= 2;
+  out.RB = RB;
+  const int V = RB * MT;
+  p.stage = ((RB * p.RP + 2 * RB * p.SP) + 127) / 128 * 128;
+  p.red_off = kQmmMaxNormRows * 4;
+  const int red_size = (p.W > 1 || out.csize > 1) ? 2 * NW * p.SPW * V * 4 : 0;
+  p.bar_off = (p.red_off + red_size + 7) / 8 * 8;
+  const int fixed = p.bar_off + NW * 8 * 8 + 128;
+  int nst = (200 * 1024 - fixed) / (NW * p.stage);
+  if (nst > 8) nst = 8;
+  if (nst < 2) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d stage too large", K);
+  p.nst = nst;
+  p.stage_off = (p.bar_off + NW * nst * 8 + 127) / 128 * 128;
+  out.smem = (size_t)p.stage_off + (size_t)NW * nst * p.stage;
+  return LMX_OK;
+}
+
 template <int BITS, int MT, int RB>
-static int launch_qmv_t(const QmmArgs& a, cudaStream_t st) {
-  constexpr int V = RB * MT, SEGB = 32 * 16 * BITS / 8, NW = kQmmThreads / 32;
-  const int nseg = (a.K + 511) / 512;
-  const int csize = nseg <= NW ? 1 : (nseg + NW - 1) / NW;
-  if (csize > 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d exceeds 32768", a.K);
-  const int rs = csize == 1 ? NW / nseg : 1;
-  const int items = a.mode == QMM_SWIGLU ? 2 * a.N : a.N;
-  const int nbatch = (items + RB - 1) / RB;
-  const size_t stage = (size_t)NW * RB * SEGB;
-  int nst = (int)((160 * 1024) / stage);
-  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
-  const size_t smem = nst * stage + (size_t)NW * nst * 8 + 2 * NW * V * 4 + kQmmMaxNormRows * 4;
+static int launch_qmv_t(const QmmArgs& a, const QmvShape& sh, cudaStream_t st) {
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
@@ -83,41 +125,53 @@ static int launch_qmv_t(const QmmArgs& a, cudaStream_t st) {
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
                         "qmm: set smem");
     if (rc) return rc;
-    if (csize > 1)
-      cudaFuncSetAttribute(qmv_kernel<BITS, MT, RB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaFuncSetAttribute(qmv_kernel<BITS, MT, RB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     attr_set[d & 63] = true;
   }
-  int nclusters = (nbatch + rs - 1) / rs;
-  const int max_clusters = device_sms() / csize;
+  const int items = a.mode == QMM_SWIGLU ? ((a.N + RB / 2 - 1) / (RB / 2)) * RB : a.N;
+  const int nbatch = (items + RB - 1) / RB;
+  int nclusters = (nbatch + sh.p.rs - 1) / sh.p.rs;
+  const int max_clusters = device_sms() / sh.csize;
   if (nclusters > max_clusters) nclusters = max_clusters;
   if (nclusters < 1) nclusters = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nclusters * csize);
+  cfg.gridDim = dim3(nclusters * sh.csize);
   cfg.blockDim = dim3(kQmmThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = sh.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   int na = 1;
-  if (csize > 1) {
+  if (sh.csize > 1) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = csize;
+    attr[1].val.clusterDim.x = sh.csize;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     na = 2;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, a, nst), "qmm: launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, a, sh.p), "qmm: launch");
 }
 
 template <int BITS>
 static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
-  if (a.M <= 1) return launch_qmv_t<BITS, 1, 8>(a, st);
-  if (a.M <= 2) return launch_qmv_t<BITS, 2, 8>(a, st);
-  if (a.M <= 4) return launch_qmv_t<BITS, 4, 8>(a, st);
-  return launch_qmv_t<BITS, 8, 4>(a, st);
+  const int MT = a.M <= 1 ? 1 : (a.M <= 2 ? 2 : (a.M <= 4 ? 4 : 8));
+  QmvShape sh;
+  int rc = qmv_plan(a.K, MT, BITS, sh);
+  if (rc) return rc;
+  switch (MT * 100 + sh.RB) {
+    case 116: return launch_qmv_t<BITS, 1, 16>(a, sh, st);
+    case 108: return launch_qmv_t<BITS, 1, 8>(a, sh, st);
+    case 104: return launch_qmv_t<BITS, 1, 4>(a, sh, st);
+    case 208: return launch_qmv_t<BITS, 2, 8>(a, sh, st);
+    case 204: return launch_qmv_t<BITS, 2, 4>(a, sh, st);
+    case 408: return launch_qmv_t<BITS, 4, 8>(a, sh, st);
+    case 404: return launch_qmv_t<BITS, 4, 4>(a, sh, st);
+    case 804: return launch_qmv_t<BITS, 8, 4>(a, sh, st);
+  }
+  return set_error(LMX_ERR_UNSUPPORTED, "qmm: no kernel for MT=%d RB=%d", MT, sh.RB);
 }
 
 int launch_qmm(const QmmCall& c, cudaStream_t st) {
@@ -129,8 +183,12 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
     return set_error(LMX_ERR_INVALID, "qmm: fused norm needs M <= %d", kQmmMaxNormRows);
   if (!c.x || !c.y || ((uintptr_t)c.x & 15))
     return set_error(LMX_ERR_INVALID, "qmm: x must be a 16-byte aligned device pointer");
+  const int ldx = c.ldx ? c.ldx : c.K;
+  if (ldx < c.K || (ldx & 7))
+    return set_error(LMX_ERR_INVALID, "qmm: ldx=%d must be >= K and a multiple of 8", ldx);
   QmmArgs a;
   a.x = c.x;
+  a.ldx = ldx;
   a.norm_w = c.norm_w;
   a.eps = c.eps;
   a.nmat = c.nmat;
@@ -234,3 +292,4 @@ extern "C" int lmx_rms_norm(const void* x, const void* w, void* y, int rows, int
 extern "C" int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream) {
   return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
 }
+#include "engine.cuh"

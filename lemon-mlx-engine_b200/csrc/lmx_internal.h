@@ -24,6 +24,7 @@ enum QmmMode { kPlain = 0, kResid = 1, kSwiglu = 2 };
 
 struct QmmCall {
   const bf16_t* x = nullptr;
+  int ldx = 0;                     // 0 = K
   const bf16_t* norm_w = nullptr;  // fused RMSNorm of x (M <= 64)
   float eps = 1e-6f;
   QMat mat[3];

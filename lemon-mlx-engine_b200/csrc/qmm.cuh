@@ -46,7 +46,8 @@ struct QmmMat {
 enum { QMM_PLAIN = 0, QMM_RESID = 1, QMM_SWIGLU = 2 };
 
 struct QmmArgs {
-  const bf16_t* x;       // [M, K]
+  const bf16_t* x;       // [M, ldx]
+  int ldx;               // row stride of x (elements, multiple of 8)
   const bf16_t* norm_w;  // optional RMSNorm weight [K] applied to x in the prologue
   float eps;
   QmmMat mat[3];         // PLAIN/RESID: virtual rows = concatenation; SWIGLU: gate, up
@@ -97,10 +98,15 @@ LMX_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, un
   return false;
 }
 
+// Item -> (matrix, row).  PLAIN/RESID: items are the concatenated rows of
+// mat[0..nmat).  SWIGLU: a batch of RB items holds RB/2 gate rows followed by
+// the same RB/2 up rows, so both runs are contiguous in memory and in smem.
+template <int RB>
 LMX_DEV bool qmm_item_row(const QmmArgs& a, int item, int& mi, int& row) {
   if (a.mode == QMM_SWIGLU) {
-    mi = item & 1;
-    row = item >> 1;
+    const int bt = item / RB, w = item % RB;
+    mi = w / (RB / 2);
+    row = bt * (RB / 2) + w % (RB / 2);
     return row < a.N;
   }
   int r = item;
@@ -142,6 +148,47 @@ LMX_DEV void rs_level(float (&v)[CAP], int off, bool up, int& base) {
 }
 __host__ __device__ constexpr int cmax1(int a) { return a < 1 ? 1 : a; }
 
+// Two independent IEEE fp32 FMAs / adds in one sm_100 instruction.  Each
+// lane of the pair rounds exactly like __fmaf_rn / __fadd_rn.
+LMX_DEV void fma2(float& d0, float& d1, float a0, float a1, float b) {
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %4};\n"
+      " mov.b64 rd, {%0, %1};\n fma.rn.f32x2 rd, ra, rb, rd;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+LMX_DEV void sub_magic2(float& a0, float& a1) {
+  asm("{\n .reg .b64 ra, rc;\n mov.b64 ra, {%0, %1};\n mov.b64 rc, {%2, %2};\n"
+      " add.rn.f32x2 ra, ra, rc;\n mov.b64 {%0, %1}, ra;\n}\n"
+      : "+f"(a0), "+f"(a1)
+      : "f"(-8388608.0f));
+}
+
+// Quarter unpack into "magic" floats 2^23 + q*scale_j (the 2^23 is removed
+// by sub_magic2 on row pairs).
+template <int BITS>
+LMX_DEV void unpack_quarter_raw(const uint8_t* p, float (&q)[16]) {
+  if (BITS == 4) {
+    uint2 w = *reinterpret_cast<const uint2*>(p);
+    const uint32_t src[4] = {w.x, w.x >> 16, w.y, w.y >> 16};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) q[4 * h + r] = __uint_as_float((src[h] & (0xFu << (4 * r))) | 0x4B000000u);
+    }
+  } else {
+    uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t lo = ws[k], hi = ws[k] >> 16;
+      q[4 * k + 0] = __uint_as_float((lo & 0xFFu) | 0x4B000000u);
+      q[4 * k + 1] = __uint_as_float((lo & 0xFF00u) | 0x4B000000u);
+      q[4 * k + 2] = __uint_as_float((hi & 0xFFu) | 0x4B000000u);
+      q[4 * k + 3] = __uint_as_float((hi & 0xFF00u) | 0x4B000000u);
+    }
+  }
+}
+
 template <int BITS>
 LMX_DEV void unpack_quarter(const uint8_t* p, float (&q)[16]) {
   const float kMagic = 8388608.0f;  // 2^23
@@ -174,249 +221,305 @@ LMX_DEV float quarter_prescale(int j) {
   return (j & 1) ? 0.00390625f : 1.0f;
 }
 
-// Shared-memory layout of qmv_kernel (per CTA, 8 warps):
-//   [warp][nst][RB][SEGB] weight ring | [warp][nst] mbarriers |
-//   [2][rs][8][V] segment partials | [kQmmMaxNormRows] RMSNorm factors
-// K <= 4096: one CTA covers a row (rs = 8 / nseg row slots per CTA).
-// K  > 4096: a cluster of ceil(nseg/8) CTAs covers a row (rs = 1); rank 0
-//            sums the segment partials of all ranks through DSMEM.
+// Launch plan (computed on the host by qmv_plan(), identical for every CTA).
+struct QmvPlan {
+  int W;          // warps per row slot inside one CTA
+  int SPW;        // segments (512 k) per warp
+  int rs;         // row slots per CTA
+  int nst;        // TMA ring depth per warp
+  int RP, SP;     // smem row pitch of weights / of scales in a stage
+  int stage;      // bytes per warp stage
+  int red_off, bar_off, stage_off;
+  int sb_bulk;    // scales / biases come through the TMA ring
+  int full_rows;  // a warp owns whole rows: runs of rows move in one copy
+};
+
+LMX_DEV void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// qmv_kernel.  Each warp owns SPW consecutive segments of the rows of its row
+// slot and streams them through its own cp.async.bulk ring (no block-wide
+// barrier in the main loop).  When a row needs more than one warp (W > 1) or
+// more than one CTA (cluster), the first warp continues the left-to-right
+// segment chain with the other warps' per-segment sums (named barrier / DSMEM).
+// Row pairs share one fma.rn.f32x2; the fp32 op sequence of every output is
+// still the canonical one above.
 template <int BITS, int MT, int RB>
-__global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, int nst) {
+__global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan p) {
   constexpr int V = RB * MT;
-  constexpr int QB = 16 * BITS / 8;
+  constexpr int QB = 2 * BITS;
   constexpr int SEGB = 32 * QB;
+  constexpr int NW = kQmmThreads / 32;
+  constexpr int SPWMAX = (8 / MT) < 1 ? 1 : 8 / MT;
   constexpr int N1 = cmax1(V / 2), N2 = cmax1(V / 4), N3 = cmax1(V / 8), N4 = cmax1(V / 16),
                 N5 = cmax1(V / 32);
-  constexpr int NW = kQmmThreads / 32;
+  static_assert(RB >= 4 && RB % 4 == 0, "RB");
   extern __shared__ __align__(128) uint8_t smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int csize = (int)cluster.num_blocks(), crank = (int)cluster.block_rank();
 
   const int K = a.K, M = a.M;
-  const int nseg = (K + 511) >> 9;
+  const int nseg = (K + 511) >> 9, G = K >> 6, KWB = K * BITS / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int rs, seg, slot, lseg;
-  if (csize == 1) {
-    rs = NW / nseg;
-    seg = warp % nseg;
-    slot = warp / nseg;
-    lseg = seg;
-  } else {
-    rs = 1;
-    seg = crank * NW + warp;
-    slot = 0;
-    lseg = warp;
-  }
-  const bool wactive = slot < rs && seg < nseg;
+  const int slot = csize == 1 ? warp / p.W : 0;
+  const int widx = csize == 1 ? warp % p.W : warp;
+  const bool inslot = slot < p.rs;
+  const int gw = (csize == 1 ? 0 : crank * NW) + widx;  // warp rank along the row
+  const int seg0 = gw * p.SPW;
+  const int nsw = inslot ? max(0, min(p.SPW, nseg - seg0)) : 0;
+  const int kend = min(K, (seg0 + nsw) * 512);
+  const int PB = nsw > 0 ? (kend - seg0 * 512) * BITS / 8 : 0;
+  const int PGB = (nsw > 0 && p.sb_bulk) ? ((kend - seg0 * 512) >> 6) * 2 : 0;
+  const int nwr = csize == 1 ? p.W : NW * csize;  // warps along a row (incl. idle ones)
 
-  uint8_t* wst = smem + (size_t)warp * nst * RB * SEGB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NW * nst * RB * SEGB) + warp * nst;
-  float* red = reinterpret_cast<float*>(smem + (size_t)NW * nst * RB * SEGB + (size_t)NW * nst * 8);
-  float* fnorm = red + 2 * NW * V;
+  float* fnorm = reinterpret_cast<float*>(smem);
+  float* red = reinterpret_cast<float*>(smem + p.red_off);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.nst;
+  uint8_t* stages = smem + p.stage_off + (size_t)warp * p.nst * p.stage;
 
-  const int k0 = seg * 512 + 16 * lane;
-  const bool qvalid = wactive && k0 < K;
-  const uint32_t segbytes = wactive ? (uint32_t)(min(512, K - seg * 512) * BITS / 8) : 0u;
-  const int G = K >> 6;
-  const int g = k0 >> 6;
-  const int KWB = K * BITS / 8;
-  const int items = a.mode == QMM_SWIGLU ? 2 * a.N : a.N;
+  const int items = a.mode == QMM_SWIGLU ? ((a.N + RB / 2 - 1) / (RB / 2)) * RB : a.N;
   const int nbatch = (items + RB - 1) / RB;
   const int cid = blockIdx.x / csize, ncl = gridDim.x / csize;
-  const int bstride = ncl * rs;
-  const int niter = (nbatch - cid * rs + bstride - 1) / bstride;
+  const int bstride = ncl * p.rs;
+  const int niter = (nbatch - cid * p.rs + bstride - 1) / bstride;
   const int nmt = (M + MT - 1) / MT;
   const int ntask = niter > 0 ? niter * nmt : 0;
+  auto batch_of = [&](int t) { return cid * p.rs + slot + (t % niter) * bstride; };
 
-  auto batch_of = [&](int t) { return cid * rs + slot + (t % niter) * bstride; };
   auto issue = [&](int t) {
-    if (!wactive || t >= ntask) return;
-    const int st = t % nst, batch = batch_of(t);
-    uint32_t bytes = 0;
+    if (nsw == 0 || t >= ntask) return;
+    const int st = t % p.nst, batch = batch_of(t);
+    uint8_t* dst = stages + (size_t)st * p.stage;
+    uint64_t* bar = &bars[st];
+    uint32_t total = 0;
     int mi, row;
 #pragma unroll
     for (int i = 0; i < RB; ++i)
-      if (batch < nbatch && qmm_item_row(a, batch * RB + i, mi, row)) bytes += segbytes;
-    mbar_arrive_expect_tx(&bars[st], bytes);
-#pragma unroll
-    for (int i = 0; i < RB; ++i)
-      if (batch < nbatch && qmm_item_row(a, batch * RB + i, mi, row)) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(qmm_mat(a, mi).w) + (size_t)row * KWB +
-                             (size_t)seg * SEGB;
-        bulk_g2s(wst + (size_t)(st * RB + i) * SEGB, src, segbytes, &bars[st]);
+      if (batch < nbatch && qmm_item_row<RB>(a, batch * RB + i, mi, row)) total += PB + 2 * PGB;
+    mbar_arrive_expect_tx(bar, total);
+    if (batch >= nbatch) return;
+    int i = 0;
+    while (i < RB) {
+      int m0, r0;
+      if (!qmm_item_row<RB>(a, batch * RB + i, m0, r0)) { ++i; continue; }
+      int len = 1;
+      if (p.full_rows) {
+        while (i + len < RB) {
+          int m1, r1;
+          if (!qmm_item_row<RB>(a, batch * RB + i + len, m1, r1) || m1 != m0 || r1 != r0 + len) break;
+          ++len;
+        }
       }
+      const QmmMat& mm = qmm_mat(a, m0);
+      bulk_g2s(dst + (size_t)i * p.RP,
+               reinterpret_cast<const uint8_t*>(mm.w) + (size_t)r0 * KWB + (size_t)seg0 * SEGB,
+               (uint32_t)(len * PB), bar);
+      if (p.sb_bulk) {
+        bulk_g2s(dst + (size_t)RB * p.RP + (size_t)i * p.SP, mm.s + (size_t)r0 * G + seg0 * 8,
+                 (uint32_t)(len * PGB), bar);
+        bulk_g2s(dst + (size_t)RB * p.RP + (size_t)RB * p.SP + (size_t)i * p.SP,
+                 mm.b + (size_t)r0 * G + seg0 * 8, (uint32_t)(len * PGB), bar);
+      }
+      i += len;
+    }
   };
 
-  if (lane == 0 && wactive) {
-    for (int s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
+  if (lane == 0 && nsw > 0) {
+    for (int s = 0; s < p.nst; ++s) mbar_init(&bars[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int t = 0; t < p.nst; ++t) issue(t);
   }
-  __syncwarp();
-  if (lane == 0)
-    for (int t = 0; t < nst; ++t) issue(t);
 
   grid_wait();
   grid_launch_dependents();
 
   if (a.norm_w) {
     for (int m = warp; m < M; m += NW) {
-      const bf16_t* xrow = a.x + (size_t)m * K;
-      float p = 0.0f;
+      const bf16_t* xrow = a.x + (size_t)m * a.ldx;
+      float pp = 0.0f;
       for (int i = lane; i < K; i += 32) {
         float v = bf2f(xrow[i]);
-        p = __fmaf_rn(v, v, p);
+        pp = __fmaf_rn(v, v, pp);
       }
-      p = warp_sum_xor(p, 16, 1);
-      if (lane == 0) fnorm[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)K), a.eps)));
+      pp = warp_sum_xor(pp, 16, 1);
+      if (lane == 0) fnorm[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(pp, (float)K), a.eps)));
     }
   }
   __syncthreads();
 
-  float nw[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) nw[j] = (a.norm_w && qvalid) ? bf2f(a.norm_w[k0 + j]) : 1.0f;
-
-  float xr[MT][16];
-  float xg[MT];
+  // which rows of a batch this lane scales after the group-level reduction
+  const int q2 = ((lane & 1) << 1) | ((lane >> 1) & 1);
+  float xr[SPWMAX][MT][16];
+  float xg[SPWMAX][MT];
   bool abort_ = false;
 
   for (int t = 0; t < ntask; ++t) {
-    const int st = t % nst;
+    const int st = t % p.nst;
     const int it = t % niter;
     const int mt0 = (t / niter) * MT;
     const int mcnt = min(MT, M - mt0);
     const int batch = batch_of(t);
+    const uint8_t* sb = stages + (size_t)st * p.stage;
 
     if (it == 0) {
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float X = 0.0f;
-        if (m < mcnt && qvalid) {
-          const bf16_t* src = a.x + (size_t)(mt0 + m) * K + k0;
-          uint4 r0 = *reinterpret_cast<const uint4*>(src);
-          uint4 r1 = *reinterpret_cast<const uint4*>(src + 8);
-          const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-          const float f = a.norm_w ? fnorm[mt0 + m] : 1.0f;
+      for (int si = 0; si < SPWMAX; ++si) {
+        const int k0 = (seg0 + si) * 512 + 16 * lane;
+        const bool qv = si < nsw && k0 < K;
+        float nwv[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float v = (j & 1) ? hi_bf(rw[j >> 1]) : lo_bf(rw[j >> 1]);
-            if (a.norm_w) v = bf2f(f2bf(__fmul_rn(__fmul_rn(v, f), nw[j])));
-            X = __fadd_rn(X, v);
-            xr[m][j] = __fmul_rn(v, quarter_prescale<BITS>(j));
+        for (int j = 0; j < 16; ++j) nwv[j] = (a.norm_w && qv) ? bf2f(a.norm_w[k0 + j]) : 1.0f;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float X = 0.0f;
+          if (m < mcnt && qv) {
+            const bf16_t* src = a.x + (size_t)(mt0 + m) * a.ldx + k0;
+            uint4 r0 = *reinterpret_cast<const uint4*>(src);
+            uint4 r1 = *reinterpret_cast<const uint4*>(src + 8);
+            const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+            const float f = a.norm_w ? fnorm[mt0 + m] : 1.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v = (j & 1) ? hi_bf(rw[j >> 1]) : lo_bf(rw[j >> 1]);
+              if (a.norm_w) v = bf2f(f2bf(__fmul_rn(__fmul_rn(v, f), nwv[j])));
+              X = __fadd_rn(X, v);
+              xr[si][m][j] = __fmul_rn(v, quarter_prescale<BITS>(j));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xr[si][m][j] = 0.0f;
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) xr[m][j] = 0.0f;
+          X = __fadd_rn(X, __shfl_xor_sync(0xffffffffu, X, 1));
+          X = __fadd_rn(X, __shfl_xor_sync(0xffffffffu, X, 2));
+          xg[si][m] = X;
         }
-        X = __fadd_rn(X, __shfl_xor_sync(0xffffffffu, X, 1));
-        X = __fadd_rn(X, __shfl_xor_sync(0xffffffffu, X, 2));
-        xg[m] = X;
       }
     }
 
-    float sv[RB], bv[RB];
-#pragma unroll
-    for (int i = 0; i < RB; ++i) {
-      int mi, row;
-      sv[i] = 0.0f;
-      bv[i] = 0.0f;
-      if (qvalid && batch < nbatch && qmm_item_row(a, batch * RB + i, mi, row)) {
-        const QmmMat& mm = qmm_mat(a, mi);
-        sv[i] = bf2f(mm.s[(size_t)row * G + g]);
-        bv[i] = bf2f(mm.b[(size_t)row * G + g]);
-      }
-    }
+    if (nsw > 0 && !abort_)
+      if (!mbar_wait_bounded(&bars[st], (uint32_t)((t / p.nst) & 1), a.err, 0x51u)) abort_ = true;
 
-    if (wactive && !abort_)
-      if (!mbar_wait_bounded(&bars[st], (uint32_t)((t / nst) & 1), a.err, 0x51u)) abort_ = true;
-
-    float v[V];
+    float tot[N5];
+    int base = 0;
+    bool owner = true;
 #pragma unroll
-    for (int i = 0; i < RB; ++i) {
-      float q[16];
-      if (qvalid) {
-        unpack_quarter<BITS>(wst + (size_t)(st * RB + i) * SEGB + lane * QB, q);
-      } else {
+    for (int si = 0; si < SPWMAX; ++si) {
+      if (si < nsw) {
+        const int k0 = (seg0 + si) * 512 + 16 * lane;
+        const bool qv = k0 < K;
+        const int lg = si * 8 + (lane >> 2);  // group index inside this warp's portion
+        float v[V];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) q[j] = 0.0f;
-      }
+        for (int i = 0; i < RB; i += 2) {
+          float qa[16], qb[16];
+          if (qv) {
+            unpack_quarter_raw<BITS>(sb + (size_t)i * p.RP + (size_t)si * SEGB + lane * QB, qa);
+            unpack_quarter_raw<BITS>(sb + (size_t)(i + 1) * p.RP + (size_t)si * SEGB + lane * QB, qb);
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float Q = 0.0f;
-        if (m < mcnt) {
+            for (int j = 0; j < 16; ++j) sub_magic2(qa[j], qb[j]);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) Q = __fmaf_rn(q[j], xr[m][j], Q);
+            for (int j = 0; j < 16; ++j) { qa[j] = 0.0f; qb[j] = 0.0f; }
+          }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float A = 0.0f, B = 0.0f;
+            if (m < mcnt) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) fma2(A, B, qa[j], qb[j], xr[si][m][j]);
+            }
+            v[i * MT + m] = A;
+            v[(i + 1) * MT + m] = B;
+          }
         }
-        v[i * MT + m] = Q;
+        base = 0;
+        owner = true;
+        rs_level<V>(v, 1, lane & 1, base);
+        rs_level<N1>(v, 2, (lane >> 1) & 1, base);
+        // e = fma(s, d, b * xs) for the RB/4 rows x MT columns this lane holds
+#pragma unroll
+        for (int c = 0; c < RB / 4; ++c) {
+          const int i = q2 * (RB / 4) + c;
+          float s = 0.0f, b = 0.0f;
+          if (qv) {
+            if (p.sb_bulk) {
+              s = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * p.RP + (size_t)i * p.SP)[lg]);
+              b = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * p.RP + (size_t)RB * p.SP +
+                                                        (size_t)i * p.SP)[lg]);
+            } else {
+              int mi, row;
+              if (batch < nbatch && qmm_item_row<RB>(a, batch * RB + i, mi, row)) {
+                const QmmMat& mm = qmm_mat(a, mi);
+                s = bf2f(mm.s[(size_t)row * G + (k0 >> 6)]);
+                b = bf2f(mm.b[(size_t)row * G + (k0 >> 6)]);
+              }
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const int k = c * MT + m;
+            v[k] = __fmaf_rn(s, v[k], __fmul_rn(b, xg[si][m]));
+          }
+        }
+        rs_level<N2>(v, 4, (lane >> 2) & 1, base);
+        if (N2 < 2) owner = owner && !((lane >> 2) & 1);
+        rs_level<N3>(v, 8, (lane >> 3) & 1, base);
+        if (N3 < 2) owner = owner && !((lane >> 3) & 1);
+        rs_level<N4>(v, 16, (lane >> 4) & 1, base);
+        if (N4 < 2) owner = owner && !((lane >> 4) & 1);
+        if (gw == 0) {
+#pragma unroll
+          for (int k = 0; k < N5; ++k) tot[k] = si == 0 ? v[k] : __fadd_rn(tot[k], v[k]);
+        } else if (owner) {
+          float* dst = red + ((size_t)((t & 1) * NW + warp) * p.SPW + si) * V;
+#pragma unroll
+          for (int k = 0; k < N5; ++k) dst[base + k] = v[k];
+        }
       }
     }
     __syncwarp();
-    if (lane == 0 && !abort_) issue(t + nst);
+    if (lane == 0 && !abort_) issue(t + p.nst);  // this warp is done with stage st
 
-    // group level (lane bits 0,1): d = (Q0+Q1)+(Q2+Q3)
-    int base = 0;
-    bool owner = true;
-    rs_level<V>(v, 1, lane & 1, base);
-    if (V < 2) owner = owner && !(lane & 1);
-    rs_level<N1>(v, 2, (lane >> 1) & 1, base);
-    if (N1 < 2) owner = owner && !((lane >> 1) & 1);
-    // e = fma(s, d, b * xs) on the N2 items this lane holds
-#pragma unroll
-    for (int k = 0; k < N2; ++k) {
-      const int idx = base + k, i = idx / MT, m = idx % MT;
-      float s = sv[0], b = bv[0], xs = xg[0];
-#pragma unroll
-      for (int r = 1; r < RB; ++r)
-        if (i == r) { s = sv[r]; b = bv[r]; }
-#pragma unroll
-      for (int r = 1; r < MT; ++r)
-        if (m == r) xs = xg[r];
-      v[k] = __fmaf_rn(s, v[k], __fmul_rn(b, xs));
-    }
-    // segment tree over 8 groups (lane bits 2,3,4)
-    rs_level<N2>(v, 4, (lane >> 2) & 1, base);
-    if (N2 < 2) owner = owner && !((lane >> 2) & 1);
-    rs_level<N3>(v, 8, (lane >> 3) & 1, base);
-    if (N3 < 2) owner = owner && !((lane >> 3) & 1);
-    rs_level<N4>(v, 16, (lane >> 4) & 1, base);
-    if (N4 < 2) owner = owner && !((lane >> 4) & 1);
+    if (csize > 1) cluster.sync();
+    else if (p.W > 1 && inslot) named_barrier(1 + slot, p.W * 32);
 
-    float* rb = red + (size_t)(t & 1) * NW * V;
-    if (wactive && owner) {
-#pragma unroll
-      for (int k = 0; k < N5; ++k) rb[(size_t)warp * V + base + k] = v[k];
-    }
-    if (csize == 1) __syncthreads();
-    else cluster.sync();
-
-    // epilogue: segment partials left to right, then the fused op
-    const bool epi = (csize == 1) ? (slot < rs && seg == 0) : (crank == 0 && warp == 0);
-    if (epi) {
-      for (int idx = lane; idx < V; idx += 32) {
-        const int i = idx / MT, m = idx % MT;
-        int mi, row;
-        if (m >= mcnt || batch >= nbatch || !qmm_item_row(a, batch * RB + i, mi, row)) continue;
-        const int item = batch * RB + i;
-        float tot = 0.0f, tu = 0.0f;
-        for (int s = 0; s < nseg; ++s) {
+    if (gw == 0 && inslot) {
+      // continue the segment chain with the other warps' sums (in row order)
+      if (owner) {
+        for (int w2 = 1; w2 < nwr; ++w2) {
+          const int n2 = max(0, min(p.SPW, nseg - w2 * p.SPW));
           const float* src;
-          if (csize == 1) src = rb + (size_t)(slot * nseg + s) * V;
-          else src = cluster.map_shared_rank(rb, s / NW) + (size_t)(s % NW) * V;
-          tot = s == 0 ? src[idx] : __fadd_rn(tot, src[idx]);
-          if (a.mode == QMM_SWIGLU) tu = s == 0 ? src[idx + MT] : __fadd_rn(tu, src[idx + MT]);
+          if (csize == 1) src = red + ((size_t)((t & 1) * NW + slot * p.W + w2) * p.SPW) * V;
+          else src = cluster.map_shared_rank(red, w2 / NW) + ((size_t)((t & 1) * NW + w2 % NW) * p.SPW) * V;
+          for (int s2 = 0; s2 < n2; ++s2)
+#pragma unroll
+            for (int k = 0; k < N5; ++k) tot[k] = __fadd_rn(tot[k], src[(size_t)s2 * V + base + k]);
         }
-        const size_t orow = (size_t)(mt0 + m) * a.ldy;
-        if (a.mode == QMM_SWIGLU) {
-          if (mi == 0) a.y[orow + row] = swiglu_c(f2bf(tot), f2bf(tu));
-        } else {
-          bf16_t yv = f2bf(tot);
-          if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[orow + item])));
-          a.y[orow + item] = yv;
+      }
+      float tu[N5];
+#pragma unroll
+      for (int k = 0; k < N5; ++k) tu[k] = __shfl_xor_sync(0xffffffffu, tot[k], 1);
+      if (owner) {
+#pragma unroll
+        for (int k = 0; k < N5; ++k) {
+          const int idx = base + k, i = idx / MT, m = idx % MT;
+          int mi, row;
+          if (m >= mcnt || batch >= nbatch || !qmm_item_row<RB>(a, batch * RB + i, mi, row)) continue;
+          const size_t orow = (size_t)(mt0 + m) * a.ldy;
+          if (a.mode == QMM_SWIGLU) {
+            if (mi == 0) a.y[orow + row] = swiglu_c(f2bf(tot[k]), f2bf(tu[k]));
+          } else {
+            const int item = batch * RB + i;
+            bf16_t yv = f2bf(tot[k]);
+            if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[orow + item])));
+            a.y[orow + item] = yv;
+          }
         }
       }
     }
   }
-  if (csize > 1) cluster.sync();  // keep every rank's shared memory alive until rank 0 is done
+  if (csize > 1) cluster.sync();
 }
 
 }  // namespace lmx

@@ -31,7 +31,118 @@ SIGNATURES = {
     "lmx_quantized_matmul": (I, [P, P, P, P, P, I, I, I, I, I, P]),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
+    "lmx_model_create": (I, [P, U64, P]),
+    "lmx_model_view": (I, [P, I, P]),
+    "lmx_model_free": (I, [P]),
+    "lmx_model_weight": (I, [P, I, I, P, P, P]),
+    "lmx_cache_create": (I, [P, I, I, I, I, I, P]),
+    "lmx_cache_free": (I, [P]),
+    "lmx_cache_set_position": (I, [P, I, I]),
+    "lmx_cache_len": (I, [P, I, P]),
+    "lmx_forward": (I, [P, P, I, P, I, I, P]),
+    "lmx_spec_create": (I, [P, P, I, P, P]),
+    "lmx_spec_prefill": (I, [P, P]),
+    "lmx_spec_decode": (I, [P, I, P]),
+    "lmx_spec_result": (I, [P, P, P]),
+    "lmx_spec_free": (I, [P]),
 }
+
+
+class ModelConfig(C.Structure):
+    """lmx_model_config"""
+    _fields_ = [("hidden", I), ("layers", I), ("inter", I), ("heads", I), ("kv_heads", I),
+                ("head_dim", I), ("vocab", I), ("rope_theta", F), ("eps", F), ("qk_norm", I),
+                ("tied", I), ("bits", I), ("group_size", I)]
+
+
+class SpecConfig(C.Structure):
+    """lmx_spec_config"""
+    _fields_ = [("batch", I), ("K", I), ("max_tokens", I), ("prompt_len", I), ("kv_bits", I),
+                ("temperature", F), ("top_p", F), ("seed", U64)]
+
+
+# The benchmark configurations' architectures (random-initialised weights).
+QWEN3_0_6B = dict(hidden=1024, layers=28, inter=3072, heads=16, kv_heads=8, head_dim=128,
+                  vocab=151936, rope_theta=1e6, eps=1e-6, qk_norm=1, tied=1, bits=4, group_size=64)
+QWEN3_8B = dict(hidden=4096, layers=36, inter=12288, heads=32, kv_heads=8, head_dim=128,
+                vocab=151936, rope_theta=1e6, eps=1e-6, qk_norm=1, tied=0, bits=4, group_size=64)
+
+
+class Model:
+    """Owns an lmx model handle (synthetic seeded weights on the device)."""
+
+    def __init__(self, cfg: dict, seed: int, _handle=None, _parent=None):
+        self.cfg = dict(cfg)
+        self._parent = _parent
+        if _handle is not None:
+            self.h = _handle
+            return
+        h = C.c_void_p()
+        call("lmx_model_create", C.byref(ModelConfig(**cfg)), seed, C.byref(h))
+        self.h = h
+
+    def view(self, n_layers):
+        h = C.c_void_p()
+        call("lmx_model_view", self.h, n_layers, C.byref(h))
+        cfg = dict(self.cfg, layers=n_layers)
+        return Model(cfg, 0, _handle=h, _parent=self)
+
+    def close(self):
+        if self.h:
+            lib().lmx_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SpecDecoder:
+    """Speculative decoder over a target and a draft (or self-draft) model:
+    the reference's generate()/TokenIterator emission contract."""
+
+    def __init__(self, target: Model, draft, draft_layers: int, batch: int, K: int,
+                 max_tokens: int, prompt_len: int, kv_bits=16, temperature=0.0, top_p=1.0,
+                 seed=0):
+        self.cfg = SpecConfig(batch, K, max_tokens, prompt_len, kv_bits, temperature, top_p, seed)
+        h = C.c_void_p()
+        call("lmx_spec_create", target.h, draft.h if draft is not None else None, draft_layers,
+             C.byref(self.cfg), C.byref(h))
+        self.h = h
+        self._keep = (target, draft)
+
+    def prefill(self, prompts):
+        import numpy as np
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        assert p.shape == (self.cfg.batch, self.cfg.prompt_len)
+        call("lmx_spec_prefill", self.h, p.ctypes.data_as(C.c_void_p))
+
+    def decode(self, use_graph=True):
+        sec = C.c_double(0.0)
+        call("lmx_spec_decode", self.h, 1 if use_graph else 0, C.byref(sec))
+        return sec.value
+
+    def result(self):
+        import numpy as np
+        out = np.zeros((self.cfg.batch, self.cfg.max_tokens), np.int32)
+        st = np.zeros(4, np.int64)
+        call("lmx_spec_result", self.h, out.ctypes.data_as(C.c_void_p),
+             st.ctypes.data_as(C.c_void_p))
+        return out, dict(steps=int(st[0]), proposed=int(st[1]), accepted=int(st[2]),
+                         emitted=int(st[3]))
+
+    def close(self):
+        if self.h:
+            lib().lmx_spec_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def lib():

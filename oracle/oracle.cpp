@@ -433,7 +433,8 @@ extern "C" void orc_argmax(const uint16_t* logits, int rows, int V, int32_t* out
 //   [128s, 128s+128) clipped to the row's visible range 0..offset+t):
 //     score_j = fma chain over d ascending from 0
 //     m_s = max score;  p_j = exp(score_j - m_s)
-//     l_s = add chain of p_j over j ascending from 0
+//     l_s: lane partials  a_l = add chain of p_j over keys j = j0+l, j0+l+32, ...
+//          (l = 0..31, ascending, from 0), then butterfly (16,8,4,2,1) -> a_0
 //     o_s[d] = fma chain of p_j * v_j[d] over j ascending from 0
 //   combine over splits ascending: M = max m_s, w_s = exp(m_s - M),
 //     L = fma(w_s, l_s, L), O[d] = fma(w_s, o_s[d], O[d]) from 0
@@ -461,11 +462,17 @@ extern "C" void orc_sdpa(const uint16_t* q, const uint16_t* k, const uint16_t* v
           sc[j - j0] = a;
           m = std::max(m, a);
         }
-        float l = 0.0f;
+        float lp[32] = {0};
         for (int j = j0; j < j1; ++j) {
           sc[j - j0] = orc_exp(sc[j - j0] - m);
-          l = l + sc[j - j0];
+          lp[(j - j0) & 31] = lp[(j - j0) & 31] + sc[j - j0];
         }
+        for (int off = 16; off >= 1; off >>= 1) {
+          float t2[32];
+          for (int i = 0; i < 32; ++i) t2[i] = lp[i] + lp[i ^ off];
+          std::memcpy(lp, t2, sizeof(lp));
+        }
+        const float l = lp[0];
         for (int d = 0; d < D; ++d) {
           float o = 0.0f;
           for (int j = j0; j < j1; ++j) o = std::fma(sc[j - j0], bf2f(vb[(size_t)j * D + d]), o);

