@@ -1,0 +1,320 @@
+#!/usr/bin/env python3
+"""bench.py -- accepted tokens/s of 4-bit speculative decoding on B200.
+
+Workload (the configuration the headline metric is
+quoted on for bs1): Qwen3-0.6B architecture (28 layers, hidden 1024, 16 q /
+8 kv heads, head_dim 128, SwiGLU 3072, vocab 151936), synthetic N(0,0.02)
+weights quantized affine 4-bit group 64; draft = the target's first 2 layers
+plus the shared embedding / lm_head; K = 4 draft tokens; batch 1; 128-token
+uniform-random prompt; 256 greedy new tokens; bf16 KV cache.
+
+A "step" is one generation of that workload through the public API
+(lmx_spec_prefill with the prompt in host memory, lmx_spec_decode,
+lmx_spec_result reading the tokens back).  value = tokens / decode time
+(device events, prefill excluded, the reference's GenerateCompletionInfo
+definition); e2e = tokens / wall time of the whole API sequence including the
+host<->device copies and the prefill.  One process per GPU; for N > 1 each
+rank decodes its own replica (bs1 does not shard: "replicas only").
+
+--impl reference times the CPU restatement of the reference's algorithm
+(oracle/, the reference's MLX CPU backend cannot be built here) on the host
+cores with the same weights, prompt and decode loop.
+"""
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _load(name, path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+WORKLOADS = {
+    "qwen3-0.6b-selfdraft2-k4-bs1": dict(arch="QWEN3_0_6B", draft_layers=2, K=4, batch=1,
+                                         prompt=128, new=256, kv_bits=16, temperature=0.0,
+                                         top_p=1.0),
+}
+DEFAULT_WORKLOAD = "qwen3-0.6b-selfdraft2-k4-bs1"
+METRIC = "accepted tokens/s (4-bit spec decode, bs1/bs8); verify-pass HBM GB/s vs 8 TB/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            v = [x.strip() for x in line.split(",")]
+            if len(v) < 9:
+                continue
+            try:
+                sm.append(float(v[1]))
+                mx = float(v[2])
+            except ValueError:
+                continue
+            for n, flag in zip(names, v[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def reduce(world, vals, op="max"):
+    if world == 1:
+        return vals
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return t.tolist()
+
+
+def cpu_sample(wl, prompts, lmx_cfg, seed, steps, warmup):
+    """Time the oracle's decode loop on the host cores (prefill untimed)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    L = O.lib()
+    cfg = dict(lmx_cfg)
+    cfg["group"] = cfg.pop("group_size")
+    t0 = time.time()
+    model = L.orc_model_create(C.byref(O.ModelCfg(**cfg)), seed)
+    setup = time.time() - t0
+    prm = O.SpecParams(K=wl["K"], max_tokens=wl["new"], temperature=wl["temperature"],
+                       top_p=wl["top_p"], seed=seed, draft_layers=wl["draft_layers"])
+    p = np.ascontiguousarray(prompts, dtype=np.int32)
+    ss = L.orc_spec_session(model, None, O.ptr(p), p.shape[0], p.shape[1], prm, wl["kv_bits"])
+    st = np.zeros(5, np.int64)
+    L.orc_spec_session_step(ss, warmup)
+    L.orc_spec_session_result(ss, None, O.ptr(st))
+    e0, t0 = int(st[3]), time.perf_counter()
+    n = L.orc_spec_session_step(ss, steps)
+    dt = time.perf_counter() - t0
+    L.orc_spec_session_result(ss, None, O.ptr(st))
+    tokens = int(st[3]) - e0
+    L.orc_spec_session_free(ss)
+    L.orc_model_free(model)
+    return dict(value=tokens / dt if dt > 0 else 0.0, tokens=tokens, seconds=dt, spec_steps=n,
+                cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup)
+
+
+def run_reference(args, wl, world, rank):
+    if rank != 0:
+        return 0
+    lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+    arch = getattr(lmx, wl["arch"])
+    prompts = np.random.RandomState(args.seed).randint(0, arch["vocab"], (wl["batch"], wl["prompt"]))
+    # each timed step is one speculative step of the same decode (bounded sample)
+    r = cpu_sample(wl, prompts, arch, args.seed, args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * r["seconds"] / max(1, r["spec_steps"]), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "batch": wl["batch"], "K": wl["K"],
+                   "prompt": wl["prompt"], "new_tokens": wl["new"], "kv_bits": wl["kv_bits"]},
+        "cpu_baseline": {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
+                         "kind": "port",
+                         "sample": f"{args.steps} speculative steps ({r['tokens']} tokens) of the "
+                                   f"workload's decode after an untimed prefill, oracle/ C++ "
+                                   f"restatement, {r['cores']} threads"},
+        "e2e": {"value": round(r["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_lmx(args, wl, world, rank, local):
+    lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+    lmx.call("lmx_set_device", local)
+    arch = getattr(lmx, wl["arch"])
+    target = lmx.Model(arch, args.seed)
+    draft = target.view(wl["draft_layers"]) if wl["draft_layers"] else None
+    B, P = wl["batch"], wl["prompt"]
+    prompts = np.random.RandomState(args.seed + rank).randint(0, arch["vocab"], (B, P)).astype(np.int32)
+    sd = lmx.SpecDecoder(target, None, wl["draft_layers"], B, wl["K"], wl["new"], P,
+                         kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
+                         seed=args.seed)
+
+    def one():
+        t0 = time.perf_counter()
+        sd.prefill(prompts)
+        dsec = sd.decode(use_graph=True)
+        out, st = sd.result()
+        return time.perf_counter() - t0, dsec, out, st
+
+    for _ in range(args.warmup):
+        one()
+    clocks = Clocks(local)
+    barrier(world)
+    clocks.start()
+    wall, dec, toks, acc, prop, steps, replays = 0.0, 0.0, 0, 0, 0, 0, 0
+    for _ in range(args.steps):
+        w, d, out, st = one()
+        wall += w
+        dec += d
+        toks += min(st["emitted"], B * wl["new"])
+        acc += st["accepted"]
+        prop += st["proposed"]
+        steps += st["steps"]
+        replays += st["replays"]
+    barrier(world)
+    ck = clocks.stop()
+    # verify-pass and lm_head rooflines (CUDA events on the decoder's stream)
+    vsec, vbytes = sd.profile(0, 20)
+    hsec, hbytes = sd.profile(3, 20)
+    launches_per_step = sd.step_launches()
+    # prefill runs eagerly in 32-token chunks: per chunk embed + 6 per layer +
+    # length advance; then lm_head + argmax (target) and the bookkeeping kernel
+    L, dl = arch["layers"], wl["draft_layers"]
+    ct, cd = -(-P // 32), -(-(P - 1) // 32)
+    prefill_launches = ct * (2 + 6 * L) + 2 + cd * (2 + 6 * dl) + 1
+    gpu_launches = args.steps * (replays // max(1, args.steps) * launches_per_step + prefill_launches)
+    wall_m, dec_m = reduce(world, [wall, dec], "max")
+    toks_all = int(reduce(world, [float(toks)], "sum")[0])
+    peak, peak_kind = peaks()
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "verify_pass_qwen3_0.6b_k4_bs1.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_verify_pass:"):
+                    traffic = float(line.split(":")[1])
+    except OSError:
+        pass
+    achieved = vbytes / vsec / 1e9
+    res = {
+        "metric": METRIC, "value": round(toks_all / dec_m, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * wall_m / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "batch": B, "K": wl["K"], "prompt": P,
+                   "new_tokens": wl["new"], "kv_bits": wl["kv_bits"], "weights": "4-bit g64",
+                   "parallelism": f"replicas{world}",
+                   "l2": "weights (335 MB per verify pass) exceed L2; no flush"},
+        "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * wl["new"] * 4 + 40},
+        "roofline": {"bound": "hbm", "kernel": "verify pass (28 layers + lm_head, M=5)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "frac_of_8000": round(achieved / 8000.0, 4),
+                     "algorithmic_bytes": vbytes, "verify_pass_us": round(vsec * 1e6, 2),
+                     "traffic": traffic},
+        "lm_head_m1": {"us": round(hsec * 1e6, 2), "GBs": round(hbytes / hsec / 1e9, 1)},
+        "acceptance": {"accepted": acc, "proposed": prop,
+                       "rate": round(acc / prop, 4) if prop else None,
+                       "tokens_per_step": round(toks / max(1, steps), 3)},
+        "clocks": ck, "gpu_launches": int(gpu_launches),
+    }
+    if world == 1 and rank == 0 and not args.no_cpu:
+        r = cpu_sample(wl, prompts, arch, args.seed, args.cpu_steps, 1)
+        res["cpu_baseline"] = {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
+                               "kind": "port",
+                               "sample": f"{args.cpu_steps} speculative steps ({r['tokens']} tokens) "
+                                         "of the same decode after an untimed prefill (oracle/ "
+                                         "C++ restatement)"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    sd.close()
+    if draft is not None:
+        draft.close()
+    target.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="lmx", choices=["lmx", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            return run_reference(args, wl, world, rank)
+        return run_lmx(args, wl, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

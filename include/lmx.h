@@ -34,6 +34,9 @@ typedef enum {
 const char* lmx_last_error(void);
 /* Library version, e.g. "lmx-b200 0.1". */
 const char* lmx_version(void);
+/* Select the CUDA device for this thread's subsequent calls (one process per
+ * GPU: the rank's local device). */
+int lmx_set_device(int device);
 
 /* ---------------------------------------------------------------------------
  * quantized_matmul
@@ -136,10 +139,19 @@ int lmx_spec_prefill(void* spec, const int32_t* prompts_host /* [batch, prompt_l
 /* Decode until every sequence has emitted max_tokens; *seconds = device time
  * of the decode loop (prefill excluded). */
 int lmx_spec_decode(void* spec, int use_graph, double* seconds);
-/* out_host [batch, max_tokens]; stats_host[4] = steps, drafts proposed,
- * drafts accepted, tokens emitted (summed over sequences). */
+/* out_host [batch, max_tokens]; stats_host[5] = steps, drafts proposed,
+ * drafts accepted, tokens emitted (summed over sequences), steps enqueued
+ * (graph replays, including those after every sequence finished). */
 int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_host);
 int lmx_spec_free(void* spec);
+/* Measurement hooks (no reference counterpart; used by bench.py): time one
+ * piece of the step on the decoder's stream with CUDA events, `iters` launches
+ * after decode.  what: 0 verify pass, 1 one draft token, 2 lm_head at
+ * M = batch*(K+1), 3 lm_head at M = batch.  *bytes = algorithmic HBM bytes of
+ * one launch (packed weights + scales/biases + KV rows + activations). */
+int lmx_spec_profile(void* spec, int what, int iters, double* seconds, double* bytes);
+/* Kernel launches in one captured speculative step (graph node count). */
+int lmx_spec_step_launches(void* spec, int64_t* launches);
 
 #ifdef __cplusplus
 }

@@ -176,22 +176,40 @@ struct SdpaArgs {
 
 static constexpr int kPartStride = kHeadDim + 2;  // m, l, o[128]
 
-LMX_DEV float kv_elem(const KvDesc& kv, bool is_k, size_t row, int d) {
-  if (kv.bits == 16) return bf2f((is_k ? kv.k : kv.v)[row * kHeadDim + d]);
-  const int bits = kv.bits, per = 32 / bits;
-  const uint32_t w = (is_k ? kv.kq : kv.vq)[row * (kHeadDim * bits / 32) + d / per];
-  const int q = (int)((w >> ((d % per) * bits)) & ((1u << bits) - 1u));
-  const float s = bf2f((is_k ? kv.ks : kv.vs)[row * 2 + d / 64]);
-  const float b = bf2f((is_k ? kv.kb : kv.vb)[row * 2 + d / 64]);
-  return bf2f(f2bf(__fmaf_rn(s, (float)q, b)));
+// Dequantize (or copy) 8 consecutive K/V values d = 8c..8c+7 of one cache
+// row into packed bf16 (bf16(fma(s, q, b)) for the affine cache).
+LMX_DEV uint4 kv_chunk8(const KvDesc& kv, bool is_k, size_t row, int c) {
+  if (kv.bits == 16)
+    return *reinterpret_cast<const uint4*>((is_k ? kv.k : kv.v) + row * kHeadDim + c * 8);
+  const float s = bf2f((is_k ? kv.ks : kv.vs)[row * 2 + c / 8]);
+  const float b = bf2f((is_k ? kv.kb : kv.vb)[row * 2 + c / 8]);
+  const uint32_t* w = (is_k ? kv.kq : kv.vq) + row * (kHeadDim * kv.bits / 32);
+  uint32_t q[8];
+  if (kv.bits == 4) {
+    const uint32_t x = w[c];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = (x >> (4 * e)) & 0xFu;
+  } else {
+    const uint32_t x0 = w[2 * c], x1 = w[2 * c + 1];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { q[e] = (x0 >> (8 * e)) & 0xFFu; q[4 + e] = (x1 >> (8 * e)) & 0xFFu; }
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    o[e] = (uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e], b)) |
+           ((uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e + 1], b)) << 16);
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
+
+static constexpr int kKPitch = kHeadDim + 8;  // bf16 elements per staged K row (16 B pad)
 
 __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  bf16_t* Kt = reinterpret_cast<bf16_t*>(smem);                 // [D][kSplit] (transposed)
-  bf16_t* Vs = Kt + kHeadDim * kSplit;                           // [kSplit][D]
-  float* Qs = reinterpret_cast<float*>(Vs + kSplit * kHeadDim);  // [32][D]
-  float* S = Qs + kRowTile * kHeadDim;                           // [32][kSplit]
+  bf16_t* Ks = reinterpret_cast<bf16_t*>(smem);                   // [kSplit][kKPitch]
+  bf16_t* Vs = Ks + kSplit * kKPitch;                              // [kSplit][D]
+  float* Qs = reinterpret_cast<float*>(Vs + kSplit * kHeadDim);    // [32][D]
+  float* S = Qs + kRowTile * kHeadDim;                             // [32][kSplit]
   __shared__ bool is_last;
 
   grid_wait();
@@ -203,55 +221,78 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   if (nr <= 0) return;
   const int off = a.kv.len[b];
   const int t_last = (r0 + nr - 1) / G;
-  const int jmax = off + t_last + 1;  // keys visible to the tile's last row
+  const int jmax = off + t_last + 1;
   const int tile_splits = (jmax + kSplit - 1) / kSplit;
   if (split >= tile_splits) return;
   const int j0 = split * kSplit, jn = min(kSplit, jmax - j0);
+  const int jn4 = (jn + 3) & ~3;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t kvrow0 = ((size_t)b * a.kv.Hk + kvh) * a.kv.cap + j0;
 
-  // stage K (transposed), V and the scaled queries
-  for (int e = tid; e < kSplit * kHeadDim; e += 256) {
-    const int j = e / kHeadDim, d = e % kHeadDim;
-    float kv_k = 0.0f, kv_v = 0.0f;
+  // stage K, V rows [0, jn) as bf16 (16-byte chunks), zero V rows [jn, jn4)
+  for (int e = tid; e < jn4 * 16; e += 256) {
+    const int j = e >> 4, c = e & 15;
+    uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
     if (j < jn) {
-      kv_k = kv_elem(a.kv, true, kvrow0 + j, d);
-      kv_v = kv_elem(a.kv, false, kvrow0 + j, d);
+      kc = kv_chunk8(a.kv, true, kvrow0 + j, c);
+      vc = kv_chunk8(a.kv, false, kvrow0 + j, c);
     }
-    Kt[d * kSplit + j] = f2bf(kv_k);
-    Vs[j * kHeadDim + d] = f2bf(kv_v);
+    *reinterpret_cast<uint4*>(Ks + j * kKPitch + c * 8) = kc;
+    *reinterpret_cast<uint4*>(Vs + j * kHeadDim + c * 8) = vc;
   }
-  for (int e = tid; e < kRowTile * kHeadDim; e += 256) {
+  for (int e = tid; e < nr * kHeadDim; e += 256) {
     const int rr = e / kHeadDim, d = e % kHeadDim;
-    float qv = 0.0f;
-    if (rr < nr) {
-      const int r = r0 + rr, t = r / G, g = r % G;
-      qv = __fmul_rn(bf2f(a.q[((size_t)b * a.T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + g) * kHeadDim + d]),
-                     a.scale);
-    }
-    Qs[e] = qv;
+    const int r = r0 + rr, t = r / G, g = r % G;
+    Qs[e] = __fmul_rn(bf2f(a.q[((size_t)b * a.T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + g) * kHeadDim + d]),
+                      a.scale);
   }
   __syncthreads();
 
-  // scores: thread (key j, row parity)
+  // scores: thread (key j, row parity rp) holds up to 16 rows' accumulators;
+  // each accumulator is an fma chain over d ascending
   {
     const int j = tid & (kSplit - 1), rp = tid >> 7;
-    for (int rr = rp; rr < nr; rr += 2) {
-      const float* qr = Qs + rr * kHeadDim;
-      float acc = 0.0f;
-#pragma unroll 8
-      for (int d = 0; d < kHeadDim; ++d) acc = __fmaf_rn(qr[d], bf2f(Kt[d * kSplit + j]), acc);
-      S[rr * kSplit + j] = acc;
+    if (j < jn) {
+      float acc[kRowTile / 2];
+#pragma unroll
+      for (int i = 0; i < kRowTile / 2; ++i) acc[i] = 0.0f;
+      const bf16_t* kr = Ks + j * kKPitch;
+#pragma unroll 2
+      for (int dc = 0; dc < kHeadDim / 8; ++dc) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(kr + dc * 8);
+        const float k8[8] = {lo_bf(kw.x), hi_bf(kw.x), lo_bf(kw.y), hi_bf(kw.y),
+                             lo_bf(kw.z), hi_bf(kw.z), lo_bf(kw.w), hi_bf(kw.w)};
+#pragma unroll
+        for (int i = 0; i < kRowTile / 2; ++i) {
+          const int rr = rp + 2 * i;
+          if (rr < nr) {
+            const float4 qa = *reinterpret_cast<const float4*>(Qs + rr * kHeadDim + dc * 8);
+            const float4 qb = *reinterpret_cast<const float4*>(Qs + rr * kHeadDim + dc * 8 + 4);
+            float x = acc[i];
+            x = __fmaf_rn(qa.x, k8[0], x);
+            x = __fmaf_rn(qa.y, k8[1], x);
+            x = __fmaf_rn(qa.z, k8[2], x);
+            x = __fmaf_rn(qa.w, k8[3], x);
+            x = __fmaf_rn(qb.x, k8[4], x);
+            x = __fmaf_rn(qb.y, k8[5], x);
+            x = __fmaf_rn(qb.z, k8[6], x);
+            x = __fmaf_rn(qb.w, k8[7], x);
+            acc[i] = x;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRowTile / 2; ++i)
+        if (rp + 2 * i < nr) S[(rp + 2 * i) * kSplit + j] = acc[i];
     }
   }
   __syncthreads();
 
-  // softmax statistics per row: one warp per row
   float* part_base = a.part + ((((size_t)b * a.kv.Hk + kvh) * a.tiles + tile) * a.nsplit + split) *
                                   (size_t)kRowTile * kPartStride;
   for (int rr = warp; rr < nr; rr += 8) {
     const int t = (r0 + rr) / G;
-    const int vis = min(jn, off + t + 1 - j0);  // visible keys of this row in the split (may be <= 0)
+    const int vis = min(jn, off + t + 1 - j0);
     float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < kSplit / 32; ++k) {
@@ -276,18 +317,35 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   }
   __syncthreads();
 
-  // o[d] = sum_j p_j v_j[d] : thread (d, row parity), chain over the split's keys
+  // o[d] for the thread's rows: fma chains over keys ascending (p = 0 past a
+  // row's visible range and V rows are finite, so the extra terms are exact)
   {
     const int d = tid & (kHeadDim - 1), rp = tid >> 7;
-    for (int rr = rp; rr < nr; rr += 2) {
-      const float* pr = S + rr * kSplit;
-      float acc = 0.0f;
-      for (int j = 0; j < jn; ++j) acc = __fmaf_rn(pr[j], bf2f(Vs[j * kHeadDim + d]), acc);
-      part_base[rr * kPartStride + 2 + d] = acc;
+    float acc[kRowTile / 2];
+#pragma unroll
+    for (int i = 0; i < kRowTile / 2; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < jn4; j += 4) {
+      const float v0 = bf2f(Vs[j * kHeadDim + d]), v1 = bf2f(Vs[(j + 1) * kHeadDim + d]);
+      const float v2 = bf2f(Vs[(j + 2) * kHeadDim + d]), v3 = bf2f(Vs[(j + 3) * kHeadDim + d]);
+#pragma unroll
+      for (int i = 0; i < kRowTile / 2; ++i) {
+        const int rr = rp + 2 * i;
+        if (rr < nr) {
+          const float4 p4 = *reinterpret_cast<const float4*>(S + rr * kSplit + j);
+          float x = acc[i];
+          x = __fmaf_rn(p4.x, v0, x);
+          if (j + 1 < jn) x = __fmaf_rn(p4.y, v1, x);
+          if (j + 2 < jn) x = __fmaf_rn(p4.z, v2, x);
+          if (j + 3 < jn) x = __fmaf_rn(p4.w, v3, x);
+          acc[i] = x;
+        }
+      }
     }
+#pragma unroll
+    for (int i = 0; i < kRowTile / 2; ++i)
+      if (rp + 2 * i < nr) part_base[(rp + 2 * i) * kPartStride + 2 + d] = acc[i];
   }
 
-  // last block of this (b, kvh, tile) combines
   __threadfence();
   __syncthreads();
   unsigned* ctr = a.counters + ((size_t)b * a.kv.Hk + kvh) * a.tiles + tile;
@@ -318,7 +376,7 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   if (tid == 0) *ctr = 0u;
 }
 
-static constexpr size_t kSdpaSmem = (size_t)kHeadDim * kSplit * 2 * 2 +
+static constexpr size_t kSdpaSmem = (size_t)kSplit * kKPitch * 2 + (size_t)kSplit * kHeadDim * 2 +
                                     (size_t)kRowTile * kHeadDim * 4 + (size_t)kRowTile * kSplit * 4;
 
 }  // namespace lmx

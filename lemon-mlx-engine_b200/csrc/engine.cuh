@@ -464,6 +464,7 @@ struct Spec {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   bool prefilled = false;
+  int64_t replays = 0;  // graph replays (steps enqueued) of the last decode
   ~Spec() {
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
@@ -600,8 +601,9 @@ static int spec_decode(Spec& sp, int use_graph, double* seconds) {
   cudaEventCreate(&e1);
   cudaEventRecord(e0, st);
   const int check_every = 4;
+  sp.replays = 0;
   for (int it = 0; it < MT + 1 && !rc; it += check_every) {
-    for (int k = 0; k < check_every && !rc; ++k)
+    for (int k = 0; k < check_every && !rc; ++k, ++sp.replays)
       rc = use_graph ? cuda_check(cudaGraphLaunch(sp.exec, st), "graph launch") : spec_step(sp);
     if (rc) break;
     rc = cuda_check(cudaMemcpyAsync(em.data(), sp.s.emitted, B * 4, cudaMemcpyDeviceToHost, st), "emitted");
@@ -631,6 +633,8 @@ static int spec_decode(Spec& sp, int use_graph, double* seconds) {
 // C ABI: models, caches, forward, speculative generation
 // ---------------------------------------------------------------------------
 using namespace lmx;
+
+extern "C" int lmx_set_device(int device) { return cuda_check(cudaSetDevice(device), "set_device"); }
 
 extern "C" int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model) {
   if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create: null argument");
@@ -775,6 +779,7 @@ extern "C" int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_hos
     stats_host[1] = st * sp->cfg.K;
     stats_host[2] = ac;
     stats_host[3] = e;
+    stats_host[4] = sp->replays;
   }
   return rc;
 }
@@ -782,4 +787,92 @@ extern "C" int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_hos
 extern "C" int lmx_spec_free(void* spec) {
   delete (Spec*)spec;
   return LMX_OK;
+}
+
+namespace lmx {
+// Algorithmic HBM bytes of one quantized matrix read plus its activations.
+static double qmm_bytes(const QWeight& w, int bits, int M) {
+  return (double)w.N * w.K * bits / 8 + (double)w.N * (w.K / 64) * 4 + (double)M * w.K * 2 + (double)M * w.N * 2;
+}
+
+// Time `what` on the spec's stream with CUDA events (iters launches, after the
+// decode): 0 verify pass (target forward over K+1 tokens incl. lm_head),
+// 1 one draft token (draft forward T=1 incl. lm_head), 2 lm_head at
+// M = B(K+1), 3 lm_head at M = B.  bytes = algorithmic bytes per launch.
+static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* bytes) {
+  if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "profile before prefill");
+  const int B = sp.cfg.batch, K = sp.cfg.K, bits = sp.tm->c.bits;
+  cudaStream_t st = sp.st;
+  std::vector<int> tl(B), dl(B);
+  int rc = cuda_check(cudaMemcpy(tl.data(), sp.tc->len, B * 4, cudaMemcpyDeviceToHost), "len");
+  if (!rc) rc = cuda_check(cudaMemcpy(dl.data(), sp.dc->len, B * 4, cudaMemcpyDeviceToHost), "len");
+  if (rc) return rc;
+  double by = 0;
+  auto model_bytes = [&](const Model& m, int nl, int M, const std::vector<int>& lens, int T, bool head) {
+    double s = 0;
+    for (int l = 0; l < nl; ++l)
+      for (int k = 0; k < 7; ++k) s += qmm_bytes(m.L[l].w[k], bits, M);
+    for (int b = 0; b < B; ++b)  // K and V rows read by attention, new rows written
+      s += (double)nl * 2 * m.c.kv_heads * (lens[b] + T) * kHeadDim * (sp.cfg.kv_bits == 16 ? 2.0 : sp.cfg.kv_bits / 8.0 + 4.0 / 64);
+    if (head) s += qmm_bytes(m.head(), bits, M);
+    return s;
+  };
+  if (what == 0) by = model_bytes(*sp.tm, sp.tm->n_layers, B * (K + 1), tl, K + 1, true);
+  else if (what == 1) by = model_bytes(*sp.dm, sp.dl, B, dl, 1, true);
+  else if (what == 2) by = qmm_bytes(sp.tm->head(), bits, B * (K + 1));
+  else if (what == 3) by = qmm_bytes(sp.tm->head(), bits, B);
+  else return set_error(LMX_ERR_INVALID, "profile: what=%d", what);
+  auto once = [&]() -> int {
+    if (what == 0)
+      return forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
+    if (what == 1)
+      return forward(*sp.dm, *sp.dc, sp.dl, sp.s.drafts, K, 0, B, 1, sp.ws, sp.ws.logits, true, st);
+    QmmCall hc;
+    hc.x = sp.ws.h;
+    hc.norm_w = sp.tm->final_norm;
+    hc.eps = sp.tm->c.eps;
+    hc.mat[0] = sp.tm->head().mat();
+    hc.N = sp.tm->c.vocab;
+    hc.y = sp.ws.logits;
+    hc.ldy = sp.tm->c.vocab;
+    hc.M = what == 2 ? B * (K + 1) : B;
+    hc.K = sp.tm->c.hidden;
+    hc.bits = bits;
+    return launch_qmm(hc, st);
+  };
+  for (int i = 0; i < 3 && !rc; ++i) rc = once();
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, st);
+  for (int i = 0; i < iters && !rc; ++i) rc = once();
+  cudaEventRecord(e1, st);
+  if (!rc) rc = cuda_check(cudaEventSynchronize(e1), "profile");
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (seconds) *seconds = ms * 1e-3 / (iters > 0 ? iters : 1);
+  if (bytes) *bytes = by;
+  return rc;
+}
+
+// Kernel launches of one speculative step (the graph's node count).
+static int spec_step_launches(Spec& sp, int64_t* n) {
+  if (!sp.graph) return set_error(LMX_ERR_INVALID, "no graph captured yet");
+  size_t nodes = 0;
+  int rc = cuda_check(cudaGraphGetNodes(sp.graph, nullptr, &nodes), "graph nodes");
+  *n = (int64_t)nodes;
+  return rc;
+}
+}  // namespace lmx
+
+extern "C" int lmx_spec_profile(void* spec, int what, int iters, double* seconds, double* bytes) {
+  if (!spec) return set_error(LMX_ERR_INVALID, "spec_profile: null argument");
+  return spec_profile(*(Spec*)spec, what, iters, seconds, bytes);
+}
+
+extern "C" int lmx_spec_step_launches(void* spec, int64_t* launches) {
+  if (!spec || !launches) return set_error(LMX_ERR_INVALID, "spec_step_launches: null argument");
+  return spec_step_launches(*(Spec*)spec, launches);
 }

@@ -1,6 +1,11 @@
 // lmx.cu -- kernels' host launchers and the op-level C ABI (include/lmx.h).
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
+#include <map>
+#include <tuple>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -62,6 +67,47 @@ int device_sms() { return dev().sms; }
 unsigned* device_error_word() { return dev().err; }
 
 // ---------------------------------------------------------------------------
+// TMA tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry
+// point), cached per (address, shape, box): weights never move, so the maps
+// of a model are encoded once.
+// ---------------------------------------------------------------------------
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_map_mu;
+std::map<std::tuple<const void*, int, uint64_t, uint64_t, int, int>, CUtensorMap> g_maps;
+}  // namespace
+
+static int tensor_map_2d(const void* base, CUtensorMapDataType dt, int esize, uint64_t cols, uint64_t rows,
+                         int box_w, int box_h, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  const auto key = std::make_tuple(base, (int)dt, cols, rows, box_w, box_h);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return LMX_OK;
+  }
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+      return set_error(LMX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_w, (cuuint32_t)box_h};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMap m;
+  CUresult r = g_encode(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LMX_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
+  g_maps[key] = m;
+  *out = m;
+  return LMX_OK;
+}
+
+// ---------------------------------------------------------------------------
 // K1 launcher
 // ---------------------------------------------------------------------------
 // Plan the K1 launch: warps per row, segments per warp, ring depth and the
@@ -72,42 +118,47 @@ struct QmvShape {
   size_t smem;
 };
 
-static int qmv_plan(int K, int MT, int bits, QmvShape& out) {
+static int qmv_plan(int K, int MT, int bits, bool sb_aligned, QmvShape& out) {
   constexpr int NW = kQmmThreads / 32;
   const int SEGB = 64 * bits;
   const int nseg = (K + 511) / 512, G = K / 64, KWB = K * bits / 8;
-  const int spw_reg = MT >= 8 ? 1 : 8 / MT;
-  const int spw_smem = bits == 4 ? 8 : 4;
-  const int spw_cap = spw_reg < spw_smem ? spw_reg : spw_smem;
-  const int Wt = (nseg + spw_cap - 1) / spw_cap;
   QmvPlan& p = out.p;
-  if (Wt <= NW) {
+  // one 512-k segment per warp: W warps per row (a cluster when W > 8)
+  if (nseg <= NW) {
     out.csize = 1;
-    p.W = Wt;
-    p.SPW = (nseg + p.W - 1) / p.W;
-    p.rs = NW / p.W;
+    p.W = nseg;
+    p.rs = NW / nseg;
   } else {
-    out.csize = (Wt + NW - 1) / NW;
+    out.csize = (nseg + NW - 1) / NW;
     p.W = NW;
-    p.SPW = (nseg + NW * out.csize - 1) / (NW * out.csize);
     p.rs = 1;
   }
-  if (out.csize > 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d too large for M=%d", K, MT);
-  p.full_rows = out.csize == 1 && p.W == 1;
-  p.sb_bulk = (G % 8) == 0;
-  p.RP = p.full_rows ? KWB : p.SPW * SEGB;
-  p.SP = p.sb_bulk ? (p.full_rows ? G * 2 : p.SPW * 16) : 0;
+  p.SPW = 1;
+  if (out.csize > 8) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d too large", K);
+  p.sb_bulk = (G % 8) == 0 && sb_aligned;
+  p.RP = SEGB;
+  (void)KWB;
   int RB = MT == 1 ? 16 : (MT == 8 ? 4 : 8);
-  while (RB > 4 && RB * (p.RP + 2 * p.SP) > 12 * 1024) RB /= 2;
+  int nst = 0;
+  for (;; RB /= 2) {
+    const int V = RB * MT;
+    // scale / bias regions: two halves at 128-byte aligned offsets (TMA
+    // destinations must be 128-byte aligned; SWIGLU loads each half apart)
+    p.SPH = ((RB / 2) * 16 + 127) / 128 * 128;
+    p.SP = p.sb_bulk ? 2 * p.SPH : 0;
+    p.stage = ((RB * p.RP + 2 * p.SP) + 127) / 128 * 128;
+    p.red_off = kQmmMaxNormRows * 4;
+    const int red_size = (p.W > 1 || out.csize > 1) ? 2 * NW * p.SPW * V * 4 : 0;
+    p.vbuf_off = (p.red_off + red_size + 127) / 128 * 128;
+    const int vbuf_size = NW * V * 32 * 4;
+    p.bar_off = p.vbuf_off + vbuf_size;
+    const int budget = MT <= 2 ? 110 * 1024 : 200 * 1024;  // two CTAs per SM for MT <= 2
+    const int fixed = p.bar_off + NW * 8 * 8 + 128;
+    nst = (budget - fixed) / (NW * p.stage);
+    if (nst >= 2 || RB <= 4) break;
+  }
   out.RB = RB;
-  const int V = RB * MT;
-  p.stage = ((RB * p.RP + 2 * RB * p.SP) + 127) / 128 * 128;
-  p.red_off = kQmmMaxNormRows * 4;
-  const int red_size = (p.W > 1 || out.csize > 1) ? 2 * NW * p.SPW * V * 4 : 0;
-  p.bar_off = (p.red_off + red_size + 7) / 8 * 8;
-  const int fixed = p.bar_off + NW * 8 * 8 + 128;
-  int nst = (200 * 1024 - fixed) / (NW * p.stage);
-  if (nst > 8) nst = 8;
+  if (nst > 6) nst = 6;
   if (nst < 2) return set_error(LMX_ERR_UNSUPPORTED, "qmm: K=%d stage too large", K);
   p.nst = nst;
   p.stage_off = (p.bar_off + NW * nst * 8 + 127) / 128 * 128;
@@ -116,7 +167,27 @@ static int qmv_plan(int K, int MT, int bits, QmvShape& out) {
 }
 
 template <int BITS, int MT, int RB>
-static int launch_qmv_t(const QmmArgs& a, const QmvShape& sh, cudaStream_t st) {
+static int launch_qmv_t(const QmmArgs& a_in, const QmvShape& sh, cudaStream_t st) {
+  QmmArgs a = a_in;
+  QmmMaps mp;
+  std::memset(&mp, 0, sizeof(mp));
+  const int boxh = a.mode == QMM_SWIGLU ? RB / 2 : RB;
+  const int G = a.K / 64, WPR = a.K * BITS / 32;
+  int pv = 0, cv = 0;
+  for (int i = 0; i < a.nmat; ++i) {
+    a.pstart[i] = pv;
+    a.cstart[i] = cv;
+    pv += (a.mat[i].rows + RB - 1) / RB * RB;
+    cv += a.mat[i].rows;
+    int rc = tensor_map_2d(a.mat[i].w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, WPR, a.mat[i].rows, 16 * BITS, boxh, &mp.w[i]);
+    if (!rc && sh.p.sb_bulk)
+      rc = tensor_map_2d(a.mat[i].s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, G, a.mat[i].rows, 8, boxh, &mp.s[i]);
+    if (!rc && sh.p.sb_bulk)
+      rc = tensor_map_2d(a.mat[i].b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, G, a.mat[i].rows, 8, boxh, &mp.b[i]);
+    if (rc) return rc;
+  }
+  a.items = a.mode == QMM_SWIGLU ? ((a.N + RB / 2 - 1) / (RB / 2)) * RB
+                                 : a.pstart[a.nmat - 1] + a.mat[a.nmat - 1].rows;
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
@@ -128,10 +199,9 @@ static int launch_qmv_t(const QmmArgs& a, const QmvShape& sh, cudaStream_t st) {
     cudaFuncSetAttribute(qmv_kernel<BITS, MT, RB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     attr_set[d & 63] = true;
   }
-  const int items = a.mode == QMM_SWIGLU ? ((a.N + RB / 2 - 1) / (RB / 2)) * RB : a.N;
-  const int nbatch = (items + RB - 1) / RB;
+  const int nbatch = (a.items + RB - 1) / RB;
   int nclusters = (nbatch + sh.p.rs - 1) / sh.p.rs;
-  const int max_clusters = device_sms() / sh.csize;
+  const int max_clusters = device_sms() * (MT <= 2 ? 2 : 1) / sh.csize;
   if (nclusters > max_clusters) nclusters = max_clusters;
   if (nclusters < 1) nclusters = 1;
   cudaLaunchConfig_t cfg = {};
@@ -152,14 +222,17 @@ static int launch_qmv_t(const QmmArgs& a, const QmvShape& sh, cudaStream_t st) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, a, sh.p), "qmm: launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, mp, a, sh.p), "qmm: launch");
 }
 
 template <int BITS>
 static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
   const int MT = a.M <= 1 ? 1 : (a.M <= 2 ? 2 : (a.M <= 4 ? 4 : 8));
   QmvShape sh;
-  int rc = qmv_plan(a.K, MT, BITS, sh);
+  bool sb_aligned = true;
+  for (int i = 0; i < a.nmat; ++i)
+    sb_aligned = sb_aligned && !((uintptr_t)a.mat[i].s & 15) && !((uintptr_t)a.mat[i].b & 15);
+  int rc = qmv_plan(a.K, MT, BITS, sb_aligned, sh);
   if (rc) return rc;
   switch (MT * 100 + sh.RB) {
     case 116: return launch_qmv_t<BITS, 1, 16>(a, sh, st);

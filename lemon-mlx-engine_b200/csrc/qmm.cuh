@@ -31,6 +31,7 @@
 //   y    = bf16(t_0 + t_1 + ... )                  segments left to right
 #pragma once
 #include <cooperative_groups.h>
+#include <cuda.h>
 #include "lmx_common.cuh"
 namespace cg = cooperative_groups;
 
@@ -59,6 +60,15 @@ struct QmmArgs {
   int M, K;
   int mode;
   unsigned* err;         // device error word (bounded-wait timeouts)
+  int pstart[3];         // PLAIN/RESID: first virtual row of each matrix (multiple of RB)
+  int cstart[3];         // PLAIN/RESID: first output column of each matrix
+  int items;             // virtual rows (incl. padding) / swiglu items
+};
+
+// TMA descriptors: weights as uint32 [rows][K*bits/32], scales and biases as
+// bf16 [rows][K/64]; box = one 512-k segment x (RB or RB/2 for SWIGLU) rows.
+struct QmmMaps {
+  CUtensorMap w[3], s[3], b[3];
 };
 
 static constexpr int kQmmThreads = 256;
@@ -83,16 +93,24 @@ LMX_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 }
 LMX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#ifdef LMX_MBAR_POLL
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+#else
   asm volatile(
       "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 // Bounded wait: gives up after ~2^22 polls (seconds), flags the error word.
 LMX_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
-  for (uint32_t i = 0; i < (1u << 22); ++i)
+  for (uint32_t i = 0; i < (1u << 26); ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicExch(err, code);
   return false;
@@ -109,19 +127,23 @@ LMX_DEV bool qmm_item_row(const QmmArgs& a, int item, int& mi, int& row) {
     row = bt * (RB / 2) + w % (RB / 2);
     return row < a.N;
   }
-  int r = item;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
-    if (i < a.nmat) {
-      if (r < a.mat[i].rows) {
-        mi = i;
-        row = r;
-        return true;
-      }
-      r -= a.mat[i].rows;
+    if (i < a.nmat && item >= a.pstart[i] && item < a.pstart[i] + a.mat[i].rows) {
+      mi = i;
+      row = item - a.pstart[i];
+      return true;
     }
   }
   return false;
+}
+
+LMX_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 LMX_DEV const QmmMat& qmm_mat(const QmmArgs& a, int mi) {
@@ -227,11 +249,11 @@ struct QmvPlan {
   int SPW;        // segments (512 k) per warp
   int rs;         // row slots per CTA
   int nst;        // TMA ring depth per warp
-  int RP, SP;     // smem row pitch of weights / of scales in a stage
+  int RP, SP;     // smem bytes of one stage's weight rows / of its scale rows
+  int SPH;        // offset of the second (SWIGLU up-rows) scale box, 128-aligned
   int stage;      // bytes per warp stage
-  int red_off, bar_off, stage_off;
+  int red_off, vbuf_off, bar_off, stage_off;
   int sb_bulk;    // scales / biases come through the TMA ring
-  int full_rows;  // a warp owns whole rows: runs of rows move in one copy
 };
 
 LMX_DEV void named_barrier(int id, int nthreads) {
@@ -246,12 +268,12 @@ LMX_DEV void named_barrier(int id, int nthreads) {
 // Row pairs share one fma.rn.f32x2; the fp32 op sequence of every output is
 // still the canonical one above.
 template <int BITS, int MT, int RB>
-__global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan p) {
+__global__ void __launch_bounds__(kQmmThreads, MT <= 2 ? 2 : 1) qmv_kernel(const __grid_constant__ QmmMaps mp, QmmArgs a, QmvPlan p) {
   constexpr int V = RB * MT;
   constexpr int QB = 2 * BITS;
   constexpr int SEGB = 32 * QB;
   constexpr int NW = kQmmThreads / 32;
-  constexpr int SPWMAX = (8 / MT) < 1 ? 1 : 8 / MT;
+  constexpr int SPWMAX = 1;
   constexpr int N1 = cmax1(V / 2), N2 = cmax1(V / 4), N3 = cmax1(V / 8), N4 = cmax1(V / 16),
                 N5 = cmax1(V / 32);
   static_assert(RB >= 4 && RB % 4 == 0, "RB");
@@ -260,7 +282,7 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
   const int csize = (int)cluster.num_blocks(), crank = (int)cluster.block_rank();
 
   const int K = a.K, M = a.M;
-  const int nseg = (K + 511) >> 9, G = K >> 6, KWB = K * BITS / 8;
+  const int nseg = (K + 511) >> 9, G = K >> 6;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = csize == 1 ? warp / p.W : 0;
   const int widx = csize == 1 ? warp % p.W : warp;
@@ -268,18 +290,15 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
   const int gw = (csize == 1 ? 0 : crank * NW) + widx;  // warp rank along the row
   const int seg0 = gw * p.SPW;
   const int nsw = inslot ? max(0, min(p.SPW, nseg - seg0)) : 0;
-  const int kend = min(K, (seg0 + nsw) * 512);
-  const int PB = nsw > 0 ? (kend - seg0 * 512) * BITS / 8 : 0;
-  const int PGB = (nsw > 0 && p.sb_bulk) ? ((kend - seg0 * 512) >> 6) * 2 : 0;
   const int nwr = csize == 1 ? p.W : NW * csize;  // warps along a row (incl. idle ones)
 
   float* fnorm = reinterpret_cast<float*>(smem);
   float* red = reinterpret_cast<float*>(smem + p.red_off);
+  float* vbuf = reinterpret_cast<float*>(smem + p.vbuf_off) + (size_t)warp * V * 32;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.nst;
   uint8_t* stages = smem + p.stage_off + (size_t)warp * p.nst * p.stage;
 
-  const int items = a.mode == QMM_SWIGLU ? ((a.N + RB / 2 - 1) / (RB / 2)) * RB : a.N;
-  const int nbatch = (items + RB - 1) / RB;
+  const int nbatch = (a.items + RB - 1) / RB;
   const int cid = blockIdx.x / csize, ncl = gridDim.x / csize;
   const int bstride = ncl * p.rs;
   const int niter = (nbatch - cid * p.rs + bstride - 1) / bstride;
@@ -287,41 +306,31 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
   const int ntask = niter > 0 ? niter * nmt : 0;
   auto batch_of = [&](int t) { return cid * p.rs + slot + (t % niter) * bstride; };
 
+  // issuer (lane 0 of each warp): one 2D tensor copy per tensor and stage
+  // (two for SWIGLU: the gate rows and the up rows of the batch)
   auto issue = [&](int t) {
     if (nsw == 0 || t >= ntask) return;
     const int st = t % p.nst, batch = batch_of(t);
     uint8_t* dst = stages + (size_t)st * p.stage;
     uint64_t* bar = &bars[st];
-    uint32_t total = 0;
-    int mi, row;
-#pragma unroll
-    for (int i = 0; i < RB; ++i)
-      if (batch < nbatch && qmm_item_row<RB>(a, batch * RB + i, mi, row)) total += PB + 2 * PGB;
-    mbar_arrive_expect_tx(bar, total);
-    if (batch >= nbatch) return;
-    int i = 0;
-    while (i < RB) {
-      int m0, r0;
-      if (!qmm_item_row<RB>(a, batch * RB + i, m0, r0)) { ++i; continue; }
-      int len = 1;
-      if (p.full_rows) {
-        while (i + len < RB) {
-          int m1, r1;
-          if (!qmm_item_row<RB>(a, batch * RB + i + len, m1, r1) || m1 != m0 || r1 != r0 + len) break;
-          ++len;
-        }
-      }
-      const QmmMat& mm = qmm_mat(a, m0);
-      bulk_g2s(dst + (size_t)i * p.RP,
-               reinterpret_cast<const uint8_t*>(mm.w) + (size_t)r0 * KWB + (size_t)seg0 * SEGB,
-               (uint32_t)(len * PB), bar);
+    int mi = 0, row = 0;
+    const bool valid = batch < nbatch && qmm_item_row<RB>(a, batch * RB, mi, row);
+    if (!valid) {
+      mbar_arrive_expect_tx(bar, 0);
+      return;
+    }
+    const int nbox = a.mode == QMM_SWIGLU ? 2 : 1;
+    const int bh = RB / nbox;
+    mbar_arrive_expect_tx(bar, (uint32_t)(nbox * bh * (SEGB + (p.sb_bulk ? 32 : 0))));
+    // every TMA destination is 128-byte aligned: weight boxes at multiples of
+    // bh*SEGB (>= 512 B), the up-rows' scale / bias boxes at p.SPH
+    for (int k = 0; k < nbox; ++k) {
+      const int m = a.mode == QMM_SWIGLU ? k : mi;
+      tma_load_2d(dst + (size_t)k * bh * SEGB, &mp.w[m], seg0 * (SEGB / 4), row, bar);
       if (p.sb_bulk) {
-        bulk_g2s(dst + (size_t)RB * p.RP + (size_t)i * p.SP, mm.s + (size_t)r0 * G + seg0 * 8,
-                 (uint32_t)(len * PGB), bar);
-        bulk_g2s(dst + (size_t)RB * p.RP + (size_t)RB * p.SP + (size_t)i * p.SP,
-                 mm.b + (size_t)r0 * G + seg0 * 8, (uint32_t)(len * PGB), bar);
+        tma_load_2d(dst + (size_t)RB * SEGB + (size_t)k * p.SPH, &mp.s[m], seg0 * 8, row, bar);
+        tma_load_2d(dst + (size_t)RB * SEGB + p.SP + (size_t)k * p.SPH, &mp.b[m], seg0 * 8, row, bar);
       }
-      i += len;
     }
   };
 
@@ -409,13 +418,15 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
         const int k0 = (seg0 + si) * 512 + 16 * lane;
         const bool qv = k0 < K;
         const int lg = si * 8 + (lane >> 2);  // group index inside this warp's portion
-        float v[V];
-#pragma unroll
+        // quarter dot-products of the RB rows, a row pair per iteration (one
+        // fma.rn.f32x2 per k); the loop is rolled to keep the kernel small, so
+        // the sums are parked in shared memory (vbuf[item][lane])
+#pragma unroll 1
         for (int i = 0; i < RB; i += 2) {
           float qa[16], qb[16];
           if (qv) {
-            unpack_quarter_raw<BITS>(sb + (size_t)i * p.RP + (size_t)si * SEGB + lane * QB, qa);
-            unpack_quarter_raw<BITS>(sb + (size_t)(i + 1) * p.RP + (size_t)si * SEGB + lane * QB, qb);
+            unpack_quarter_raw<BITS>(sb + (size_t)i * SEGB + lane * QB, qa);
+            unpack_quarter_raw<BITS>(sb + (size_t)(i + 1) * SEGB + lane * QB, qb);
 #pragma unroll
             for (int j = 0; j < 16; ++j) sub_magic2(qa[j], qb[j]);
           } else {
@@ -429,10 +440,14 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
 #pragma unroll
               for (int j = 0; j < 16; ++j) fma2(A, B, qa[j], qb[j], xr[si][m][j]);
             }
-            v[i * MT + m] = A;
-            v[(i + 1) * MT + m] = B;
+            vbuf[(i * MT + m) * 32 + lane] = A;
+            vbuf[((i + 1) * MT + m) * 32 + lane] = B;
           }
         }
+        __syncwarp();
+        float v[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) v[k] = vbuf[k * 32 + lane];
         base = 0;
         owner = true;
         rs_level<V>(v, 1, lane & 1, base);
@@ -444,9 +459,10 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
           float s = 0.0f, b = 0.0f;
           if (qv) {
             if (p.sb_bulk) {
-              s = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * p.RP + (size_t)i * p.SP)[lg]);
-              b = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * p.RP + (size_t)RB * p.SP +
-                                                        (size_t)i * p.SP)[lg]);
+              const size_t so = (a.mode == QMM_SWIGLU && i >= RB / 2) ? (size_t)p.SPH + (size_t)(i - RB / 2) * 16
+                                                                      : (size_t)i * 16;
+              s = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * SEGB + so)[lg]);
+              b = bf2f(reinterpret_cast<const bf16_t*>(sb + (size_t)RB * SEGB + p.SP + so)[lg]);
             } else {
               int mi, row;
               if (batch < nbatch && qmm_item_row<RB>(a, batch * RB + i, mi, row)) {
@@ -510,10 +526,10 @@ __global__ void __launch_bounds__(kQmmThreads, 1) qmv_kernel(QmmArgs a, QmvPlan 
           if (a.mode == QMM_SWIGLU) {
             if (mi == 0) a.y[orow + row] = swiglu_c(f2bf(tot[k]), f2bf(tu[k]));
           } else {
-            const int item = batch * RB + i;
+            const int col = (mi == 0 ? a.cstart[0] : (mi == 1 ? a.cstart[1] : a.cstart[2])) + row;
             bf16_t yv = f2bf(tot[k]);
-            if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[orow + item])));
-            a.y[orow + item] = yv;
+            if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[orow + col])));
+            a.y[orow + col] = yv;
           }
         }
       }

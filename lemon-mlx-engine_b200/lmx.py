@@ -27,6 +27,7 @@ class LmxError(RuntimeError):
 SIGNATURES = {
     "lmx_last_error": (C.c_char_p, []),
     "lmx_version": (C.c_char_p, []),
+    "lmx_set_device": (I, [I]),
     "lmx_device_error": (I, [C.POINTER(C.c_uint), I]),
     "lmx_quantized_matmul": (I, [P, P, P, P, P, I, I, I, I, I, P]),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
@@ -45,6 +46,8 @@ SIGNATURES = {
     "lmx_spec_decode": (I, [P, I, P]),
     "lmx_spec_result": (I, [P, P, P]),
     "lmx_spec_free": (I, [P]),
+    "lmx_spec_profile": (I, [P, I, I, P, P]),
+    "lmx_spec_step_launches": (I, [P, P]),
 }
 
 
@@ -127,11 +130,21 @@ class SpecDecoder:
     def result(self):
         import numpy as np
         out = np.zeros((self.cfg.batch, self.cfg.max_tokens), np.int32)
-        st = np.zeros(4, np.int64)
+        st = np.zeros(5, np.int64)
         call("lmx_spec_result", self.h, out.ctypes.data_as(C.c_void_p),
              st.ctypes.data_as(C.c_void_p))
         return out, dict(steps=int(st[0]), proposed=int(st[1]), accepted=int(st[2]),
-                         emitted=int(st[3]))
+                         emitted=int(st[3]), replays=int(st[4]))
+
+    def profile(self, what, iters=20):
+        sec, by = C.c_double(0.0), C.c_double(0.0)
+        call("lmx_spec_profile", self.h, what, iters, C.byref(sec), C.byref(by))
+        return sec.value, by.value
+
+    def step_launches(self):
+        n = C.c_int64(0)
+        call("lmx_spec_step_launches", self.h, C.byref(n))
+        return n.value
 
     def close(self):
         if self.h:

@@ -10,6 +10,7 @@
 #include "oracle.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -886,53 +887,93 @@ extern "C" int orc_forward(void* model, void* cache, int n_layers, const int32_t
 //   accept: greedy prefix match, or rejection sampling (streams 1 and 2);
 //   emit y, d1..d_acc; the next y is the correction / bonus token;
 //   rollback: target length p+acc+1, draft length p+acc.
-extern "C" int orc_spec_generate(void* target, void* draft, const int32_t* prompts, int B, int P,
-                                 const orc_spec_params* prm, int kv_bits, int32_t* out,
-                                 int64_t* stats) {
-  Model& tm = *(Model*)target;
-  Model& dm = draft ? *(Model*)draft : tm;
-  const int dl = draft ? dm.c.layers : prm->draft_layers;
-  const int K = prm->K, V = tm.c.vocab, MT = prm->max_tokens;
-  const bool greedy = !(prm->temperature > 0.0f);
-  if (K < 1 || dl < 1 || dl > dm.c.layers || P < 2 || dm.c.vocab != V) return 1;
-  const int cap = P + MT + K + 8;
-  std::unique_ptr<Cache> tc((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, kv_bits));
-  std::unique_ptr<Cache> dc((Cache*)orc_cache_create(&dm, dl, B, cap, kv_bits));
-  if (!tc || !dc) return 1;
+namespace {
+struct Session {
+  Model* tm;
+  Model* dm;
+  int dl, B, P, K, V, MT;
+  orc_spec_params prm;
+  bool greedy;
+  std::unique_ptr<Cache> tc, dc;
+  std::vector<int32_t> y, last, out;
+  std::vector<int> emitted;
+  uint32_t step = 1;
+  int64_t steps = 0, proposed = 0, accepted = 0, prefill_ns = 0;
+};
+}  // namespace
+
+extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prompts, int B, int P,
+                                  const orc_spec_params* prm, int kv_bits) {
+  auto ss = std::make_unique<Session>();
+  ss->tm = (Model*)target;
+  ss->dm = draft ? (Model*)draft : ss->tm;
+  ss->dl = draft ? ss->dm->c.layers : prm->draft_layers;
+  ss->B = B;
+  ss->P = P;
+  ss->K = prm->K;
+  ss->V = ss->tm->c.vocab;
+  ss->MT = prm->max_tokens;
+  ss->prm = *prm;
+  ss->greedy = !(prm->temperature > 0.0f);
+  Model& tm = *ss->tm;
+  Model& dm = *ss->dm;
+  const int K = ss->K, V = ss->V, dl = ss->dl;
+  if (K < 1 || dl < 1 || dl > dm.c.layers || P < 2 || dm.c.vocab != V) return nullptr;
+  const int cap = P + ss->MT + K + 8;
+  ss->tc.reset((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, kv_bits));
+  ss->dc.reset((Cache*)orc_cache_create(&dm, dl, B, cap, kv_bits));
+  if (!ss->tc || !ss->dc) return nullptr;
+  const auto t0 = std::chrono::steady_clock::now();
   std::vector<uint16_t> lg((size_t)B * V);
-  int rc = forward_impl(tm, *tc, tm.c.layers, prompts, B, P, lg.data(), true);
-  if (rc) return rc;
-  std::vector<int32_t> y(B), last(B), pp((size_t)B * (P - 1));
+  if (forward_impl(tm, *ss->tc, tm.c.layers, prompts, B, P, lg.data(), true)) return nullptr;
+  ss->y.resize(B);
+  ss->last.resize(B);
+  std::vector<int32_t> pp((size_t)B * (P - 1));
   for (int b = 0; b < B; ++b) {
-    y[b] = greedy ? orc_sample(&lg[(size_t)b * V], V, 0.0f, 1.0f, 0)
-                  : orc_sample(&lg[(size_t)b * V], V, prm->temperature, prm->top_p,
-                               orc_uniform24(prm->seed, b, 0, 0, 3));
-    last[b] = prompts[(size_t)b * P + P - 1];
+    ss->y[b] = ss->greedy ? orc_sample(&lg[(size_t)b * V], V, 0.0f, 1.0f, 0)
+                          : orc_sample(&lg[(size_t)b * V], V, prm->temperature, prm->top_p,
+                                       orc_uniform24(prm->seed, b, 0, 0, 3));
+    ss->last[b] = prompts[(size_t)b * P + P - 1];
     std::memcpy(&pp[(size_t)b * (P - 1)], &prompts[(size_t)b * P], (P - 1) * 4);
   }
-  rc = forward_impl(dm, *dc, dl, pp.data(), B, P - 1, nullptr, true);
-  if (rc) return rc;
-  std::vector<int> emitted(B, 0);
-  std::vector<int32_t> d((size_t)B * K), tok2((size_t)B * 2), vt((size_t)B * (K + 1)),
-      outt(K + 1);
-  std::vector<uint16_t> qlog((size_t)B * K * V), tlog((size_t)B * (K + 1) * V);
-  int64_t steps = 0, proposed = 0, accepted = 0;
-  for (uint32_t step = 1;; ++step) {
+  if (forward_impl(dm, *ss->dc, dl, pp.data(), B, P - 1, nullptr, true)) return nullptr;
+  ss->prefill_ns =
+      std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
+  ss->emitted.assign(B, 0);
+  ss->out.assign((size_t)B * ss->MT, 0);
+  return ss.release();
+}
+
+// Run up to n speculative steps (stops early once every sequence has
+// max_tokens).  Returns the number of steps run, or -1 on error.
+extern "C" int orc_spec_session_step(void* sp, int n) {
+  Session& ss = *(Session*)sp;
+  Model& tm = *ss.tm;
+  Model& dm = *ss.dm;
+  const int B = ss.B, K = ss.K, V = ss.V, MT = ss.MT, dl = ss.dl;
+  const orc_spec_params* prm = &ss.prm;
+  const bool greedy = ss.greedy;
+  std::vector<int32_t> d((size_t)B * K), tok2((size_t)B * 2), vt((size_t)B * (K + 1)), outt(K + 1);
+  std::vector<uint16_t> lg((size_t)B * V), qlog((size_t)B * K * V), tlog((size_t)B * (K + 1) * V);
+  int done_steps = 0;
+  for (; done_steps < n; ++done_steps) {
     bool any = false;
-    for (int b = 0; b < B; ++b) any |= emitted[b] < MT;
+    for (int b = 0; b < B; ++b) any |= ss.emitted[b] < MT;
     if (!any) break;
+    const uint32_t step = ss.step++;
     for (int b = 0; b < B; ++b) {
-      tok2[2 * b] = last[b];
-      tok2[2 * b + 1] = y[b];
+      tok2[2 * b] = ss.last[b];
+      tok2[2 * b + 1] = ss.y[b];
     }
     for (int i = 0; i < K; ++i) {
-      if (i == 0) rc = forward_impl(dm, *dc, dl, tok2.data(), B, 2, lg.data(), true);
+      int rc;
+      if (i == 0) rc = forward_impl(dm, *ss.dc, dl, tok2.data(), B, 2, lg.data(), true);
       else {
         std::vector<int32_t> t1(B);
         for (int b = 0; b < B; ++b) t1[b] = d[(size_t)b * K + i - 1];
-        rc = forward_impl(dm, *dc, dl, t1.data(), B, 1, lg.data(), true);
+        rc = forward_impl(dm, *ss.dc, dl, t1.data(), B, 1, lg.data(), true);
       }
-      if (rc) return rc;
+      if (rc) return -1;
       for (int b = 0; b < B; ++b) {
         std::memcpy(&qlog[((size_t)b * K + i) * V], &lg[(size_t)b * V], (size_t)V * 2);
         d[(size_t)b * K + i] =
@@ -942,14 +983,18 @@ extern "C" int orc_spec_generate(void* target, void* draft, const int32_t* promp
       }
     }
     for (int b = 0; b < B; ++b) {
-      vt[(size_t)b * (K + 1)] = y[b];
+      vt[(size_t)b * (K + 1)] = ss.y[b];
       for (int i = 0; i < K; ++i) vt[(size_t)b * (K + 1) + 1 + i] = d[(size_t)b * K + i];
     }
     std::vector<int> p0(B);
-    for (int b = 0; b < B; ++b) p0[b] = tc->len[b];
-    rc = forward_impl(tm, *tc, tm.c.layers, vt.data(), B, K + 1, tlog.data(), false);
-    if (rc) return rc;
+    for (int b = 0; b < B; ++b) p0[b] = ss.tc->len[b];
+    if (forward_impl(tm, *ss.tc, tm.c.layers, vt.data(), B, K + 1, tlog.data(), false)) return -1;
     for (int b = 0; b < B; ++b) {
+      if (ss.emitted[b] >= MT) {  // finished: recompute the same step, never advance
+        ss.tc->len[b] = p0[b];
+        ss.dc->len[b] = p0[b] - 1;
+        continue;
+      }
       int acc;
       if (greedy) {
         acc = orc_accept_greedy(&tlog[(size_t)b * (K + 1) * V], &d[(size_t)b * K], K, V, outt.data());
@@ -960,29 +1005,73 @@ extern "C" int orc_spec_generate(void* target, void* draft, const int32_t* promp
                                     &d[(size_t)b * K], K, V, prm->temperature, prm->top_p,
                                     ua.data(), orc_uniform24(prm->seed, b, step, 0, 2), outt.data());
       }
-      if (emitted[b] >= MT) {  // finished: recompute the same step, never advance
-        tc->len[b] = p0[b];
-        dc->len[b] = p0[b] - 1;
-        continue;
-      }
-      out[(size_t)b * MT + emitted[b]++] = y[b];
+      ss.out[(size_t)b * MT + ss.emitted[b]++] = ss.y[b];
       for (int i = 0; i < acc; ++i)
-        if (emitted[b] < MT) out[(size_t)b * MT + emitted[b]++] = outt[i];
-      last[b] = acc > 0 ? outt[acc - 1] : y[b];
-      y[b] = outt[acc];
-      tc->len[b] = p0[b] + acc + 1;
-      dc->len[b] = p0[b] + acc;
-      accepted += acc;
-      proposed += K;
+        if (ss.emitted[b] < MT) ss.out[(size_t)b * MT + ss.emitted[b]++] = outt[i];
+      ss.last[b] = acc > 0 ? outt[acc - 1] : ss.y[b];
+      ss.y[b] = outt[acc];
+      ss.tc->len[b] = p0[b] + acc + 1;
+      ss.dc->len[b] = p0[b] + acc;
+      ss.accepted += acc;
+      ss.proposed += K;
     }
-    steps += 1;
+    ss.steps += 1;
   }
+  return done_steps;
+}
+
+// out [B, max_tokens]; stats: steps, proposed, accepted, emitted, prefill ns.
+extern "C" void orc_spec_session_result(void* sp, int32_t* out, int64_t* stats) {
+  Session& ss = *(Session*)sp;
+  if (out) std::memcpy(out, ss.out.data(), ss.out.size() * 4);
   if (stats) {
-    stats[0] = steps;
-    stats[1] = proposed;
-    stats[2] = accepted;
+    int64_t e = 0;
+    for (int v : ss.emitted) e += v;
+    stats[0] = ss.steps;
+    stats[1] = ss.proposed;
+    stats[2] = ss.accepted;
+    stats[3] = e;
+    stats[4] = ss.prefill_ns;
   }
-  return 0;
+}
+
+extern "C" void orc_spec_session_free(void* sp) { delete (Session*)sp; }
+
+// Speculative decode (src/common/generate.cpp:669-933 generalised to a draft
+// model).  Per step and sequence, with p = target length and y = the token at
+// position p (already decided, emitted first -- "d0"):
+//   draft forward over [x_(p-1), y] (re-writes position p-1 so a fully
+//   accepted previous step needs no catch-up), then K-1 single-token forwards;
+//   each draft token is argmax (greedy) or a draw from q (uniform stream 0);
+//   verify: target forward over [y, d1..dK] (K+1 tokens);
+//   accept: greedy prefix match, or rejection sampling (streams 1 and 2);
+//   emit y, d1..d_acc; the next y is the correction / bonus token;
+//   rollback: target length p+acc+1, draft length p+acc.
+extern "C" int orc_spec_generate(void* target, void* draft, const int32_t* prompts, int B, int P,
+                                 const orc_spec_params* prm, int kv_bits, int32_t* out,
+                                 int64_t* stats) {
+  void* ss = orc_spec_session(target, draft, prompts, B, P, prm, kv_bits);
+  if (!ss) return 1;
+  const auto t0 = std::chrono::steady_clock::now();
+  int rc = 0;
+  while (true) {
+    int n = orc_spec_session_step(ss, 1 << 20);
+    if (n < 0) { rc = 2; break; }
+    if (n < (1 << 20)) break;
+  }
+  const int64_t dec =
+      std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
+  int64_t st[5];
+  orc_spec_session_result(ss, out, st);
+  if (stats) {
+    stats[0] = st[0];
+    stats[1] = st[1];
+    stats[2] = st[2];
+    stats[3] = st[4];
+    stats[4] = dec;
+  }
+  orc_spec_session_free(ss);
+  return rc;
 }
 
 extern "C" int orc_generate(void* target, const int32_t* prompts, int B, int P, int max_tokens,
@@ -1004,4 +1093,12 @@ extern "C" int orc_generate(void* target, const int32_t* prompts, int B, int P, 
     orc_argmax(lg.data(), B, V, y.data());
   }
   return 0;
+}
+
+extern "C" int orc_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
 }

@@ -130,10 +130,18 @@ typedef struct {
 
 /* Speculative decode with a separate draft model (draft may be the target
  * itself with draft_layers > 0).  prompts [B, P].  out [B, max_tokens].
- * stats[0]=steps, [1]=proposed, [2]=accepted (summed over sequences). */
+ * stats[0]=steps, [1]=proposed, [2]=accepted (summed over sequences),
+ * [3]=prefill ns, [4]=decode ns (wall clock). */
 int orc_spec_generate(void* target, void* draft, const int32_t* prompts, int B, int P,
                       const orc_spec_params* prm, int kv_bits, int32_t* out, int64_t* stats);
-/* Plain (non-speculative) greedy/stochastic decode, same emission contract. */
+/* The same loop as a session: prefill once, then run steps (CPU baseline). */
+void* orc_spec_session(void* target, void* draft, const int32_t* prompts, int B, int P,
+                       const orc_spec_params* prm, int kv_bits);
+int orc_spec_session_step(void* session, int n_steps);
+void orc_spec_session_result(void* session, int32_t* out, int64_t* stats);
+void orc_spec_session_free(void* session);
+int orc_threads(void);
+/* Plain (non-speculative) greedy decode, same emission contract. */
 int orc_generate(void* target, const int32_t* prompts, int B, int P, int max_tokens,
                  int kv_bits, int32_t* out);
 

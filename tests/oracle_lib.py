@@ -84,6 +84,11 @@ def _declare(L):
         "orc_forward": (I, [P, P, I, P, I, I, P]),
         "orc_spec_generate": (I, [P, P, P, I, I, C.POINTER(SpecParams), I, P, P]),
         "orc_generate": (I, [P, P, I, I, I, I, P]),
+        "orc_threads": (I, []),
+        "orc_spec_session": (P, [P, P, P, I, I, C.POINTER(SpecParams), I]),
+        "orc_spec_session_step": (I, [P, I]),
+        "orc_spec_session_result": (None, [P, P, P]),
+        "orc_spec_session_free": (None, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

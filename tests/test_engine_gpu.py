@@ -93,7 +93,7 @@ def test_forward_logits_bit_exact_with_rollback(lmx, models, bits, kv_bits):
 def oracle_spec(o, prompts, K, MT, kv_bits, draft_layers, temperature=0.0, top_p=1.0, seed=0):
     B, P = prompts.shape
     out = np.zeros((B, MT), np.int32)
-    st = np.zeros(3, np.int64)
+    st = np.zeros(5, np.int64)
     prm = O.SpecParams(K=K, max_tokens=MT, temperature=temperature, top_p=top_p, seed=seed,
                        draft_layers=draft_layers)
     assert O.lib().orc_spec_generate(o, None, O.ptr(np.ascontiguousarray(prompts)), B, P, prm,

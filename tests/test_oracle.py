@@ -179,7 +179,7 @@ def test_speculative_equals_plain_greedy(tiny_model, kv_bits):
     prompts = np.random.RandomState(1).randint(0, TINY["vocab"], (B, P)).astype(np.int32)
     spec = np.zeros((B, MT), np.int32)
     plain = np.zeros((B, MT), np.int32)
-    st = np.zeros(3, np.int64)
+    st = np.zeros(5, np.int64)
     prm = O.SpecParams(K=4, max_tokens=MT, temperature=0.0, top_p=1.0, seed=0, draft_layers=1)
     assert L.orc_spec_generate(tiny_model, None, O.ptr(prompts), B, P, prm, kv_bits, O.ptr(spec),
                                O.ptr(st)) == 0
