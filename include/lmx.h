@@ -69,6 +69,38 @@ int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream);
 
 
 /* ---------------------------------------------------------------------------
+ * KV cache view and decode / verify attention.
+ * Replaces cache->update + sdpa() -> mx::fast::scaled_dot_product_attention
+ * (include/mlx-lm/common/attention_utils.h:60-77, src/common/kv_cache.cpp:
+ * 34-110, 271-298) for the speculative step.  lengths[b] is the number of
+ * cached rows BEFORE the current block; the block's T rows are already
+ * written at rows [lengths[b], lengths[b]+T).  Query row t of sequence b sees
+ * keys 0 .. lengths[b]+t (the reference's [T, offset+T] causal mask,
+ * src/common/kv_cache.cpp:15-30).  head_dim must be 128, group size 64.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  int batch, kv_heads, head_dim, capacity;
+  int bits;                 /* 16 = bf16 cache, 8 or 4 = affine quantized      */
+  void* k;                  /* bits 16: bf16 [batch][kv_heads][capacity][128]  */
+  void* v;
+  uint32_t* k_packed;       /* bits 4/8: [batch][kv_heads][capacity][128*bits/32] */
+  uint32_t* v_packed;
+  void* k_scales;           /* bits 4/8: bf16 [batch][kv_heads][capacity][2]   */
+  void* k_biases;
+  void* v_scales;
+  void* v_biases;
+  int32_t* lengths;         /* [batch] rows cached before the current block    */
+} lmx_kv;
+
+/* Scratch bytes lmx_sdpa_decode needs for this shape (split partials and
+ * per-tile counters).  The scratch must be zero-filled before its first use;
+ * every call leaves it ready for the next. */
+size_t lmx_sdpa_scratch_bytes(int batch, int T, int heads, int kv_heads, int capacity);
+/* q, out: bf16 [batch*T, heads*128] (q already normed and roped). */
+int lmx_sdpa_decode(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* scratch,
+                    size_t scratch_bytes, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Models.  Replaces the ModelContext function table of a loaded Qwen3 /
  * Llama model (include/mlx-lm/common/model_container.h:20-51; graphs
  * src/llm/models/qwen3.cpp:69-220, llama.cpp:203-469).  Weights are synthetic

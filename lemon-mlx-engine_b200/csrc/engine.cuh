@@ -876,3 +876,91 @@ extern "C" int lmx_spec_step_launches(void* spec, int64_t* launches) {
   if (!spec || !launches) return set_error(LMX_ERR_INVALID, "spec_step_launches: null argument");
   return spec_step_launches(*(Spec*)spec, launches);
 }
+
+// ---------------------------------------------------------------------------
+// C ABI: attention over a caller-described KV cache
+// ---------------------------------------------------------------------------
+namespace lmx {
+static int kv_from_c(const lmx_kv* c, KvDesc& d) {
+  if (!c || c->head_dim != kHeadDim || c->batch < 1 || c->kv_heads < 1 || c->capacity < 1 || !c->lengths)
+    return set_error(LMX_ERR_INVALID, "lmx_kv: bad descriptor (head_dim must be 128)");
+  std::memset(&d, 0, sizeof(d));
+  d.B = c->batch;
+  d.Hk = c->kv_heads;
+  d.cap = c->capacity;
+  d.bits = c->bits;
+  d.len = c->lengths;
+  if (c->bits == 16) {
+    if (!c->k || !c->v || ((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15))
+      return set_error(LMX_ERR_INVALID, "lmx_kv: k/v must be 16-byte aligned");
+    d.k = (bf16_t*)c->k;
+    d.v = (bf16_t*)c->v;
+  } else if (c->bits == 4 || c->bits == 8) {
+    if (!c->k_packed || !c->v_packed || !c->k_scales || !c->k_biases || !c->v_scales || !c->v_biases)
+      return set_error(LMX_ERR_INVALID, "lmx_kv: packed cache pointers missing");
+    d.kq = c->k_packed;
+    d.vq = c->v_packed;
+    d.ks = (bf16_t*)c->k_scales;
+    d.kb = (bf16_t*)c->k_biases;
+    d.vs = (bf16_t*)c->v_scales;
+    d.vb = (bf16_t*)c->v_biases;
+  } else {
+    return set_error(LMX_ERR_UNSUPPORTED, "lmx_kv: bits %d", c->bits);
+  }
+  return LMX_OK;
+}
+
+static void sdpa_geometry(int T, int heads, int kv_heads, int capacity, int& tiles, int& splits) {
+  const int G = heads / kv_heads;
+  tiles = (G * T + kRowTile - 1) / kRowTile;
+  splits = (capacity + kSplit - 1) / kSplit;
+}
+
+static size_t sdpa_scratch_bytes(int B, int T, int heads, int kv_heads, int capacity) {
+  int tiles, splits;
+  sdpa_geometry(T, heads, kv_heads, capacity, tiles, splits);
+  const size_t part = (size_t)B * kv_heads * tiles * splits * kRowTile * kPartStride * 4;
+  const size_t ctr = (size_t)B * kv_heads * tiles * 4;
+  return (part + 255) / 256 * 256 + (ctr + 255) / 256 * 256;
+}
+
+// Shared by lmx_sdpa_decode and its no-allocation variant: checks the shape
+// and launches sdpa_split_kernel with the given scratch (partials first, then
+// the counters).
+static int sdpa_call(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* scratch,
+                     size_t scratch_bytes, void* out, cudaStream_t st) {
+  KvDesc d;
+  int rc = kv_from_c(kv, d);
+  if (rc) return rc;
+  if (!q || !out || T < 1 || heads < 1 || heads % d.Hk)
+    return set_error(LMX_ERR_INVALID, "sdpa: bad shape");
+  const size_t need = sdpa_scratch_bytes(d.B, T, heads, d.Hk, d.cap);
+  if (!scratch || scratch_bytes < need)
+    return set_error(LMX_ERR_INVALID, "sdpa: scratch needs %zu bytes", need);
+  int tiles, splits;
+  sdpa_geometry(T, heads, d.Hk, d.cap, tiles, splits);
+  SdpaArgs sa;
+  sa.q = (const bf16_t*)q;
+  sa.kv = d;
+  sa.T = T;
+  sa.Hq = heads;
+  sa.scale = scale;
+  sa.nsplit = splits;
+  sa.tiles = tiles;
+  sa.part = (float*)scratch;
+  const size_t part = (size_t)d.B * d.Hk * tiles * splits * kRowTile * kPartStride * 4;
+  sa.counters = (unsigned*)((char*)scratch + (part + 255) / 256 * 256);
+  sa.out = (bf16_t*)out;
+  return launch_sdpa(sa, d.B, st);
+}
+}  // namespace lmx
+
+extern "C" size_t lmx_sdpa_scratch_bytes(int batch, int T, int heads, int kv_heads, int capacity) {
+  if (batch < 1 || T < 1 || heads < 1 || kv_heads < 1 || capacity < 1 || heads % kv_heads) return 0;
+  return sdpa_scratch_bytes(batch, T, heads, kv_heads, capacity);
+}
+
+extern "C" int lmx_sdpa_decode(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* scratch,
+                               size_t scratch_bytes, void* out, void* stream) {
+  return sdpa_call(q, kv, T, heads, scale, scratch, scratch_bytes, out, (cudaStream_t)stream);
+}

@@ -32,6 +32,8 @@ SIGNATURES = {
     "lmx_quantized_matmul": (I, [P, P, P, P, P, I, I, I, I, I, P]),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
+    "lmx_sdpa_scratch_bytes": (C.c_size_t, [I, I, I, I, I]),
+    "lmx_sdpa_decode": (I, [P, P, I, I, F, P, C.c_size_t, P, P]),
     "lmx_model_create": (I, [P, U64, P]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
@@ -49,6 +51,13 @@ SIGNATURES = {
     "lmx_spec_profile": (I, [P, I, I, P, P]),
     "lmx_spec_step_launches": (I, [P, P]),
 }
+
+
+class KvDesc(C.Structure):
+    """lmx_kv"""
+    _fields_ = [("batch", I), ("kv_heads", I), ("head_dim", I), ("capacity", I), ("bits", I),
+                ("k", P), ("v", P), ("k_packed", P), ("v_packed", P), ("k_scales", P),
+                ("k_biases", P), ("v_scales", P), ("v_biases", P), ("lengths", P)]
 
 
 class ModelConfig(C.Structure):
