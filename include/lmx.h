@@ -99,6 +99,19 @@ size_t lmx_sdpa_scratch_bytes(int batch, int T, int heads, int kv_heads, int cap
 /* q, out: bf16 [batch*T, heads*128] (q already normed and roped). */
 int lmx_sdpa_decode(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* scratch,
                     size_t scratch_bytes, void* out, void* stream);
+/* lmx_sdpa_decode for callers that cannot allocate device memory (a host
+ * framework that owns every device allocation and forbids cudaMalloc in its
+ * callbacks, or a caller that must not enter the allocator).  It has no
+ * counterpart in the reference.  Instead of caller scratch it uses one
+ * built-in device array of 16 MiB that every GPU loading this library holds
+ * until exit; shapes whose lmx_sdpa_scratch_bytes exceeds 16 MiB are rejected
+ * with LMX_ERR_CAPACITY.  It allocates nothing (no cudaMalloc / cudaFree).
+ * The first call on each device looks up the array's device address (one-time
+ * set-up); make that first call before any stream capture.  All calls share
+ * the array and it keeps the last call's contents: calls that overlap on the
+ * GPU race, so serialise them.  Results equal lmx_sdpa_decode's. */
+int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* out,
+                            void* stream);
 
 /* ---------------------------------------------------------------------------
  * Models.  Replaces the ModelContext function table of a loaded Qwen3 /

@@ -366,3 +366,66 @@ extern "C" int lmx_argmax(const void* logits, int rows, int V, int32_t* out, voi
   return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
 }
 #include "engine.cuh"
+
+// ---------------------------------------------------------------------------
+// Attention for callers that cannot allocate device memory: a host framework
+// that owns every device allocation and forbids cudaMalloc in its callbacks,
+// or a latency-critical caller that must not enter the allocator.  Instead of
+// caller scratch it uses one file-scope device array of kNoAllocScratchBytes,
+// which every GPU that loads this library holds until the process exits.
+// All calls share the array and it keeps the last call's contents, so calls
+// that overlap on the GPU (different streams, or different host threads on the
+// same device) race; the split counters are cleared at the start of each call.
+// ---------------------------------------------------------------------------
+static constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_sdpa_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+struct NoAllocDevice {
+  bool init = false;
+  void* ptr = nullptr;  // device address of g_sdpa_noalloc_scratch on this device
+};
+NoAllocDevice g_noalloc[64];
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, int heads, float scale,
+                                       void* out, void* stream) {
+  int device = 0;
+  int rc = cuda_check(cudaGetDevice(&device), "sdpa_noalloc: device");
+  if (rc) return rc;
+  if (device < 0 || device >= 64) return set_error(LMX_ERR_UNSUPPORTED, "sdpa_noalloc: device %d", device);
+  void* scratch = nullptr;
+  {
+    // one-time set-up per device (with that device current): in host code the
+    // array's name is only a stand-in, so its device address is looked up
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDevice& nd = g_noalloc[device];
+    if (!nd.init) {
+      void* p = nullptr;
+      rc = cuda_check(cudaGetSymbolAddress(&p, g_sdpa_noalloc_scratch), "sdpa_noalloc: symbol address");
+      if (rc) return rc;
+      nd.ptr = p;
+      nd.init = true;
+    }
+    scratch = nd.ptr;
+  }
+  KvDesc d;
+  rc = kv_from_c(kv, d);
+  if (rc) return rc;
+  if (T < 1 || heads < 1 || heads % d.Hk) return set_error(LMX_ERR_INVALID, "sdpa_noalloc: bad shape");
+  const size_t need = sdpa_scratch_bytes(d.B, T, heads, d.Hk, d.cap);
+  if (need > kNoAllocScratchBytes)
+    return set_error(LMX_ERR_CAPACITY,
+                     "sdpa_noalloc: this shape needs %zu bytes of scratch; the built-in array holds %zu "
+                     "(use lmx_sdpa_decode with caller scratch)",
+                     need, kNoAllocScratchBytes);
+  int tiles, splits;
+  sdpa_geometry(T, heads, d.Hk, d.cap, tiles, splits);
+  const size_t part = (size_t)d.B * d.Hk * tiles * splits * kRowTile * kPartStride * 4;
+  const size_t ctr_off = (part + 255) / 256 * 256;
+  rc = cuda_check(cudaMemsetAsync((char*)scratch + ctr_off, 0, (size_t)d.B * d.Hk * tiles * 4, (cudaStream_t)stream),
+                  "sdpa_noalloc: clear counters");
+  if (rc) return rc;
+  return sdpa_call(q, kv, T, heads, scale, scratch, kNoAllocScratchBytes, out, (cudaStream_t)stream);
+}

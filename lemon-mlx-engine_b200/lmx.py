@@ -34,6 +34,7 @@ SIGNATURES = {
     "lmx_argmax": (I, [P, I, I, P, P]),
     "lmx_sdpa_scratch_bytes": (C.c_size_t, [I, I, I, I, I]),
     "lmx_sdpa_decode": (I, [P, P, I, I, F, P, C.c_size_t, P, P]),
+    "lmx_sdpa_decode_noalloc": (I, [P, P, I, I, F, P, P]),
     "lmx_model_create": (I, [P, U64, P]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
