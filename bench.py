@@ -208,6 +208,14 @@ def run_lmx(args, wl, world, rank, local):
                          kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
                          seed=args.seed)
 
+    if args.profile_verify:
+        sd.prefill(prompts)
+        sd.decode(use_graph=True)
+        sd.profile(0, args.profile_verify)
+        sd.close()
+        target.close()
+        return 0
+
     def one():
         t0 = time.perf_counter()
         sd.prefill(prompts)
@@ -303,6 +311,9 @@ def main():
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-verify", type=int, default=0,
+                    help="only prefill, decode the workload and run N verify passes inside the "
+                         "NVTX range lmx_verify_pass (for ncu --nvtx-include)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     world, rank, local = dist_setup()

@@ -29,11 +29,13 @@ struct KvDesc {
 };
 
 // ---------------------------------------------------------------------------
-// K4: one warp per (token row, head).  Lane l holds d = l, l+32, l+64, l+96,
-// i.e. both halves of the rope pairs (l, l+64) and (l+32, l+96).
-// RMSNorm canonical order as in norm_argmax.cuh (32 lane partials, butterfly).
-// Quantize rule (per group of 64): scale = bf16((max-min)/(2^bits-1)) (1 if
-// zero), bias = bf16(min), q = clamp(rint((x - bias)/scale)).
+// K4: one warp per (token row, head).  Lane l < 16 holds the 8-element chunk
+// d = 8l..8l+7 of the head (lanes 16..31 hold nothing): the canonical RMSNorm
+// partition (norm_argmax.cuh), rope pairs (d, d+64) sit in lanes l and l+8,
+// and for the affine cache lane l packs exactly its own word(s).
+// Quantize rule (per group of 64, group 0 = lanes 0..7, group 1 = lanes
+// 8..15): scale = bf16((max-min)/(2^bits-1)) (1 if zero), bias = bf16(min),
+// q = clamp(rint((x - bias)/scale)).
 // ---------------------------------------------------------------------------
 struct PrepArgs {
   const bf16_t* qkv;      // [R, ldq]: q heads, k heads, v heads
@@ -50,29 +52,19 @@ struct PrepArgs {
   unsigned* err;
 };
 
-LMX_DEV void quant_pack_group(const float* vals /*smem [64]*/, int bits, uint32_t* words,
-                              bf16_t* s_out, bf16_t* b_out, int lane, float mn, float mx) {
-  const int nb = (1 << bits) - 1;
-  bf16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), (float)nb));
-  float sc = bf2f(sb);
-  if (sc == 0.0f) { sb = f2bf(1.0f); sc = 1.0f; }
-  bf16_t bb = f2bf(mn);
-  const float bi = bf2f(bb);
-  const int per = 32 / bits, nwords = 64 / per;
-  if (lane < nwords) {
-    uint32_t w = 0;
-    for (int j = 0; j < per; ++j) {
-      int q = (int)rintf(__fdiv_rn(__fsub_rn(vals[lane * per + j], bi), sc));
-      q = q < 0 ? 0 : (q > nb ? nb : q);
-      w |= (uint32_t)q << (j * bits);
-    }
-    words[lane] = w;
-  }
-  if (lane == 0) { *s_out = sb; *b_out = bb; }
+LMX_DEV void unpack8(const uint4 v, float (&x)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = (e & 1) ? hi_bf(w[e >> 1]) : lo_bf(w[e >> 1]);
+}
+LMX_DEV uint4 pack8(const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = (uint32_t)f2bf(x[2 * k]) | ((uint32_t)f2bf(x[2 * k + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __global__ void __launch_bounds__(256) attn_prep_kernel(PrepArgs a) {
-  __shared__ float stage[8][kHeadDim];
   grid_wait();
   grid_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,65 +78,89 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepArgs a) {
     if (lane == 0 && a.err) atomicExch(a.err, 0x41u);
     return;
   }
-  const bf16_t* src = a.qkv + (size_t)r * a.ldq + (size_t)h * kHeadDim;
-  float x[4];
+  const bool has = lane < 16;
+  float x[8];
+  if (has) unpack8(*reinterpret_cast<const uint4*>(a.qkv + (size_t)r * a.ldq + (size_t)h * kHeadDim + 8 * lane), x);
+  else
 #pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = bf2f(src[lane + 32 * i]);
+    for (int e = 0; e < 8; ++e) x[e] = 0.0f;
   const bool is_q = h < a.Hq, is_k = !is_q && h < a.Hq + a.Hk;
   if (is_q || is_k) {
     const bf16_t* nw = is_q ? a.qn : a.kn;
     if (nw) {
       float p = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) p = __fmaf_rn(x[i], x[i], p);
+      for (int e = 0; e < 8; ++e) p = __fmaf_rn(x[e], x[e], p);
       p = warp_sum_xor(p, 16, 1);
       const float f = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)kHeadDim), a.eps)));
+      if (has) {
+        float w8[8];
+        unpack8(*reinterpret_cast<const uint4*>(nw + 8 * lane), w8);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = bf2f(f2bf(__fmul_rn(__fmul_rn(x[i], f), bf2f(nw[lane + 32 * i]))));
+        for (int e = 0; e < 8; ++e) x[e] = bf2f(f2bf(__fmul_rn(__fmul_rn(x[e], f), w8[e])));
+      }
     }
-    // NeoX rope: pairs (d, d+64)
-    const float* ct = a.cos_t + (size_t)pos * (kHeadDim / 2);
-    const float* st = a.sin_t + (size_t)pos * (kHeadDim / 2);
+    // NeoX rope: lane l < 8 holds d = 8l+e, its partner lane l+8 holds d+64
+    float y[8];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int d = lane + 32 * i;
-      const float c = ct[d], s = st[d];
-      const float u = x[i], w = x[i + 2];
-      x[i] = bf2f(f2bf(__fsub_rn(__fmul_rn(u, c), __fmul_rn(w, s))));
-      x[i + 2] = bf2f(f2bf(__fadd_rn(__fmul_rn(w, c), __fmul_rn(u, s))));
+    for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 8);
+    if (has) {
+      const int i0 = 8 * (lane & 7);
+      const float* ct = a.cos_t + (size_t)pos * (kHeadDim / 2) + i0;
+      const float* st = a.sin_t + (size_t)pos * (kHeadDim / 2) + i0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float c = ct[e], s = st[e];
+        if (lane < 8) x[e] = bf2f(f2bf(__fsub_rn(__fmul_rn(x[e], c), __fmul_rn(y[e], s))));
+        else x[e] = bf2f(f2bf(__fadd_rn(__fmul_rn(x[e], c), __fmul_rn(y[e], s))));
+      }
     }
   }
   if (is_q) {
-    bf16_t* dst = a.q_out + (size_t)r * a.Hq * kHeadDim + (size_t)h * kHeadDim;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f2bf(x[i]);
+    if (has)
+      *reinterpret_cast<uint4*>(a.q_out + (size_t)r * a.Hq * kHeadDim + (size_t)h * kHeadDim + 8 * lane) = pack8(x);
     return;
   }
   const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hk;
   const size_t row = ((size_t)b * a.kv.Hk + hk) * a.kv.cap + pos;
   if (a.kv.bits == 16) {
-    bf16_t* dst = (is_k ? a.kv.k : a.kv.v) + row * kHeadDim;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f2bf(x[i]);
+    if (has) *reinterpret_cast<uint4*>((is_k ? a.kv.k : a.kv.v) + row * kHeadDim + 8 * lane) = pack8(x);
     return;
   }
-  // quantize two groups of 64 (group 0 = d < 64 -> x[0], x[1]; group 1 -> x[2], x[3])
-  float* sv = stage[warp];
+  // group-64 min / max over the 8 lanes of each group (lanes 16..31 mirror lanes 0..15)
+  float mn = x[0], mx = x[0];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) sv[lane + 32 * i] = x[i];
-  __syncwarp();
-  const int bits = a.kv.bits, wpr = kHeadDim * bits / 32;
-  uint32_t* words = (is_k ? a.kv.kq : a.kv.vq) + row * wpr;
-  bf16_t* so = (is_k ? a.kv.ks : a.kv.vs) + row * 2;
-  bf16_t* bo = (is_k ? a.kv.kb : a.kv.vb) + row * 2;
+  for (int e = 1; e < 8; ++e) { mn = fminf(mn, x[e]); mx = fmaxf(mx, x[e]); }
+  for (int off = 4; off >= 1; off >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  }
+  if (!has) return;
+  const int bits = a.kv.bits, nb = (1 << bits) - 1;
+  bf16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), (float)nb));
+  float sc = bf2f(sb);
+  if (sc == 0.0f) { sb = f2bf(1.0f); sc = 1.0f; }
+  const bf16_t bb = f2bf(mn);
+  const float bi = bf2f(bb);
+  uint32_t q[8];
 #pragma unroll
-  for (int gi = 0; gi < 2; ++gi) {
-    float mn = fminf(x[2 * gi], x[2 * gi + 1]), mx = fmaxf(x[2 * gi], x[2 * gi + 1]);
-    for (int off = 16; off >= 1; off >>= 1) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    }
-    quant_pack_group(sv + 64 * gi, bits, words + gi * (64 * bits / 32), so + gi, bo + gi, lane, mn, mx);
+  for (int e = 0; e < 8; ++e) {
+    int v = (int)rintf(__fdiv_rn(__fsub_rn(x[e], bi), sc));
+    q[e] = (uint32_t)(v < 0 ? 0 : (v > nb ? nb : v));
+  }
+  uint32_t* words = (is_k ? a.kv.kq : a.kv.vq) + row * (kHeadDim * bits / 32);
+  if (bits == 4) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w |= q[e] << (4 * e);
+    words[lane] = w;
+  } else {
+    words[2 * lane] = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
+    words[2 * lane + 1] = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
+  }
+  if ((lane & 7) == 0) {
+    (is_k ? a.kv.ks : a.kv.vs)[row * 2 + (lane >> 3)] = sb;
+    (is_k ? a.kv.kb : a.kv.vb)[row * 2 + (lane >> 3)] = bb;
   }
 }
 
@@ -204,6 +220,10 @@ LMX_DEV uint4 kv_chunk8(const KvDesc& kv, bool is_k, size_t row, int c) {
 
 static constexpr int kKPitch = kHeadDim + 8;  // bf16 elements per staged K row (16 B pad)
 
+// RPT = query rows per thread (rows of the tile are split by parity between
+// the two halves of the block), a template parameter so the row loops are
+// short and unrolled.
+template <int RPT>
 __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   bf16_t* Ks = reinterpret_cast<bf16_t*>(smem);                   // [kSplit][kKPitch]
@@ -248,14 +268,14 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   }
   __syncthreads();
 
-  // scores: thread (key j, row parity rp) holds up to 16 rows' accumulators;
-  // each accumulator is an fma chain over d ascending
+  // scores: thread (key j, row parity rp) holds RPT rows' accumulators; each
+  // accumulator is an fma chain over d ascending
   {
     const int j = tid & (kSplit - 1), rp = tid >> 7;
     if (j < jn) {
-      float acc[kRowTile / 2];
+      float acc[RPT];
 #pragma unroll
-      for (int i = 0; i < kRowTile / 2; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < RPT; ++i) acc[i] = 0.0f;
       const bf16_t* kr = Ks + j * kKPitch;
 #pragma unroll 2
       for (int dc = 0; dc < kHeadDim / 8; ++dc) {
@@ -263,7 +283,7 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
         const float k8[8] = {lo_bf(kw.x), hi_bf(kw.x), lo_bf(kw.y), hi_bf(kw.y),
                              lo_bf(kw.z), hi_bf(kw.z), lo_bf(kw.w), hi_bf(kw.w)};
 #pragma unroll
-        for (int i = 0; i < kRowTile / 2; ++i) {
+        for (int i = 0; i < RPT; ++i) {
           const int rr = rp + 2 * i;
           if (rr < nr) {
             const float4 qa = *reinterpret_cast<const float4*>(Qs + rr * kHeadDim + dc * 8);
@@ -282,7 +302,7 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
         }
       }
 #pragma unroll
-      for (int i = 0; i < kRowTile / 2; ++i)
+      for (int i = 0; i < RPT; ++i)
         if (rp + 2 * i < nr) S[(rp + 2 * i) * kSplit + j] = acc[i];
     }
   }
@@ -317,32 +337,34 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   }
   __syncthreads();
 
-  // o[d] for the thread's rows: fma chains over keys ascending (p = 0 past a
-  // row's visible range and V rows are finite, so the extra terms are exact)
+  // o[d] for the thread's rows: fma chains over keys ascending.  Keys past a
+  // row's visible range have p = 0 and the V rows past jn are zero-filled, so
+  // the extra fma(0, v, acc) terms leave every chain exactly unchanged.
   {
     const int d = tid & (kHeadDim - 1), rp = tid >> 7;
-    float acc[kRowTile / 2];
+    float acc[RPT];
 #pragma unroll
-    for (int i = 0; i < kRowTile / 2; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < RPT; ++i) acc[i] = 0.0f;
+#pragma unroll 2
     for (int j = 0; j < jn4; j += 4) {
       const float v0 = bf2f(Vs[j * kHeadDim + d]), v1 = bf2f(Vs[(j + 1) * kHeadDim + d]);
       const float v2 = bf2f(Vs[(j + 2) * kHeadDim + d]), v3 = bf2f(Vs[(j + 3) * kHeadDim + d]);
 #pragma unroll
-      for (int i = 0; i < kRowTile / 2; ++i) {
+      for (int i = 0; i < RPT; ++i) {
         const int rr = rp + 2 * i;
         if (rr < nr) {
           const float4 p4 = *reinterpret_cast<const float4*>(S + rr * kSplit + j);
           float x = acc[i];
           x = __fmaf_rn(p4.x, v0, x);
-          if (j + 1 < jn) x = __fmaf_rn(p4.y, v1, x);
-          if (j + 2 < jn) x = __fmaf_rn(p4.z, v2, x);
-          if (j + 3 < jn) x = __fmaf_rn(p4.w, v3, x);
+          x = __fmaf_rn(p4.y, v1, x);
+          x = __fmaf_rn(p4.z, v2, x);
+          x = __fmaf_rn(p4.w, v3, x);
           acc[i] = x;
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < kRowTile / 2; ++i)
+    for (int i = 0; i < RPT; ++i)
       if (rp + 2 * i < nr) part_base[(rp + 2 * i) * kPartStride + 2 + d] = acc[i];
   }
 

@@ -11,6 +11,8 @@
 #include <memory>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "lmx_internal.h"
 
 namespace lmx {
@@ -25,20 +27,34 @@ static int launch_attn_prep(const PrepArgs& a, cudaStream_t st) {
                     "attn_prep: launch");
 }
 
-static int launch_sdpa(const SdpaArgs& a, int B, cudaStream_t st) {
+template <int RPT>
+static int launch_sdpa_t(const SdpaArgs& a, int B, cudaStream_t st) {
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
   if (!attr_set[d & 63]) {
-    int rc = cuda_check(cudaFuncSetAttribute(sdpa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    int rc = cuda_check(cudaFuncSetAttribute(sdpa_split_kernel<RPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSdpaSmem),
                         "sdpa: set smem");
     if (rc) return rc;
     attr_set[d & 63] = true;
   }
-  return cuda_check(lmx_launch(sdpa_split_kernel, dim3(a.nsplit * a.tiles, a.kv.Hk, B), dim3(256), kSdpaSmem,
-                               st, true, a),
+  return cuda_check(lmx_launch(sdpa_split_kernel<RPT>, dim3(a.nsplit * a.tiles, a.kv.Hk, B), dim3(256),
+                               kSdpaSmem, st, true, a),
                     "sdpa: launch");
+}
+
+static int launch_sdpa(const SdpaArgs& a, int B, cudaStream_t st) {
+  const int rows = (a.Hq / a.kv.Hk) * a.T;
+  const int half = ((rows < kRowTile ? rows : kRowTile) + 1) / 2;  // rows per thread needed
+  if (half <= 1) return launch_sdpa_t<1>(a, B, st);
+  if (half <= 2) return launch_sdpa_t<2>(a, B, st);
+  if (half <= 3) return launch_sdpa_t<3>(a, B, st);
+  if (half <= 4) return launch_sdpa_t<4>(a, B, st);
+  if (half <= 5) return launch_sdpa_t<5>(a, B, st);
+  if (half <= 6) return launch_sdpa_t<6>(a, B, st);
+  if (half <= 8) return launch_sdpa_t<8>(a, B, st);
+  return launch_sdpa_t<16>(a, B, st);
 }
 
 static int launch_cluster_rows(void (*kern)(const bf16_t*, int, SpecState, int, int), int rows,
@@ -845,7 +861,9 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   cudaEventRecord(e0, st);
+  nvtxRangePushA(what == 0 ? "lmx_verify_pass" : (what == 1 ? "lmx_draft_token" : "lmx_lm_head"));
   for (int i = 0; i < iters && !rc; ++i) rc = once();
+  nvtxRangePop();
   cudaEventRecord(e1, st);
   if (!rc) rc = cuda_check(cudaEventSynchronize(e1), "profile");
   float ms = 0;

@@ -287,8 +287,9 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
 int launch_rms_norm(const bf16_t* x, const bf16_t* w, bf16_t* y, int rows, int dim, float eps,
                     cudaStream_t st) {
   if (rows == 0) return LMX_OK;
-  if (!x || !w || !y || rows < 0 || dim <= 0)
-    return set_error(LMX_ERR_INVALID, "rms_norm: bad arguments");
+  if (!x || !w || !y || rows < 0 || dim <= 0 || (dim & 7) || ((uintptr_t)x & 15) || ((uintptr_t)w & 15) ||
+      ((uintptr_t)y & 15))
+    return set_error(LMX_ERR_INVALID, "rms_norm: bad arguments (16-byte aligned rows, dim %% 8 == 0)");
   return cuda_check(lmx_launch(rms_norm_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, true, x, w, y,
                                rows, dim, eps),
                     "rms_norm: launch");

@@ -7,10 +7,38 @@ namespace cg = cooperative_groups;
 
 namespace lmx {
 
-// RMSNorm (mx::fast::rms_norm, e.g. src/llm/models/qwen3.cpp:78,145), one warp
-// per row.  Canonical order: lane partials p_l = fma chain of x_i^2 over
-// i = l, l+32, ..., butterfly (16,8,4,2,1), r = 1/sqrt(ss/dim + eps),
-// y = bf16((x*r)*w).  Bit-identical to the prologue fused into qmv_kernel.
+// Canonical RMSNorm factor of one row, computed by a whole warp:
+//   chunk c = elements [8c, 8c+8); lane l owns chunks l, l+32, l+64, ...
+//   p_l = fma chain of x^2 over its chunks ascending, elements ascending;
+//   butterfly (16,8,4,2,1); factor = 1 / sqrt(ss / dim + eps).
+// Chunks are read as 16-byte vectors, up to 8 per lane in flight.  Needs x
+// 16-byte aligned and dim % 8 == 0.
+LMX_DEV float rms_factor_warp(const bf16_t* x, int dim, float eps, int lane) {
+  float p = 0.0f;
+  const int nch = dim >> 3;
+  for (int c0 = lane; c0 < nch; c0 += 256) {
+    uint4 buf[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (c0 + 32 * k < nch) buf[k] = *reinterpret_cast<const uint4*>(x + 8 * (c0 + 32 * k));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (c0 + 32 * k < nch) {
+        const uint32_t w[4] = {buf[k].x, buf[k].y, buf[k].z, buf[k].w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float v = (e & 1) ? hi_bf(w[e >> 1]) : lo_bf(w[e >> 1]);
+          p = __fmaf_rn(v, v, p);
+        }
+      }
+    }
+  }
+  p = warp_sum_xor(p, 16, 1);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)dim), eps)));
+}
+
+// RMSNorm (mx::fast::rms_norm, e.g. src/llm/models/qwen3.cpp:78,145): one warp
+// per row, factor as above, y = bf16((x * r) * w).
 __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16_t* x, const bf16_t* w, bf16_t* y,
                                                        int rows, int dim, float eps) {
   grid_wait();
@@ -19,15 +47,21 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16_t* x, const bf
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const bf16_t* xr = x + (size_t)row * dim;
-  float p = 0.0f;
-  for (int i = lane; i < dim; i += 32) {
-    float v = bf2f(xr[i]);
-    p = __fmaf_rn(v, v, p);
-  }
-  p = warp_sum_xor(p, 16, 1);
-  const float f = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)dim), eps)));
+  const float f = rms_factor_warp(xr, dim, eps, lane);
   bf16_t* yr = y + (size_t)row * dim;
-  for (int i = lane; i < dim; i += 32) yr[i] = f2bf(__fmul_rn(__fmul_rn(bf2f(xr[i]), f), bf2f(w[i])));
+  for (int c = lane; c < (dim >> 3); c += 32) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + 8 * c);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * c);
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const bf16_t lo = f2bf(__fmul_rn(__fmul_rn(lo_bf(xa[k]), f), lo_bf(wa[k])));
+      const bf16_t hi = f2bf(__fmul_rn(__fmul_rn(hi_bf(xa[k]), f), hi_bf(wa[k])));
+      o[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(yr + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // (value, index) max with the lowest index winning ties; NaN never wins.

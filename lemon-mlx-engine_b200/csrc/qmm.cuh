@@ -33,6 +33,7 @@
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include "lmx_common.cuh"
+#include "norm_argmax.cuh"
 namespace cg = cooperative_groups;
 
 namespace lmx {
@@ -345,14 +346,8 @@ __global__ void __launch_bounds__(kQmmThreads, MT <= 2 ? 2 : 1) qmv_kernel(const
 
   if (a.norm_w) {
     for (int m = warp; m < M; m += NW) {
-      const bf16_t* xrow = a.x + (size_t)m * a.ldx;
-      float pp = 0.0f;
-      for (int i = lane; i < K; i += 32) {
-        float v = bf2f(xrow[i]);
-        pp = __fmaf_rn(v, v, pp);
-      }
-      pp = warp_sum_xor(pp, 16, 1);
-      if (lane == 0) fnorm[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(pp, (float)K), a.eps)));
+      const float f = rms_factor_warp(a.x + (size_t)m * a.ldx, K, a.eps, lane);
+      if (lane == 0) fnorm[m] = f;
     }
   }
   __syncthreads();

@@ -332,15 +332,17 @@ extern "C" int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* sc
 
 // ---------------------------------------------------------------------------
 // rms_norm (mx::fast::rms_norm; formula debug_numerical_trace.py:103-108)
-//   p_l = fma chain of x_i^2 over i = l, l+32, ... (l = 0..31), from 0
+//   chunk c = elements [8c, 8c+8); lane l (0..31) owns chunks l, l+32, l+64, ...
+//   p_l = fma chain of x_i^2 over its chunks ascending, elements ascending, from 0
 //   butterfly: for off in 16,8,4,2,1: p_l = p_l + p_(l^off);  ss = p_0
 //   r = 1 / sqrt(ss / dim + eps);   y_i = bf16((x_i * r) * w_i)
-// ---------------------------------------------------------------------------
+// (dim is a multiple of 8.)
 static float rms_factor(const float* xr, int dim, float eps) {
   float p[32];
   for (int l = 0; l < 32; ++l) {
     float a = 0.0f;
-    for (int i = l; i < dim; i += 32) a = std::fma(xr[i], xr[i], a);
+    for (int c = l; c * 8 < dim; c += 32)
+      for (int e = 0; e < 8; ++e) a = std::fma(xr[8 * c + e], xr[8 * c + e], a);
     p[l] = a;
   }
   for (int off = 16; off >= 1; off >>= 1) {
