@@ -69,6 +69,29 @@ int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream);
 
 
 /* ---------------------------------------------------------------------------
+ * Sampling and speculative acceptance (K3).  The reference samples with
+ * mx::random::categorical (temperature-scaled Gumbel, src/common/generate.cpp:
+ * 83-120; TopPSampler leaves top-p unapplied) and has no rejection sampler.
+ * Here both take caller-supplied 24-bit uniforms and decide in exact integer
+ * arithmetic: w_j = rint(exp((l_j - max)/T) * 2^32); top-p keeps the smallest
+ * prefix by (w desc, index asc) with 2^24*mass >= rint(top_p*2^24)*Z; a draw
+ * is the smallest index t with 2^24*cumsum_t > u24*Z_kept.
+ * ------------------------------------------------------------------------- */
+/* logits [rows, V] bf16 -> out [rows]; temperature <= 0 is argmax (u24 unused). */
+int lmx_sample(const void* logits, int rows, int V, float temperature, float top_p, const uint32_t* u24,
+               int32_t* out, void* stream);
+/* Rejection sampling (Leviathan et al. 2023): target_logits [B, K+1, V],
+ * draft_logits [B, K, V], drafts [B, K] (d1..dK), u_accept [B, K], u_final [B].
+ * Accept d_i iff u*q(d_i)*Zp < 2^24*p(d_i)*Zq; on the first rejection draw from
+ * max(0, p*Zq - q*Zp); after K acceptances draw the bonus from p_K.
+ * n_accepted [B]; out_tokens [B, K+1]: accepted drafts then the correction /
+ * bonus token.  temperature must be > 0 (greedy acceptance is in
+ * lmx_spec_decode). */
+int lmx_spec_accept(const void* target_logits, const void* draft_logits, const int32_t* drafts, int B, int K,
+                    int V, float temperature, float top_p, const uint32_t* u_accept, const uint32_t* u_final,
+                    int32_t* n_accepted, int32_t* out_tokens, void* stream);
+
+/* ---------------------------------------------------------------------------
  * KV cache view and decode / verify attention.
  * Replaces cache->update + sdpa() -> mx::fast::scaled_dot_product_attention
  * (include/mlx-lm/common/attention_utils.h:60-77, src/common/kv_cache.cpp:

@@ -304,7 +304,8 @@ static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_
 // (+RMSNorm, SwiGLU) -> down GEMV (+residual); then the final norm and the
 // lm_head for every row or only each sequence's last row.
 static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, int tok_ld, int tok_off,
-                   int B, int T, Workspace& ws, bf16_t* logits, bool last_only, cudaStream_t st) {
+                   int B, int T, Workspace& ws, bf16_t* logits, bool last_only, cudaStream_t st,
+                   int logits_ld = 0) {
   const lmx_model_config& cf = m.c;
   const int H = cf.hidden, I = cf.inter, Hq = cf.heads, Hk = cf.kv_heads;
   const int NQ = Hq * kHeadDim, NK = Hk * kHeadDim, G = Hq / Hk, R = B * T;
@@ -438,7 +439,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   hc.mat[0] = m.head().mat();
   hc.N = cf.vocab;
   hc.y = logits;
-  hc.ldy = cf.vocab;
+  hc.ldy = logits_ld ? logits_ld : cf.vocab;
   hc.M = M;
   hc.K = H;
   hc.bits = cf.bits;
@@ -488,22 +489,45 @@ struct Spec {
   }
 };
 
+static StochParams stoch_params(const Spec& sp) {
+  StochParams p;
+  p.temperature = sp.cfg.temperature;
+  p.top_p = sp.cfg.top_p;
+  p.seed = sp.cfg.seed;
+  return p;
+}
+
 static int spec_step(Spec& sp) {
   const int B = sp.cfg.batch, K = sp.cfg.K, V = sp.tm->c.vocab;
   cudaStream_t st = sp.st;
+  const bool stoch = sp.cfg.temperature > 0.0f;
   int rc = LMX_OK;
   for (int i = 0; i < K && !rc; ++i) {
-    if (i == 0)
-      rc = forward(*sp.dm, *sp.dc, sp.dl, sp.s.tok2, 2, 0, B, 2, sp.ws, sp.ws.logits, true, st);
-    else
-      rc = forward(*sp.dm, *sp.dc, sp.dl, sp.s.drafts, K, i - 1, B, 1, sp.ws, sp.ws.logits, true, st);
-    if (!rc) rc = launch_cluster_rows(draft_argmax_kernel, B, sp.ws.logits, V, sp.s, i, i == 0 ? 2 : 1, st);
+    const int32_t* tok = i == 0 ? sp.s.tok2 : sp.s.drafts;
+    const int ld = i == 0 ? 2 : K, off = i == 0 ? 0 : i - 1, T = i == 0 ? 2 : 1;
+    if (stoch) {
+      rc = forward(*sp.dm, *sp.dc, sp.dl, tok, ld, off, B, T, sp.ws, sp.s.qlog + (size_t)i * V, true, st, K * V);
+      if (!rc)
+        rc = cuda_check(lmx_launch(draft_sample_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+                                   (const bf16_t*)sp.s.qlog, V, sp.s, stoch_params(sp), i, T),
+                        "draft_sample");
+    } else {
+      rc = forward(*sp.dm, *sp.dc, sp.dl, tok, ld, off, B, T, sp.ws, sp.ws.logits, true, st);
+      if (!rc) rc = launch_cluster_rows(draft_argmax_kernel, B, sp.ws.logits, V, sp.s, i, T, st);
+    }
   }
   if (!rc) rc = forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
-  if (!rc) rc = launch_argmax(sp.ws.logits, B * (K + 1), V, sp.s.pred, st);
-  if (!rc)
-    rc = cuda_check(lmx_launch(accept_greedy_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s),
-                    "accept");
+  if (stoch) {
+    if (!rc)
+      rc = cuda_check(lmx_launch(accept_stochastic_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+                                 (const bf16_t*)sp.ws.logits, V, sp.s, stoch_params(sp)),
+                      "accept_stochastic");
+  } else {
+    if (!rc) rc = launch_argmax(sp.ws.logits, B * (K + 1), V, sp.s.pred, st);
+    if (!rc)
+      rc = cuda_check(lmx_launch(accept_greedy_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s),
+                      "accept");
+  }
   return rc;
 }
 
@@ -514,8 +538,6 @@ namespace lmx {
 static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
   if (cfg.batch < 1 || cfg.K < 1 || cfg.max_tokens < 1 || cfg.prompt_len < 2)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
-  if (cfg.temperature > 0.0f)
-    return set_error(LMX_ERR_UNSUPPORTED, "spec: stochastic acceptance not built yet");
   if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
     return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
   auto sp = std::make_unique<Spec>();
@@ -557,6 +579,12 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   if (!rc) rc = sp->ar.alloc(&s.accepted, (size_t)B);
   if (!rc) rc = sp->ar.alloc(&s.steps, (size_t)B);
   if (!rc) rc = sp->ar.alloc(&s.out, (size_t)B * cfg.max_tokens);
+  s.qlog = nullptr;
+  s.ustep = nullptr;
+  if (!rc && cfg.temperature > 0.0f) {
+    rc = sp->ar.alloc(&s.qlog, (size_t)B * K * tm->c.vocab);
+    if (!rc) rc = sp->ar.alloc(&s.ustep, (size_t)B);
+  }
   if (!rc) rc = sp->ar.alloc(&sp->prompts, (size_t)B * P);
   if (!rc) rc = sp->ar.alloc(&sp->yprefill, (size_t)B);
   if (rc) return rc;
@@ -579,7 +607,13 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
   if (!rc) rc = cuda_check(cudaMemsetAsync(sp.tc->len, 0, B * 4, st), "len");
   if (!rc) rc = cuda_check(cudaMemsetAsync(sp.dc->len, 0, B * 4, st), "len");
   if (!rc) rc = forward_chunked(*sp.tm, *sp.tc, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
-  if (!rc) rc = launch_argmax(sp.ws.logits, B, sp.tm->c.vocab, sp.yprefill, st);
+  if (!rc && sp.cfg.temperature > 0.0f)
+    rc = cuda_check(lmx_launch(sample_rows_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+                               (const bf16_t*)sp.ws.logits, sp.tm->c.vocab, sp.tm->c.vocab, stoch_params(sp),
+                               0u, 0u, 3u, sp.yprefill),
+                    "prefill sample");
+  else if (!rc)
+    rc = launch_argmax(sp.ws.logits, B, sp.tm->c.vocab, sp.yprefill, st);
   if (!rc) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
   if (!rc)
     rc = cuda_check(lmx_launch(prefill_done_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
@@ -981,4 +1015,33 @@ extern "C" size_t lmx_sdpa_scratch_bytes(int batch, int T, int heads, int kv_hea
 extern "C" int lmx_sdpa_decode(const void* q, const lmx_kv* kv, int T, int heads, float scale, void* scratch,
                                size_t scratch_bytes, void* out, void* stream) {
   return sdpa_call(q, kv, T, heads, scale, scratch, scratch_bytes, out, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: sampling and speculative acceptance with caller uniforms
+// ---------------------------------------------------------------------------
+extern "C" int lmx_sample(const void* logits, int rows, int V, float temperature, float top_p,
+                          const uint32_t* u24, int32_t* out, void* stream) {
+  if (rows == 0) return LMX_OK;
+  if (!logits || !out || rows < 0 || V < 1) return set_error(LMX_ERR_INVALID, "sample: bad arguments");
+  if (!(temperature > 0.0f)) return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
+  if (!u24) return set_error(LMX_ERR_INVALID, "sample: uniforms required when temperature > 0");
+  return cuda_check(lmx_launch(sample_u_kernel, dim3(rows), dim3(kSampThreads), 0, (cudaStream_t)stream, true,
+                               (const bf16_t*)logits, V, temperature, top_p, u24, out),
+                    "sample");
+}
+
+extern "C" int lmx_spec_accept(const void* target_logits, const void* draft_logits, const int32_t* drafts, int B,
+                               int K, int V, float temperature, float top_p, const uint32_t* u_accept,
+                               const uint32_t* u_final, int32_t* n_accepted, int32_t* out_tokens, void* stream) {
+  if (B == 0) return LMX_OK;
+  if (!target_logits || !drafts || !n_accepted || !out_tokens || B < 0 || K < 1 || V < 1)
+    return set_error(LMX_ERR_INVALID, "spec_accept: bad arguments");
+  if (!(temperature > 0.0f))
+    return set_error(LMX_ERR_INVALID, "spec_accept: greedy acceptance runs inside lmx_spec_decode");
+  if (!draft_logits || !u_accept || !u_final) return set_error(LMX_ERR_INVALID, "spec_accept: null argument");
+  return cuda_check(lmx_launch(accept_u_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, true,
+                               (const bf16_t*)target_logits, (const bf16_t*)draft_logits, drafts, K, V, temperature,
+                               top_p, u_accept, u_final, n_accepted, out_tokens),
+                    "spec_accept");
 }

@@ -100,6 +100,8 @@ struct SpecState {
   int* accepted;     // [B] accepted drafts (sum)
   int* steps;        // [B] speculative steps taken while unfinished
   int32_t* out;      // [B][max_tokens]
+  bf16_t* qlog;      // stochastic: draft logits [B][K][V]
+  int* ustep;        // stochastic: per-sequence step index of the uniform draws
 };
 
 // Greedy draft token i of every sequence: cluster argmax of the draft logits
@@ -148,6 +150,26 @@ __global__ void __launch_bounds__(512) draft_argmax_kernel(const bf16_t* logits,
   cluster.sync();
 }
 
+// Emit / commit / rollback shared by the greedy and stochastic acceptance:
+// emit y, d1..d_acc; next y = `next`; target length p+acc+1, draft p+acc.
+LMX_DEV void commit_step(const SpecState& s, int b, int acc, int next) {
+  const int p = s.tlen[b];
+  const int32_t* d = s.drafts + b * s.K;
+  const int y = s.tok2[2 * b + 1];
+  int e = s.emitted[b];
+  int32_t* o = s.out + (size_t)b * s.max_tokens;
+  if (e < s.max_tokens) o[e++] = y;
+  for (int k = 0; k < acc; ++k)
+    if (e < s.max_tokens) o[e++] = d[k];
+  s.emitted[b] = e;
+  s.accepted[b] += acc;
+  s.steps[b] += 1;
+  s.tok2[2 * b] = acc > 0 ? d[acc - 1] : y;
+  s.tok2[2 * b + 1] = next;
+  s.tlen[b] = p + acc + 1;
+  s.dlen[b] = p + acc;
+}
+
 // Greedy acceptance (src/common/generate.cpp:800-823) and commit/rollback
 // (:850-888): accept while pred[i] == d_{i+1}; emit y, d1..d_acc; the next y
 // is the correction or bonus token; target length p+acc+1, draft length p+acc.
@@ -167,19 +189,7 @@ __global__ void accept_greedy_kernel(SpecState s) {
   const int32_t* d = s.drafts + b * K;
   int acc = 0;
   while (acc < K && pr[acc] == d[acc]) ++acc;
-  const int y = s.tok2[2 * b + 1];
-  int e = s.emitted[b];
-  int32_t* o = s.out + (size_t)b * s.max_tokens;
-  if (e < s.max_tokens) o[e++] = y;
-  for (int k = 0; k < acc; ++k)
-    if (e < s.max_tokens) o[e++] = d[k];
-  s.emitted[b] = e;
-  s.accepted[b] += acc;
-  s.steps[b] += 1;
-  s.tok2[2 * b] = acc > 0 ? d[acc - 1] : y;
-  s.tok2[2 * b + 1] = pr[acc];
-  s.tlen[b] = p + acc + 1;
-  s.dlen[b] = p + acc;
+  commit_step(s, b, acc, pr[acc]);
 }
 
 // Prefill bookkeeping: y = argmax of the last prompt position (already in
@@ -196,6 +206,7 @@ __global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, 
   s.emitted[b] = 0;
   s.accepted[b] = 0;
   s.steps[b] = 0;
+  if (s.ustep) s.ustep[b] = 1;
 }
 
 __global__ void add_len_kernel(int* len, int B, int n) {

@@ -14,6 +14,7 @@
 #include "qmm.cuh"
 #include "attn.cuh"
 #include "engine_kernels.cuh"
+#include "sample.cuh"
 
 // Device error word: bounded waits that give up record a code here.
 __device__ unsigned g_lmx_kernel_error;

@@ -32,6 +32,8 @@ SIGNATURES = {
     "lmx_quantized_matmul": (I, [P, P, P, P, P, I, I, I, I, I, P]),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
+    "lmx_sample": (I, [P, I, I, F, F, P, P, P]),
+    "lmx_spec_accept": (I, [P, P, P, I, I, I, F, F, P, P, P, P, P]),
     "lmx_sdpa_scratch_bytes": (C.c_size_t, [I, I, I, I, I]),
     "lmx_sdpa_decode": (I, [P, P, I, I, F, P, C.c_size_t, P, P]),
     "lmx_sdpa_decode_noalloc": (I, [P, P, I, I, F, P, P]),
