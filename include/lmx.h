@@ -47,12 +47,19 @@ int lmx_set_device(int device);
  *   row in word j/(32/bits), bits (j%(32/bits))*bits, LSB first);
  *   scales, biases [N, K/group_size] bf16;  y [M,N] bf16.
  * Supported: bits 4 or 8, group_size 64, K % 64 == 0, K <= 16384.
- * M < 16 runs the fused-dequant GEMV (bit-exact canonical order); M >= 16 may
- * run the tcgen05 path.
+ * M below the tensor-core threshold runs the fused-dequant GEMV (bit-exact
+ * canonical order); M at or above it runs the tcgen05 path (weights
+ * dequantized to bf16 in shared memory, fp32 accumulation: within tolerance).
  * ------------------------------------------------------------------------- */
 int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                          const void* biases, void* y, int M, int N, int K,
                          int group_size, int bits, void* stream);
+
+/* Smallest M routed to the tcgen05 path (default 16, as MLX switches from
+ * its qmv to its tiled qmm for batched rows); 0 = never (every M runs the
+ * canonical GEMV order).  Process-wide; no reference counterpart. */
+int lmx_set_mma_min_m(int m);
+int lmx_mma_min_m(void);
 
 /* mx::fast::rms_norm(x, w, eps) over the last axis (e.g. qwen3.cpp:78,145).
  * x, y [rows, dim] bf16 (may alias), w [dim] bf16. */

@@ -314,7 +314,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   const int tiles = (G * T + kRowTile - 1) / kRowTile, splits = (c.cap + kSplit - 1) / kSplit;
   if (tiles > ws.tiles || splits > ws.splits || B > ws.B || Hk != ws.Hk)
     return set_error(LMX_ERR_INVALID, "forward: attention scratch too small");
-  const bool fuse = R <= kQmmMaxNormRows;
+  const bool fuse = R <= kQmmMaxNormRows && !qmm_uses_mma(R);
   int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
                                  (const uint32_t*)m.embed.w, (const bf16_t*)m.embed.s,
                                  (const bf16_t*)m.embed.b, H, cf.bits, ws.h, R),
@@ -426,7 +426,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   QmmCall hc;
   const int M = last_only ? B : R;
   const bf16_t* src = ws.h;
-  if (M > kQmmMaxNormRows) {
+  if (M > kQmmMaxNormRows || qmm_uses_mma(M)) {
     rc = launch_rms_norm(ws.h, m.final_norm, ws.xn, R, H, cf.eps, st);
     if (rc) return rc;
     src = ws.xn;
@@ -878,14 +878,20 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     if (what == 1)
       return forward(*sp.dm, *sp.dc, sp.dl, sp.s.drafts, K, 0, B, 1, sp.ws, sp.ws.logits, true, st);
     QmmCall hc;
+    hc.M = what == 2 ? B * (K + 1) : B;
     hc.x = sp.ws.h;
-    hc.norm_w = sp.tm->final_norm;
+    if (qmm_uses_mma(hc.M)) {  // the tensor-core path takes normalised rows
+      const int r2 = launch_rms_norm(sp.ws.h, sp.tm->final_norm, sp.ws.xn, hc.M, sp.tm->c.hidden, sp.tm->c.eps, st);
+      if (r2) return r2;
+      hc.x = sp.ws.xn;
+    } else {
+      hc.norm_w = sp.tm->final_norm;
+    }
     hc.eps = sp.tm->c.eps;
     hc.mat[0] = sp.tm->head().mat();
     hc.N = sp.tm->c.vocab;
     hc.y = sp.ws.logits;
     hc.ldy = sp.tm->c.vocab;
-    hc.M = what == 2 ? B * (K + 1) : B;
     hc.K = sp.tm->c.hidden;
     hc.bits = bits;
     return launch_qmm(hc, st);

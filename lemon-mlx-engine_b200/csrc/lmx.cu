@@ -12,6 +12,7 @@
 #include "lmx_internal.h"
 #include "norm_argmax.cuh"
 #include "qmm.cuh"
+#include "qmm_mma.cuh"
 #include "attn.cuh"
 #include "engine_kernels.cuh"
 #include "sample.cuh"
@@ -248,6 +249,138 @@ static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
   return set_error(LMX_ERR_UNSUPPORTED, "qmm: no kernel for MT=%d RB=%d", MT, sh.RB);
 }
 
+// ---------------------------------------------------------------------------
+// K1 tensor-core path (M >= the threshold, default 16; 0 disables it)
+// ---------------------------------------------------------------------------
+static int g_mma_min_m = 16;
+int qmm_mma_min_m() { return g_mma_min_m; }
+bool qmm_uses_mma(int M) { return g_mma_min_m > 0 && M >= g_mma_min_m; }
+
+// Activation map: bf16 [M][ldx], box {64, box_h}, 128-byte swizzle (the UMMA
+// K-major canonical layout).  Encoded per launch: activation buffers vary.
+static int tensor_map_x(const void* base, uint64_t K, uint64_t M, uint64_t ldx, int box_h, CUtensorMap* out) {
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+        return set_error(LMX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+      g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }
+  }
+  cuuint64_t dims[2] = {K, M};
+  cuuint64_t strides[1] = {ldx * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_h};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LMX_ERR_INVALID, "activation tensor map encode failed (%d)", (int)r);
+  return LMX_OK;
+}
+
+struct MmaShape {
+  int Mpad = 0, mtiles = 0, stages = 0, per_sm = 1;
+  size_t smem = 0;
+};
+
+// Token tiles of at most 256 (UMMA N), padded to 16; pipeline depth from the
+// shared-memory budget: two CTAs per SM when four or more stages fit in half
+// of it, else one CTA with up to kMmaMaxStages.
+static int mma_plan(int M, int bits, MmaShape& sh) {
+  sh.mtiles = (M + 255) / 256;
+  const int mper = (M + sh.mtiles - 1) / sh.mtiles;
+  sh.Mpad = (mper + 15) / 16 * 16;
+  const int stage = kMmaRows * kMmaK * 2 + sh.Mpad * kMmaK * 2 + kMmaRows * kMmaK * bits / 8;
+  const int fixed = 1024 + (4 * kMmaMaxStages + 1) * 8 + 16;
+  int st = (112 * 1024 - fixed) / stage;
+  sh.per_sm = 2;
+  if (st < 4) {
+    st = (227 * 1024 - fixed) / stage;
+    sh.per_sm = 1;
+  }
+  if (st > kMmaMaxStages) st = kMmaMaxStages;
+  if (st < 2) return set_error(LMX_ERR_UNSUPPORTED, "qmm: token tile %d too large", sh.Mpad);
+  if ((size_t)sh.Mpad * kMmaRows * 4 > (size_t)st * stage)
+    return set_error(LMX_ERR_UNSUPPORTED, "qmm: reduction tile does not fit");
+  sh.stages = st;
+  sh.smem = (size_t)fixed + (size_t)st * stage;
+  return LMX_OK;
+}
+
+template <int BITS>
+static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
+  MmaShape sh;
+  int rc = mma_plan(q.M, BITS, sh);
+  if (rc) return rc;
+  MmaArgs a;
+  std::memset(&a, 0, sizeof(a));
+  MmaMaps mp;
+  std::memset(&mp, 0, sizeof(mp));
+  const bool swiglu = q.mode == QMM_SWIGLU;
+  const int WPR = q.K * BITS / 32, boxh = swiglu ? kMmaRows / 2 : kMmaRows;
+  int ntiles = 0, cv = 0;
+  for (int i = 0; i < q.nmat; ++i) {
+    a.mat[i] = q.mat[i];
+    a.tstart[i] = ntiles;
+    a.cstart[i] = cv;
+    ntiles += (q.mat[i].rows + kMmaRows - 1) / kMmaRows;
+    cv += q.mat[i].rows;
+    rc = tensor_map_2d(q.mat[i].w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, WPR, q.mat[i].rows, 2 * BITS, boxh, &mp.w[i]);
+    if (rc) return rc;
+  }
+  if (swiglu) ntiles = (q.N + kMmaRows / 2 - 1) / (kMmaRows / 2);
+  rc = tensor_map_x(q.x, q.K, q.M, q.ldx, sh.Mpad, &mp.x);
+  if (rc) return rc;
+  a.nmat = q.nmat;
+  a.N = q.N;
+  a.M = q.M;
+  a.Mpad = sh.Mpad;
+  a.K = q.K;
+  a.mode = q.mode;
+  a.stages = sh.stages;
+  a.y = q.y;
+  a.ldy = q.ldy;
+  a.res = q.res;
+  a.err = q.err;
+  // split K over a cluster until the grid covers the SMs (>= 2 chunks per CTA)
+  const int nk = q.K / kMmaK, target = device_sms() * sh.per_sm, base = ntiles * sh.mtiles;
+  int ks = target / (base > 0 ? base : 1);
+  if (ks > kMmaMaxSplit) ks = kMmaMaxSplit;
+  if (ks > nk / 2) ks = nk / 2;
+  if (ks < 1) ks = 1;
+  a.ks = ks;
+  static bool attr_set[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (!attr_set[d & 63]) {
+    rc = cuda_check(cudaFuncSetAttribute(qmm_mma_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                    "qmm_mma: set smem");
+    if (rc) return rc;
+    attr_set[d & 63] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ntiles * ks, sh.mtiles);
+  cfg.blockDim = dim3(kMmaThreads);
+  cfg.dynamicSmemBytes = sh.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (ks > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = ks;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cuda_check(cudaLaunchKernelEx(&cfg, qmm_mma_kernel<BITS>, mp, a), "qmm_mma: launch");
+}
+
 int launch_qmm(const QmmCall& c, cudaStream_t st) {
   if (c.M == 0 || c.N == 0) return LMX_OK;
   if (c.M < 0 || c.N < 0 || c.K <= 0 || c.K % 64)
@@ -282,6 +415,7 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
   a.K = c.K;
   a.mode = c.mode;
   a.err = device_error_word();
+  if (!c.norm_w && qmm_uses_mma(c.M)) return c.bits == 4 ? launch_mma_t<4>(a, st) : launch_mma_t<8>(a, st);
   return c.bits == 4 ? launch_qmv_bits<4>(a, st) : launch_qmv_bits<8>(a, st);
 }
 
@@ -336,6 +470,13 @@ extern "C" int lmx_device_error(unsigned* code, int clear) {
   }
   return rc;
 }
+
+extern "C" int lmx_set_mma_min_m(int m) {
+  if (m < 0) return set_error(LMX_ERR_INVALID, "mma threshold must be >= 0");
+  g_mma_min_m = m;
+  return LMX_OK;
+}
+extern "C" int lmx_mma_min_m(void) { return g_mma_min_m; }
 
 extern "C" int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                                     const void* biases, void* y, int M, int N, int K, int group_size,

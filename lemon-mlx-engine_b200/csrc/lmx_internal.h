@@ -45,6 +45,9 @@ unsigned* device_error_word();
 
 // Kernel launchers (lmx.cu).  All launch with programmatic dependent launch.
 int launch_qmm(const QmmCall& c, cudaStream_t st);
+// Tensor-core path for M >= the threshold (un-normalised x only).
+bool qmm_uses_mma(int M);
+int qmm_mma_min_m();
 int launch_rms_norm(const bf16_t* x, const bf16_t* w, bf16_t* y, int rows, int dim, float eps,
                     cudaStream_t st);
 int launch_argmax(const bf16_t* logits, int rows, int V, int32_t* out, cudaStream_t st);

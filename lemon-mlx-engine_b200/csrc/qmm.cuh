@@ -109,10 +109,20 @@ LMX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 #endif
   return ok != 0;
 }
-// Bounded wait: gives up after ~2^22 polls (seconds), flags the error word.
+LMX_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after 4 s of wall time (checked every 256 polls) or
+// 2^26 polls, whichever comes first, and flags the error word.
 LMX_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
-  for (uint32_t i = 0; i < (1u << 26); ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1; i < (1u << 26); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && global_ns() - t0 > 4000000000ull) break;
+  }
   if (err) atomicExch(err, code);
   return false;
 }

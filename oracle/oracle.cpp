@@ -303,11 +303,53 @@ static void qmm_block8(const float* xf, const float* xsum, int M, int K, const u
   }
 }
 
+// Tensor-core path (batched verify, prefill): for M >= the threshold the
+// product is taken over dequantized weights, as MLX's tiled qmm does
+// (dequantize the tile to the activation type, then MMA with fp32
+// accumulation):  y = bf16( sum_k bf16(fma(s, q, b)) * x_k ).  The sum is
+// formed in double here; the device accumulates in fp32 on the tensor cores
+// in an order the hardware chooses, so this path is compared with a
+// tolerance.  threshold 0 = never (canonical order for every M).
+static int g_mma_min_m = 16;
+extern "C" void orc_set_mma_min_m(int m) { g_mma_min_m = m < 0 ? 0 : m; }
+extern "C" int orc_mma_min_m(void) { return g_mma_min_m; }
+
+static void qmm_dequant_rows(const float* xf, int M, int K, const uint32_t* wq, const uint16_t* sc,
+                             const uint16_t* bi, int n0, int nr, int N, int bits, uint16_t* y) {
+  const int KW = K * bits / 32, G = K / 64;
+  std::vector<double> wd((size_t)K);
+  for (int r = 0; r < nr; ++r) {
+    const int n = n0 + r;
+    const uint32_t* row = wq + (size_t)n * KW;
+    for (int k = 0; k < K; ++k) {
+      const float s = bf2f(sc[(size_t)n * G + k / 64]), b = bf2f(bi[(size_t)n * G + k / 64]);
+      wd[k] = (double)bf2f(f2bf(std::fma(s, (float)qcode(row, k, bits), b)));
+    }
+    for (int m = 0; m < M; ++m) {
+      const float* xr = xf + (size_t)m * K;
+      double acc = 0.0;
+      for (int k = 0; k < K; ++k) acc += wd[k] * (double)xr[k];
+      y[(size_t)m * N + n] = f2bf((float)acc);
+    }
+  }
+}
+
 extern "C" int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* scales,
                        const uint16_t* biases, uint16_t* y, int M, int N, int K, int group,
                        int bits) {
   if (group != 64 || (bits != 4 && bits != 8) || K % 64 || M < 0 || N < 0) return 1;
   if (M == 0 || N == 0) return 0;
+  if (g_mma_min_m > 0 && M >= g_mma_min_m) {
+    std::vector<float> xf((size_t)M * K);
+    for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf2f(x[i]);
+    const int nblk = (N + 7) / 8;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int n0 = blk * 8, nr = std::min(8, N - n0);
+      qmm_dequant_rows(xf.data(), M, K, wq, scales, biases, n0, nr, N, bits, y);
+    }
+    return 0;
+  }
   const int G = K / 64;
   std::vector<float> xf((size_t)M * K), xsum((size_t)M * G);
   for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf2f(x[i]);
@@ -874,6 +916,24 @@ static int forward_impl(Model& m, Cache& c, int n_layers, const int32_t* tokens,
   return 0;
 }
 
+// Prefill in chunks of kPrefillChunk tokens per sequence (the device engine's
+// prefill chunking), so that every quantized matmul sees the same M on both
+// sides and takes the same path; logits of each sequence's last token.
+static constexpr int kPrefillChunk = 32;
+static int prefill_chunked(Model& m, Cache& c, int n_layers, const int32_t* tokens, int ld, int B, int T,
+                           uint16_t* last_logits) {
+  std::vector<int32_t> chunk;
+  for (int t0 = 0; t0 < T; t0 += kPrefillChunk) {
+    const int tn = std::min(kPrefillChunk, T - t0);
+    chunk.resize((size_t)B * tn);
+    for (int b = 0; b < B; ++b) std::memcpy(&chunk[(size_t)b * tn], tokens + (size_t)b * ld + t0, tn * 4);
+    const bool last = t0 + tn >= T;
+    const int rc = forward_impl(m, c, n_layers, chunk.data(), B, tn, last ? last_logits : nullptr, true);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
 extern "C" int orc_forward(void* model, void* cache, int n_layers, const int32_t* tokens, int B,
                            int T, uint16_t* logits) {
   return forward_impl(*(Model*)model, *(Cache*)cache, n_layers, tokens, B, T, logits, false);
@@ -927,7 +987,7 @@ extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prom
   if (!ss->tc || !ss->dc) return nullptr;
   const auto t0 = std::chrono::steady_clock::now();
   std::vector<uint16_t> lg((size_t)B * V);
-  if (forward_impl(tm, *ss->tc, tm.c.layers, prompts, B, P, lg.data(), true)) return nullptr;
+  if (prefill_chunked(tm, *ss->tc, tm.c.layers, prompts, P, B, P, lg.data())) return nullptr;
   ss->y.resize(B);
   ss->last.resize(B);
   std::vector<int32_t> pp((size_t)B * (P - 1));
@@ -938,7 +998,7 @@ extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prom
     ss->last[b] = prompts[(size_t)b * P + P - 1];
     std::memcpy(&pp[(size_t)b * (P - 1)], &prompts[(size_t)b * P], (P - 1) * 4);
   }
-  if (forward_impl(dm, *ss->dc, dl, pp.data(), B, P - 1, nullptr, true)) return nullptr;
+  if (prefill_chunked(dm, *ss->dc, dl, pp.data(), P - 1, B, P - 1, nullptr)) return nullptr;
   ss->prefill_ns =
       std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
   ss->emitted.assign(B, 0);
@@ -1083,7 +1143,7 @@ extern "C" int orc_generate(void* target, const int32_t* prompts, int B, int P, 
   std::unique_ptr<Cache> tc((Cache*)orc_cache_create(&tm, tm.c.layers, B, P + max_tokens + 8, kv_bits));
   if (!tc) return 1;
   std::vector<uint16_t> lg((size_t)B * V);
-  int rc = forward_impl(tm, *tc, tm.c.layers, prompts, B, P, lg.data(), true);
+  int rc = prefill_chunked(tm, *tc, tm.c.layers, prompts, P, B, P, lg.data());
   if (rc) return rc;
   std::vector<int32_t> y(B);
   orc_argmax(lg.data(), B, V, y.data());

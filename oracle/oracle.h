@@ -67,6 +67,9 @@ int orc_gen_sweep_weights(uint64_t seed, uint32_t tensor_id, int N, int K, int b
 /* ---- ops ---- */
 int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* scales,
             const uint16_t* biases, uint16_t* y, int M, int N, int K, int group, int bits);
+/* M >= threshold: dequantize-then-dot (the tensor-core path); 0 = never */
+void orc_set_mma_min_m(int m);
+int orc_mma_min_m(void);
 void orc_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int dim,
                   float eps);
 void orc_rope_table(int max_pos, int dims, float base, float* cos_t, float* sin_t);

@@ -34,3 +34,17 @@ def cuda():
         pytest.fail("GPU test collected on a machine without CUDA")
     torch.cuda.init()
     return torch
+
+
+@pytest.fixture
+def mma_threshold(lmx):
+    """Set the tensor-core threshold (smallest M routed to the tcgen05 path;
+    0 = never) on the library and the oracle alike; restores the default."""
+    import oracle_lib as O
+
+    def set_(m):
+        lmx.call("lmx_set_mma_min_m", m)
+        O.lib().orc_set_mma_min_m(m)
+
+    yield set_
+    set_(16)

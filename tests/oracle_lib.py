@@ -64,6 +64,8 @@ def _declare(L):
         "orc_dequantize": (I, [P, P, P, I, I, I, I, P]),
         "orc_gen_sweep_weights": (I, [U64, U32, I, I, I, P, P, P]),
         "orc_qmm": (I, [P, P, P, P, P, I, I, I, I, I]),
+        "orc_set_mma_min_m": (None, [I]),
+        "orc_mma_min_m": (I, []),
         "orc_rms_norm": (None, [P, P, P, I, I, F]),
         "orc_rope_table": (None, [I, I, F, P, P]),
         "orc_rope": (None, [P, P, I, I, I, P, P]),

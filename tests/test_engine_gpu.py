@@ -53,9 +53,27 @@ def test_generated_weights_bit_exact(lmx, models, bits):
             np.testing.assert_array_equal(gb, ob)
 
 
+def assert_logits_close(got, ref, what, kv_bits=16):
+    # 2e-2 max-abs, widened by one bf16 ulp of the logit: above |4| the bf16
+    # grid itself is coarser than 2e-2, and both sides round nearly equal
+    # fp32 values to it.  With a 4-bit KV cache the bound is doubled: its
+    # min/max quantizer is discontinuous, so a one-ulp difference in a K/V
+    # projection can move a code by a whole quantization step (1/15 of the
+    # group's range) and the attention output with it.
+    g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
+    tol = (4e-2 if kv_bits == 4 else 2e-2) + np.abs(r) * 2.0 ** -7
+    bad = np.abs(g - r) > tol
+    assert not bad.any(), f"{what}: {int(bad.sum())} logits out of tolerance, max |diff| {np.abs(g - r).max():.4g}"
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("kv_bits", [16, 8, 4])
-def test_forward_logits_bit_exact_with_rollback(lmx, models, bits, kv_bits):
+@pytest.mark.parametrize("mma", [0, 16])
+def test_forward_logits_with_rollback(lmx, models, mma_threshold, bits, kv_bits, mma):
+    # mma 0: every matmul on the canonical GEMV -> bit-exact logits.
+    # mma 16: blocks of >= 16 rows run the tcgen05 path -> logits within
+    # 2e-2 max-abs of the oracle (which takes the same path choice).
+    mma_threshold(mma)
     cfg, g, o = models[bits]
     L, V, B = cfg["layers"], cfg["vocab"], 2
     cap = 160
@@ -66,6 +84,7 @@ def test_forward_logits_bit_exact_with_rollback(lmx, models, bits, kv_bits):
     # prefill 37 tokens (crosses a 32-key split), then a 5-token verify block,
     # roll one sequence back, re-run; then decode steps crossing 128 keys
     blocks = [37, 5, 5, 1, 1] + [30, 30, 5]
+    mma_seen = False
     for i, T in enumerate(blocks):
         if i == 2:
             for b, pos in enumerate([39, 38]):
@@ -80,8 +99,12 @@ def test_forward_logits_bit_exact_with_rollback(lmx, models, bits, kv_bits):
         ol = np.zeros((B, T, V), np.uint16)
         lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
         assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
-        bad = np.argwhere(gl != ol)
-        assert bad.size == 0, f"block {i}: {len(bad)} mismatching logits, first {bad[:3].tolist()}"
+        mma_seen = mma_seen or (mma and B * T >= mma)
+        if mma_seen:  # the cache now holds rows written by the tensor-core path
+            assert_logits_close(gl, ol, f"block {i}", kv_bits)
+        else:
+            bad = np.argwhere(gl != ol)
+            assert bad.size == 0, f"block {i}: {len(bad)} mismatching logits, first {bad[:3].tolist()}"
         for b in range(B):
             n = C.c_int()
             lmx.call("lmx_cache_len", gc, b, C.byref(n))
@@ -103,7 +126,11 @@ def oracle_spec(o, prompts, K, MT, kv_bits, draft_layers, temperature=0.0, top_p
 
 @pytest.mark.parametrize("kv_bits", [16, 4])
 @pytest.mark.parametrize("use_graph", [True, False])
-def test_spec_greedy_stream_matches_oracle(lmx, models, kv_bits, use_graph):
+def test_spec_greedy_stream_matches_oracle(lmx, models, mma_threshold, kv_bits, use_graph):
+    # exact mode: every matmul in the canonical order, so the streams are
+    # bit-identical (with the tensor-core path on, logits agree only within
+    # tolerance and near-ties may flip a token)
+    mma_threshold(0)
     cfg, g, o = models[4]
     B, P, K, MT = 3, 20, 4, 48
     prompts = np.random.RandomState(7).randint(0, cfg["vocab"], (B, P)).astype(np.int32)
@@ -119,3 +146,33 @@ def test_spec_greedy_stream_matches_oracle(lmx, models, kv_bits, use_graph):
     plain = np.zeros((B, MT), np.int32)
     assert O.lib().orc_generate(o, O.ptr(prompts), B, P, MT, kv_bits, O.ptr(plain)) == 0
     np.testing.assert_array_equal(got, plain)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_batched_verify_logits_tensor_core(lmx, models, mma_threshold, bits):
+    # config-3-shaped verify blocks (8 sequences x 6 tokens = 48 rows) on the
+    # tcgen05 path after an exact-mode prefill: logits within tolerance
+    cfg, g, o = models[bits]
+    L, V, B, cap = cfg["layers"], cfg["vocab"], 8, 128
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, cap, 4, 48, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, cap, 4)
+    rng = np.random.RandomState(bits)
+    for i, (T, mma) in enumerate([(12, 0), (6, 16), (6, 16), (1, 16), (6, 16)]):
+        mma_threshold(mma)
+        tok = rng.randint(0, V, (B, T)).astype(np.int32)
+        gl = np.zeros((B, T, V), np.uint16)
+        ol = np.zeros((B, T, V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+        if i == 0:
+            np.testing.assert_array_equal(gl, ol)
+        else:
+            assert_logits_close(gl, ol, f"block {i}", 4)
+        if i == 2:  # roll every sequence back by a different amount
+            for b in range(B):
+                pos = 12 + 6 + (b % 6)
+                lmx.call("lmx_cache_set_position", gc, b, pos)
+                O.lib().orc_cache_set_position(oc, b, pos)
+    lmx.call("lmx_cache_free", gc)
+    O.lib().orc_cache_free(oc)

@@ -10,6 +10,12 @@ import oracle_lib as O
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def canonical(mma_threshold):
+    # every M on the CUDA-core GEMV (the tcgen05 path has its own tests)
+    mma_threshold(0)
+
+
 def dev(torch, a):
     t = torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else
                          (a.view(np.int32) if a.dtype == np.uint32 else a))

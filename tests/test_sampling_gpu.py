@@ -89,9 +89,12 @@ TINY = dict(hidden=512, layers=3, inter=1024, heads=4, kv_heads=2, head_dim=128,
             rope_theta=1e6, eps=1e-6, qk_norm=1, tied=1, bits=4, group_size=64)
 
 
-@pytest.mark.parametrize("kv_bits,top_p", [(16, 0.9), (4, 1.0)])
-def test_stochastic_spec_stream_matches_oracle(lmx, cuda, kv_bits, top_p):
-    B, P, K, MT, T, seed = 3, 20, 4, 40, 0.7, 77
+@pytest.mark.parametrize("kv_bits,top_p,B,K", [(16, 0.9, 3, 4), (4, 1.0, 3, 4), (4, 0.9, 8, 5)])
+def test_stochastic_spec_stream_matches_oracle(lmx, cuda, mma_threshold, kv_bits, top_p, B, K):
+    # exact mode (canonical matmul order everywhere): identical streams; the
+    # last case has config 3's batch 8, K = 5, 4-bit KV, T 0.7, top-p 0.9
+    mma_threshold(0)
+    P, MT, T, seed = 20, 40, 0.7, 77
     g = lmx.Model(TINY, 4321)
     ocfg = dict(TINY)
     ocfg["group"] = ocfg.pop("group_size")
