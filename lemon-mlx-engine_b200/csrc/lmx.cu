@@ -76,13 +76,14 @@ unsigned* device_error_word() { return dev().err; }
 namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_map_mu;
-std::map<std::tuple<const void*, int, uint64_t, uint64_t, int, int>, CUtensorMap> g_maps;
+std::map<std::tuple<const void*, int, uint64_t, uint64_t, int, int, int>, CUtensorMap> g_maps;
 }  // namespace
 
 static int tensor_map_2d(const void* base, CUtensorMapDataType dt, int esize, uint64_t cols, uint64_t rows,
-                         int box_w, int box_h, CUtensorMap* out) {
+                         int box_w, int box_h, CUtensorMap* out,
+                         CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE) {
   std::lock_guard<std::mutex> lk(g_map_mu);
-  const auto key = std::make_tuple(base, (int)dt, cols, rows, box_w, box_h);
+  const auto key = std::make_tuple(base, (int)dt, cols, rows, box_w, box_h, (int)swz);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
     *out = it->second;
@@ -101,8 +102,7 @@ static int tensor_map_2d(const void* base, CUtensorMapDataType dt, int esize, ui
   cuuint32_t estr[2] = {1, 1};
   CUtensorMap m;
   CUresult r = g_encode(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(LMX_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
   g_maps[key] = m;
   *out = m;
@@ -281,31 +281,43 @@ static int tensor_map_x(const void* base, uint64_t K, uint64_t M, uint64_t ldx, 
 }
 
 struct MmaShape {
-  int Mpad = 0, mtiles = 0, stages = 0, per_sm = 1;
+  int Mpad = 0, mtiles = 0, np = 0, na = 0, per_sm = 1, acc_cols = 0, tmem_cols = 0;
   size_t smem = 0;
 };
 
-// Token tiles of at most 256 (UMMA N), padded to 16; pipeline depth from the
-// shared-memory budget: two CTAs per SM when four or more stages fit in half
-// of it, else one CTA with up to kMmaMaxStages.
+// Token tiles of at most 256 (UMMA N), padded to 16.  TMEM: accumulator
+// (power of two >= Mpad, >= 32 columns) + na A stages of 64 columns (one
+// step of two chunks each).  Two CTAs per SM (256 TMEM columns, ~112 KB of
+// shared memory each) when two or more A stages and three or more packed
+// stages fit; else one CTA per SM with the whole TMEM and shared memory.
 static int mma_plan(int M, int bits, MmaShape& sh) {
+  (void)bits;
   sh.mtiles = (M + 255) / 256;
   const int mper = (M + sh.mtiles - 1) / sh.mtiles;
   sh.Mpad = (mper + 15) / 16 * 16;
-  const int stage = kMmaRows * kMmaK * 2 + sh.Mpad * kMmaK * 2 + kMmaRows * kMmaK * bits / 8;
-  const int fixed = 1024 + (4 * kMmaMaxStages + 1) * 8 + 16;
-  int st = (112 * 1024 - fixed) / stage;
-  sh.per_sm = 2;
-  if (st < 4) {
-    st = (227 * 1024 - fixed) / stage;
-    sh.per_sm = 1;
+  sh.acc_cols = sh.Mpad <= 32 ? 32 : (sh.Mpad <= 64 ? 64 : (sh.Mpad <= 128 ? 128 : 256));
+  const int xstage = kMmaStep * sh.Mpad * kMmaK * 2, pstage = kMmaRows * 128;
+  const int fixed = 1024 + (2 * kMmaMaxPStages + 3 * kMmaMaxAStages + 1) * 8 + 16;
+  for (sh.per_sm = 2; sh.per_sm >= 1; --sh.per_sm) {
+    sh.tmem_cols = sh.per_sm == 2 ? 256 : 512;
+    const int budget = sh.per_sm == 2 ? 112 * 1024 : 227 * 1024;
+    const int min_np = sh.per_sm == 2 ? 3 : 2;
+    int na = (sh.tmem_cols - sh.acc_cols) / 64;
+    const int na_smem = (budget - fixed - min_np * pstage) / xstage;
+    if (na > na_smem) na = na_smem;
+    if (na > kMmaMaxAStages) na = kMmaMaxAStages;
+    if (na < 2) continue;
+    int np = (budget - fixed - na * xstage) / pstage;
+    if (np > kMmaMaxPStages) np = kMmaMaxPStages;
+    if (np < min_np) continue;
+    sh.na = na;
+    sh.np = np;
+    break;
   }
-  if (st > kMmaMaxStages) st = kMmaMaxStages;
-  if (st < 2) return set_error(LMX_ERR_UNSUPPORTED, "qmm: token tile %d too large", sh.Mpad);
-  if ((size_t)sh.Mpad * kMmaRows * 4 > (size_t)st * stage)
+  if (sh.per_sm < 1) return set_error(LMX_ERR_UNSUPPORTED, "qmm: token tile %d too large", sh.Mpad);
+  if ((size_t)sh.Mpad * kMmaRows * 4 > (size_t)sh.na * xstage + (size_t)sh.np * pstage)
     return set_error(LMX_ERR_UNSUPPORTED, "qmm: reduction tile does not fit");
-  sh.stages = st;
-  sh.smem = (size_t)fixed + (size_t)st * stage;
+  sh.smem = (size_t)fixed + (size_t)sh.na * xstage + (size_t)sh.np * pstage;
   return LMX_OK;
 }
 
@@ -327,7 +339,9 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
     a.cstart[i] = cv;
     ntiles += (q.mat[i].rows + kMmaRows - 1) / kMmaRows;
     cv += q.mat[i].rows;
-    rc = tensor_map_2d(q.mat[i].w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, WPR, q.mat[i].rows, 2 * BITS, boxh, &mp.w[i]);
+    // 128-byte rows (kMmaPackChunks chunks), 128-byte swizzle
+    rc = tensor_map_2d(q.mat[i].w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, WPR, q.mat[i].rows, 32, boxh, &mp.w[i],
+                       CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   if (swiglu) ntiles = (q.N + kMmaRows / 2 - 1) / (kMmaRows / 2);
@@ -339,7 +353,13 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
   a.Mpad = sh.Mpad;
   a.K = q.K;
   a.mode = q.mode;
-  a.stages = sh.stages;
+  a.np = sh.np;
+  a.na = sh.na;
+  a.sb_vec = (q.K % 512) == 0;
+  for (int i = 0; i < q.nmat; ++i)
+    a.sb_vec = a.sb_vec && !((uintptr_t)q.mat[i].s & 15) && !((uintptr_t)q.mat[i].b & 15);
+  a.acc_cols = sh.acc_cols;
+  a.tmem_cols = sh.tmem_cols;
   a.y = q.y;
   a.ldy = q.ldy;
   a.res = q.res;

@@ -101,10 +101,12 @@ LMX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
 #else
+  // suspend-time hint 1 ms: the thread sleeps in hardware until the phase
+  // completes (or the hint expires) instead of spinning on issue slots
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
 #endif
   return ok != 0;
@@ -114,17 +116,27 @@ LMX_DEV uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: gives up after 4 s of wall time (checked every 256 polls) or
-// 2^26 polls, whichever comes first, and flags the error word.
-LMX_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Bounded wait: gives up after 4 s of wall time or 2^26 polls, whichever
+// comes first, and flags the error word.  The polling loop is out of line so
+// that the common case (phase already complete) stays a few instructions,
+// and it backs off with nanosleep (32 ns doubling to 256 ns): warps that run
+// ahead of a pipeline would otherwise spin and take issue slots from the
+// warps whose work they are waiting for.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
   const uint64_t t0 = global_ns();
+  uint32_t ns = 32;
   for (uint32_t i = 1; i < (1u << 26); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > 4000000000ull) break;
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+    if (global_ns() - t0 > 4000000000ull) break;
   }
   if (err) atomicExch(err, code);
   return false;
+}
+LMX_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, code);
 }
 
 // Item -> (matrix, row).  PLAIN/RESID: items are the concatenated rows of

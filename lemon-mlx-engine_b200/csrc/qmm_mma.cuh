@@ -1,25 +1,33 @@
 // qmm_mma.cuh -- K1 tensor-core path for M >= 16 (batched verify, prefill):
-// dequantize-to-shared-memory + tcgen05.mma with a TMEM accumulator.
+// dequantize into tensor memory + tcgen05.mma with a TMEM accumulator.
 //
-// Swap-AB: D[n, m] = sum_k W[n, k] * X[m, k].  The weight tile is the MMA's A
-// operand (128 weight rows = UMMA M), the activations are B (the token count
-// padded to 16 = UMMA N), both K-major in the 128-byte-swizzled canonical
-// layout (8-row x 128-byte atoms, 16-byte chunk index XOR row % 8).  Per CTA
-// and 64-k chunk (one quantization group):
-//   warp 0      TMA producer: packed weight tile [128 (or 2 x 64) rows x 64 k]
-//               on `wfull`, activation tile [Mpad x 64 k] (TMA 128B swizzle)
-//               on `xfull`.  Weight loads for the first stages are issued
-//               before the programmatic-launch wait (weights are constant).
-//   warps 2..5  one weight row per thread: bf16(fma(scale, q, bias)) written
-//               into the swizzled A tile, then a proxy fence and `deq` arrive.
-//   warp 1      allocates TMEM; one lane issues 4 x tcgen05.mma (K = 16) per
-//               chunk and commits each stage back to `empty`, the whole
-//               accumulation to `accf`.
+// Swap-AB: D[n, m] = sum_k W[n, k] * X[m, k].  The dequantized weight tile is
+// the MMA's A operand, held in TMEM (128 weight rows = 128 lanes, two bf16 k
+// per 32-bit column); the activations are B, TMA-loaded into shared memory in
+// the 128-byte-swizzled K-major layout (8-row x 128-byte atoms); the fp32
+// accumulator [128 rows x Mpad tokens] sits in TMEM.  Per 64-k chunk (one
+// quantization group):
+//   warp 0      W producer: packed weight tile [128 (or 2 x 64) rows x 64 k]
+//               into a deep ring of `NP` stages (`pfull` / `pfree`); weights
+//               are constant, so it runs ahead of the programmatic-launch
+//               wait.
+//   warp 10     X producer: activation tiles [Mpad x 64 k] of a step (two
+//               chunks) into the `na`-stage ring shared with the A stages
+//               (`xfull` / `mdone`).
+//   warps 2..9  dequantizers, two threads per weight row (k halves of 32):
+//               packed words -> bf16(fma(scale, q, bias)) -> tcgen05.st into
+//               the A stage (`afull`); they free the packed stage as soon as
+//               its words are in registers.
+//   warp 1      allocates TMEM; one lane issues 4 x tcgen05.mma (K = 16, A
+//               from TMEM, B from shared memory) per chunk and commits each
+//               step's stage to `mdone`, the whole accumulation to `accf`.
+// A and X stages hold one step = kMmaStep chunks, so the per-stage
+// synchronisation (waits, arrives, TMEM store fences) is paid once per 128 k.
 // Split-K: a cluster of `ks` CTAs shares one output tile, each accumulating a
 // contiguous range of chunks; the fp32 tiles meet in shared memory and each
 // rank reduces a slice of the outputs over the ranks in rank order (DSMEM).
-// Epilogue: tcgen05.ld (warps 2..5, one TMEM lane quarter each) -> fp32 tile
-// [m][row] in shared memory -> coalesced PLAIN / RESID / SWIGLU stores.
+// Epilogue: tcgen05.ld (lane quarter = warp % 4) -> fp32 tile [m][row] in
+// shared memory -> coalesced PLAIN / RESID / SWIGLU stores.
 // Every mbarrier wait is bounded and sets the device error word on timeout.
 // No TMA multicast.  Numerics: bf16 dequantized weights, fp32 tensor-core
 // accumulation in the hardware's order (compared with a tolerance).
@@ -30,12 +38,16 @@ namespace lmx {
 
 static constexpr int kMmaRows = 128;  // weight rows per tile (UMMA M)
 static constexpr int kMmaK = 64;      // k per pipeline stage (one group)
-static constexpr int kMmaThreads = 192;
-static constexpr int kMmaMaxStages = 8;
+static constexpr int kMmaWarps = 11;  // W producer, MMA, 8 dequantizers, X producer
+static constexpr int kMmaThreads = 32 * kMmaWarps;
+static constexpr int kMmaDeqWarps = 8;
+static constexpr int kMmaStep = 2;        // chunks per A (TMEM) / X (shared) stage
+static constexpr int kMmaMaxAStages = 4;
+static constexpr int kMmaMaxPStages = 16;
 static constexpr int kMmaMaxSplit = 8;
 
 struct MmaMaps {
-  CUtensorMap w[3];  // uint32 [rows][K*bits/32], box {2*bits words, 128 (SWIGLU: 64) rows}
+  CUtensorMap w[3];  // uint32 [rows][K*bits/32], box {32 words, 128 (SWIGLU: 64) rows}, 128B swizzle
   CUtensorMap x;     // bf16 [M][ldx], box {64, Mpad}, 128-byte swizzle
 };
 
@@ -46,7 +58,9 @@ struct MmaArgs {
   int cstart[3];  // PLAIN/RESID: first output column of each matrix
   int N;          // SWIGLU: rows per matrix
   int M, Mpad, K, mode;
-  int stages, ks;
+  int np, na, ks;      // packed-weight stages, A/X stages, split-K factor (cluster size)
+  int acc_cols, tmem_cols;
+  int sb_vec;          // scales / biases readable as 16-byte vectors (K % 512 == 0, aligned)
   bf16_t* y;
   int ldy;
   const bf16_t* res;
@@ -68,11 +82,12 @@ LMX_DEV uint32_t umma_idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kMmaRows >> 4) << 24);
 }
 
-LMX_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T, 128 x N x 16.
+LMX_DEV void umma_ts_bf16(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -97,6 +112,16 @@ LMX_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 16 columns of 32 bits: lane i of the warp's quarter gets v[0..15].
+LMX_DEV void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 LMX_DEV uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
   asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -104,12 +129,13 @@ LMX_DEV uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
 }
 
 // Eight 4-bit codes of one word (k = 8c .. 8c+7) -> eight bf16 weights
-// bf16(s*q + b) in k order.  Codes become exact bf16 values 128 + q by OR-ing
-// the exponent of 128 (0x4300) over a nibble; subtracting 128 is exact; the
-// bf16x2 fma rounds s*q + b once.  That equals bf16(fmaf(s, q, b)) whenever
-// fmaf is exact, i.e. whenever s*q + b fits 24 significant bits (always the
-// case unless |bias| and |scale| lie more than ~2^12 apart).
-LMX_DEV uint4 deq8_b4(uint32_t w, uint32_t s2, uint32_t b2) {
+// bf16(s*q + b) in k order, two per word of `o`.  Codes become exact bf16
+// values 128 + q by OR-ing the exponent of 128 (0x4300) over a nibble;
+// subtracting 128 is exact; the bf16x2 fma rounds s*q + b once.  That equals
+// bf16(fmaf(s, q, b)) whenever fmaf is exact, i.e. whenever s*q + b fits 24
+// significant bits (always, unless |bias| and |scale| lie more than ~2^12
+// apart).
+LMX_DEV void deq8_b4(uint32_t w, uint32_t s2, uint32_t b2, uint32_t* o) {
   const uint32_t one = 0x3F803F80u, m128 = 0xC300C300u;
   uint32_t v[4];
 #pragma unroll
@@ -117,14 +143,15 @@ LMX_DEV uint4 deq8_b4(uint32_t w, uint32_t s2, uint32_t b2) {
     const uint32_t x = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;  // (q_i, q_{i+4})
     v[i] = bf2_fma(s2, bf2_fma(x, one, m128), b2);
   }
-  return make_uint4(__byte_perm(v[0], v[1], 0x5410), __byte_perm(v[2], v[3], 0x5410),
-                    __byte_perm(v[0], v[1], 0x7632), __byte_perm(v[2], v[3], 0x7632));
+  o[0] = __byte_perm(v[0], v[1], 0x5410);
+  o[1] = __byte_perm(v[2], v[3], 0x5410);
+  o[2] = __byte_perm(v[0], v[1], 0x7632);
+  o[3] = __byte_perm(v[2], v[3], 0x7632);
 }
 
 // Eight 8-bit codes (two words) -> bf16(fmaf(s, q, b)) in k order: the code
 // becomes an exact fp32 (2^23 + q) - 2^23, the fma runs in fp32.
-LMX_DEV uint4 deq8_b8(uint32_t w0, uint32_t w1, float s, float b) {
-  uint32_t o[4];
+LMX_DEV void deq8_b8(uint32_t w0, uint32_t w1, float s, float b, uint32_t* o) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t w = i < 2 ? w0 : w1;
@@ -133,7 +160,6 @@ LMX_DEV uint4 deq8_b8(uint32_t w0, uint32_t w1, float s, float b) {
     const float q1 = __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541 + e)), 8388608.0f);
     o[i] = (uint32_t)f2bf(__fmaf_rn(s, q0, b)) | ((uint32_t)f2bf(__fmaf_rn(s, q1, b)) << 16);
   }
-  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 LMX_DEV const QmmMat& mma_mat(const MmaArgs& a, int mi) {
@@ -162,27 +188,35 @@ LMX_DEV bool warp_wait(uint64_t* bar, uint32_t parity, unsigned* err, unsigned c
   return __all_sync(0xffffffffu, ok);
 }
 
+LMX_DEV uint32_t u4_word(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
 // Shared memory (base rounded up to 1024 bytes):
-//   A[stages][16 KB]  B[stages][Mpad * 128 B]  P[stages][128 * 64 * BITS / 8 B]
-//   barriers: wfull, xfull, deq, empty [stages] + accf;  tmem slot;  fail flag
-//   red = fp32 [Mpad][128] over the A/B/P region once the MMAs are done
+//   X[na][2 x Mpad * 128 B]  P[np][128 rows * 128 B] (16/BITS chunks per
+//   stage, 16-byte units swizzled by row % 8, as TMA's 128-byte swizzle
+//   writes them)
+//   barriers: pfull, pfree [np]; xfull, afull, mdone [na]; accf;  tmem slot;  fail flag
+//   red = fp32 [Mpad][128] over the X/P region once the MMAs are done
+// TMEM: accumulator columns [0, acc_cols), A stage s at acc_cols + 64 s
+// (chunk u of the step at + 32 u, k half h of a chunk at + 16 h).
 template <int BITS>
-__global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_constant__ MmaMaps mp, MmaArgs a) {
+__global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_constant__ MmaMaps mp, MmaArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  constexpr int ABYTES = kMmaRows * kMmaK * 2;
-  constexpr int PBYTES = kMmaRows * kMmaK * BITS / 8;
-  constexpr int PROW = kMmaK * BITS / 8;  // packed bytes of one row per chunk
-  const int NS = a.stages;
-  const int BBYTES = a.Mpad * kMmaK * 2;
-  uint8_t* As = smem;
-  uint8_t* Bs = As + NS * ABYTES;
-  uint8_t* Ps = Bs + NS * BBYTES;
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(Ps + NS * PBYTES);
-  uint64_t* xfull = wfull + NS;
-  uint64_t* deq = xfull + NS;
-  uint64_t* empty = deq + NS;
-  uint64_t* accf = empty + NS;
+  constexpr int PBYTES = kMmaRows * 128;
+  constexpr int CH = 16 / BITS;  // chunks per packed stage (128 bytes of a row)
+  const int NP = a.np, NA = a.na;
+  const int XBYTES = a.Mpad * kMmaK * 2;  // one chunk's activation tile
+  const int XSTAGE = kMmaStep * XBYTES;
+  uint8_t* Xs = smem;
+  uint8_t* Ps = Xs + NA * XSTAGE;
+  uint64_t* pfull = reinterpret_cast<uint64_t*>(Ps + NP * PBYTES);
+  uint64_t* pfree = pfull + NP;
+  uint64_t* xfull = pfree + NP;
+  uint64_t* afull = xfull + NA;
+  uint64_t* mdone = afull + NA;
+  uint64_t* accf = mdone + NA;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
   int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem);
@@ -194,19 +228,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_co
   const int nk = a.K / kMmaK;
   const int kc0 = (int)((long)rank * nk / ks), kc1 = (int)((long)(rank + 1) * nk / ks);
   const int nloc = kc1 - kc0;
+  const int nsteps = (nloc + kMmaStep - 1) / kMmaStep;
   const int G = a.K / 64;
   const bool swiglu = a.mode == QMM_SWIGLU;
   int mi = 0, row0 = 0;
   if (swiglu) row0 = tile * (kMmaRows / 2);
   else mma_tile(a, tile, mi, row0);
-  const uint32_t ncols = a.Mpad <= 32 ? 32u : (a.Mpad <= 64 ? 64u : (a.Mpad <= 128 ? 128u : 256u));
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&wfull[s], 1);
+    for (int s = 0; s < NP; ++s) {
+      mbar_init(&pfull[s], 1);
+      mbar_init(&pfree[s], kMmaDeqWarps);
+    }
+    for (int s = 0; s < NA; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&deq[s], 4);
-      mbar_init(&empty[s], 1);
+      mbar_init(&afull[s], kMmaDeqWarps);
+      mbar_init(&mdone[s], 1);
     }
     mbar_init(accf, 1);
     *s_fail = 0;
@@ -214,7 +251,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_co
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(ncols)
+                 "r"((uint32_t)a.tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -222,128 +259,200 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_co
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + (uint32_t)a.acc_cols;
   grid_launch_dependents();
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- W producer (no dependency on earlier kernels) ----------------
     if (lane == 0) {
-      const int wx_step = kMmaK * BITS / 32;
-      auto load_w = [&](int j) {
-        const int s = j % NS, kc = kc0 + j;
-        mbar_arrive_expect_tx(&wfull[s], (uint32_t)PBYTES);
-        if (swiglu) {
-          tma_load_2d(Ps + s * PBYTES, &mp.w[0], kc * wx_step, row0, &wfull[s]);
-          tma_load_2d(Ps + s * PBYTES + PBYTES / 2, &mp.w[1], kc * wx_step, row0, &wfull[s]);
-        } else {
-          tma_load_2d(Ps + s * PBYTES, &mp.w[mi], kc * wx_step, row0, &wfull[s]);
-        }
-      };
-      auto load_x = [&](int j) {
-        const int s = j % NS, kc = kc0 + j;
-        mbar_arrive_expect_tx(&xfull[s], (uint32_t)BBYTES);
-        tma_load_2d(Bs + s * BBYTES, &mp.x, kc * kMmaK, m0, &xfull[s]);
-      };
-      const int npre = nloc < NS ? nloc : NS;
-      for (int j = 0; j < npre; ++j) load_w(j);
-      grid_wait();
-      for (int j = 0; j < npre; ++j) load_x(j);
-      for (int j = npre; j < nloc; ++j) {
-        if (!mbar_wait_bounded(&empty[j % NS], (uint32_t)(((j / NS) - 1) & 1), a.err, 0x61u)) {
+      const int nst = (nloc + CH - 1) / CH;
+      int s = 0;
+      uint32_t ph = 0;  // parity of the pfree phase that frees stage s
+      for (int t = 0; t < nst; ++t) {
+        const int wx = (kc0 + t * CH) * 2 * BITS;  // word column of the stage's first chunk
+        if (t >= NP && !mbar_wait_bounded(&pfree[s], ph, a.err, 0x61u)) {
           ok = false;
           break;
         }
-        load_w(j);
-        load_x(j);
+        mbar_arrive_expect_tx(&pfull[s], (uint32_t)PBYTES);
+        if (swiglu) {
+          tma_load_2d(Ps + s * PBYTES, &mp.w[0], wx, row0, &pfull[s]);
+          tma_load_2d(Ps + s * PBYTES + PBYTES / 2, &mp.w[1], wx, row0, &pfull[s]);
+        } else {
+          tma_load_2d(Ps + s * PBYTES, &mp.w[mi], wx, row0, &pfull[s]);
+        }
+        if (++s == NP) {
+          s = 0;
+          if (t >= NP) ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == kMmaWarps - 1) {
+    // ---------------- X producer (after the programmatic-launch wait) ----------------
+    if (lane == 0) {
+      grid_wait();
+      int s = 0;
+      uint32_t ph = 0;  // parity of the mdone phase that frees stage s
+      for (int t = 0; t < nsteps; ++t) {
+        const int kc = kc0 + kMmaStep * t, cnt = min(kMmaStep, nloc - kMmaStep * t);
+        if (t >= NA && !mbar_wait_bounded(&mdone[s], ph, a.err, 0x62u)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&xfull[s], (uint32_t)(cnt * XBYTES));
+        for (int u = 0; u < cnt; ++u)
+          tma_load_2d(Xs + s * XSTAGE + u * XBYTES, &mp.x, (kc + u) * kMmaK, m0, &xfull[s]);
+        if (++s == NA) {
+          s = 0;
+          if (t >= NA) ph ^= 1u;
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(a.Mpad);
-      for (int j = 0; j < nloc; ++j) {
-        const int s = j % NS;
-        const uint32_t par = (uint32_t)((j / NS) & 1);
-        if (!mbar_wait_bounded(&deq[s], par, a.err, 0x62u) || !mbar_wait_bounded(&xfull[s], par, a.err, 0x63u)) {
+      int s = 0;
+      uint32_t ph = 0;  // parity of the afull / xfull phase of stage s
+      for (int t = 0; t < nsteps; ++t) {
+        if (!mbar_wait_bounded(&afull[s], ph, a.err, 0x63u) || !mbar_wait_bounded(&xfull[s], ph, a.err, 0x64u)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t abase = smem_u32(As + s * ABYTES), bbase = smem_u32(Bs + s * BBYTES);
+        const int cnt = min(kMmaStep, nloc - kMmaStep * t);
+        const uint32_t bbase = smem_u32(Xs + s * XSTAGE);
+        for (int u = 0; u < cnt; ++u) {
 #pragma unroll
-        for (int k16 = 0; k16 < kMmaK / 16; ++k16)
-          umma_bf16(tmem, umma_desc_sw128(abase + 32 * k16), umma_desc_sw128(bbase + 32 * k16), idesc,
-                    (j > 0 || k16 > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int k16 = 0; k16 < kMmaK / 16; ++k16)
+            umma_ts_bf16(tmem, tmem_a + (uint32_t)(64 * s + 32 * u + 8 * k16),
+                         umma_desc_sw128(bbase + u * XBYTES + 32 * k16), idesc, (t > 0 || u > 0 || k16 > 0) ? 1u : 0u);
+        }
+        umma_commit(&mdone[s]);
+        if (++s == NA) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       // arrives once every MMA issued above has completed
       umma_commit(accf);
     }
   } else {
-    // ---------------- dequantizers: thread r owns weight row r of the tile ----------------
-    const int r = threadIdx.x - 64;
-    int wmi = mi, wrow = row0 + r;
+    // ---------------- dequantizers: row rr of the tile, k half h ----------------
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const int rr = 32 * q + lane;
+    int wmi = mi, wrow = row0 + rr;
     if (swiglu) {
-      wmi = r < 64 ? 0 : 1;
-      wrow = row0 + (r & 63);
+      wmi = rr < 64 ? 0 : 1;
+      wrow = row0 + (rr & 63);
     }
     const QmmMat& wm = mma_mat(a, wmi);
     const bool rvalid = wrow < (swiglu ? a.N : wm.rows);
     const bf16_t* srow = wm.s + (size_t)(rvalid ? wrow : 0) * G;
     const bf16_t* brow = wm.b + (size_t)(rvalid ? wrow : 0) * G;
-    bf16_t sc = rvalid && nloc > 0 ? srow[kc0] : (bf16_t)0, bi = rvalid && nloc > 0 ? brow[kc0] : (bf16_t)0;
-    uint8_t* arow0 = As + (r >> 3) * 1024 + (r & 7) * 128;
-    for (int j = 0; j < nloc; ++j) {
-      const int s = j % NS, kc = kc0 + j;
-      const bf16_t sn = (rvalid && j + 1 < nloc) ? srow[kc + 1] : (bf16_t)0;
-      const bf16_t bn = (rvalid && j + 1 < nloc) ? brow[kc + 1] : (bf16_t)0;
-      if (j >= NS && !warp_wait(&empty[s], (uint32_t)(((j / NS) - 1) & 1), a.err, 0x64u)) {
-        ok = false;
-        break;
+    const bool vec = a.sb_vec != 0;
+    // scales / biases: 8-group blocks as 16-byte vectors (current and next)
+    uint4 cs = make_uint4(0, 0, 0, 0), cb = cs, ns = cs, nb = cs;
+    if (vec && nloc > 0) {
+      const int blk = kc0 >> 3;
+      cs = *reinterpret_cast<const uint4*>(srow + 8 * blk);
+      cb = *reinterpret_cast<const uint4*>(brow + 8 * blk);
+      if (8 * (blk + 1) < G) {
+        ns = *reinterpret_cast<const uint4*>(srow + 8 * (blk + 1));
+        nb = *reinterpret_cast<const uint4*>(brow + 8 * (blk + 1));
       }
-      if (!warp_wait(&wfull[s], (uint32_t)((j / NS) & 1), a.err, 0x65u)) {
-        ok = false;
-        break;
-      }
-      const uint4* prow = reinterpret_cast<const uint4*>(Ps + s * PBYTES + r * PROW);
-      uint8_t* arow = arow0 + s * ABYTES;
-      if (BITS == 4) {
-        const uint4 p0 = prow[0], p1 = prow[1];
-        const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        const uint32_t s2 = (uint32_t)sc | ((uint32_t)sc << 16), b2 = (uint32_t)bi | ((uint32_t)bi << 16);
+    }
+    const uint32_t tlane = (uint32_t)(32 * q) << 16;
+    const uint8_t* prow0 = Ps + rr * 128;
+    const int sw = rr & 7;
+    int sp = 0;
+    uint32_t pph = 0;  // parity of the pfull phase of stage sp
+    int s = 0;
+    uint32_t aph = 0;  // parity of the mdone phase that frees A stage s
+    for (int t = 0; t < nsteps && ok; ++t) {
+      const int cnt = min(kMmaStep, nloc - kMmaStep * t);
+      for (int u = 0; u < cnt; ++u) {
+        const int j = kMmaStep * t + u, kc = kc0 + j, c = j % CH;
+        bf16_t sc, bi;
+        if (vec) {
+          if (j > 0 && (kc & 7) == 0) {
+            cs = ns;
+            cb = nb;
+            if (8 * ((kc >> 3) + 1) < G) {
+              ns = *reinterpret_cast<const uint4*>(srow + 8 * ((kc >> 3) + 1));
+              nb = *reinterpret_cast<const uint4*>(brow + 8 * ((kc >> 3) + 1));
+            }
+          }
+          const int g = kc & 7, sh = 16 * (g & 1);
+          sc = (bf16_t)(u4_word(cs, g >> 1) >> sh);
+          bi = (bf16_t)(u4_word(cb, g >> 1) >> sh);
+        } else {
+          sc = srow[kc];
+          bi = brow[kc];
+        }
+        if (c == 0 && !warp_wait(&pfull[sp], pph, a.err, 0x65u)) {
+          ok = false;
+          break;
+        }
+        // this thread's 32 k of row rr: 16-byte units 2c+h (4-bit) or 4c+2h, 4c+2h+1 (8-bit)
+        const uint8_t* pst = prow0 + sp * PBYTES;
+        uint32_t wv[BITS];  // 4 or 8 words
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = deq8_b4(wv[c], s2, b2);
-      } else {
-        uint32_t wv[16];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 p = prow[i];
+        for (int i = 0; i < BITS / 4; ++i) {
+          const int un = (BITS == 4) ? (2 * c + h) : (4 * c + 2 * h + i);
+          const uint4 p = *reinterpret_cast<const uint4*>(pst + ((un ^ sw) << 4));
           wv[4 * i] = p.x;
           wv[4 * i + 1] = p.y;
           wv[4 * i + 2] = p.z;
           wv[4 * i + 3] = p.w;
         }
-        const float sf = bf2f(sc), bf = bf2f(bi);
+        uint32_t o[16];
+        if (BITS == 4) {
+          if (!rvalid) sc = bi = 0;
+          const uint32_t s2 = (uint32_t)sc | ((uint32_t)sc << 16), b2 = (uint32_t)bi | ((uint32_t)bi << 16);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = deq8_b8(wv[2 * c], wv[2 * c + 1], sf, bf);
+          for (int cc = 0; cc < 4; ++cc) deq8_b4(wv[cc], s2, b2, &o[4 * cc]);
+        } else {
+          const float sf = rvalid ? bf2f(sc) : 0.0f, bf = rvalid ? bf2f(bi) : 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) deq8_b8(wv[2 * cc], wv[2 * cc + 1], sf, bf, &o[4 * cc]);
+        }
+        // after the packed stage's last chunk has been consumed (its loads are
+        // complete) it may be refilled; an arrive issued right after the loads
+        // could let the TMA overwrite words still in flight
+        if (c == CH - 1 || j == nloc - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pfree[sp]);
+          if (++sp == NP) {
+            sp = 0;
+            pph ^= 1u;
+          }
+        }
+        if (u == 0 && t >= NA && !warp_wait(&mdone[s], aph, a.err, 0x66u)) {
+          ok = false;
+          break;
+        }
+        tmem_st16(tlane + tmem_a + (uint32_t)(64 * s + 32 * u + 16 * h), o);
       }
-      // generic-proxy stores -> visible to the tensor core, then signal
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (!ok) break;
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq[s]);
-      sc = sn;
-      bi = bn;
+      if (lane == 0) mbar_arrive(&afull[s]);
+      if (++s == NA) {
+        s = 0;
+        if (t >= NA) aph ^= 1u;
+      }
     }
-    // accumulator -> red[m][row] (fp32), lane quarter q = warp % 4
-    if (ok) ok = warp_wait(accf, 0u, a.err, 0x66u);
+    // accumulator -> red[m][row] (fp32); the two warps of a lane quarter
+    // take alternate 16-column blocks
+    if (ok) ok = warp_wait(accf, 0u, a.err, 0x67u);
     if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int q = warp & 3, rr = 32 * q + lane;
-      for (int c0 = 0; c0 < a.Mpad; c0 += 16) {
+      for (int c0 = 16 * h; c0 < a.Mpad; c0 += 32) {
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        tmem_ld16(tlane + tmem + (uint32_t)c0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) red[(c0 + i) * kMmaRows + rr] = v[i];
       }
@@ -364,19 +473,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_co
     const int per = (total + ks - 1) / ks;
     const int i0 = rank * per, i1 = min(total, i0 + per);
     for (int idx = i0 + (int)threadIdx.x; idx < i1; idx += kMmaThreads) {
-      const int m = idx / rows_out, rr = idx % rows_out;
+      const int m = idx / rows_out, r2 = idx % rows_out;
       float acc = 0.0f, acc2 = 0.0f;
       for (int k = 0; k < ks; ++k) {
         const float* rb = ks > 1 ? cluster.map_shared_rank(red, k) : red;
-        acc = __fadd_rn(acc, rb[m * kMmaRows + rr]);
-        if (swiglu) acc2 = __fadd_rn(acc2, rb[m * kMmaRows + 64 + rr]);
+        acc = __fadd_rn(acc, rb[m * kMmaRows + r2]);
+        if (swiglu) acc2 = __fadd_rn(acc2, rb[m * kMmaRows + 64 + r2]);
       }
       const size_t orow = (size_t)(m0 + m) * a.ldy;
       if (swiglu) {
-        const int col = row0 + rr;
+        const int col = row0 + r2;
         if (col < a.N) a.y[orow + col] = swiglu_c(f2bf(acc), f2bf(acc2));
       } else {
-        const int row = row0 + rr;
+        const int row = row0 + r2;
         if (row < mma_mat(a, mi).rows) {
           const size_t o = orow + a.cstart[mi] + row;
           bf16_t yv = f2bf(acc);
@@ -389,10 +498,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmm_mma_kernel(const __grid_co
   if (ks > 1) cluster.sync();  // peers may still read this CTA's red tile
   // the accumulator must be idle before TMEM is released
   if (warp == 1) {
-    if (lane == 0 && *s_fail) mbar_wait_bounded(accf, 0u, a.err, 0x67u);
+    if (lane == 0 && *s_fail) mbar_wait_bounded(accf, 0u, a.err, 0x68u);
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)a.tmem_cols)
+                 : "memory");
   }
 }
 
