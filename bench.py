@@ -43,10 +43,18 @@ def _load(name, path):
     return mod
 
 
+# configs[0] (bs1, greedy, self-draft) and configs[2] (bs8, stochastic, separate
+# Qwen3-0.6B draft over a Qwen3-8B target, 4-bit KV).  `cpu_prompt` shortens
+# the prompt of the bounded CPU sample only (its prefill is untimed).
 WORKLOADS = {
-    "qwen3-0.6b-selfdraft2-k4-bs1": dict(arch="QWEN3_0_6B", draft_layers=2, K=4, batch=1,
-                                         prompt=128, new=256, kv_bits=16, temperature=0.0,
-                                         top_p=1.0),
+    "qwen3-0.6b-selfdraft2-k4-bs1": dict(arch="QWEN3_0_6B", draft=None, draft_layers=2, K=4,
+                                         batch=1, prompt=128, new=256, kv_bits=16,
+                                         temperature=0.0, top_p=1.0, cpu_prompt=None,
+                                         profile="verify_pass_qwen3_0.6b_k4_bs1.md"),
+    "qwen3-8b-draft0.6b-k5-bs8-t0.7": dict(arch="QWEN3_8B", draft="QWEN3_0_6B", draft_layers=28,
+                                           K=5, batch=8, prompt=512, new=512, kv_bits=4,
+                                           temperature=0.7, top_p=0.9, cpu_prompt=32, cpu_steps=3,
+                                           profile="verify_pass_qwen3_8b_k5_bs8.md"),
 }
 DEFAULT_WORKLOAD = "qwen3-0.6b-selfdraft2-k4-bs1"
 METRIC = "accepted tokens/s (4-bit spec decode, bs1/bs8); verify-pass HBM GB/s vs 8 TB/s"
@@ -140,20 +148,29 @@ def reduce(world, vals, op="max"):
     return t.tolist()
 
 
-def cpu_sample(wl, prompts, lmx_cfg, seed, steps, warmup):
-    """Time the oracle's decode loop on the host cores (prefill untimed)."""
+def cpu_sample(wl, prompts, lmx_cfg, draft_cfg, seed, steps, warmup):
+    """Time the oracle's decode loop on the host cores (prefill untimed).
+    The oracle runs every quantized matmul in its canonical order (the
+    reference's affine identity, its fastest CPU form)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as O
     L = O.lib()
-    cfg = dict(lmx_cfg)
-    cfg["group"] = cfg.pop("group_size")
+
+    def create(c, sd):
+        cfg = dict(c)
+        cfg["group"] = cfg.pop("group_size")
+        return L.orc_model_create(C.byref(O.ModelCfg(**cfg)), sd)
+
+    L.orc_set_mma_min_m(0)
     t0 = time.time()
-    model = L.orc_model_create(C.byref(O.ModelCfg(**cfg)), seed)
+    model = create(lmx_cfg, seed)
+    dmodel = create(draft_cfg, seed + 1) if draft_cfg else None
     setup = time.time() - t0
     prm = O.SpecParams(K=wl["K"], max_tokens=wl["new"], temperature=wl["temperature"],
                        top_p=wl["top_p"], seed=seed, draft_layers=wl["draft_layers"])
-    p = np.ascontiguousarray(prompts, dtype=np.int32)
-    ss = L.orc_spec_session(model, None, O.ptr(p), p.shape[0], p.shape[1], prm, wl["kv_bits"])
+    p = np.ascontiguousarray(prompts if not wl["cpu_prompt"] else prompts[:, :wl["cpu_prompt"]],
+                             dtype=np.int32)
+    ss = L.orc_spec_session(model, dmodel, O.ptr(p), p.shape[0], p.shape[1], prm, wl["kv_bits"])
     st = np.zeros(5, np.int64)
     L.orc_spec_session_step(ss, warmup)
     L.orc_spec_session_result(ss, None, O.ptr(st))
@@ -164,8 +181,11 @@ def cpu_sample(wl, prompts, lmx_cfg, seed, steps, warmup):
     tokens = int(st[3]) - e0
     L.orc_spec_session_free(ss)
     L.orc_model_free(model)
+    if dmodel:
+        L.orc_model_free(dmodel)
+    L.orc_set_mma_min_m(16)
     return dict(value=tokens / dt if dt > 0 else 0.0, tokens=tokens, seconds=dt, spec_steps=n,
-                cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup)
+                cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup, prompt=p.shape[1])
 
 
 def run_reference(args, wl, world, rank):
@@ -173,9 +193,10 @@ def run_reference(args, wl, world, rank):
         return 0
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     arch = getattr(lmx, wl["arch"])
+    darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     prompts = np.random.RandomState(args.seed).randint(0, arch["vocab"], (wl["batch"], wl["prompt"]))
     # each timed step is one speculative step of the same decode (bounded sample)
-    r = cpu_sample(wl, prompts, arch, args.seed, args.steps, args.warmup)
+    r = cpu_sample(wl, prompts, arch, darch, args.seed, args.steps, args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -187,8 +208,8 @@ def run_reference(args, wl, world, rank):
         "cpu_baseline": {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
                          "kind": "port",
                          "sample": f"{args.steps} speculative steps ({r['tokens']} tokens) of the "
-                                   f"workload's decode after an untimed prefill, oracle/ C++ "
-                                   f"restatement, {r['cores']} threads"},
+                                   f"workload's decode after an untimed {r['prompt']}-token "
+                                   f"prefill, oracle/ C++ restatement, {r['cores']} threads"},
         "e2e": {"value": round(r["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -200,11 +221,13 @@ def run_lmx(args, wl, world, rank, local):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", local)
     arch = getattr(lmx, wl["arch"])
+    darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     target = lmx.Model(arch, args.seed)
-    draft = target.view(wl["draft_layers"]) if wl["draft_layers"] else None
+    # separate draft model (seed + 1) or the target's first layers (self-draft)
+    draft = lmx.Model(darch, args.seed + 1) if darch else None
     B, P = wl["batch"], wl["prompt"]
     prompts = np.random.RandomState(args.seed + rank).randint(0, arch["vocab"], (B, P)).astype(np.int32)
-    sd = lmx.SpecDecoder(target, None, wl["draft_layers"], B, wl["K"], wl["new"], P,
+    sd = lmx.SpecDecoder(target, draft, wl["draft_layers"], B, wl["K"], wl["new"], P,
                          kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
                          seed=args.seed)
 
@@ -227,6 +250,7 @@ def run_lmx(args, wl, world, rank, local):
         one()
     clocks = Clocks(local)
     barrier(world)
+    launches0 = lmx.lib().lmx_launch_count()
     clocks.start()
     wall, dec, toks, acc, prop, steps, replays = 0.0, 0.0, 0, 0, 0, 0, 0
     for _ in range(args.steps):
@@ -240,22 +264,19 @@ def run_lmx(args, wl, world, rank, local):
         replays += st["replays"]
     barrier(world)
     ck = clocks.stop()
+    # eager launches (prefill) counted by the library + graph replays x the
+    # kernels captured in one step
+    gpu_launches = lmx.lib().lmx_launch_count() - launches0 + replays * sd.step_launches()
     # verify-pass and lm_head rooflines (CUDA events on the decoder's stream)
     vsec, vbytes = sd.profile(0, 20)
     hsec, hbytes = sd.profile(3, 20)
-    launches_per_step = sd.step_launches()
-    # prefill runs eagerly in 32-token chunks: per chunk embed + 6 per layer +
-    # length advance; then lm_head + argmax (target) and the bookkeeping kernel
-    L, dl = arch["layers"], wl["draft_layers"]
-    ct, cd = -(-P // 32), -(-(P - 1) // 32)
-    prefill_launches = ct * (2 + 6 * L) + 2 + cd * (2 + 6 * dl) + 1
-    gpu_launches = args.steps * (replays // max(1, args.steps) * launches_per_step + prefill_launches)
+    L = arch["layers"]
     wall_m, dec_m = reduce(world, [wall, dec], "max")
     toks_all = int(reduce(world, [float(toks)], "sum")[0])
     peak, peak_kind = peaks()
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "verify_pass_qwen3_0.6b_k4_bs1.md")) as f:
+        with open(os.path.join(ROOT, "profiles", wl["profile"])) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_verify_pass:"):
                     traffic = float(line.split(":")[1])
@@ -269,29 +290,31 @@ def run_lmx(args, wl, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": args.workload, "batch": B, "K": wl["K"], "prompt": P,
                    "new_tokens": wl["new"], "kv_bits": wl["kv_bits"], "weights": "4-bit g64",
-                   "parallelism": f"replicas{world}",
-                   "l2": "weights (335 MB per verify pass) exceed L2; no flush"},
+                   "draft": wl["draft"] or f"target's first {wl['draft_layers']} layers",
+                   "temperature": wl["temperature"], "top_p": wl["top_p"],
+                   "parallelism": f"dp{world} (independent sequences per rank)",
+                   "l2": f"weights ({vbytes / 1e6:.0f} MB per verify pass) exceed L2; no flush"},
         "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * wl["new"] * 4 + 40},
-        "roofline": {"bound": "hbm", "kernel": "verify pass (28 layers + lm_head, M=5)",
+        "roofline": {"bound": "hbm", "kernel": f"verify pass ({L} layers + lm_head, M={B * (wl['K'] + 1)})",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "frac_of_8000": round(achieved / 8000.0, 4),
                      "algorithmic_bytes": vbytes, "verify_pass_us": round(vsec * 1e6, 2),
                      "traffic": traffic},
-        "lm_head_m1": {"us": round(hsec * 1e6, 2), "GBs": round(hbytes / hsec / 1e9, 1)},
+        f"lm_head_m{B}": {"us": round(hsec * 1e6, 2), "GBs": round(hbytes / hsec / 1e9, 1)},
         "acceptance": {"accepted": acc, "proposed": prop,
                        "rate": round(acc / prop, 4) if prop else None,
                        "tokens_per_step": round(toks / max(1, steps), 3)},
         "clocks": ck, "gpu_launches": int(gpu_launches),
     }
     if world == 1 and rank == 0 and not args.no_cpu:
-        r = cpu_sample(wl, prompts, arch, args.seed, args.cpu_steps, 1)
+        r = cpu_sample(wl, prompts, arch, darch, args.seed, args.cpu_steps, 1)
         res["cpu_baseline"] = {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
                                "kind": "port",
                                "sample": f"{args.cpu_steps} speculative steps ({r['tokens']} tokens) "
-                                         "of the same decode after an untimed prefill (oracle/ "
-                                         "C++ restatement)"}
+                                         f"of the same decode after an untimed {r['prompt']}-token "
+                                         "prefill (oracle/ C++ restatement, canonical order)"}
     if rank == 0:
         print(json.dumps(res), flush=True)
     sd.close()
@@ -309,13 +332,16 @@ def main():
     ap.add_argument("--impl", default="lmx", choices=["lmx", "reference"])
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--seed", type=int, default=2026)
-    ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--cpu-steps", type=int, default=None,
+                    help="speculative steps in the CPU sample (default: 6, or the workload's own)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-verify", type=int, default=0,
                     help="only prefill, decode the workload and run N verify passes inside the "
                          "NVTX range lmx_verify_pass (for ncu --nvtx-include)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
+    if args.cpu_steps is None:
+        args.cpu_steps = wl.get("cpu_steps", 6)
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":

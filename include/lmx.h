@@ -70,6 +70,12 @@ int lmx_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float
  * kernels set when they give up (0 = none). */
 int lmx_device_error(unsigned* code, int clear);
 
+/* Kernel launches this library has issued so far in the process (eager
+ * launches plus launches recorded into captured graphs; a graph replay adds
+ * nothing here: lmx_spec_step_launches gives the kernels per replayed step).
+ * No reference counterpart (measurement hook). */
+long long lmx_launch_count(void);
+
 /* argmax over the last axis, first maximum wins (mx::argmax,
  * src/common/generate.cpp:43,801).  logits [rows, V] bf16 -> out [rows] int32. */
 int lmx_argmax(const void* logits, int rows, int V, int32_t* out, void* stream);

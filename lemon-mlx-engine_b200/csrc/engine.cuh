@@ -73,7 +73,7 @@ static int launch_cluster_rows(void (*kern)(const bf16_t*, int, SpecState, int, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cuda_check(cudaLaunchKernelEx(&cfg, kern, logits, V, s, i, adv), "draft_argmax: launch");
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, kern, logits, V, s, i, adv)), "draft_argmax: launch");
 }
 
 // ---------------------------------------------------------------------------
@@ -312,7 +312,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   if (R > ws.Rmax || B != c.B || n_layers > c.n_layers || n_layers > m.n_layers)
     return set_error(LMX_ERR_INVALID, "forward: shape exceeds workspace");
   const int tiles = (G * T + kRowTile - 1) / kRowTile, splits = (c.cap + kSplit - 1) / kSplit;
-  if (tiles > ws.tiles || splits > ws.splits || B > ws.B || Hk != ws.Hk)
+  if (tiles > ws.tiles || splits > ws.splits || B > ws.B || Hk > ws.Hk)
     return set_error(LMX_ERR_INVALID, "forward: attention scratch too small");
   const bool fuse = R <= kQmmMaxNormRows && !qmm_uses_mma(R);
   int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
@@ -554,17 +554,18 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   rc = cache_create(*dm, dl, B, cap, cfg.kv_bits, &dc);
   if (rc) return rc;
   sp->dc.reset(dc);
-  // one workspace serves both models (sized by the larger of each dimension)
+  // one workspace serves both models: every dimension is the larger of the
+  // two, the attention scratch is sized for the larger group (q heads per KV
+  // head) and KV head count (its layout follows each call's own shape)
   lmx_model_config big = tm->c;
+  const int gmax = std::max(tm->c.heads / tm->c.kv_heads, dm->c.heads / dm->c.kv_heads);
   big.hidden = std::max(tm->c.hidden, dm->c.hidden);
   big.inter = std::max(tm->c.inter, dm->c.inter);
-  big.heads = std::max(tm->c.heads, dm->c.heads);
   big.kv_heads = std::max(tm->c.kv_heads, dm->c.kv_heads);
+  big.heads = gmax * big.kv_heads;
   Model shape;
   shape.c = big;
   const int Tmax = std::max(K + 1, kPrefillChunk);
-  if (tm->c.kv_heads != dm->c.kv_heads || tm->c.heads / tm->c.kv_heads != dm->c.heads / dm->c.kv_heads)
-    return set_error(LMX_ERR_UNSUPPORTED, "spec: draft and target must share the GQA layout");
   rc = workspace_create(shape, B, Tmax, cap, B * (K + 1), sp->ws);
   if (rc) return rc;
   SpecState& s = sp->s;

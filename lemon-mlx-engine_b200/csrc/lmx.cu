@@ -224,7 +224,7 @@ static int launch_qmv_t(const QmmArgs& a_in, const QmvShape& sh, cudaStream_t st
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cuda_check(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, mp, a, sh.p), "qmm: launch");
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, MT, RB>, mp, a, sh.p)), "qmm: launch");
 }
 
 template <int BITS>
@@ -398,7 +398,7 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cuda_check(cudaLaunchKernelEx(&cfg, qmm_mma_kernel<BITS>, mp, a), "qmm_mma: launch");
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmm_mma_kernel<BITS>, mp, a)), "qmm_mma: launch");
 }
 
 int launch_qmm(const QmmCall& c, cudaStream_t st) {
@@ -466,7 +466,7 @@ int launch_argmax(const bf16_t* logits, int rows, int V, int32_t* out, cudaStrea
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cuda_check(cudaLaunchKernelEx(&cfg, argmax_kernel, logits, V, out), "argmax: launch");
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, argmax_kernel, logits, V, out)), "argmax: launch");
 }
 
 }  // namespace lmx
@@ -490,6 +490,8 @@ extern "C" int lmx_device_error(unsigned* code, int clear) {
   }
   return rc;
 }
+
+extern "C" long long lmx_launch_count(void) { return g_lmx_launches.load(); }
 
 extern "C" int lmx_set_mma_min_m(int m) {
   if (m < 0) return set_error(LMX_ERR_INVALID, "mma threshold must be >= 0");

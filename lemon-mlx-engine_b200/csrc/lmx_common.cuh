@@ -6,6 +6,7 @@
 // the library is built with --fmad=false), so its results are bit-identical
 // to any implementation of that order.
 #pragma once
+#include <atomic>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -93,6 +94,14 @@ LMX_DEV float warp_sum_xor(float v, int first, int last) {
 
 }  // namespace lmx
 
+// Kernel launches issued by this library (eager launches and launches being
+// captured into a graph), for the host-side launch accounting.
+static std::atomic<long long> g_lmx_launches{0};
+static inline cudaError_t lmx_counted(cudaError_t e) {
+  if (e == cudaSuccess) g_lmx_launches.fetch_add(1, std::memory_order_relaxed);
+  return e;
+}
+
 // Launch helper: every kernel is launched with the programmatic-stream-
 // serialization attribute so it can overlap its predecessor's tail.
 template <typename Kern, typename... Args>
@@ -108,5 +117,5 @@ static inline cudaError_t lmx_launch(Kern kern, dim3 grid, dim3 block, size_t sm
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, args...);
+  return lmx_counted(cudaLaunchKernelEx(&cfg, kern, args...));
 }

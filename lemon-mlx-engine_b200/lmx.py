@@ -31,6 +31,7 @@ SIGNATURES = {
     "lmx_device_error": (I, [C.POINTER(C.c_uint), I]),
     "lmx_quantized_matmul": (I, [P, P, P, P, P, I, I, I, I, I, P]),
     "lmx_set_mma_min_m": (I, [I]),
+    "lmx_launch_count": (C.c_longlong, []),
     "lmx_mma_min_m": (I, []),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
