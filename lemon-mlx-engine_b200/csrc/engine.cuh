@@ -508,7 +508,7 @@ static int spec_step(Spec& sp) {
     if (stoch) {
       rc = forward(*sp.dm, *sp.dc, sp.dl, tok, ld, off, B, T, sp.ws, sp.s.qlog + (size_t)i * V, true, st, K * V);
       if (!rc)
-        rc = cuda_check(lmx_launch(draft_sample_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+        rc = cuda_check(samp_launch(draft_sample_kernel, B, st,
                                    (const bf16_t*)sp.s.qlog, V, sp.s, stoch_params(sp), i, T),
                         "draft_sample");
     } else {
@@ -519,7 +519,7 @@ static int spec_step(Spec& sp) {
   if (!rc) rc = forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
   if (stoch) {
     if (!rc)
-      rc = cuda_check(lmx_launch(accept_stochastic_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+      rc = cuda_check(samp_launch(accept_stochastic_kernel, B, st,
                                  (const bf16_t*)sp.ws.logits, V, sp.s, stoch_params(sp)),
                       "accept_stochastic");
   } else {
@@ -609,7 +609,7 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
   if (!rc) rc = cuda_check(cudaMemsetAsync(sp.dc->len, 0, B * 4, st), "len");
   if (!rc) rc = forward_chunked(*sp.tm, *sp.tc, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
   if (!rc && sp.cfg.temperature > 0.0f)
-    rc = cuda_check(lmx_launch(sample_rows_kernel, dim3(B), dim3(kSampThreads), 0, st, true,
+    rc = cuda_check(samp_launch(sample_rows_kernel, B, st,
                                (const bf16_t*)sp.ws.logits, sp.tm->c.vocab, sp.tm->c.vocab, stoch_params(sp),
                                0u, 0u, 3u, sp.yprefill),
                     "prefill sample");
@@ -1033,7 +1033,7 @@ extern "C" int lmx_sample(const void* logits, int rows, int V, float temperature
   if (!logits || !out || rows < 0 || V < 1) return set_error(LMX_ERR_INVALID, "sample: bad arguments");
   if (!(temperature > 0.0f)) return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
   if (!u24) return set_error(LMX_ERR_INVALID, "sample: uniforms required when temperature > 0");
-  return cuda_check(lmx_launch(sample_u_kernel, dim3(rows), dim3(kSampThreads), 0, (cudaStream_t)stream, true,
+  return cuda_check(samp_launch(sample_u_kernel, rows, (cudaStream_t)stream,
                                (const bf16_t*)logits, V, temperature, top_p, u24, out),
                     "sample");
 }
@@ -1047,7 +1047,7 @@ extern "C" int lmx_spec_accept(const void* target_logits, const void* draft_logi
   if (!(temperature > 0.0f))
     return set_error(LMX_ERR_INVALID, "spec_accept: greedy acceptance runs inside lmx_spec_decode");
   if (!draft_logits || !u_accept || !u_final) return set_error(LMX_ERR_INVALID, "spec_accept: null argument");
-  return cuda_check(lmx_launch(accept_u_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, true,
+  return cuda_check(samp_launch(accept_u_kernel, B, (cudaStream_t)stream,
                                (const bf16_t*)target_logits, (const bf16_t*)draft_logits, drafts, K, V, temperature,
                                top_p, u_accept, u_final, n_accepted, out_tokens),
                     "spec_accept");
