@@ -163,7 +163,7 @@ static int fill_ones(Arena& ar, bf16_t** p, int n, cudaStream_t st) {
 static int model_create(const lmx_model_config& c, uint64_t seed, Model** out) {
   if (c.group_size != 64 || (c.bits != 4 && c.bits != 8) || c.head_dim != kHeadDim ||
       c.hidden % 512 || c.heads % c.kv_heads || c.layers < 1 || c.vocab < 1)
-    return set_error(LMX_ERR_UNSUPPORTED, "model config not supported (head_dim 128, group 64, 4/8-bit)");
+    return set_error(LMX_ERR_UNSUPPORTED, "model config not supported (head_dim 128, hidden %% 512 == 0, group 64, 4/8-bit)");
   auto m = std::make_unique<Model>();
   m->c = c;
   m->n_layers = c.layers;

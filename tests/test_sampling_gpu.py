@@ -113,3 +113,38 @@ def test_stochastic_spec_stream_matches_oracle(lmx, cuda, mma_threshold, kv_bits
     O.lib().orc_model_free(o)
     np.testing.assert_array_equal(got, ref)
     assert stats["accepted"] == st[2]
+
+
+def test_separate_draft_other_gqa_stream_matches_oracle(lmx, cuda, mma_threshold):
+    # config 3's structure at test size: a separate draft model whose width,
+    # head count and KV-head count differ from the target's (one workspace
+    # serves both), batch 8, K = 5, 4-bit KV, T 0.7, top-p 0.9; exact mode
+    mma_threshold(0)
+    draft_cfg = dict(TINY, hidden=512, layers=2, inter=512, heads=8, kv_heads=1)
+    B, P, K, MT, T, tp, seed = 8, 20, 5, 30, 0.7, 0.9, 5
+    g = lmx.Model(TINY, 111)
+    gd = lmx.Model(draft_cfg, 222)
+
+    def ocfg(c):
+        d = dict(c)
+        d["group"] = d.pop("group_size")
+        return O.ModelCfg(**d)
+
+    o = O.lib().orc_model_create(C.byref(ocfg(TINY)), 111)
+    od = O.lib().orc_model_create(C.byref(ocfg(draft_cfg)), 222)
+    prompts = np.random.RandomState(13).randint(0, TINY["vocab"], (B, P)).astype(np.int32)
+    sd = lmx.SpecDecoder(g, gd, draft_cfg["layers"], B, K, MT, P, kv_bits=4, temperature=T, top_p=tp, seed=seed)
+    sd.prefill(prompts)
+    sd.decode(use_graph=True)
+    got, stats = sd.result()
+    sd.close()
+    g.close()
+    gd.close()
+    ref = np.zeros((B, MT), np.int32)
+    st = np.zeros(5, np.int64)
+    prm = O.SpecParams(K=K, max_tokens=MT, temperature=T, top_p=tp, seed=seed, draft_layers=draft_cfg["layers"])
+    assert O.lib().orc_spec_generate(o, od, O.ptr(prompts), B, P, prm, 4, O.ptr(ref), O.ptr(st)) == 0
+    O.lib().orc_model_free(o)
+    O.lib().orc_model_free(od)
+    np.testing.assert_array_equal(got, ref)
+    assert stats["accepted"] == st[2]
