@@ -1,24 +1,31 @@
 #!/usr/bin/env python3
 """bench.py -- accepted tokens/s of 4-bit speculative decoding on B200.
 
-Workload (the configuration the headline metric is
-quoted on for bs1): Qwen3-0.6B architecture (28 layers, hidden 1024, 16 q /
-8 kv heads, head_dim 128, SwiGLU 3072, vocab 151936), synthetic N(0,0.02)
-weights quantized affine 4-bit group 64; draft = the target's first 2 layers
-plus the shared embedding / lm_head; K = 4 draft tokens; batch 1; 128-token
-uniform-random prompt; 256 greedy new tokens; bf16 KV cache.
+Workloads (--workload):
+  qwen3-8b-draft0.6b-k5-bs8-t0.7 (default, configs[2]): Qwen3-8B architecture
+    target (36 layers, hidden 4096, 32 q / 8 kv heads, FFN 12288, vocab 151936)
+    with a separate Qwen3-0.6B draft (28 layers), both synthetic N(0,0.02)
+    weights quantized affine 4-bit group 64 (seeds 2026 / 2027); K = 5;
+    8 sequences of 512 uniform-random prompt tokens; 512 new tokens each;
+    temperature 0.7, top-p 0.9 rejection sampling; 4-bit group-64 KV cache.
+    The verify pass (M = 48) runs the tcgen05 path.
+  qwen3-0.6b-selfdraft2-k4-bs1: Qwen3-0.6B target, draft = its
+    first 2 layers + shared embedding / lm_head; K = 4; batch 1; 128-token
+    prompt; 256 greedy new tokens; bf16 KV cache.
+  --qmm-sweep: the op-level quantized_matmul sweep.
 
-A "step" is one generation of that workload through the public API
-(lmx_spec_prefill with the prompt in host memory, lmx_spec_decode,
+A "step" is one generation of the workload through the public API
+(lmx_spec_prefill with the prompts in host memory, lmx_spec_decode,
 lmx_spec_result reading the tokens back).  value = tokens / decode time
 (device events, prefill excluded, the reference's GenerateCompletionInfo
 definition); e2e = tokens / wall time of the whole API sequence including the
 host<->device copies and the prefill.  One process per GPU; for N > 1 each
-rank decodes its own replica (bs1 does not shard: "replicas only").
+rank decodes its own sequences (independent batches, no data-path
+collective: weak scaling; bs1 is "replicas only").
 
 --impl reference times the CPU restatement of the reference's algorithm
 (oracle/, the reference's MLX CPU backend cannot be built here) on the host
-cores with the same weights, prompt and decode loop.
+cores with the same weights, prompts and decode loop.
 """
 import argparse
 import ctypes as C
@@ -53,10 +60,10 @@ WORKLOADS = {
                                          profile="verify_pass_qwen3_0.6b_k4_bs1.md"),
     "qwen3-8b-draft0.6b-k5-bs8-t0.7": dict(arch="QWEN3_8B", draft="QWEN3_0_6B", draft_layers=28,
                                            K=5, batch=8, prompt=512, new=512, kv_bits=4,
-                                           temperature=0.7, top_p=0.9, cpu_prompt=32, cpu_steps=3,
+                                           temperature=0.7, top_p=0.9, cpu_prompt=32, cpu_steps=3, steps=5,
                                            profile="verify_pass_qwen3_8b_k5_bs8.md"),
 }
-DEFAULT_WORKLOAD = "qwen3-0.6b-selfdraft2-k4-bs1"
+DEFAULT_WORKLOAD = "qwen3-8b-draft0.6b-k5-bs8-t0.7"
 METRIC = "accepted tokens/s (4-bit spec decode, bs1/bs8); verify-pass HBM GB/s vs 8 TB/s"
 
 
@@ -232,8 +239,8 @@ def run_lmx(args, wl, world, rank, local):
                          seed=args.seed)
 
     if args.profile_verify:
+        # prefill only (KV cache at the prompt length), then N verify passes
         sd.prefill(prompts)
-        sd.decode(use_graph=True)
         sd.profile(0, args.profile_verify)
         sd.close()
         target.close()
@@ -324,10 +331,80 @@ def run_lmx(args, wl, world, rank, local):
     return 0
 
 
+QMM_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+QMM_MS = [1, 2, 5, 8, 16, 32]
+
+
+def qmm_time(lmx, N, K, M, bits, seed=2026):
+    """Device time of one quantized matmul launch (BASELINE configs[1] data:
+    uniform random codes, scales |N(0,0.02)|/7.5, biases -8 scale): R launches
+    over R weight copies (together > 2x L2) captured in one CUDA graph."""
+    import torch
+    torch.cuda.init()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    KW = K * bits // 32
+    wbytes = N * K * bits // 8
+    R = max(2, min(64, (320 << 20) // wbytes))
+    ws = [torch.randint(-2**31, 2**31 - 1, (N, KW), dtype=torch.int32, device="cuda", generator=gen)
+          for _ in range(R)]
+    sc = (torch.randn(N, K // 64, device="cuda", generator=gen).abs() * (0.02 / 7.5)).to(torch.bfloat16)
+    bi = (-8 * sc.float()).to(torch.bfloat16)
+    x = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    st = torch.cuda.Stream()
+    S = C.c_void_p(st.cuda_stream)
+
+    def run():
+        for w in ws:
+            lmx.call("lmx_quantized_matmul", x.data_ptr(), w.data_ptr(), sc.data_ptr(), bi.data_ptr(),
+                     y.data_ptr(), M, N, K, 64, bits, S)
+
+    with torch.cuda.stream(st):
+        run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        run()
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3 / R)
+    t = statistics.median(ts)
+    del g
+    byts = wbytes + N * (K // 64) * 4 + M * K * 2 + M * N * 2
+    return dict(N=N, K=K, M=M, bits=bits, us=round(t * 1e6, 2), GBs=round(byts / t / 1e9, 1),
+                path="tcgen05" if M >= lmx.lib().lmx_mma_min_m() > 0 else "gemv")
+
+
+def run_qmm(args):
+    lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+    lmx.call("lmx_set_device", 0)
+    peak, kind = peaks()
+    if args.qmm:
+        N, K, M, bits = [int(v) for v in args.qmm.split(",")]
+        rows = [qmm_time(lmx, N, K, M, bits)]
+    else:
+        rows = [qmm_time(lmx, N, K, M, bits) for bits in (4, 8) for N, K in QMM_SHAPES for M in QMM_MS]
+    best = max(r["GBs"] for r in rows)
+    print(json.dumps({"metric": "quantized_matmul GB/s (BASELINE configs[1] sweep)", "value": best,
+                      "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
+                      "peak": peak, "peak_source": kind, "l2": "weight copies > 2x L2 per graph",
+                      "sweep": rows}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed generations (default: the workload's, about a minute of decode)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="lmx", choices=["lmx", "reference"])
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
@@ -336,10 +413,17 @@ def main():
                     help="speculative steps in the CPU sample (default: 6, or the workload's own)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-verify", type=int, default=0,
-                    help="only prefill, decode the workload and run N verify passes inside the "
-                         "NVTX range lmx_verify_pass (for ncu --nvtx-include)")
+                    help="only prefill the workload and run N verify passes inside the NVTX "
+                         "range lmx_verify_pass (for ncu --nvtx-include)")
+    ap.add_argument("--qmm-sweep", action="store_true",
+                    help="op-level quantized_matmul sweep (BASELINE configs[1]) instead of decoding")
+    ap.add_argument("--qmm", default="", help="one op-level shape N,K,M,bits (e.g. for ncu)")
     args = ap.parse_args()
+    if args.qmm_sweep or args.qmm:
+        return run_qmm(args)
     wl = WORKLOADS[args.workload]
+    if args.steps is None:
+        args.steps = wl.get("steps", 10)
     if args.cpu_steps is None:
         args.cpu_steps = wl.get("cpu_steps", 6)
     world, rank, local = dist_setup()

@@ -54,6 +54,7 @@ static int launch_sdpa(const SdpaArgs& a, int B, cudaStream_t st) {
   if (half <= 5) return launch_sdpa_t<5>(a, B, st);
   if (half <= 6) return launch_sdpa_t<6>(a, B, st);
   if (half <= 8) return launch_sdpa_t<8>(a, B, st);
+  if (half <= 12) return launch_sdpa_t<12>(a, B, st);
   return launch_sdpa_t<16>(a, B, st);
 }
 
