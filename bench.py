@@ -133,7 +133,8 @@ def dist_setup():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
     return world, rank, local
 
 
@@ -238,10 +239,15 @@ def run_lmx(args, wl, world, rank, local):
                          kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
                          seed=args.seed)
 
-    if args.profile_verify:
+    if args.profile_verify or args.profile_draft:
         # prefill only (KV cache at the prompt length), then N verify passes
+        # (NVTX range lmx_verify_pass) or N single-token draft forwards
+        # (lmx_draft_token)
         sd.prefill(prompts)
-        sd.profile(0, args.profile_verify)
+        if args.profile_verify:
+            sd.profile(0, args.profile_verify)
+        else:
+            sd.profile(1, args.profile_draft)
         sd.close()
         target.close()
         return 0
@@ -415,6 +421,9 @@ def main():
     ap.add_argument("--profile-verify", type=int, default=0,
                     help="only prefill the workload and run N verify passes inside the NVTX "
                          "range lmx_verify_pass (for ncu --nvtx-include)")
+    ap.add_argument("--profile-draft", type=int, default=0,
+                    help="only prefill the workload and run N single-token draft forwards inside the "
+                         "NVTX range lmx_draft_token (for ncu --nvtx-include)")
     ap.add_argument("--qmm-sweep", action="store_true",
                     help="op-level quantized_matmul sweep (BASELINE configs[1]) instead of decoding")
     ap.add_argument("--qmm", default="", help="one op-level shape N,K,M,bits (e.g. for ncu)")

@@ -62,10 +62,13 @@ def oracle_attention(q, kd, vd, lens, T, Hq, Hk, cap, scale):
 
 
 @pytest.mark.parametrize("bits", [16, 8, 4])
-@pytest.mark.parametrize("T,Hq,Hk", [(1, 16, 8), (5, 16, 8), (6, 32, 8), (40, 4, 2)])
-def test_sdpa_decode_bit_exact(lmx, cuda, bits, T, Hq, Hk):
+@pytest.mark.parametrize("T,Hq,Hk,cap", [(1, 16, 8, 420), (5, 16, 8, 420), (6, 32, 8, 420), (40, 4, 2, 420),
+                                         (1, 16, 8, 3300), (6, 32, 8, 3300)])
+def test_sdpa_decode_bit_exact(lmx, cuda, bits, T, Hq, Hk, cap):
+    # cap 420: 4 splits of 128 keys; cap 3300: 26 splits (long cache, the
+    # combine over many partials)
     rng = np.random.RandomState(bits * 100 + T)
-    B, cap = 3, 420
+    B = 3
     lens = np.array([0, 123, cap - T - 1][:B], np.int32)
     host, kd, vd = make_cache(rng, B, Hk, cap, bits)
     dev = {k: to_dev(cuda, v) for k, v in host.items()}
