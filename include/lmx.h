@@ -163,6 +163,8 @@ typedef struct {
   int tied;        /* lm_head shares the packed embedding                 */
   int bits;        /* 4 or 8                                              */
   int group_size;  /* 64                                                  */
+  /* Llama-3 RoPE frequency scaling (rope_type "llama3"); factor <= 1: none */
+  float rope_factor, rope_low_freq, rope_high_freq, rope_orig_max_pos;
 } lmx_model_config;
 
 int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model);
@@ -172,8 +174,34 @@ int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model);
 int lmx_model_view(void* model, int n_layers, void** view);
 int lmx_model_free(void* model);
 /* Copy one packed weight to host memory (kind: 0 q,1 k,2 v,3 o,4 gate,5 up,
- * 6 down,7 embed,8 lm_head). */
+ * 6 down,7 embed,8 lm_head).  For a tensor-parallel shard: the shard. */
 int lmx_model_weight(void* model, int layer, int kind, void* w_host, void* s_host, void* b_host);
+
+/* ---------------------------------------------------------------------------
+ * Tensor parallelism across the GPUs of one node (one process per GPU).  The
+ * reference runs on one device and has no counterpart; this is the
+ * multi-GPU form of the same model calls.  Megatron split: q/k/v by heads,
+ * gate/up by FFN rows, o_proj / down_proj by the matching input columns, the
+ * lm_head by vocabulary rows; one all-reduce after o_proj and one after
+ * down_proj (fused with the residual add and the next RMSNorm), a
+ * (value, index) exchange for the vocab-parallel argmax -- all over NVLink
+ * peer memory, summed in rank order, so every rank and every run computes
+ * the same bits.  Setup: every rank creates its communicator, exports its
+ * handle (LMX_TP_HANDLE_BYTES), gathers all handles in rank order (any host
+ * transport, e.g. torch.distributed.all_gather_object), opens them, and
+ * meets the others at a host barrier before its first forward.
+ * lmx_model_create_tp then builds this rank's shard of the same seeded
+ * weights (comm NULL or size 1: the whole model).  Every rank must issue the
+ * same forwards in the same order; a peer that stops arriving makes the
+ * waiting kernels give up after 2 s and report LMX_ERR_CUDA ("kernel
+ * reported error 0x71").
+ * ------------------------------------------------------------------------- */
+#define LMX_TP_HANDLE_BYTES 64
+int lmx_tp_comm_create(int rank, int size, int max_rows, int max_hidden, void** comm);
+int lmx_tp_comm_handle(void* comm, void* handle_out);
+int lmx_tp_comm_open(void* comm, const void* handles);  /* size x LMX_TP_HANDLE_BYTES */
+int lmx_tp_comm_free(void* comm);  /* after every model that uses it */
+int lmx_model_create_tp(const lmx_model_config* cfg, uint64_t seed, void* comm, void** model);
 
 /* ---------------------------------------------------------------------------
  * KV cache: KVCacheSimple / QuantizedKVCache (src/common/kv_cache.cpp:34-142,
@@ -187,6 +215,11 @@ int lmx_cache_free(void* cache);
  * back to `pos` rows (no-op if pos >= its length). */
 int lmx_cache_set_position(void* cache, int seq, int pos);
 int lmx_cache_len(void* cache, int seq, int* len);
+/* Synthetic context: rows [0, rows) of every layer's K and V hold seeded
+ * N(0,1) values (Philox normal, tensor id tid_base + 2*layer + (0 K, 1 V),
+ * element ((b*kv_heads + head)*rows + row)*128 + d over the whole model's KV
+ * heads), quantized like an append; every length becomes `rows`. */
+int lmx_cache_fill_synthetic(void* cache, int rows, uint64_t seed, uint32_t tid_base);
 /* ModelContext::call_fn for a [B, T] token block (host ints): runs the first
  * n_layers, appends K/V at each sequence's length, writes logits [B, T, V]
  * bf16 to logits_host (may be NULL) and advances the lengths. */
@@ -211,6 +244,11 @@ typedef struct {
   float temperature;/* 0 = greedy (ArgMaxSampler)                        */
   float top_p;
   uint64_t seed;    /* uniform draws of the stochastic path              */
+  /* Synthetic context: context_len cache rows per sequence, before the
+   * prompt, filled with seeded N(0,1) K/V (a stand-in for prefilling a long
+   * random-token prefix; lmx_cache_fill_synthetic).  0: none.            */
+  int context_len;
+  uint64_t context_seed;
 } lmx_spec_config;
 
 /* draft may be NULL (self-draft: the first draft_layers of target). */

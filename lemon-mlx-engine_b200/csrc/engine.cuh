@@ -106,6 +106,123 @@ struct Arena {
 };
 
 // ---------------------------------------------------------------------------
+// tensor-parallel communicator: this rank's IPC-exported block (two partial
+// slots, the argmax pairs, the arrival flags) and the peers' blocks opened
+// through their handles.  Layout and protocol: tp.cuh.
+// ---------------------------------------------------------------------------
+struct TpComm {
+  int n = 1, rank = 0, max_rows = 0, max_hidden = 0;
+  void* block = nullptr;  // local, from cudaMalloc (exportable)
+  uint32_t* epoch = nullptr;
+  void* peer[kTpMaxRanks] = {};
+  bool opened = false;
+  TpPeers t;
+  ~TpComm() {
+    for (int p = 0; p < kTpMaxRanks; ++p)
+      if (peer[p]) cudaIpcCloseMemHandle(peer[p]);
+    if (block) cudaFree(block);
+    if (epoch) cudaFree(epoch);
+  }
+};
+
+static int tp_comm_create(int rank, int n, int max_rows, int max_hidden, TpComm** out) {
+  if (n < 1 || n > kTpMaxRanks || rank < 0 || rank >= n || max_rows < 1 || max_hidden < 8 || max_hidden % 8)
+    return set_error(LMX_ERR_INVALID, "tp_comm: bad arguments (size <= %d, hidden %% 8 == 0)", kTpMaxRanks);
+  auto c = std::make_unique<TpComm>();
+  c->n = n;
+  c->rank = rank;
+  c->max_rows = max_rows;
+  c->max_hidden = max_hidden;
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  c->t.n = n;
+  c->t.rank = rank;
+  c->t.slot_bytes = up((size_t)max_rows * max_hidden * sizeof(bf16_t));
+  c->t.pairs_off = 2 * c->t.slot_bytes;
+  c->t.flags_off = c->t.pairs_off + up((size_t)max_rows * 8);
+  const size_t bytes = c->t.flags_off + up((size_t)kTpSlots * kTpMaxRanks * 4);
+  int rc = cuda_check(cudaMalloc(&c->block, bytes), "tp_comm: block");
+  if (!rc) rc = cuda_check(cudaMemset(c->block, 0, bytes), "tp_comm: zero");
+  if (!rc) rc = cuda_check(cudaMalloc(&c->epoch, (size_t)kTpSlots * 4), "tp_comm: epoch");
+  if (!rc) rc = cuda_check(cudaMemset(c->epoch, 0, (size_t)kTpSlots * 4), "tp_comm: zero");
+  if (!rc) rc = cuda_check(cudaDeviceSynchronize(), "tp_comm: init");
+  if (rc) return rc;
+  c->t.base[rank] = (uint8_t*)c->block;
+  c->t.epoch = c->epoch;
+  c->opened = n == 1;
+  *out = c.release();
+  return LMX_OK;
+}
+
+// handles: n cudaIpcMemHandle_t blobs in rank order (this rank's is skipped).
+static int tp_comm_open(TpComm& c, const void* handles) {
+  if (c.opened) return set_error(LMX_ERR_INVALID, "tp_comm: already open");
+  for (int p = 0; p < c.n; ++p) {
+    if (p == c.rank) continue;
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, (const uint8_t*)handles + (size_t)p * sizeof(cudaIpcMemHandle_t), sizeof(hd));
+    int rc = cuda_check(cudaIpcOpenMemHandle(&c.peer[p], hd, cudaIpcMemLazyEnablePeerAccess),
+                        "tp_comm: open peer handle");
+    if (rc) return rc;
+    c.t.base[p] = (uint8_t*)c.peer[p];
+  }
+  c.opened = true;
+  return LMX_OK;
+}
+
+static bf16_t* tp_slot(const TpComm& c, int sel) {
+  return (bf16_t*)((uint8_t*)c.block + (size_t)sel * c.t.slot_bytes);
+}
+
+static int launch_tp_allreduce_norm(const TpComm& c, int sel, int R, int H, bf16_t* h, const bf16_t* w, float eps,
+                                    bf16_t* xn, cudaStream_t st) {
+  if (R > c.max_rows || H > c.max_hidden) return set_error(LMX_ERR_INVALID, "tp all-reduce: %dx%d exceeds comm", R, H);
+  static bool attr_set[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  const size_t smem = (size_t)H * sizeof(bf16_t);
+  if (!attr_set[d & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(tp_allreduce_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             64 * 1024),
+                        "tp all-reduce: smem");
+    if (rc) return rc;
+    attr_set[d & 63] = true;
+  }
+  if (smem > 64 * 1024) return set_error(LMX_ERR_UNSUPPORTED, "tp all-reduce: hidden %d too large", H);
+  const int grid = R < kTpArCtas ? R : kTpArCtas;
+  return cuda_check(lmx_launch(tp_allreduce_norm_kernel, dim3(grid), dim3(256), smem, st, true, c.t, sel, R, H, h, w,
+                               eps, xn, device_error_word()),
+                    "tp all-reduce: launch");
+}
+
+// Vocab-parallel argmax: rows of this rank's logits slice [rows][ld] (V local
+// columns starting at global index base) -> out[rows] global argmax.
+static int launch_tp_argmax(const TpComm& c, const bf16_t* logits, int rows, int V, int ld, int base, int32_t* out,
+                            cudaStream_t st) {
+  if (rows > c.max_rows || rows > 1024) return set_error(LMX_ERR_INVALID, "tp argmax: %d rows", rows);
+  uint2* pairs = (uint2*)((uint8_t*)c.block + c.t.pairs_off);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows * kArgmaxCluster);
+  cfg.blockDim = dim3(512);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kArgmaxCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  int rc = cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, tp_argmax_local_kernel, logits, V, ld, base, pairs)),
+                      "tp argmax: launch");
+  if (rc) return rc;
+  const int threads = rows < 32 ? 32 : (rows + 31) / 32 * 32;
+  return cuda_check(lmx_launch(tp_argmax_exchange_kernel, dim3(1), dim3(threads), 0, st, true, c.t, rows, out,
+                               device_error_word()),
+                    "tp argmax exchange: launch");
+}
+
+// ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
 struct QWeight {
@@ -137,11 +254,19 @@ struct Model {
   float *cos_t = nullptr, *sin_t = nullptr;
   int max_pos = 16384;
   std::shared_ptr<Arena> arena;  // shared by views
-  const QWeight& head() const { return c.tied ? embed : lm_head; }
+  // tensor parallelism: this rank's share of the heads, FFN columns and
+  // vocabulary rows (the whole model when tp == 1); comm is not owned
+  int tp = 1, tp_rank = 0;
+  TpComm* comm = nullptr;
+  int hq = 0, hk = 0, il = 0, vl = 0;
+  QWeight head_tp;  // vocab rows [tp_rank*vl, +vl) of the lm_head (tp > 1)
+  const QWeight& head() const { return tp > 1 ? head_tp : (c.tied ? embed : lm_head); }
 };
 
+// Rows [row0, row0+N) x columns [col0, col0+K) of tensor tid, a [*, Kfull]
+// matrix (Kfull 0: the block is the whole width K).
 static int gen_qweight(Arena& ar, QWeight& q, uint64_t seed, uint32_t tid, int N, int K, int bits,
-                       cudaStream_t st) {
+                       cudaStream_t st, int64_t row0 = 0, int64_t col0 = 0, int64_t Kfull = 0) {
   q.N = N;
   q.K = K;
   int rc = ar.alloc(&q.w, (size_t)N * K * bits / 32, false);
@@ -150,7 +275,8 @@ static int gen_qweight(Arena& ar, QWeight& q, uint64_t seed, uint32_t tid, int N
   if (rc) return rc;
   const float C = (float)((double)0.02f * std::sqrt(3.0) / 4194304.0);
   const int64_t groups = (int64_t)N * (K / 64);
-  gen_qweight_kernel<<<(unsigned)((groups + 127) / 128), 128, 0, st>>>(seed, tid, N, K, bits, C, q.w, q.s, q.b);
+  gen_qweight_kernel<<<(unsigned)((groups + 127) / 128), 128, 0, st>>>(seed, tid, N, K, bits, C, row0, col0,
+                                                                        Kfull ? Kfull : K, q.w, q.s, q.b);
   return cuda_check(cudaGetLastError(), "gen_qweight");
 }
 
@@ -161,22 +287,50 @@ static int fill_ones(Arena& ar, bf16_t** p, int n, cudaStream_t st) {
   return cuda_check(cudaGetLastError(), "fill");
 }
 
-static int model_create(const lmx_model_config& c, uint64_t seed, Model** out) {
+// comm == nullptr (or a size-1 comm): the whole model.  Otherwise this
+// rank's tensor-parallel shard (Megatron split, tp.cuh): q/k/v by heads,
+// gate/up by FFN rows, o/down by the matching input columns, the lm_head by
+// vocabulary rows (a view into the packed embedding when tied); embedding
+// table and norms are replicated.  Every shard holds exactly the values of
+// its block of the unsharded weights.
+static int model_create(const lmx_model_config& c, uint64_t seed, TpComm* comm, Model** out) {
   if (c.group_size != 64 || (c.bits != 4 && c.bits != 8) || c.head_dim != kHeadDim ||
       c.hidden % 512 || c.heads % c.kv_heads || c.layers < 1 || c.vocab < 1)
     return set_error(LMX_ERR_UNSUPPORTED, "model config not supported (head_dim 128, hidden %% 512 == 0, group 64, 4/8-bit)");
+  const int tp = comm ? comm->n : 1, r = comm ? comm->rank : 0;
+  if (tp > 1) {
+    if (!comm->opened) return set_error(LMX_ERR_INVALID, "model_create: tp comm not opened");
+    if (c.heads % tp || c.kv_heads % tp || c.inter % (64 * tp) || c.vocab % tp || c.hidden > comm->max_hidden)
+      return set_error(LMX_ERR_UNSUPPORTED,
+                       "model_create: tp=%d needs heads, kv_heads, vocab %% tp == 0, inter %% (64 tp) == 0, "
+                       "hidden <= comm max_hidden", tp);
+  }
   auto m = std::make_unique<Model>();
   m->c = c;
   m->n_layers = c.layers;
+  m->tp = tp;
+  m->tp_rank = r;
+  m->comm = tp > 1 ? comm : nullptr;
+  m->hq = c.heads / tp;
+  m->hk = c.kv_heads / tp;
+  m->il = c.inter / tp;
+  m->vl = c.vocab / tp;
   m->arena = std::make_shared<Arena>();
   Arena& ar = *m->arena;
   const int H = c.hidden, D = c.head_dim, I = c.inter, NQ = c.heads * D, NK = c.kv_heads * D;
+  const int nq = m->hq * D, nk = m->hk * D, il = m->il;
   cudaStream_t st = 0;
   m->L.resize(c.layers);
   for (int l = 0; l < c.layers; ++l) {
-    const int shp[7][2] = {{NQ, H}, {NK, H}, {NK, H}, {H, NQ}, {I, H}, {I, H}, {H, I}};
+    // {rows, cols, row0, col0, full width}
+    const int64_t shp[7][5] = {{nq, H, (int64_t)r * nq, 0, H},  {nk, H, (int64_t)r * nk, 0, H},
+                               {nk, H, (int64_t)r * nk, 0, H},  {H, nq, 0, (int64_t)r * nq, NQ},
+                               {il, H, (int64_t)r * il, 0, H},  {il, H, (int64_t)r * il, 0, H},
+                               {H, il, 0, (int64_t)r * il, I}};
+    (void)NK;
     for (int k = 0; k < 7; ++k) {
-      int rc = gen_qweight(ar, m->L[l].w[k], seed, (uint32_t)((l + 1) * 16 + k), shp[k][0], shp[k][1], c.bits, st);
+      int rc = gen_qweight(ar, m->L[l].w[k], seed, (uint32_t)((l + 1) * 16 + k), (int)shp[k][0], (int)shp[k][1],
+                           c.bits, st, shp[k][2], shp[k][3], shp[k][4]);
       if (rc) return rc;
     }
     int rc = fill_ones(ar, &m->L[l].in_norm, H, st);
@@ -186,14 +340,43 @@ static int model_create(const lmx_model_config& c, uint64_t seed, Model** out) {
     if (rc) return rc;
   }
   int rc = gen_qweight(ar, m->embed, seed, 1, c.vocab, H, c.bits, st);
-  if (!rc && !c.tied) rc = gen_qweight(ar, m->lm_head, seed, 2, c.vocab, H, c.bits, st);
+  if (!rc && !c.tied) {
+    if (tp == 1) rc = gen_qweight(ar, m->lm_head, seed, 2, c.vocab, H, c.bits, st);
+    else rc = gen_qweight(ar, m->head_tp, seed, 2, m->vl, H, c.bits, st, (int64_t)r * m->vl, 0, H);
+  } else if (!rc && tp > 1) {  // vocab rows of the tied table
+    QWeight& v = m->head_tp;
+    v.N = m->vl;
+    v.K = H;
+    v.w = m->embed.w + (size_t)r * m->vl * (H * c.bits / 32);
+    v.s = m->embed.s + (size_t)r * m->vl * (H / 64);
+    v.b = m->embed.b + (size_t)r * m->vl * (H / 64);
+  }
   if (!rc) rc = fill_ones(ar, &m->final_norm, H, st);
   if (rc) return rc;
-  // RoPE table: inv_freq_i = base^(-2i/D), theta = pos*inv_freq (double), fp32 cos/sin
+  // RoPE table: period_i = base^(2i/D) (with the Llama-3 frequency scaling of
+  // LlamaDynamicNTKScalingRoPE::compute_freqs, src/llm/models/llama.cpp:122-183,
+  // when rope_factor > 1), theta = pos / period (double), fp32 cos/sin
+  std::vector<double> period(D / 2);
+  for (int i = 0; i < D / 2; ++i) {
+    double pd = std::pow((double)c.rope_theta, 2.0 * (double)i / (double)D);
+    if (c.rope_factor > 1.0f) {
+      const double wl = 2.0 * M_PI * pd;
+      const double low_wl = (double)c.rope_orig_max_pos / (double)c.rope_low_freq;
+      const double high_wl = (double)c.rope_orig_max_pos / (double)c.rope_high_freq;
+      if (wl > low_wl) {
+        pd = pd * (double)c.rope_factor;
+      } else if (wl > high_wl) {
+        const double s = ((double)c.rope_orig_max_pos / wl - (double)c.rope_low_freq) /
+                         ((double)c.rope_high_freq - (double)c.rope_low_freq);
+        pd = pd / ((1.0 - s) / (double)c.rope_factor + s);
+      }
+    }
+    period[i] = pd;
+  }
   std::vector<float> ct((size_t)m->max_pos * D / 2), stt(ct.size());
   for (int p = 0; p < m->max_pos; ++p)
     for (int i = 0; i < D / 2; ++i) {
-      const double th = (double)p * std::pow((double)c.rope_theta, -2.0 * (double)i / (double)D);
+      const double th = (double)p / period[i];
       ct[(size_t)p * D / 2 + i] = (float)std::cos(th);
       stt[(size_t)p * D / 2 + i] = (float)std::sin(th);
     }
@@ -214,10 +397,30 @@ static int model_create(const lmx_model_config& c, uint64_t seed, Model** out) {
 // ---------------------------------------------------------------------------
 struct Cache {
   int n_layers = 0, B = 0, cap = 0, bits = 16, Hk = 0;
+  int hk0 = 0, Hk_total = 0;  // first KV head of this shard, KV heads of the whole model
   std::vector<KvDesc> kv;
   int* len = nullptr;
   Arena ar;
 };
+
+// Synthetic context (fill_kv_kernel): rows [0, n) of every layer's K and V,
+// tensor ids tid_base + 2*layer + (0 K, 1 V), N(0,1); every length set to n.
+static int cache_fill_synthetic(Cache& c, int n, uint64_t seed, uint32_t tid_base, cudaStream_t st) {
+  if (n < 0 || n > c.cap) return set_error(LMX_ERR_INVALID, "fill_synthetic: %d rows > capacity %d", n, c.cap);
+  const float C = (float)(std::sqrt(3.0) / 4194304.0);
+  const int64_t threads = (int64_t)c.B * c.Hk * n * (kHeadDim / 64);
+  for (int l = 0; l < c.n_layers && threads > 0; ++l)
+    for (int v = 0; v < 2; ++v) {
+      fill_kv_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(seed, tid_base + 2u * l + v, c.kv[l], v, n,
+                                                                       c.hk0, c.Hk_total, C);
+      int rc = cuda_check(cudaGetLastError(), "fill_kv");
+      if (rc) return rc;
+    }
+  std::vector<int> lens(c.B, n);
+  int rc = cuda_check(cudaMemcpyAsync(c.len, lens.data(), (size_t)c.B * 4, cudaMemcpyHostToDevice, st), "len");
+  if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "fill_synthetic");
+  return rc;
+}
 
 static int cache_create(const Model& m, int n_layers, int B, int cap, int bits, Cache** out) {
   if (bits != 16 && bits != 4 && bits != 8) return set_error(LMX_ERR_UNSUPPORTED, "kv_bits %d", bits);
@@ -228,7 +431,9 @@ static int cache_create(const Model& m, int n_layers, int B, int cap, int bits, 
   c->B = B;
   c->cap = cap;
   c->bits = bits;
-  c->Hk = m.c.kv_heads;
+  c->Hk = m.hk;
+  c->hk0 = m.tp_rank * m.hk;
+  c->Hk_total = m.c.kv_heads;
   int rc = c->ar.alloc(&c->len, B);
   if (rc) return rc;
   const size_t rows = (size_t)B * c->Hk * cap;
@@ -276,25 +481,26 @@ struct Workspace {
   Arena ar;
 };
 
+// Sized by m's per-rank shapes (hq, hk, il, vl; hidden from m.c).
 static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_rows, Workspace& ws) {
   const lmx_model_config& c = m.c;
-  const int R = B * Tmax, NQ = c.heads * kHeadDim, NK = c.kv_heads * kHeadDim;
-  const int G = c.heads / c.kv_heads;
+  const int R = B * Tmax, NQ = m.hq * kHeadDim, NK = m.hk * kHeadDim;
+  const int G = m.hq / m.hk;
   ws.Rmax = R;
   ws.B = B;
-  ws.Hk = c.kv_heads;
+  ws.Hk = m.hk;
   ws.tiles = (G * Tmax + kRowTile - 1) / kRowTile;
   ws.splits = (cap + kSplit - 1) / kSplit;
   int rc = ws.ar.alloc(&ws.h, (size_t)R * c.hidden);
-  if (!rc) rc = ws.ar.alloc(&ws.xn, (size_t)R * (c.hidden > c.inter ? c.hidden : c.inter));
+  if (!rc) rc = ws.ar.alloc(&ws.xn, (size_t)R * (c.hidden > m.il ? c.hidden : m.il));
   if (!rc) rc = ws.ar.alloc(&ws.qkv, (size_t)R * (NQ + 2 * NK));
   if (!rc) rc = ws.ar.alloc(&ws.q, (size_t)R * NQ);
   if (!rc) rc = ws.ar.alloc(&ws.o, (size_t)R * NQ);
-  if (!rc) rc = ws.ar.alloc(&ws.act, (size_t)R * c.inter);
-  if (!rc) rc = ws.ar.alloc(&ws.logits, (size_t)logit_rows * c.vocab);
+  if (!rc) rc = ws.ar.alloc(&ws.act, (size_t)R * m.il);
+  if (!rc) rc = ws.ar.alloc(&ws.logits, (size_t)logit_rows * m.vl);
   if (!rc)
-    rc = ws.ar.alloc(&ws.part, (size_t)B * c.kv_heads * ws.tiles * ws.splits * kRowTile * kPartStride, false);
-  if (!rc) rc = ws.ar.alloc(&ws.counters, (size_t)B * c.kv_heads * ws.tiles);
+    rc = ws.ar.alloc(&ws.part, (size_t)B * m.hk * ws.tiles * ws.splits * kRowTile * kPartStride, false);
+  if (!rc) rc = ws.ar.alloc(&ws.counters, (size_t)B * m.hk * ws.tiles);
   return rc;
 }
 
@@ -304,24 +510,33 @@ static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_
 // RoPE, KV append -> SDPA -> o_proj GEMV (+residual) -> gate|up GEMV
 // (+RMSNorm, SwiGLU) -> down GEMV (+residual); then the final norm and the
 // lm_head for every row or only each sequence's last row.
+// Tensor-parallel shard (m.tp > 1): o_proj and down write this rank's
+// partial into the comm's slot and tp_allreduce_norm_kernel adds the sum to
+// the residual and applies the next RMSNorm (post-attention, the next
+// layer's input norm, or the final norm); the lm_head produces this rank's
+// vocabulary slice [rows][vl].
 static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, int tok_ld, int tok_off,
                    int B, int T, Workspace& ws, bf16_t* logits, bool last_only, cudaStream_t st,
                    int logits_ld = 0) {
   const lmx_model_config& cf = m.c;
-  const int H = cf.hidden, I = cf.inter, Hq = cf.heads, Hk = cf.kv_heads;
+  const int H = cf.hidden, I = m.il, Hq = m.hq, Hk = m.hk;
   const int NQ = Hq * kHeadDim, NK = Hk * kHeadDim, G = Hq / Hk, R = B * T;
-  if (R > ws.Rmax || B != c.B || n_layers > c.n_layers || n_layers > m.n_layers)
+  const bool tp = m.tp > 1;
+  if (R > ws.Rmax || B != c.B || n_layers > c.n_layers || n_layers > m.n_layers || c.Hk != Hk)
     return set_error(LMX_ERR_INVALID, "forward: shape exceeds workspace");
   const int tiles = (G * T + kRowTile - 1) / kRowTile, splits = (c.cap + kSplit - 1) / kSplit;
   if (tiles > ws.tiles || splits > ws.splits || B > ws.B || Hk > ws.Hk)
     return set_error(LMX_ERR_INVALID, "forward: attention scratch too small");
-  const bool fuse = R <= kQmmMaxNormRows && !qmm_uses_mma(R);
+  if (tp && (R > m.comm->max_rows || H > m.comm->max_hidden))
+    return set_error(LMX_ERR_INVALID, "forward: %d rows exceed the tp comm", R);
+  const bool fuse = !tp && R <= kQmmMaxNormRows && !qmm_uses_mma(R);
   int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
                                  (const uint32_t*)m.embed.w, (const bf16_t*)m.embed.s,
                                  (const bf16_t*)m.embed.b, H, cf.bits, ws.h, R),
                       "embed");
   if (rc) return rc;
   const float scale = (float)(1.0 / std::sqrt((double)kHeadDim));
+  int sel = 0;  // tp partial slot, alternating per exchange
   for (int l = 0; l < n_layers && !rc; ++l) {
     const Layer& L = m.L[l];
     QmmCall qc;
@@ -329,7 +544,8 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
       qc.x = ws.h;
       qc.norm_w = L.in_norm;
     } else {
-      rc = launch_rms_norm(ws.h, L.in_norm, ws.xn, R, H, cf.eps, st);
+      // tp: layers > 0 get xn from the previous layer's all-reduce
+      if (!tp || l == 0) rc = launch_rms_norm(ws.h, L.in_norm, ws.xn, R, H, cf.eps, st);
       qc.x = ws.xn;
     }
     qc.eps = cf.eps;
@@ -380,21 +596,29 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     oc.x = ws.o;
     oc.mat[0] = L.w[3].mat();
     oc.N = H;
-    oc.y = ws.h;
     oc.ldy = H;
-    oc.res = ws.h;
     oc.M = R;
     oc.K = NQ;
     oc.bits = cf.bits;
-    oc.mode = kResid;
-    if (!rc) rc = launch_qmm(oc, st);
+    if (tp) {
+      oc.y = tp_slot(*m.comm, sel);
+      oc.mode = kPlain;
+      if (!rc) rc = launch_qmm(oc, st);
+      if (!rc) rc = launch_tp_allreduce_norm(*m.comm, sel, R, H, ws.h, L.post_norm, cf.eps, ws.xn, st);
+      sel ^= 1;
+    } else {
+      oc.y = ws.h;
+      oc.res = ws.h;
+      oc.mode = kResid;
+      if (!rc) rc = launch_qmm(oc, st);
+    }
 
     QmmCall gc;
     if (fuse) {
       gc.x = ws.h;
       gc.norm_w = L.post_norm;
     } else {
-      if (!rc) rc = launch_rms_norm(ws.h, L.post_norm, ws.xn, R, H, cf.eps, st);
+      if (!tp && !rc) rc = launch_rms_norm(ws.h, L.post_norm, ws.xn, R, H, cf.eps, st);
       gc.x = ws.xn;
     }
     gc.eps = cf.eps;
@@ -414,20 +638,31 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     dc.x = ws.act;
     dc.mat[0] = L.w[6].mat();
     dc.N = H;
-    dc.y = ws.h;
     dc.ldy = H;
-    dc.res = ws.h;
     dc.M = R;
     dc.K = I;
     dc.bits = cf.bits;
-    dc.mode = kResid;
-    if (!rc) rc = launch_qmm(dc, st);
+    if (tp) {
+      dc.y = tp_slot(*m.comm, sel);
+      dc.mode = kPlain;
+      const bf16_t* next_norm = l + 1 < n_layers ? m.L[l + 1].in_norm : m.final_norm;
+      if (!rc) rc = launch_qmm(dc, st);
+      if (!rc) rc = launch_tp_allreduce_norm(*m.comm, sel, R, H, ws.h, next_norm, cf.eps, ws.xn, st);
+      sel ^= 1;
+    } else {
+      dc.y = ws.h;
+      dc.res = ws.h;
+      dc.mode = kResid;
+      if (!rc) rc = launch_qmm(dc, st);
+    }
   }
   if (rc || !logits) return rc;
   QmmCall hc;
   const int M = last_only ? B : R;
   const bf16_t* src = ws.h;
-  if (M > kQmmMaxNormRows || qmm_uses_mma(M)) {
+  if (tp) {
+    src = ws.xn;  // final-normed by the last all-reduce
+  } else if (M > kQmmMaxNormRows || qmm_uses_mma(M)) {
     rc = launch_rms_norm(ws.h, m.final_norm, ws.xn, R, H, cf.eps, st);
     if (rc) return rc;
     src = ws.xn;
@@ -438,13 +673,21 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   hc.ldx = last_only ? T * H : H;
   hc.eps = cf.eps;
   hc.mat[0] = m.head().mat();
-  hc.N = cf.vocab;
+  hc.N = m.vl;
   hc.y = logits;
-  hc.ldy = logits_ld ? logits_ld : cf.vocab;
+  hc.ldy = logits_ld ? logits_ld : m.vl;
   hc.M = M;
   hc.K = H;
   hc.bits = cf.bits;
   return launch_qmm(hc, st);
+}
+
+// Greedy token of each of `rows` logits rows (ld columns apart): the cluster
+// argmax, or the vocab-parallel argmax across the ranks of a tp model.
+static int model_argmax(const Model& m, const bf16_t* logits, int rows, int ld, int32_t* out, cudaStream_t st) {
+  if (m.tp > 1) return launch_tp_argmax(*m.comm, logits, rows, m.vl, ld, m.tp_rank * m.vl, out, st);
+  if (ld != m.vl) return set_error(LMX_ERR_INVALID, "argmax: ld %d != vocab %d", ld, m.vl);
+  return launch_argmax(logits, rows, m.vl, out, st);
 }
 
 static int add_len(int* len, int B, int n, cudaStream_t st) {
@@ -524,7 +767,7 @@ static int spec_step(Spec& sp) {
                                  (const bf16_t*)sp.ws.logits, V, sp.s, stoch_params(sp)),
                       "accept_stochastic");
   } else {
-    if (!rc) rc = launch_argmax(sp.ws.logits, B * (K + 1), V, sp.s.pred, st);
+    if (!rc) rc = model_argmax(*sp.tm, sp.ws.logits, B * (K + 1), sp.tm->vl, sp.s.pred, st);
     if (!rc)
       rc = cuda_check(lmx_launch(accept_greedy_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s),
                       "accept");
@@ -541,13 +784,17 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
     return set_error(LMX_ERR_INVALID, "spec: bad config");
   if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
     return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
+  if (dm->tp > 1) return set_error(LMX_ERR_UNSUPPORTED, "spec: the draft runs replicated (tp 1) on every rank");
+  if (tm->tp > 1 && cfg.temperature > 0.0f)
+    return set_error(LMX_ERR_UNSUPPORTED, "spec: a tensor-parallel target decodes greedily (temperature 0)");
   auto sp = std::make_unique<Spec>();
   sp->tm = tm;
   sp->dm = dm;
   sp->dl = dl;
   sp->cfg = cfg;
   const int B = cfg.batch, K = cfg.K, P = cfg.prompt_len;
-  const int cap = P + cfg.max_tokens + K + 8;
+  if (cfg.context_len < 0) return set_error(LMX_ERR_INVALID, "spec: context_len < 0");
+  const int cap = cfg.context_len + P + cfg.max_tokens + K + 8;
   Cache *tc = nullptr, *dc = nullptr;
   int rc = cache_create(*tm, tm->n_layers, B, cap, cfg.kv_bits, &tc);
   if (rc) return rc;
@@ -558,14 +805,13 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   // one workspace serves both models: every dimension is the larger of the
   // two, the attention scratch is sized for the larger group (q heads per KV
   // head) and KV head count (its layout follows each call's own shape)
-  lmx_model_config big = tm->c;
-  const int gmax = std::max(tm->c.heads / tm->c.kv_heads, dm->c.heads / dm->c.kv_heads);
-  big.hidden = std::max(tm->c.hidden, dm->c.hidden);
-  big.inter = std::max(tm->c.inter, dm->c.inter);
-  big.kv_heads = std::max(tm->c.kv_heads, dm->c.kv_heads);
-  big.heads = gmax * big.kv_heads;
   Model shape;
-  shape.c = big;
+  shape.c = tm->c;
+  shape.c.hidden = std::max(tm->c.hidden, dm->c.hidden);
+  shape.hk = std::max(tm->hk, dm->hk);
+  shape.hq = std::max(tm->hq / tm->hk, dm->hq / dm->hk) * shape.hk;
+  shape.il = std::max(tm->il, dm->il);
+  shape.vl = std::max(tm->vl, dm->vl);
   const int Tmax = std::max(K + 1, kPrefillChunk);
   rc = workspace_create(shape, B, Tmax, cap, B * (K + 1), sp->ws);
   if (rc) return rc;
@@ -598,6 +844,8 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   return LMX_OK;
 }
 
+static constexpr uint32_t kCtxTidTarget = 0x40000000u, kCtxTidDraft = 0x50000000u;
+
 // Prefill (TokenIterator::prepare, src/common/generate.cpp:508-549): the
 // target runs the prompt and its argmax at the last position is d0 of the
 // first step; the draft runs prompt[0, P-1) (its first step re-runs P-1).
@@ -606,8 +854,9 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
   cudaStream_t st = sp.st;
   int rc = cuda_check(cudaMemcpyAsync(sp.prompts, prompts_host, (size_t)B * P * 4, cudaMemcpyHostToDevice, st),
                       "prompts");
-  if (!rc) rc = cuda_check(cudaMemsetAsync(sp.tc->len, 0, B * 4, st), "len");
-  if (!rc) rc = cuda_check(cudaMemsetAsync(sp.dc->len, 0, B * 4, st), "len");
+  // the synthetic context (if any) precedes the prompt in both caches
+  if (!rc) rc = cache_fill_synthetic(*sp.tc, sp.cfg.context_len, sp.cfg.context_seed, kCtxTidTarget, st);
+  if (!rc) rc = cache_fill_synthetic(*sp.dc, sp.cfg.context_len, sp.cfg.context_seed, kCtxTidDraft, st);
   if (!rc) rc = forward_chunked(*sp.tm, *sp.tc, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
   if (!rc && sp.cfg.temperature > 0.0f)
     rc = cuda_check(samp_launch(sample_rows_kernel, B, st,
@@ -615,11 +864,11 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
                                0u, 0u, 3u, sp.yprefill),
                     "prefill sample");
   else if (!rc)
-    rc = launch_argmax(sp.ws.logits, B, sp.tm->c.vocab, sp.yprefill, st);
+    rc = model_argmax(*sp.tm, sp.ws.logits, B, sp.tm->vl, sp.yprefill, st);
   if (!rc) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
   if (!rc)
     rc = cuda_check(lmx_launch(prefill_done_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
-                               (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill),
+                               (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill, sp.cfg.context_len),
                     "prefill_done");
   if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "prefill");
   if (!rc) sp.prefilled = true;
@@ -691,9 +940,46 @@ extern "C" int lmx_set_device(int device) { return cuda_check(cudaSetDevice(devi
 extern "C" int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model) {
   if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create: null argument");
   Model* m = nullptr;
-  int rc = model_create(*cfg, seed, &m);
+  int rc = model_create(*cfg, seed, nullptr, &m);
   if (!rc) *model = m;
   return rc;
+}
+
+extern "C" int lmx_model_create_tp(const lmx_model_config* cfg, uint64_t seed, void* comm, void** model) {
+  if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create_tp: null argument");
+  Model* m = nullptr;
+  int rc = model_create(*cfg, seed, (TpComm*)comm, &m);
+  if (!rc) *model = m;
+  return rc;
+}
+
+extern "C" int lmx_tp_comm_create(int rank, int size, int max_rows, int max_hidden, void** comm) {
+  if (!comm) return set_error(LMX_ERR_INVALID, "tp_comm_create: null argument");
+  TpComm* c = nullptr;
+  int rc = tp_comm_create(rank, size, max_rows, max_hidden, &c);
+  if (!rc) *comm = c;
+  return rc;
+}
+
+extern "C" int lmx_tp_comm_handle(void* comm, void* handle) {
+  TpComm* c = (TpComm*)comm;
+  if (!c || !handle) return set_error(LMX_ERR_INVALID, "tp_comm_handle: null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == LMX_TP_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  int rc = cuda_check(cudaIpcGetMemHandle(&h, c->block), "tp_comm_handle");
+  if (!rc) std::memcpy(handle, &h, sizeof(h));
+  return rc;
+}
+
+extern "C" int lmx_tp_comm_open(void* comm, const void* handles) {
+  TpComm* c = (TpComm*)comm;
+  if (!c || !handles) return set_error(LMX_ERR_INVALID, "tp_comm_open: null argument");
+  return tp_comm_open(*c, handles);
+}
+
+extern "C" int lmx_tp_comm_free(void* comm) {
+  delete (TpComm*)comm;
+  return LMX_OK;
 }
 
 extern "C" int lmx_model_view(void* model, int n_layers, void** view) {
@@ -762,6 +1048,12 @@ extern "C" int lmx_cache_set_position(void* cache, int seq, int pos) {
   return rc;
 }
 
+extern "C" int lmx_cache_fill_synthetic(void* cache, int rows, uint64_t seed, uint32_t tid_base) {
+  CacheHandle* h = (CacheHandle*)cache;
+  if (!h) return set_error(LMX_ERR_INVALID, "fill_synthetic: null cache");
+  return cache_fill_synthetic(*h->c, rows, seed, tid_base, 0);
+}
+
 extern "C" int lmx_cache_len(void* cache, int seq, int* len) {
   CacheHandle* h = (CacheHandle*)cache;
   if (!h || !len || seq < 0 || seq >= h->c->B) return set_error(LMX_ERR_INVALID, "cache_len: bad arguments");
@@ -784,7 +1076,7 @@ extern "C" int lmx_forward(void* model, void* cache, int n_layers, const int32_t
   if (!rc) rc = add_len(h->c->len, B, T, 0);
   if (!rc) rc = cuda_check(cudaDeviceSynchronize(), "forward");
   if (!rc && logits_host)
-    rc = cuda_check(cudaMemcpy(logits_host, h->ws.logits, (size_t)B * T * m->c.vocab * 2, cudaMemcpyDeviceToHost),
+    rc = cuda_check(cudaMemcpy(logits_host, h->ws.logits, (size_t)B * T * m->vl * 2, cudaMemcpyDeviceToHost),
                     "logits");
   return rc;
 }
@@ -865,7 +1157,7 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     for (int l = 0; l < nl; ++l)
       for (int k = 0; k < 7; ++k) s += qmm_bytes(m.L[l].w[k], bits, M);
     for (int b = 0; b < B; ++b)  // K and V rows read by attention, new rows written
-      s += (double)nl * 2 * m.c.kv_heads * (lens[b] + T) * kHeadDim * (sp.cfg.kv_bits == 16 ? 2.0 : sp.cfg.kv_bits / 8.0 + 4.0 / 64);
+      s += (double)nl * 2 * m.hk * (lens[b] + T) * kHeadDim * (sp.cfg.kv_bits == 16 ? 2.0 : sp.cfg.kv_bits / 8.0 + 4.0 / 64);
     if (head) s += qmm_bytes(m.head(), bits, M);
     return s;
   };
@@ -891,9 +1183,9 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     }
     hc.eps = sp.tm->c.eps;
     hc.mat[0] = sp.tm->head().mat();
-    hc.N = sp.tm->c.vocab;
+    hc.N = sp.tm->vl;
     hc.y = sp.ws.logits;
-    hc.ldy = sp.tm->c.vocab;
+    hc.ldy = sp.tm->vl;
     hc.K = sp.tm->c.hidden;
     hc.bits = bits;
     return launch_qmm(hc, st);

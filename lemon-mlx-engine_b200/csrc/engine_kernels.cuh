@@ -5,6 +5,7 @@
 #include <cooperative_groups.h>
 
 #include "lmx_common.cuh"
+#include "attn.cuh"
 #include "norm_argmax.cuh"
 namespace cg = cooperative_groups;
 
@@ -15,7 +16,10 @@ namespace lmx {
 // orc_quantize: element e of tensor tid is Irwin-Hall(4) of 22-bit Philox
 // uniforms (counter (e_lo, e_hi, tid, 0x243F6A88)), bf16(z * C); each group of
 // 64 is quantized with scale = bf16((max-min)/(2^bits-1)), bias = bf16(min).
-// One thread per group.
+// One thread per group.  A tensor-parallel shard is the block of rows
+// [row0, row0+N) and columns [col0, col0+K) of the full [*, Kfull] matrix:
+// element (n, k) keeps its full-matrix index (row0+n)*Kfull + col0+k, so a
+// shard holds exactly the values of that block of the unsharded weight.
 // ---------------------------------------------------------------------------
 LMX_DEV bf16_t gen_normal(uint64_t seed, uint32_t tid, uint64_t e, float C) {
   uint32_t c[4] = {(uint32_t)e, (uint32_t)(e >> 32), tid, 0x243F6A88u};
@@ -24,20 +28,12 @@ LMX_DEV bf16_t gen_normal(uint64_t seed, uint32_t tid, uint64_t e, float C) {
   return f2bf(__fmul_rn((float)(S - (1 << 23)), C));
 }
 
-__global__ void gen_qweight_kernel(uint64_t seed, uint32_t tid, int N, int K, int bits, float C,
-                                   uint32_t* wq, bf16_t* scales, bf16_t* biases) {
-  const int G = K / 64;
-  const int64_t grp = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (grp >= (int64_t)N * G) return;
-  const int n = (int)(grp / G), g = (int)(grp % G);
-  const uint64_t e0 = (uint64_t)n * K + (uint64_t)g * 64;
-  float v[64];
-  float mn = 0.0f, mx = 0.0f;
-#pragma unroll 4
-  for (int j = 0; j < 64; ++j) {
-    v[j] = bf2f(gen_normal(seed, tid, e0 + j, C));
-    mn = j == 0 ? v[j] : fminf(mn, v[j]);
-    mx = j == 0 ? v[j] : fmaxf(mx, v[j]);
+// One group of 64 values quantized as above into `bits`-bit codes.
+LMX_DEV void quantize_group64(const float (&v)[64], int bits, uint32_t* wout, bf16_t* s_out, bf16_t* b_out) {
+  float mn = v[0], mx = v[0];
+  for (int j = 1; j < 64; ++j) {
+    mn = fminf(mn, v[j]);
+    mx = fmaxf(mx, v[j]);
   }
   const int nb = (1 << bits) - 1;
   bf16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), (float)nb));
@@ -46,7 +42,6 @@ __global__ void gen_qweight_kernel(uint64_t seed, uint32_t tid, int N, int K, in
   const bf16_t bb = f2bf(mn);
   const float bi = bf2f(bb);
   const int per = 32 / bits;
-  uint32_t* wout = wq + (size_t)n * (K * bits / 32) + (size_t)g * (64 * bits / 32);
   for (int w = 0; w < 64 / per; ++w) {
     uint32_t word = 0;
     for (int j = 0; j < per; ++j) {
@@ -56,8 +51,52 @@ __global__ void gen_qweight_kernel(uint64_t seed, uint32_t tid, int N, int K, in
     }
     wout[w] = word;
   }
-  scales[grp] = sb;
-  biases[grp] = bb;
+  *s_out = sb;
+  *b_out = bb;
+}
+
+__global__ void gen_qweight_kernel(uint64_t seed, uint32_t tid, int N, int K, int bits, float C,
+                                   int64_t row0, int64_t col0, int64_t Kfull,
+                                   uint32_t* wq, bf16_t* scales, bf16_t* biases) {
+  const int G = K / 64;
+  const int64_t grp = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (grp >= (int64_t)N * G) return;
+  const int n = (int)(grp / G), g = (int)(grp % G);
+  const uint64_t e0 = (uint64_t)(row0 + n) * (uint64_t)Kfull + (uint64_t)col0 + (uint64_t)g * 64;
+  float v[64];
+#pragma unroll 4
+  for (int j = 0; j < 64; ++j) v[j] = bf2f(gen_normal(seed, tid, e0 + j, C));
+  quantize_group64(v, bits, wq + (size_t)n * (K * bits / 32) + (size_t)g * (64 * bits / 32), &scales[grp],
+                   &biases[grp]);
+}
+
+// Synthetic context (a stand-in for prefilling a long random-token prefix):
+// rows [0, n) of one layer's K or V cache hold N(0, std) values from the same
+// Philox normal, tensor id tid, element ((b*Hk_total + hk0+hk)*n + j)*128 + d
+// (hk0 = the first KV head of this tensor-parallel shard), quantized per
+// group of 64 exactly like an append.  One thread per (b, hk, j, group).
+__global__ void fill_kv_kernel(uint64_t seed, uint32_t tid, KvDesc kv, int is_v, int n, int hk0, int Hk_total,
+                               float C) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int gpr = kHeadDim / 64;
+  if (t >= (int64_t)kv.B * kv.Hk * n * gpr) return;
+  const int g = (int)(t % gpr);
+  const int64_t rowi = t / gpr;  // (b, hk, j)
+  const int j = (int)(rowi % n);
+  const int hk = (int)((rowi / n) % kv.Hk), b = (int)(rowi / ((int64_t)n * kv.Hk));
+  const uint64_t e0 = (((uint64_t)b * Hk_total + hk0 + hk) * (uint64_t)n + j) * kHeadDim + (uint64_t)g * 64;
+  const size_t row = ((size_t)b * kv.Hk + hk) * kv.cap + j;
+  if (kv.bits == 16) {
+    bf16_t* dst = (is_v ? kv.v : kv.k) + row * kHeadDim + g * 64;
+    for (int d = 0; d < 64; ++d) dst[d] = gen_normal(seed, tid, e0 + d, C);
+    return;
+  }
+  float v[64];
+#pragma unroll 4
+  for (int d = 0; d < 64; ++d) v[d] = bf2f(gen_normal(seed, tid, e0 + d, C));
+  const int wpr = kHeadDim * kv.bits / 32;
+  quantize_group64(v, kv.bits, (is_v ? kv.vq : kv.kq) + row * wpr + g * (64 * kv.bits / 32),
+                   (is_v ? kv.vs : kv.ks) + row * gpr + g, (is_v ? kv.vb : kv.kb) + row * gpr + g);
 }
 
 __global__ void fill_bf16_kernel(bf16_t* p, int64_t n, bf16_t v) {
@@ -193,16 +232,17 @@ __global__ void accept_greedy_kernel(SpecState s) {
 }
 
 // Prefill bookkeeping: y = argmax of the last prompt position (already in
-// pred[b*(K+1)]), tok2 = (prompt[P-1], y), lengths P and P-1.
-__global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, const int32_t* y) {
+// pred[b*(K+1)]), tok2 = (prompt[P-1], y), lengths ctx+P and ctx+P-1 (ctx:
+// synthetic context rows before the prompt).
+__global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, const int32_t* y, int ctx) {
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= s.B) return;
   s.tok2[2 * b] = prompts[(size_t)b * P + P - 1];
   s.tok2[2 * b + 1] = y[b];
-  s.tlen[b] = P;
-  s.dlen[b] = P - 1;
+  s.tlen[b] = ctx + P;
+  s.dlen[b] = ctx + P - 1;
   s.emitted[b] = 0;
   s.accepted[b] = 0;
   s.steps[b] = 0;

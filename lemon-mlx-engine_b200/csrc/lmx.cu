@@ -16,6 +16,7 @@
 #include "attn.cuh"
 #include "engine_kernels.cuh"
 #include "sample.cuh"
+#include "tp.cuh"
 
 // Device error word: bounded waits that give up record a code here.
 __device__ unsigned g_lmx_kernel_error;

@@ -396,13 +396,22 @@ __global__ void __launch_bounds__(kQmmThreads, MT <= 2 ? 2 : 1) qmv_kernel(const
         float nwv[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) nwv[j] = (a.norm_w && qv) ? bf2f(a.norm_w[k0 + j]) : 1.0f;
+        // every row's loads first (one L2 round trip for the tile), then the
+        // conversions
+        uint4 raw[MT][2];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < mcnt && qv) {
+            const bf16_t* src = a.x + (size_t)(mt0 + m) * a.ldx + k0;
+            raw[m][0] = *reinterpret_cast<const uint4*>(src);
+            raw[m][1] = *reinterpret_cast<const uint4*>(src + 8);
+          }
+        }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           float X = 0.0f;
           if (m < mcnt && qv) {
-            const bf16_t* src = a.x + (size_t)(mt0 + m) * a.ldx + k0;
-            uint4 r0 = *reinterpret_cast<const uint4*>(src);
-            uint4 r1 = *reinterpret_cast<const uint4*>(src + 8);
+            const uint4 r0 = raw[m][0], r1 = raw[m][1];
             const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
             const float f = a.norm_w ? fnorm[mt0 + m] : 1.0f;
 #pragma unroll

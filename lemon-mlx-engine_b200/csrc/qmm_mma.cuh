@@ -29,8 +29,9 @@
 // Epilogue: tcgen05.ld (lane quarter = warp % 4) -> fp32 tile [m][row] in
 // shared memory -> coalesced PLAIN / RESID / SWIGLU stores.
 // Every mbarrier wait is bounded and sets the device error word on timeout.
-// No TMA multicast.  Numerics: bf16 dequantized weights, fp32 tensor-core
-// accumulation in the hardware's order (compared with a tolerance).
+// Each TMA load fills only its own CTA's shared memory.  Numerics: bf16
+// dequantized weights, fp32 tensor-core accumulation in the hardware's order
+// (compared with a tolerance).
 #pragma once
 #include "qmm.cuh"
 

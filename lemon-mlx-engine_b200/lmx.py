@@ -41,6 +41,12 @@ SIGNATURES = {
     "lmx_sdpa_decode": (I, [P, P, I, I, F, P, C.c_size_t, P, P]),
     "lmx_sdpa_decode_noalloc": (I, [P, P, I, I, F, P, P]),
     "lmx_model_create": (I, [P, U64, P]),
+    "lmx_model_create_tp": (I, [P, U64, P, P]),
+    "lmx_tp_comm_create": (I, [I, I, I, I, P]),
+    "lmx_tp_comm_handle": (I, [P, P]),
+    "lmx_tp_comm_open": (I, [P, P]),
+    "lmx_tp_comm_free": (I, [P]),
+    "lmx_cache_fill_synthetic": (I, [P, I, U64, C.c_uint32]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
     "lmx_model_weight": (I, [P, I, I, P, P, P]),
@@ -70,13 +76,15 @@ class ModelConfig(C.Structure):
     """lmx_model_config"""
     _fields_ = [("hidden", I), ("layers", I), ("inter", I), ("heads", I), ("kv_heads", I),
                 ("head_dim", I), ("vocab", I), ("rope_theta", F), ("eps", F), ("qk_norm", I),
-                ("tied", I), ("bits", I), ("group_size", I)]
+                ("tied", I), ("bits", I), ("group_size", I), ("rope_factor", F), ("rope_low_freq", F),
+                ("rope_high_freq", F), ("rope_orig_max_pos", F)]
 
 
 class SpecConfig(C.Structure):
     """lmx_spec_config"""
     _fields_ = [("batch", I), ("K", I), ("max_tokens", I), ("prompt_len", I), ("kv_bits", I),
-                ("temperature", F), ("top_p", F), ("seed", U64)]
+                ("temperature", F), ("top_p", F), ("seed", U64), ("context_len", I),
+                ("context_seed", U64)]
 
 
 # The benchmark configurations' architectures (random-initialised weights).
@@ -84,19 +92,88 @@ QWEN3_0_6B = dict(hidden=1024, layers=28, inter=3072, heads=16, kv_heads=8, head
                   vocab=151936, rope_theta=1e6, eps=1e-6, qk_norm=1, tied=1, bits=4, group_size=64)
 QWEN3_8B = dict(hidden=4096, layers=36, inter=12288, heads=32, kv_heads=8, head_dim=128,
                 vocab=151936, rope_theta=1e6, eps=1e-6, qk_norm=1, tied=0, bits=4, group_size=64)
+LLAMA3_70B = dict(hidden=8192, layers=80, inter=28672, heads=64, kv_heads=8, head_dim=128,
+                  vocab=128256, rope_theta=5e5, eps=1e-5, qk_norm=0, tied=0, bits=4, group_size=64)
+LLAMA32_1B = dict(hidden=2048, layers=16, inter=8192, heads=32, kv_heads=8, head_dim=128,
+                  vocab=128256, rope_theta=5e5, eps=1e-5, qk_norm=0, tied=1, bits=4, group_size=64,
+                  rope_factor=32.0, rope_low_freq=1.0, rope_high_freq=4.0, rope_orig_max_pos=8192.0)
+
+
+TP_HANDLE_BYTES = 64
+
+
+def exchange_handles(handle: bytes, group=None):
+    """All ranks' communicator handles in rank order, gathered over an
+    initialised torch.distributed process group (any backend)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    for i, h in enumerate(out):
+        if not isinstance(h, bytes) or len(h) != TP_HANDLE_BYTES:
+            raise LmxError(f"tp handle of rank {i} is malformed")
+    return out
+
+
+class TpComm:
+    """Tensor-parallel communicator of this rank (include/lmx.h, 'Tensor
+    parallelism'): an IPC-exported device block, opened by every peer."""
+
+    def __init__(self, rank: int, size: int, max_rows: int, max_hidden: int):
+        h = C.c_void_p()
+        call("lmx_tp_comm_create", rank, size, max_rows, max_hidden, C.byref(h))
+        self.h, self.rank, self.size = h, rank, size
+        self._models = []
+
+    def handle(self) -> bytes:
+        buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        call("lmx_tp_comm_handle", self.h, buf)
+        return buf.raw
+
+    def open(self, handles):
+        if len(handles) != self.size:
+            raise LmxError(f"tp_comm_open: {len(handles)} handles for size {self.size}")
+        blob = b"".join(handles)
+        call("lmx_tp_comm_open", self.h, C.c_char_p(blob))
+
+    @classmethod
+    def from_process_group(cls, max_rows: int, max_hidden: int, group=None):
+        """Create, exchange handles over torch.distributed, open, barrier."""
+        import torch.distributed as dist
+        rank, size = dist.get_rank(group), dist.get_world_size(group)
+        comm = cls(rank, size, max_rows, max_hidden)
+        if size > 1:
+            comm.open(exchange_handles(comm.handle(), group))
+        dist.barrier(group)
+        return comm
+
+    def close(self):
+        if self.h:
+            lib().lmx_tp_comm_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Model:
-    """Owns an lmx model handle (synthetic seeded weights on the device)."""
+    """Owns an lmx model handle (synthetic seeded weights on the device);
+    with a TpComm of size > 1, this rank's tensor-parallel shard."""
 
-    def __init__(self, cfg: dict, seed: int, _handle=None, _parent=None):
+    def __init__(self, cfg: dict, seed: int, _handle=None, _parent=None, comm=None):
         self.cfg = dict(cfg)
         self._parent = _parent
+        self._comm = comm
         if _handle is not None:
             self.h = _handle
             return
         h = C.c_void_p()
-        call("lmx_model_create", C.byref(ModelConfig(**cfg)), seed, C.byref(h))
+        if comm is not None:
+            call("lmx_model_create_tp", C.byref(ModelConfig(**cfg)), seed, comm.h, C.byref(h))
+        else:
+            call("lmx_model_create", C.byref(ModelConfig(**cfg)), seed, C.byref(h))
         self.h = h
 
     def view(self, n_layers):
@@ -123,8 +200,9 @@ class SpecDecoder:
 
     def __init__(self, target: Model, draft, draft_layers: int, batch: int, K: int,
                  max_tokens: int, prompt_len: int, kv_bits=16, temperature=0.0, top_p=1.0,
-                 seed=0):
-        self.cfg = SpecConfig(batch, K, max_tokens, prompt_len, kv_bits, temperature, top_p, seed)
+                 seed=0, context_len=0, context_seed=0):
+        self.cfg = SpecConfig(batch, K, max_tokens, prompt_len, kv_bits, temperature, top_p, seed,
+                              context_len, context_seed)
         h = C.c_void_p()
         call("lmx_spec_create", target.h, draft.h if draft is not None else None, draft_layers,
              C.byref(self.cfg), C.byref(h))

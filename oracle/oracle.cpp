@@ -413,11 +413,37 @@ extern "C" void orc_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, 
 //   separately, one bf16 rounding at the end)
 // ---------------------------------------------------------------------------
 extern "C" void orc_rope_table(int max_pos, int dims, float base, float* cos_t, float* sin_t) {
+  orc_rope_table_scaled(max_pos, dims, base, 0.0f, 1.0f, 4.0f, 8192.0f, cos_t, sin_t);
+}
+
+// Period of rotation pair i: base^(2i/dims), with the Llama-3 frequency
+// scaling of LlamaDynamicNTKScalingRoPE::compute_freqs
+// (src/llm/models/llama.cpp:122-183) when factor > 1: wavelength 2*pi*period
+// above old/low_freq -> period * factor; strictly between old/high_freq and
+// old/low_freq -> period / ((1 - s)/factor + s), s = (old/wavelength -
+// low_freq) / (high_freq - low_freq); shorter wavelengths unchanged.
+extern "C" void orc_rope_table_scaled(int max_pos, int dims, float base, float factor, float low_freq,
+                                      float high_freq, float orig_max_pos, float* cos_t, float* sin_t) {
   const int half = dims / 2;
+  std::vector<double> period(half);
+  for (int i = 0; i < half; ++i) {
+    double pd = std::pow((double)base, 2.0 * (double)i / (double)dims);
+    if (factor > 1.0f) {
+      const double wl = 2.0 * M_PI * pd;
+      const double low_wl = (double)orig_max_pos / (double)low_freq;
+      const double high_wl = (double)orig_max_pos / (double)high_freq;
+      if (wl > low_wl) {
+        pd = pd * (double)factor;
+      } else if (wl > high_wl) {
+        const double s = ((double)orig_max_pos / wl - (double)low_freq) / ((double)high_freq - (double)low_freq);
+        pd = pd / ((1.0 - s) / (double)factor + s);
+      }
+    }
+    period[i] = pd;
+  }
   for (int p = 0; p < max_pos; ++p)
     for (int i = 0; i < half; ++i) {
-      double inv = std::pow((double)base, -2.0 * (double)i / (double)dims);
-      double th = (double)p * inv;
+      const double th = (double)p / period[i];
       cos_t[(size_t)p * half + i] = (float)std::cos(th);
       sin_t[(size_t)p * half + i] = (float)std::sin(th);
     }
@@ -705,6 +731,7 @@ struct Model {
   std::vector<uint16_t> final_norm;
   int max_pos = 16384;
   std::vector<float> cos_t, sin_t;
+  int tp = 1;  // tensor-parallel emulation of o_proj / down_proj
   const QW& head() const { return c.tied ? embed : lm_head; }
 };
 struct Cache {
@@ -729,7 +756,45 @@ void gen_qw(QW& q, uint64_t seed, uint32_t tid, int N, int K, int bits, int grou
 void qmm(const Model& m, const QW& w, const uint16_t* x, uint16_t* y, int M) {
   orc_qmm(x, w.w.data(), w.s.data(), w.b.data(), y, M, w.N, w.K, m.group, m.bits);
 }
+
+// h = h + x W^T for the row-split projections (o_proj, down_proj).  With
+// m.tp ranks (the device engine's tensor-parallel all-reduce, tp.cuh): rank
+// r's partial p_r = bf16(x[:, r-th K/tp columns] W[:, same]^T) in the
+// canonical order for K/tp, the sum s = p_0 + p_1 + ... in fp32 in rank
+// order, then h = bf16(h + bf16(s)).  tp == 1 is the plain residual add.
+void qmm_resid(const Model& m, const QW& w, const uint16_t* x, uint16_t* h, int M) {
+  const int N = w.N, K = w.K, tp = m.tp;
+  std::vector<uint16_t> a((size_t)M * N);
+  if (tp <= 1) {
+    qmm(m, w, x, a.data(), M);
+    orc_add(h, a.data(), h, (int64_t)M * N);
+    return;
+  }
+  const int Ks = K / tp, G = K / 64, Gs = Ks / 64, WPR = K * m.bits / 32, WPRs = Ks * m.bits / 32;
+  std::vector<float> sum((size_t)M * N);
+  std::vector<uint16_t> xs((size_t)M * Ks), ss((size_t)N * Gs), bs((size_t)N * Gs);
+  std::vector<uint32_t> ws((size_t)N * WPRs);
+  for (int r = 0; r < tp; ++r) {
+    for (int i = 0; i < M; ++i) std::memcpy(&xs[(size_t)i * Ks], x + (size_t)i * K + (size_t)r * Ks, Ks * 2);
+    for (int n = 0; n < N; ++n) {
+      std::memcpy(&ws[(size_t)n * WPRs], &w.w[(size_t)n * WPR + (size_t)r * WPRs], WPRs * 4);
+      std::memcpy(&ss[(size_t)n * Gs], &w.s[(size_t)n * G + (size_t)r * Gs], Gs * 2);
+      std::memcpy(&bs[(size_t)n * Gs], &w.b[(size_t)n * G + (size_t)r * Gs], Gs * 2);
+    }
+    orc_qmm(xs.data(), ws.data(), ss.data(), bs.data(), a.data(), M, N, Ks, m.group, m.bits);
+    for (size_t i = 0; i < sum.size(); ++i) sum[i] = r == 0 ? bf2f(a[i]) : sum[i] + bf2f(a[i]);
+  }
+  for (size_t i = 0; i < sum.size(); ++i) h[i] = f2bf(bf2f(f2bf(sum[i])) + bf2f(h[i]));
+}
 }  // namespace
+
+extern "C" int orc_model_set_tp(void* mp, int tp) {
+  Model& m = *(Model*)mp;
+  const orc_model_cfg& c = m.c;
+  if (tp < 1 || c.heads % tp || c.kv_heads % tp || c.inter % (64 * tp) || c.vocab % tp) return 1;
+  m.tp = tp;
+  return 0;
+}
 
 extern "C" void* orc_model_create(const orc_model_cfg* cfg, uint64_t seed) {
   if (cfg->group != 64 || (cfg->bits != 4 && cfg->bits != 8)) return nullptr;
@@ -755,7 +820,8 @@ extern "C" void* orc_model_create(const orc_model_cfg* cfg, uint64_t seed) {
   m->final_norm.assign(H, f2bf(1.0f));
   m->cos_t.resize((size_t)m->max_pos * D / 2);
   m->sin_t.resize(m->cos_t.size());
-  orc_rope_table(m->max_pos, D, cfg->rope_theta, m->cos_t.data(), m->sin_t.data());
+  orc_rope_table_scaled(m->max_pos, D, cfg->rope_theta, cfg->rope_factor, cfg->rope_low_freq, cfg->rope_high_freq,
+                        cfg->rope_orig_max_pos, m->cos_t.data(), m->sin_t.data());
   return m;
 }
 
@@ -799,6 +865,39 @@ extern "C" void* orc_cache_create(void* mp, int n_layers, int batch, int capacit
   }
   return c;
 }
+// Synthetic context (the device engine's fill_kv_kernel): rows [0, rows) of
+// every layer's K and V are N(0,1) bf16 from the Philox normal, tensor id
+// tid_base + 2*layer + (0 K, 1 V), element ((b*Hk + hk)*rows + j)*D + d,
+// quantized per group of 64 like an append; every length becomes rows.
+extern "C" int orc_cache_fill_synthetic(void* cp, int rows, uint64_t seed, uint32_t tid_base) {
+  Cache& c = *(Cache*)cp;
+  if (rows < 0 || rows > c.cap) return 1;
+  const float C = orc_normal_scale(1.0f);
+  const int D = c.D;
+  for (int l = 0; l < c.L; ++l)
+    for (int v = 0; v < 2; ++v) {
+      const uint32_t tid = tid_base + 2u * (uint32_t)l + (uint32_t)v;
+#pragma omp parallel for schedule(static)
+      for (int64_t t = 0; t < (int64_t)c.B * c.Hk * rows; ++t) {
+        const int j = (int)(t % rows);
+        const int64_t bh = t / rows;  // b * Hk + hk
+        const size_t row = (size_t)bh * c.cap + j;
+        uint16_t vals[256];
+        for (int d = 0; d < D; ++d) vals[d] = normal_bf16(seed, tid, (uint64_t)t * D + d, C);
+        if (c.bits == 16) {
+          std::memcpy(&(v ? c.v : c.k)[l][row * D], vals, D * 2);
+        } else {
+          const int WPR = D * c.bits / 32, gpr = D / 64;
+          for (int gi = 0; gi < gpr; ++gi)
+            quantize_group(vals + 64 * gi, 64, c.bits, &(v ? c.vq : c.kq)[l][row * WPR + gi * 64 * c.bits / 32],
+                           &(v ? c.vs : c.ks)[l][row * gpr + gi], &(v ? c.vb : c.kb)[l][row * gpr + gi]);
+        }
+      }
+    }
+  for (int b = 0; b < c.B; ++b) c.len[b] = rows;
+  return 0;
+}
+
 extern "C" void orc_cache_free(void* c) { delete (Cache*)c; }
 extern "C" int orc_cache_len(void* c, int b) { return ((Cache*)c)->len[b]; }
 extern "C" void orc_cache_set_position(void* cp, int b, int pos) {
@@ -892,14 +991,12 @@ static int forward_impl(Model& m, Cache& c, int n_layers, const int32_t* tokens,
       orc_sdpa(&q[(size_t)b * T * NQ], kb, vb, &o[(size_t)b * T * NQ], T, Hq, Hk, D, c.cap,
                c.len[b], scale);
     }
-    qmm(m, L.w[3], o.data(), a.data(), R);
-    orc_add(h.data(), a.data(), h.data(), (int64_t)R * H);
+    qmm_resid(m, L.w[3], o.data(), h.data(), R);
     orc_rms_norm(h.data(), L.post_norm.data(), xn.data(), R, H, cf.eps);
     qmm(m, L.w[4], xn.data(), g.data(), R);
     qmm(m, L.w[5], xn.data(), u.data(), R);
     orc_swiglu(g.data(), u.data(), g.data(), (int64_t)R * I);
-    qmm(m, L.w[6], g.data(), a.data(), R);
-    orc_add(h.data(), a.data(), h.data(), (int64_t)R * H);
+    qmm_resid(m, L.w[6], g.data(), h.data(), R);
   }
   for (int b = 0; b < B; ++b) c.len[b] += T;
   if (!logits) return 0;
@@ -981,10 +1078,17 @@ extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prom
   Model& dm = *ss->dm;
   const int K = ss->K, V = ss->V, dl = ss->dl;
   if (K < 1 || dl < 1 || dl > dm.c.layers || P < 2 || dm.c.vocab != V) return nullptr;
-  const int cap = P + ss->MT + K + 8;
+  if (prm->context_len < 0) return nullptr;
+  const int cap = prm->context_len + P + ss->MT + K + 8;
   ss->tc.reset((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, kv_bits));
   ss->dc.reset((Cache*)orc_cache_create(&dm, dl, B, cap, kv_bits));
   if (!ss->tc || !ss->dc) return nullptr;
+  // the synthetic context precedes the prompt in both caches (tensor ids as
+  // the device engine: target 0x40000000, draft 0x50000000)
+  if (prm->context_len > 0 &&
+      (orc_cache_fill_synthetic(ss->tc.get(), prm->context_len, prm->context_seed, 0x40000000u) ||
+       orc_cache_fill_synthetic(ss->dc.get(), prm->context_len, prm->context_seed, 0x50000000u)))
+    return nullptr;
   const auto t0 = std::chrono::steady_clock::now();
   std::vector<uint16_t> lg((size_t)B * V);
   if (prefill_chunked(tm, *ss->tc, tm.c.layers, prompts, P, B, P, lg.data())) return nullptr;

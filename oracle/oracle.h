@@ -73,6 +73,8 @@ int orc_mma_min_m(void);
 void orc_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int dim,
                   float eps);
 void orc_rope_table(int max_pos, int dims, float base, float* cos_t, float* sin_t);
+void orc_rope_table_scaled(int max_pos, int dims, float base, float factor, float low_freq,
+                           float high_freq, float orig_max_pos, float* cos_t, float* sin_t);
 void orc_rope(uint16_t* x, const int32_t* pos, int rows, int heads, int dim,
               const float* cos_t, const float* sin_t);
 void orc_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* y, int64_t n);
@@ -103,6 +105,8 @@ typedef struct {
   int qk_norm;   /* Qwen3: 1, Llama: 0 */
   int tied;      /* lm_head shares the packed embedding */
   int bits, group;
+  /* Llama-3 RoPE frequency scaling; factor <= 1: none */
+  float rope_factor, rope_low_freq, rope_high_freq, rope_orig_max_pos;
 } orc_model_cfg;
 
 void* orc_model_create(const orc_model_cfg* cfg, uint64_t seed);
@@ -113,6 +117,10 @@ int orc_model_weight(void* m, int layer, int kind, uint32_t* wq, uint16_t* s, ui
 
 /* kv_bits: 16 = bf16 cache, 4/8 = affine group-64 quantized cache. */
 void* orc_cache_create(void* model, int n_layers, int batch, int capacity, int kv_bits);
+int orc_cache_fill_synthetic(void* cache, int rows, uint64_t seed, uint32_t tid_base);
+/* Emulate a tp-rank tensor-parallel split of o_proj / down_proj (partials
+ * over column slices summed in fp32 in rank order); 0 = ok. */
+int orc_model_set_tp(void* model, int tp);
 void orc_cache_free(void* c);
 int orc_cache_len(void* c, int b);
 void orc_cache_set_position(void* c, int b, int pos);
@@ -129,6 +137,8 @@ typedef struct {
   float top_p;
   uint64_t seed;      /* uniforms */
   int draft_layers;   /* >0: draft = first draft_layers of target (self-draft) */
+  int context_len;    /* synthetic context rows before the prompt (0: none) */
+  uint64_t context_seed;
 } orc_spec_params;
 
 /* Speculative decode with a separate draft model (draft may be the target

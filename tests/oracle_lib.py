@@ -41,12 +41,13 @@ F = C.c_float
 class ModelCfg(C.Structure):
     _fields_ = [("hidden", I), ("layers", I), ("inter", I), ("heads", I), ("kv_heads", I),
                 ("head_dim", I), ("vocab", I), ("rope_theta", F), ("eps", F), ("qk_norm", I),
-                ("tied", I), ("bits", I), ("group", I)]
+                ("tied", I), ("bits", I), ("group", I), ("rope_factor", F), ("rope_low_freq", F),
+                ("rope_high_freq", F), ("rope_orig_max_pos", F)]
 
 
 class SpecParams(C.Structure):
     _fields_ = [("K", I), ("max_tokens", I), ("temperature", F), ("top_p", F), ("seed", U64),
-                ("draft_layers", I)]
+                ("draft_layers", I), ("context_len", I), ("context_seed", U64)]
 
 
 def _declare(L):
@@ -68,6 +69,7 @@ def _declare(L):
         "orc_mma_min_m": (I, []),
         "orc_rms_norm": (None, [P, P, P, I, I, F]),
         "orc_rope_table": (None, [I, I, F, P, P]),
+        "orc_rope_table_scaled": (None, [I, I, F, F, F, F, F, P, P]),
         "orc_rope": (None, [P, P, I, I, I, P, P]),
         "orc_swiglu": (None, [P, P, P, I64]),
         "orc_add": (None, [P, P, P, I64]),
@@ -80,6 +82,8 @@ def _declare(L):
         "orc_model_free": (None, [P]),
         "orc_model_weight": (I, [P, I, I, P, P, P]),
         "orc_cache_create": (P, [P, I, I, I, I]),
+        "orc_cache_fill_synthetic": (I, [P, I, U64, U32]),
+        "orc_model_set_tp": (I, [P, I]),
         "orc_cache_free": (None, [P]),
         "orc_cache_len": (I, [P, I]),
         "orc_cache_set_position": (None, [P, I, I]),

@@ -176,3 +176,95 @@ def test_batched_verify_logits_tensor_core(lmx, models, mma_threshold, bits):
                 O.lib().orc_cache_set_position(oc, b, pos)
     lmx.call("lmx_cache_free", gc)
     O.lib().orc_cache_free(oc)
+
+
+def test_llama_rope_scaled_forward_bit_exact(lmx, cuda, mma_threshold):
+    # Llama-style decoder (no q/k norm, tied embedding) with Llama-3 RoPE
+    # frequency scaling (factor 32, original context 64 so the scaled and
+    # interpolated bands both occur inside 128 dims); exact mode
+    mma_threshold(0)
+    cfg = dict(hidden=512, layers=2, inter=1024, heads=8, kv_heads=2, head_dim=128, vocab=1000,
+               rope_theta=5e5, eps=1e-5, qk_norm=0, tied=1, bits=4, group_size=64,
+               rope_factor=32.0, rope_low_freq=1.0, rope_high_freq=4.0, rope_orig_max_pos=64.0)
+    g = lmx.Model(cfg, 77)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), 77)
+    L, V, B, cap = cfg["layers"], cfg["vocab"], 2, 96
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, cap, 8, 40, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, cap, 8)
+    rng = np.random.RandomState(5)
+    for T in (40, 5, 1):
+        tok = rng.randint(0, V, (B, T)).astype(np.int32)
+        gl = np.zeros((B, T, V), np.uint16)
+        ol = np.zeros((B, T, V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+        np.testing.assert_array_equal(gl, ol)
+    lmx.call("lmx_cache_free", gc)
+    O.lib().orc_cache_free(oc)
+    g.close()
+    O.lib().orc_model_free(o)
+
+
+LLAMA_TINY = dict(hidden=512, layers=2, inter=1024, heads=8, kv_heads=2, head_dim=128, vocab=1024,
+                  rope_theta=5e5, eps=1e-5, qk_norm=0, tied=0, bits=4, group_size=64)
+LLAMA_DRAFT = dict(LLAMA_TINY, layers=1, tied=1)
+
+
+@pytest.mark.parametrize("kv_bits", [16, 8, 4])
+def test_synthetic_context_forward_bit_exact(lmx, cuda, mma_threshold, kv_bits):
+    # lmx_cache_fill_synthetic == orc_cache_fill_synthetic (Philox normal,
+    # quantized like an append), then forwards on top of the 70-row context
+    mma_threshold(0)
+    cfg = LLAMA_TINY
+    g = lmx.Model(cfg, 31)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), 31)
+    L, V, B, cap, ctx = cfg["layers"], cfg["vocab"], 3, 128, 70
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, cap, kv_bits, 8, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, cap, kv_bits)
+    lmx.call("lmx_cache_fill_synthetic", gc, ctx, 99, 0x40000000)
+    assert O.lib().orc_cache_fill_synthetic(oc, ctx, 99, 0x40000000) == 0
+    rng = np.random.RandomState(kv_bits)
+    for T in (8, 5, 1):
+        tok = rng.randint(0, V, (B, T)).astype(np.int32)
+        gl = np.zeros((B, T, V), np.uint16)
+        ol = np.zeros((B, T, V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+        np.testing.assert_array_equal(gl, ol)
+    n = C.c_int()
+    lmx.call("lmx_cache_len", gc, 0, C.byref(n))
+    assert n.value == ctx + 14
+    lmx.call("lmx_cache_free", gc)
+    O.lib().orc_cache_free(oc)
+    g.close()
+    O.lib().orc_model_free(o)
+
+
+def test_synthetic_context_spec_stream_matches_oracle(lmx, cuda, mma_threshold):
+    # config-5-shaped session in miniature: Llama target, separate Llama
+    # draft, greedy, 8-bit KV, a synthetic context before the prompt
+    mma_threshold(0)
+    tg = lmx.Model(LLAMA_TINY, 41)
+    dg = lmx.Model(LLAMA_DRAFT, 42)
+    to = O.lib().orc_model_create(C.byref(oracle_cfg(LLAMA_TINY)), 41)
+    do = O.lib().orc_model_create(C.byref(oracle_cfg(LLAMA_DRAFT)), 42)
+    B, P, K, MT, ctx = 4, 12, 4, 40, 150
+    prompts = np.random.RandomState(3).randint(0, LLAMA_TINY["vocab"], (B, P)).astype(np.int32)
+    sd = lmx.SpecDecoder(tg, dg, 1, B, K, MT, P, kv_bits=8, context_len=ctx, context_seed=11)
+    sd.prefill(prompts)
+    sd.decode()
+    got, stats = sd.result()
+    sd.close()
+    out = np.zeros((B, MT), np.int32)
+    st = np.zeros(5, np.int64)
+    prm = O.SpecParams(K=K, max_tokens=MT, temperature=0.0, top_p=1.0, seed=0, draft_layers=1,
+                       context_len=ctx, context_seed=11)
+    assert O.lib().orc_spec_generate(to, do, O.ptr(prompts), B, P, prm, 8, O.ptr(out), O.ptr(st)) == 0
+    np.testing.assert_array_equal(got, out)
+    assert stats["accepted"] == st[2]
+    for m in (tg, dg):
+        m.close()
+    O.lib().orc_model_free(to)
+    O.lib().orc_model_free(do)
