@@ -62,6 +62,13 @@ WORKLOADS = {
                                            K=5, batch=8, prompt=512, new=512, kv_bits=4,
                                            temperature=0.7, top_p=0.9, cpu_prompt=32, cpu_steps=3, steps=5,
                                            profile="verify_pass_qwen3_8b_k5_bs8.md"),
+    # tensor-parallel over the N GPUs (strong scaling); the draft
+    # runs replicated on every rank.  The 8192-token random prefix is an
+    # 8160-row synthetic KV context plus a 32-token random prompt.
+    "llama3-70b-draft1b-k4-bs16-ctx8k-tp": dict(arch="LLAMA3_70B", draft="LLAMA32_1B", draft_layers=16,
+                                                K=4, batch=16, prompt=32, context=8160, new=64, kv_bits=8,
+                                                temperature=0.0, top_p=1.0, cpu_prompt=None, steps=3,
+                                                tp=True, profile="verify_pass_llama3_70b_k4_bs16.md"),
 }
 DEFAULT_WORKLOAD = "qwen3-8b-draft0.6b-k5-bs8-t0.7"
 METRIC = "accepted tokens/s (4-bit spec decode, bs1/bs8); verify-pass HBM GB/s vs 8 TB/s"
@@ -196,6 +203,61 @@ def cpu_sample(wl, prompts, lmx_cfg, draft_cfg, seed, steps, warmup):
                 cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup, prompt=p.shape[1])
 
 
+def cpu_sample_composed(wl, arch, darch, seed, reps, tokens_per_step):
+    """Bounded CPU sample of a workload too large for the host (configs[4]:
+    80 layers of 8192-wide weights): the oracle times one decoder layer of
+    the full-size target at the verify shape (M = B(K+1)) over the full
+    synthetic context, with and without its lm_head, and the same for one
+    draft layer at M = B; a speculative step is composed as
+    L_t * layer_t + head_t + K (L_d * layer_d + head_d), and tokens/s =
+    tokens_per_step * B / step."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    L = O.lib()
+    L.orc_set_mma_min_m(0)
+    B, K, ctx = wl["batch"], wl["K"], wl.get("context", 0) + wl["prompt"]
+    rng = np.random.RandomState(seed)
+
+    def layer_times(c, T, sd, tid_base):
+        cfg = dict(c, layers=1)
+        cfg["group"] = cfg.pop("group_size")
+        m = L.orc_model_create(C.byref(O.ModelCfg(**cfg)), sd)
+        oc = L.orc_cache_create(m, 1, B, ctx + (2 * reps + 2) * T + 8, wl["kv_bits"])
+        L.orc_cache_fill_synthetic(oc, ctx, seed, tid_base)
+        logits = np.zeros((B, T, c["vocab"]), np.uint16)
+        out = []
+        for with_head in (False, True):
+            for i in range(reps + 1):  # the first forward is warm-up
+                tok = rng.randint(0, c["vocab"], (B, T)).astype(np.int32)
+                t0 = time.perf_counter()
+                L.orc_forward(m, oc, 1, O.ptr(tok), B, T, O.ptr(logits) if with_head else None)
+                dt = time.perf_counter() - t0
+                if i:
+                    out.append((with_head, dt))
+        L.orc_cache_free(oc)
+        L.orc_model_free(m)
+        body = statistics.median([d for h, d in out if not h])
+        head = max(0.0, statistics.median([d for h, d in out if h]) - body)
+        return body, head
+
+    t0 = time.time()
+    tl, th = layer_times(arch, K + 1, seed, 0x40000000)
+    dl, dh = layer_times(darch, 1, seed + 1, 0x50000000)
+    step = arch["layers"] * tl + th + K * (wl["draft_layers"] * dl + dh)
+    L.orc_set_mma_min_m(16)
+    return dict(value=tokens_per_step * B / step, step_s=step, layer_s=tl, head_s=th, dlayer_s=dl,
+                dhead_s=dh, cores=L.orc_threads(), wall_s=time.time() - t0)
+
+
+def cpu_composed_sample_text(wl, arch, r, tps):
+    return (f"oracle/ C++ restatement, {r['cores']} threads: one full-size target layer at "
+            f"M={wl['batch'] * (wl['K'] + 1)} over a {wl['context'] + wl['prompt']}-row context "
+            f"({r['layer_s'] * 1e3:.0f} ms) x {arch['layers']} + lm_head ({r['head_s'] * 1e3:.0f} ms) + "
+            f"K={wl['K']} x (draft layer {r['dlayer_s'] * 1e3:.0f} ms x {wl['draft_layers']} + draft head "
+            f"{r['dhead_s'] * 1e3:.0f} ms) = {r['step_s']:.2f} s per step at {tps:.3f} tokens per "
+            f"sequence-step ({r['wall_s']:.0f} s of CPU sampling)")
+
+
 def run_reference(args, wl, world, rank):
     if rank != 0:
         return 0
@@ -203,6 +265,25 @@ def run_reference(args, wl, world, rank):
     arch = getattr(lmx, wl["arch"])
     darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     prompts = np.random.RandomState(args.seed).randint(0, arch["vocab"], (wl["batch"], wl["prompt"]))
+    if wl.get("tp"):
+        # composed sample; a step emits at least one token per sequence (the
+        # lower bound is used: no device run here to measure acceptance)
+        r = cpu_sample_composed(wl, arch, darch, args.seed, max(1, args.steps), 1.0)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * r["step_s"], 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "batch": wl["batch"], "K": wl["K"],
+                       "prompt": wl["prompt"], "context": wl["context"] + wl["prompt"],
+                       "new_tokens": wl["new"], "kv_bits": wl["kv_bits"]},
+            "cpu_baseline": {"value": round(r["value"], 4), "unit": "tokens/s", "cores": r["cores"],
+                             "kind": "port", "sample": cpu_composed_sample_text(wl, arch, r, 1.0)},
+            "e2e": {"value": round(r["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
     # each timed step is one speculative step of the same decode (bounded sample)
     r = cpu_sample(wl, prompts, arch, darch, args.seed, args.steps, args.warmup)
     line = {
@@ -230,14 +311,20 @@ def run_lmx(args, wl, world, rank, local):
     lmx.call("lmx_set_device", local)
     arch = getattr(lmx, wl["arch"])
     darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
-    target = lmx.Model(arch, args.seed)
+    tp = bool(wl.get("tp"))
+    B, P, ctx = wl["batch"], wl["prompt"], wl.get("context", 0)
+    comm = None
+    if tp and world > 1:  # one shard per rank; handles exchanged over the process group
+        comm = lmx.TpComm.from_process_group(max_rows=B * 32, max_hidden=arch["hidden"])
+    target = lmx.Model(arch, args.seed, comm=comm)
     # separate draft model (seed + 1) or the target's first layers (self-draft)
     draft = lmx.Model(darch, args.seed + 1) if darch else None
-    B, P = wl["batch"], wl["prompt"]
-    prompts = np.random.RandomState(args.seed + rank).randint(0, arch["vocab"], (B, P)).astype(np.int32)
+    # data parallel: each rank its own sequences; tensor parallel: the same
+    prompts = np.random.RandomState(args.seed + (0 if tp else rank)).randint(
+        0, arch["vocab"], (B, P)).astype(np.int32)
     sd = lmx.SpecDecoder(target, draft, wl["draft_layers"], B, wl["K"], wl["new"], P,
                          kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
-                         seed=args.seed)
+                         seed=args.seed, context_len=ctx, context_seed=args.seed)
 
     if args.profile_verify or args.profile_draft:
         # prefill only (KV cache at the prompt length), then N verify passes
@@ -250,6 +337,9 @@ def run_lmx(args, wl, world, rank, local):
             sd.profile(1, args.profile_draft)
         sd.close()
         target.close()
+        if comm is not None:
+            barrier(world)
+            comm.close()
         return 0
 
     def one():
@@ -285,7 +375,8 @@ def run_lmx(args, wl, world, rank, local):
     hsec, hbytes = sd.profile(3, 20)
     L = arch["layers"]
     wall_m, dec_m = reduce(world, [wall, dec], "max")
-    toks_all = int(reduce(world, [float(toks)], "sum")[0])
+    # tensor parallel: every rank emits the same tokens
+    toks_all = toks if tp else int(reduce(world, [float(toks)], "sum")[0])
     peak, peak_kind = peaks()
     traffic = None
     try:
@@ -300,16 +391,19 @@ def run_lmx(args, wl, world, rank, local):
         "metric": METRIC, "value": round(toks_all / dec_m, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * wall_m / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": args.workload, "batch": B, "K": wl["K"], "prompt": P,
                    "new_tokens": wl["new"], "kv_bits": wl["kv_bits"], "weights": "4-bit g64",
+                   "context": ctx + P,
                    "draft": wl["draft"] or f"target's first {wl['draft_layers']} layers",
                    "temperature": wl["temperature"], "top_p": wl["top_p"],
-                   "parallelism": f"dp{world} (independent sequences per rank)",
+                   "parallelism": (f"tp{world} (target sharded, draft replicated)" if tp
+                                   else f"dp{world} (independent sequences per rank)"),
                    "l2": f"weights ({vbytes / 1e6:.0f} MB per verify pass) exceed L2; no flush"},
         "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * wl["new"] * 4 + 40},
-        "roofline": {"bound": "hbm", "kernel": f"verify pass ({L} layers + lm_head, M={B * (wl['K'] + 1)})",
+        "roofline": {"bound": "hbm", "kernel": f"verify pass ({L} layers + lm_head, M={B * (wl['K'] + 1)}"
+                                               + (f", per rank of tp{world})" if tp and world > 1 else ")"),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "frac_of_8000": round(achieved / 8000.0, 4),
@@ -321,7 +415,12 @@ def run_lmx(args, wl, world, rank, local):
                        "tokens_per_step": round(toks / max(1, steps), 3)},
         "clocks": ck, "gpu_launches": int(gpu_launches),
     }
-    if world == 1 and rank == 0 and not args.no_cpu:
+    if world == 1 and rank == 0 and not args.no_cpu and tp:
+        tps = toks / max(1, steps)
+        r = cpu_sample_composed(wl, arch, darch, args.seed, 2, tps)
+        res["cpu_baseline"] = {"value": round(r["value"], 4), "unit": "tokens/s", "cores": r["cores"],
+                               "kind": "port", "sample": cpu_composed_sample_text(wl, arch, r, tps)}
+    elif world == 1 and rank == 0 and not args.no_cpu:
         r = cpu_sample(wl, prompts, arch, darch, args.seed, args.cpu_steps, 1)
         res["cpu_baseline"] = {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
                                "kind": "port",
@@ -334,6 +433,9 @@ def run_lmx(args, wl, world, rank, local):
     if draft is not None:
         draft.close()
     target.close()
+    if comm is not None:
+        barrier(world)
+        comm.close()
     return 0
 
 
