@@ -310,6 +310,8 @@ def run_lmx(args, wl, world, rank, local):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", local)
     arch = getattr(lmx, wl["arch"])
+    if args.layers:
+        arch = dict(arch, layers=args.layers)
     darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     tp = bool(wl.get("tp"))
     B, P, ctx = wl["batch"], wl["prompt"], wl.get("context", 0)
@@ -491,6 +493,77 @@ def qmm_time(lmx, N, K, M, bits, seed=2026):
                 path="tcgen05" if M >= lmx.lib().lmx_mma_min_m() > 0 else "gemv")
 
 
+def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):
+    """Device time of one lmx_sdpa_decode launch over an affine (4/8-bit) or
+    bf16 cache with every sequence at length cap - T (uniform random codes,
+    scales |N(0,0.2)|/(2^bits-1), biases N(0,1)): R launches over R cache
+    copies (together > 2x L2) captured in one CUDA graph."""
+    import torch
+    torch.cuda.init()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    D = 128
+    rows = B * Hk * cap
+    row_bytes = D * 2 if bits == 16 else D * bits // 8 + 8
+    cbytes = 2 * rows * row_bytes
+    R = max(1, min(16, (320 << 20) // cbytes))
+    keep, descs = [], []
+    lens = torch.full((B,), cap - T, dtype=torch.int32, device="cuda")
+    for _ in range(R):
+        d = lmx.KvDesc(batch=B, kv_heads=Hk, head_dim=D, capacity=cap, bits=bits, lengths=lens.data_ptr())
+        if bits == 16:
+            k = torch.randn(rows * D, device="cuda", generator=gen).to(torch.bfloat16)
+            v = torch.randn(rows * D, device="cuda", generator=gen).to(torch.bfloat16)
+            d.k, d.v = k.data_ptr(), v.data_ptr()
+            keep += [k, v]
+        else:
+            t = [torch.randint(-2**31, 2**31 - 1, (rows * D * bits // 32,), dtype=torch.int32, device="cuda",
+                               generator=gen) for _ in range(2)]
+            sc = [(torch.randn(rows * 2, device="cuda", generator=gen).abs() * (0.2 / (2**bits - 1)))
+                  .to(torch.bfloat16) for _ in range(2)]
+            bi = [torch.randn(rows * 2, device="cuda", generator=gen).to(torch.bfloat16) for _ in range(2)]
+            d.k_packed, d.v_packed = t[0].data_ptr(), t[1].data_ptr()
+            d.k_scales, d.v_scales = sc[0].data_ptr(), sc[1].data_ptr()
+            d.k_biases, d.v_biases = bi[0].data_ptr(), bi[1].data_ptr()
+            keep += t + sc + bi
+        descs.append(d)
+    q = torch.randn(B * T * Hq * D, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    nbytes = lmx.lib().lmx_sdpa_scratch_bytes(B, T, Hq, Hk, cap)
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.Stream()
+    S = C.c_void_p(st.cuda_stream)
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+
+    def run():
+        for d in descs:
+            lmx.call("lmx_sdpa_decode", q.data_ptr(), C.byref(d), T, Hq, scale, scratch.data_ptr(), nbytes,
+                     out.data_ptr(), S)
+
+    with torch.cuda.stream(st):
+        run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        run()
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3 / R)
+    t = statistics.median(ts)
+    del g
+    byts = 2 * B * Hk * cap * row_bytes + 2 * B * T * Hq * D * 2  # every row is visible (lengths cap - T)
+    G = Hq // Hk
+    return dict(B=B, T=T, Hq=Hq, Hk=Hk, cap=cap, bits=bits, us=round(t * 1e6, 2), GBs=round(byts / t / 1e9, 1),
+                path="tensor-core" if G * T >= lmx.lib().lmx_mma_min_m() > 0 else "cuda-core")
+
+
 def run_qmm(args):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", 0)
@@ -526,13 +599,26 @@ def main():
     ap.add_argument("--profile-draft", type=int, default=0,
                     help="only prefill the workload and run N single-token draft forwards inside the "
                          "NVTX range lmx_draft_token (for ncu --nvtx-include)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="with --profile-verify / --profile-draft only: build the target with this many "
+                         "layers (same per-layer shapes; a small case for ncu captures)")
     ap.add_argument("--qmm-sweep", action="store_true",
                     help="op-level quantized_matmul sweep (BASELINE configs[1]) instead of decoding")
     ap.add_argument("--qmm", default="", help="one op-level shape N,K,M,bits (e.g. for ncu)")
+    ap.add_argument("--sdpa", default="", help="one op-level attention shape B,T,Hq,Hk,cap,bits (e.g. "
+                                               "16,5,64,8,8300,8 = one Llama-3-70B verify layer)")
     args = ap.parse_args()
     if args.qmm_sweep or args.qmm:
         return run_qmm(args)
+    if args.sdpa:
+        lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+        lmx.call("lmx_set_device", 0)
+        B, T, Hq, Hk, cap, bits = [int(v) for v in args.sdpa.split(",")]
+        print(json.dumps(sdpa_time(lmx, B, T, Hq, Hk, cap, bits)), flush=True)
+        return 0
     wl = WORKLOADS[args.workload]
+    if args.layers and not (args.profile_verify or args.profile_draft):
+        ap.error("--layers is only for the profiling runs")
     if args.steps is None:
         args.steps = wl.get("steps", 10)
     if args.cpu_steps is None:

@@ -119,7 +119,8 @@ typedef struct {
   int bits;                 /* 16 = bf16 cache, 8 or 4 = affine quantized      */
   void* k;                  /* bits 16: bf16 [batch][kv_heads][capacity][128]  */
   void* v;
-  uint32_t* k_packed;       /* bits 4/8: [batch][kv_heads][capacity][128*bits/32] */
+  uint32_t* k_packed;       /* bits 4/8: [batch][kv_heads][capacity][128*bits/32],
+                             * 16-byte aligned (k, v and the packed arrays)   */
   uint32_t* v_packed;
   void* k_scales;           /* bits 4/8: bf16 [batch][kv_heads][capacity][2]   */
   void* k_biases;

@@ -188,6 +188,9 @@ struct SdpaArgs {
   float* part;            // scratch partials
   unsigned* counters;     // scratch counters
   bf16_t* out;            // [B*T, Hq*D]
+  size_t part_floats;     // capacity of part (floats), checked by the launcher
+  size_t n_counters;      // capacity of counters
+  unsigned* err;          // device error word (bounded waits of the tensor-core path)
 };
 
 static constexpr int kPartStride = kHeadDim + 2;  // m, l, o[128]

@@ -44,8 +44,85 @@ static int launch_sdpa_t(const SdpaArgs& a, int B, cudaStream_t st) {
                     "sdpa: launch");
 }
 
-static int launch_sdpa(const SdpaArgs& a, int B, cudaStream_t st) {
-  const int rows = (a.Hq / a.kv.Hk) * a.T;
+static constexpr int kSdpaLongCache = 2048;  // cache rows from which every block takes the tensor-core SDPA
+
+// Tensor-core SDPA geometry (attn_mma.cuh): row tiles of 16*MT <= 64 rows,
+// splits of cpc 128-key chunks, about 4 CTAs per SM over the capacity.
+struct SdpaMmaPlan {
+  int MT = 1, tiles = 1, nsplit = 1, cpc = 1;
+};
+static SdpaMmaPlan sdpa_mma_plan(int B, int Hk, int rows, int cap) {
+  SdpaMmaPlan p;
+  const int r = rows < kAttnMmaRows ? rows : kAttnMmaRows;
+  p.MT = (r + 15) / 16;
+  p.tiles = (rows + 16 * p.MT - 1) / (16 * p.MT);
+  const int chunks = (cap + kAttnChunk - 1) / kAttnChunk;
+  const int base = B * Hk * p.tiles;
+  const int want = std::max(1, (4 * device_sms() + base - 1) / base);
+  p.cpc = std::max(1, (chunks + want - 1) / want);
+  p.nsplit = (chunks + p.cpc - 1) / p.cpc;
+  return p;
+}
+
+// Scratch (floats / counters) that covers both SDPA paths for up to Tmax
+// query tokens per sequence.
+static void sdpa_scratch_need(int B, int Tmax, int G, int Hk, int cap, size_t& part_floats, size_t& counters) {
+  const int chunks = (cap + kSplit - 1) / kSplit;
+  const size_t rows32 = (size_t)((G * Tmax + kRowTile - 1) / kRowTile) * kRowTile;
+  const size_t rows64 = (size_t)((G * Tmax + kAttnMmaRows - 1) / kAttnMmaRows) * kAttnMmaRows;
+  part_floats = (size_t)B * Hk * chunks * kPartStride * std::max(rows32, rows64);
+  counters = (size_t)B * Hk * ((G * Tmax + kRowTile - 1) / kRowTile);
+}
+
+template <int MT, int BITS>
+static int launch_sdpa_mma_tb(const SdpaArgs& a, int B, int cpc, cudaStream_t st) {
+  static bool attr_set[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (!attr_set[d & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(sdpa_mma_kernel<MT, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sdpa_mma_smem<MT, BITS>()),
+                        "sdpa_mma: set smem");
+    if (rc) return rc;
+    attr_set[d & 63] = true;
+  }
+  return cuda_check(lmx_launch(sdpa_mma_kernel<MT, BITS>, dim3(a.nsplit * a.tiles, a.kv.Hk, B), dim3(kAttnThreads),
+                               sdpa_mma_smem<MT, BITS>(), st, true, a, cpc),
+                    "sdpa_mma: launch");
+}
+template <int MT>
+static int launch_sdpa_mma_t(const SdpaArgs& a, int B, int cpc, cudaStream_t st) {
+  if (a.kv.bits == 8) return launch_sdpa_mma_tb<MT, 8>(a, B, cpc, st);
+  if (a.kv.bits == 4) return launch_sdpa_mma_tb<MT, 4>(a, B, cpc, st);
+  return launch_sdpa_mma_tb<MT, 16>(a, B, cpc, st);
+}
+
+static int launch_sdpa(const SdpaArgs& a_in, int B, cudaStream_t st) {
+  const int rows = (a_in.Hq / a_in.kv.Hk) * a_in.T;
+  // tensor-core kernel (unless in exact mode): blocks of >= threshold query
+  // rows per KV head (verify), and any block over a long cache, where its
+  // bulk-copy pipeline streams the cache far faster than the canonical
+  // kernel's per-split loads
+  if (qmm_uses_mma(rows) || (qmm_mma_min_m() > 0 && a_in.kv.cap >= kSdpaLongCache)) {
+    SdpaArgs a = a_in;
+    const SdpaMmaPlan p = sdpa_mma_plan(B, a.kv.Hk, rows, a.kv.cap);
+    a.err = device_error_word();
+    a.tiles = p.tiles;
+    a.nsplit = p.nsplit;
+    if ((size_t)B * a.kv.Hk * p.tiles * p.nsplit * kAttnMmaRows * kPartStride > a.part_floats ||
+        (size_t)B * a.kv.Hk * p.tiles > a.n_counters)
+      return set_error(LMX_ERR_INVALID, "sdpa: scratch too small for the tensor-core path");
+    switch (p.MT) {
+      case 1: return launch_sdpa_mma_t<1>(a, B, p.cpc, st);
+      case 2: return launch_sdpa_mma_t<2>(a, B, p.cpc, st);
+      case 3: return launch_sdpa_mma_t<3>(a, B, p.cpc, st);
+      default: return launch_sdpa_mma_t<4>(a, B, p.cpc, st);
+    }
+  }
+  const SdpaArgs& a = a_in;
+  if ((size_t)B * a.kv.Hk * a.tiles * a.nsplit * kRowTile * kPartStride > a.part_floats ||
+      (size_t)B * a.kv.Hk * a.tiles > a.n_counters)
+    return set_error(LMX_ERR_INVALID, "sdpa: scratch too small");
   const int half = ((rows < kRowTile ? rows : kRowTile) + 1) / 2;  // rows per thread needed
   if (half <= 1) return launch_sdpa_t<1>(a, B, st);
   if (half <= 2) return launch_sdpa_t<2>(a, B, st);
@@ -474,6 +551,7 @@ static constexpr int kPrefillChunk = 32;
 
 struct Workspace {
   int Rmax = 0, tiles = 0, splits = 0, B = 0, Hk = 0;
+  size_t part_floats = 0, n_counters = 0;
   bf16_t *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *o = nullptr, *act = nullptr,
          *logits = nullptr;
   float* part = nullptr;
@@ -498,9 +576,9 @@ static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_
   if (!rc) rc = ws.ar.alloc(&ws.o, (size_t)R * NQ);
   if (!rc) rc = ws.ar.alloc(&ws.act, (size_t)R * m.il);
   if (!rc) rc = ws.ar.alloc(&ws.logits, (size_t)logit_rows * m.vl);
-  if (!rc)
-    rc = ws.ar.alloc(&ws.part, (size_t)B * m.hk * ws.tiles * ws.splits * kRowTile * kPartStride, false);
-  if (!rc) rc = ws.ar.alloc(&ws.counters, (size_t)B * m.hk * ws.tiles);
+  sdpa_scratch_need(B, Tmax, G, m.hk, cap, ws.part_floats, ws.n_counters);
+  if (!rc) rc = ws.ar.alloc(&ws.part, ws.part_floats, false);
+  if (!rc) rc = ws.ar.alloc(&ws.counters, ws.n_counters);
   return rc;
 }
 
@@ -589,6 +667,9 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     sa.tiles = tiles;
     sa.part = ws.part;
     sa.counters = ws.counters;
+    sa.part_floats = ws.part_floats;
+    sa.n_counters = ws.n_counters;
+    sa.err = device_error_word();
     sa.out = ws.o;
     if (!rc) rc = launch_sdpa(sa, B, st);
 
@@ -1250,6 +1331,8 @@ static int kv_from_c(const lmx_kv* c, KvDesc& d) {
   } else if (c->bits == 4 || c->bits == 8) {
     if (!c->k_packed || !c->v_packed || !c->k_scales || !c->k_biases || !c->v_scales || !c->v_biases)
       return set_error(LMX_ERR_INVALID, "lmx_kv: packed cache pointers missing");
+    if (((uintptr_t)c->k_packed | (uintptr_t)c->v_packed) & 15)
+      return set_error(LMX_ERR_INVALID, "lmx_kv: packed k/v must be 16-byte aligned");
     d.kq = c->k_packed;
     d.vq = c->v_packed;
     d.ks = (bf16_t*)c->k_scales;
@@ -1269,11 +1352,9 @@ static void sdpa_geometry(int T, int heads, int kv_heads, int capacity, int& til
 }
 
 static size_t sdpa_scratch_bytes(int B, int T, int heads, int kv_heads, int capacity) {
-  int tiles, splits;
-  sdpa_geometry(T, heads, kv_heads, capacity, tiles, splits);
-  const size_t part = (size_t)B * kv_heads * tiles * splits * kRowTile * kPartStride * 4;
-  const size_t ctr = (size_t)B * kv_heads * tiles * 4;
-  return (part + 255) / 256 * 256 + (ctr + 255) / 256 * 256;
+  size_t pf = 0, nc = 0;
+  sdpa_scratch_need(B, T, heads / kv_heads, kv_heads, capacity, pf, nc);
+  return (pf * 4 + 255) / 256 * 256 + (nc * 4 + 255) / 256 * 256;
 }
 
 // Shared by lmx_sdpa_decode and its no-allocation variant: checks the shape
@@ -1300,8 +1381,8 @@ static int sdpa_call(const void* q, const lmx_kv* kv, int T, int heads, float sc
   sa.nsplit = splits;
   sa.tiles = tiles;
   sa.part = (float*)scratch;
-  const size_t part = (size_t)d.B * d.Hk * tiles * splits * kRowTile * kPartStride * 4;
-  sa.counters = (unsigned*)((char*)scratch + (part + 255) / 256 * 256);
+  sdpa_scratch_need(d.B, T, heads / d.Hk, d.Hk, d.cap, sa.part_floats, sa.n_counters);
+  sa.counters = (unsigned*)((char*)scratch + (sa.part_floats * 4 + 255) / 256 * 256);
   sa.out = (bf16_t*)out;
   return launch_sdpa(sa, d.B, st);
 }

@@ -14,6 +14,7 @@
 #include "qmm.cuh"
 #include "qmm_mma.cuh"
 #include "attn.cuh"
+#include "attn_mma.cuh"
 #include "engine_kernels.cuh"
 #include "sample.cuh"
 #include "tp.cuh"
@@ -586,11 +587,10 @@ extern "C" int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, i
                      "sdpa_noalloc: this shape needs %zu bytes of scratch; the built-in array holds %zu "
                      "(use lmx_sdpa_decode with caller scratch)",
                      need, kNoAllocScratchBytes);
-  int tiles, splits;
-  sdpa_geometry(T, heads, d.Hk, d.cap, tiles, splits);
-  const size_t part = (size_t)d.B * d.Hk * tiles * splits * kRowTile * kPartStride * 4;
-  const size_t ctr_off = (part + 255) / 256 * 256;
-  rc = cuda_check(cudaMemsetAsync((char*)scratch + ctr_off, 0, (size_t)d.B * d.Hk * tiles * 4, (cudaStream_t)stream),
+  size_t part_floats = 0, n_counters = 0;
+  sdpa_scratch_need(d.B, T, heads / d.Hk, d.Hk, d.cap, part_floats, n_counters);
+  const size_t ctr_off = (part_floats * 4 + 255) / 256 * 256;
+  rc = cuda_check(cudaMemsetAsync((char*)scratch + ctr_off, 0, n_counters * 4, (cudaStream_t)stream),
                   "sdpa_noalloc: clear counters");
   if (rc) return rc;
   return sdpa_call(q, kv, T, heads, scale, scratch, kNoAllocScratchBytes, out, (cudaStream_t)stream);

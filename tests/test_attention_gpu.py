@@ -1,5 +1,7 @@
-"""lmx_sdpa_decode (K2) vs the oracle's SDPA over the same cache: bit-exact for
-bf16 and for 8/4-bit affine caches (dequantized the same way on both sides)."""
+"""lmx_sdpa_decode (K2) vs the oracle's SDPA over the same cache.  Exact mode
+(tensor-core threshold 0): bit-exact for bf16 and for 8/4-bit affine caches
+(dequantized the same way on both sides).  Tensor-core mode (blocks of >= 16
+query rows per KV head on mma.sync): within a tolerance."""
 import ctypes as C
 import math
 
@@ -64,9 +66,10 @@ def oracle_attention(q, kd, vd, lens, T, Hq, Hk, cap, scale):
 @pytest.mark.parametrize("bits", [16, 8, 4])
 @pytest.mark.parametrize("T,Hq,Hk,cap", [(1, 16, 8, 420), (5, 16, 8, 420), (6, 32, 8, 420), (40, 4, 2, 420),
                                          (1, 16, 8, 3300), (6, 32, 8, 3300)])
-def test_sdpa_decode_bit_exact(lmx, cuda, bits, T, Hq, Hk, cap):
+def test_sdpa_decode_bit_exact(lmx, cuda, mma_threshold, bits, T, Hq, Hk, cap):
     # cap 420: 4 splits of 128 keys; cap 3300: 26 splits (long cache, the
     # combine over many partials)
+    mma_threshold(0)
     rng = np.random.RandomState(bits * 100 + T)
     B = 3
     lens = np.array([0, 123, cap - T - 1][:B], np.int32)
@@ -100,3 +103,45 @@ def test_sdpa_decode_rejects_small_scratch(lmx, cuda):
     rc = lmx.lib().lmx_sdpa_decode(q.data_ptr(), C.byref(desc), 1, 16, 0.088, q.data_ptr(), 16,
                                    q.data_ptr(), None)
     assert rc == 1 and b"scratch" in lmx.lib().lmx_last_error()
+
+
+@pytest.mark.parametrize("bits", [16, 8, 4])
+@pytest.mark.parametrize("T,Hq,Hk,cap", [(5, 64, 8, 8300), (6, 32, 8, 1100), (40, 4, 2, 420),
+                                         (2, 16, 2, 300), (5, 8, 1, 700), (1, 32, 8, 2100),
+                                         (1, 16, 8, 3000)])
+def test_sdpa_tensor_core_within_tolerance(lmx, cuda, mma_threshold, bits, T, Hq, Hk, cap):
+    # G*T query rows per KV head: 40 (Llama-3-70B verify, 8k cache), 24
+    # (Qwen3-8B verify), 80 (two row tiles), 16 (one m16 tile), 40 with a
+    # single KV head; and single-token decode (4 and 2 rows) over caches of
+    # >= 2048 rows, which also take the tensor-core kernel.  Tolerance: the
+    # products accumulate in the tensor core's order, exponentials come from
+    # the hardware ex2 and p keeps ~16 bits -> at most a few bf16 ulps.
+    mma_threshold(16)
+    rng = np.random.RandomState(bits * 7 + T + Hq)
+    B = 3
+    lens = np.array([0, 123, cap - T - 1], np.int32)
+    host, kd, vd = make_cache(rng, B, Hk, cap, bits)
+    dev = {k: to_dev(cuda, v) for k, v in host.items()}
+    dlen = to_dev(cuda, lens)
+    q = O.gen_normal_bf16(rng.randint(1 << 30), 3, 1.0, B * T * Hq * D).reshape(B, T, Hq, D)
+    dq = to_dev(cuda, q)
+    out = cuda.empty((B, T, Hq, D), dtype=cuda.int16, device="cuda")
+    desc = kv_desc(lmx, dev, B, Hk, cap, bits, dlen)
+    nbytes = lmx.lib().lmx_sdpa_scratch_bytes(B, T, Hq, Hk, cap)
+    scratch = cuda.zeros(nbytes, dtype=cuda.uint8, device="cuda")
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    ref = O.bf16_to_f32(oracle_attention(q, kd, vd, lens, T, Hq, Hk, cap, np.float32(scale)))
+    first = None
+    for _ in range(2):  # deterministic, and the scratch is left ready
+        lmx.call("lmx_sdpa_decode", dq.data_ptr(), C.byref(desc), T, Hq, scale, scratch.data_ptr(), nbytes,
+                 out.data_ptr(), None)
+        cuda.cuda.synchronize()
+        got = out.cpu().numpy().view(np.uint16).copy()
+        g = O.bf16_to_f32(got)
+        tol = 1e-2 + np.abs(ref) * 2.0 ** -7
+        bad = np.abs(g - ref) > tol
+        assert not bad.any(), f"{int(bad.sum())} out of tolerance, max |diff| {np.abs(g - ref).max():.4g}"
+        if first is None:
+            first = got
+        else:
+            np.testing.assert_array_equal(got, first)

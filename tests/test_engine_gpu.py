@@ -59,11 +59,19 @@ def assert_logits_close(got, ref, what, kv_bits=16):
     # fp32 values to it.  With a 4-bit KV cache the bound is doubled: its
     # min/max quantizer is discontinuous, so a one-ulp difference in a K/V
     # projection can move a code by a whole quantization step (1/15 of the
-    # group's range) and the attention output with it.
+    # group's range) and the attention output with it.  Such flips are rare
+    # but unbounded in number by any fixed max-abs: with a 4-bit cache, at
+    # most 0.05% of the logits may exceed 4e-2 (+ ulp), and none 1e-1 (+ ulp).
     g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
-    tol = (4e-2 if kv_bits == 4 else 2e-2) + np.abs(r) * 2.0 ** -7
-    bad = np.abs(g - r) > tol
-    assert not bad.any(), f"{what}: {int(bad.sum())} logits out of tolerance, max |diff| {np.abs(g - r).max():.4g}"
+    ulp = np.abs(r) * 2.0 ** -7
+    diff = np.abs(g - r)
+    if kv_bits == 4:
+        over = int((diff > 4e-2 + ulp).sum())
+        assert over <= 5e-4 * diff.size and not (diff > 1e-1 + ulp).any(), \
+            f"{what}: {over} logits beyond 4e-2 (of {diff.size}), max |diff| {diff.max():.4g}"
+        return
+    bad = diff > 2e-2 + ulp
+    assert not bad.any(), f"{what}: {int(bad.sum())} logits out of tolerance, max |diff| {diff.max():.4g}"
 
 
 @pytest.mark.parametrize("bits", [4, 8])
@@ -268,3 +276,37 @@ def test_synthetic_context_spec_stream_matches_oracle(lmx, cuda, mma_threshold):
         m.close()
     O.lib().orc_model_free(to)
     O.lib().orc_model_free(do)
+
+
+def test_verify_blocks_tensor_core_attention(lmx, cuda, mma_threshold):
+    # G = 8 q heads per KV head (the Llama-3-70B layout): a 5-token verify
+    # block gives 40 query rows per KV head, so with the tensor-core
+    # threshold on, both the matmuls and SDPA run on the tensor cores, over a
+    # 700-row synthetic context (6 key chunks); logits within the contract's
+    # tolerance of the oracle (whose SDPA keeps the canonical fp32 order)
+    cfg = dict(LLAMA_TINY, heads=16, kv_heads=2)
+    g = lmx.Model(cfg, 51)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), 51)
+    L, V, B, cap, ctx = cfg["layers"], cfg["vocab"], 4, 768, 700
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, cap, 8, 8, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, cap, 8)
+    lmx.call("lmx_cache_fill_synthetic", gc, ctx, 5, 0x40000000)
+    assert O.lib().orc_cache_fill_synthetic(oc, ctx, 5, 0x40000000) == 0
+    rng = np.random.RandomState(8)
+    for i, T in enumerate((5, 5, 1, 5)):
+        mma_threshold(16)
+        tok = rng.randint(0, V, (B, T)).astype(np.int32)
+        gl = np.zeros((B, T, V), np.uint16)
+        ol = np.zeros((B, T, V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+        assert_logits_close(gl, ol, f"block {i}", 8)
+        if i == 1:  # roll back two sequences
+            for b, pos in ((0, ctx + 6), (2, ctx + 3)):
+                lmx.call("lmx_cache_set_position", gc, b, pos)
+                O.lib().orc_cache_set_position(oc, b, pos)
+    lmx.call("lmx_cache_free", gc)
+    O.lib().orc_cache_free(oc)
+    g.close()
+    O.lib().orc_model_free(o)
