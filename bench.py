@@ -564,6 +564,106 @@ def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):
                 path="tensor-core" if G * T >= lmx.lib().lmx_mma_min_m() > 0 else "cuda-core")
 
 
+def _graph_time(run, reps=5):
+    """Median device time of one replay of run() captured in a CUDA graph."""
+    import torch
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        run(st)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        run(st)
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3)
+    del g
+    return statistics.median(ts)
+
+
+def moe_time(lmx, M, H, I, E, k, bits, seed=2026):
+    """Device time of lmx_moe_experts (configuration 4's routed experts):
+    E experts of uniform random codes, top-k expert ids drawn per token; R
+    expert sets (together > 2x L2) rotated inside one graph.  Algorithmic
+    bytes = the unique experts touched x (gate + up + down packed weights and
+    scales / biases) + activations."""
+    import torch
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    rng = np.random.RandomState(seed)
+    per_expert = 3 * I * H * bits // 8 + 3 * I * (H // 64) * 4
+    R = max(1, min(8, (320 << 20) // (E * per_expert)))
+
+    def qw(N, K):
+        w = torch.randint(-2**31, 2**31 - 1, (E, N, K * bits // 32), dtype=torch.int32, device="cuda", generator=gen)
+        s = (torch.rand(E, N, K // 64, device="cuda", generator=gen) * 0.01 + 0.002).to(torch.bfloat16)
+        b = (-torch.rand(E, N, K // 64, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+        return (w, s, b), lmx.QWeights(w=w.data_ptr(), scales=s.data_ptr(), biases=b.data_ptr())
+
+    sets = [[qw(I, H), qw(I, H), qw(H, I)] for _ in range(R)]
+    idx_np = np.stack([rng.choice(E, k, replace=False) for _ in range(M)]).astype(np.int32)
+    idx = torch.from_numpy(idx_np).cuda()
+    w = torch.full((M, k), 1.0 / k, dtype=torch.float32, device="cuda")
+    x = torch.randn(M, H, device="cuda", generator=gen).to(torch.bfloat16)
+    act = torch.empty(M, k, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
+
+    def run(st):
+        for g3 in sets:
+            lmx.call("lmx_moe_experts", x.data_ptr(), M, H, I, E, k, idx.data_ptr(), w.data_ptr(), C.byref(g3[0][1]),
+                     C.byref(g3[1][1]), C.byref(g3[2][1]), bits, act.data_ptr(), y.data_ptr(),
+                     C.c_void_p(st.cuda_stream))
+
+    t = _graph_time(run) / R
+    uniq = len(set(idx_np.ravel().tolist()))
+    byts = uniq * per_expert + M * H * 2 * 2 + M * k * I * 2 * 2
+    return dict(op="moe_experts", M=M, H=H, I=I, E=E, k=k, bits=bits, unique_experts=uniq,
+                us=round(t * 1e6, 2), GBs=round(byts / t / 1e9, 1), bytes=byts)
+
+
+def gdn_time(lmx, B, T, Hk, Hv, seed=2026):
+    """Device time of lmx_gdn_verify + lmx_gdn_commit (configuration 4's
+    Gated DeltaNet layer core).  Algorithmic bytes = fp32 state read + T
+    snapshots written + the state rewritten by the commit + inputs / output."""
+    import torch
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    D = 128
+    CD = 2 * Hk * D + Hv * D
+    bf = lambda *s: (torch.randn(*s, device="cuda", generator=gen)).to(torch.bfloat16)
+    t_ = dict(qkv=bf(B, T, CD), z=bf(B, T, Hv * D), b=bf(B, T, Hv), a=bf(B, T, Hv), conv_w=bf(CD, 4) * 0.5,
+              a_log=torch.zeros(Hv, device="cuda"), dt_bias=bf(Hv), norm_w=torch.ones(D, dtype=torch.bfloat16,
+                                                                                      device="cuda"),
+              conv_state=bf(B, 3, CD), state=torch.randn(B, Hv, D, D, device="cuda", generator=gen) * 0.05,
+              snap=torch.empty(B, T, Hv, D, D, device="cuda"), out=torch.empty(B, T, Hv * D, dtype=torch.bfloat16,
+                                                                              device="cuda"))
+    t_["scratch"] = torch.empty(lmx.lib().lmx_gdn_scratch_bytes(B, T, Hk, Hv), dtype=torch.uint8, device="cuda")
+    g = lmx.GdnDesc(batch=B, T=T, k_heads=Hk, v_heads=Hv, eps=1e-6)
+    for f, k in (("qkv", "qkv"), ("z", "z"), ("b", "b"), ("a", "a"), ("conv_w", "conv_w"), ("a_log", "a_log"),
+                 ("dt_bias", "dt_bias"), ("norm_w", "norm_w"), ("conv_state", "conv_state"), ("state", "state"),
+                 ("state_snap", "snap"), ("out", "out"), ("scratch", "scratch")):
+        setattr(g, f, t_[k].data_ptr())
+    acc = torch.full((B,), T - 1, dtype=torch.int32, device="cuda")
+
+    def run(st):
+        s = C.c_void_p(st.cuda_stream)
+        lmx.call("lmx_gdn_verify", C.byref(g), s)
+        lmx.call("lmx_gdn_commit", C.byref(g), acc.data_ptr(), s)
+
+    t = _graph_time(run)
+    st_bytes = B * Hv * D * D * 4
+    byts = st_bytes * (2 + T) + B * T * (CD + 2 * Hv * D) * 2 + B * 3 * CD * 2 * 2
+    return dict(op="gdn_verify+commit", B=B, T=T, Hk=Hk, Hv=Hv, us=round(t * 1e6, 2),
+                GBs=round(byts / t / 1e9, 1), bytes=byts)
+
+
 def run_qmm(args):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", 0)
@@ -605,11 +705,25 @@ def main():
     ap.add_argument("--qmm-sweep", action="store_true",
                     help="op-level quantized_matmul sweep (BASELINE configs[1]) instead of decoding")
     ap.add_argument("--qmm", default="", help="one op-level shape N,K,M,bits (e.g. for ncu)")
+    ap.add_argument("--moe", default="", help="op-level routed experts M,H,I,E,k,bits (configuration 4: "
+                                              "12,2048,512,512,10,4)")
+    ap.add_argument("--gdn", default="", help="op-level Gated DeltaNet verify + commit B,T,Hk,Hv (configuration 4: "
+                                              "4,3,16,32)")
     ap.add_argument("--sdpa", default="", help="one op-level attention shape B,T,Hq,Hk,cap,bits (e.g. "
                                                "16,5,64,8,8300,8 = one Llama-3-70B verify layer)")
     args = ap.parse_args()
     if args.qmm_sweep or args.qmm:
         return run_qmm(args)
+    if args.moe or args.gdn:
+        lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+        lmx.call("lmx_set_device", 0)
+        if args.moe:
+            M, H_, I, E, k, bits = [int(v) for v in args.moe.split(",")]
+            print(json.dumps(moe_time(lmx, M, H_, I, E, k, bits)), flush=True)
+        if args.gdn:
+            B, T, Hk, Hv = [int(v) for v in args.gdn.split(",")]
+            print(json.dumps(gdn_time(lmx, B, T, Hk, Hv)), flush=True)
+        return 0
     if args.sdpa:
         lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
         lmx.call("lmx_set_device", 0)

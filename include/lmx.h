@@ -151,6 +151,66 @@ int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, int heads, f
                             void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Hybrid-model ops (configuration 4, Qwen3-Next-style decoder).
+ *
+ * Gated DeltaNet verify step: replaces Qwen3NextGatedDeltaNet's core between
+ * in_proj and out_proj (src/llm/models/qwen3_next.cpp:252-402) --
+ * gdn_conv_step / depthwise conv1d + SiLU with a 3-row state
+ * (src/common/gated_delta.cpp:885-921), q/k RMSNorm, beta / g
+ * (gated_delta.cpp:603-633), gated_delta_update_seq with per-token states
+ * (gated_delta.cpp:1067-1138), gated RMSNorm (gated_delta.cpp:948-971).
+ * Head dims 128.  The recurrent state is fp32 [B][Hv][128 (v)][128 (k)] (the
+ * reference keeps it in bf16).  lmx_gdn_verify reads state / conv_state and
+ * writes the state after every token (state_snap) and the output; it never
+ * modifies state or conv_state.  lmx_gdn_commit then keeps the state after
+ * token acc[b] of each sequence (MambaCache rollback_spec,
+ * include/mlx-lm/common/kv_cache.h:178-288; acc read on the device) and
+ * advances conv_state (in place) to the window ending at that token.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  int batch, T;            /* sequences, tokens per sequence in this block     */
+  int k_heads, v_heads;    /* linear_num_key_heads / value_heads (v % k == 0)  */
+  const void* qkv;         /* bf16 [batch][T][2*k_heads*128 + v_heads*128] pre-conv q|k|v */
+  const void* z;           /* bf16 [batch][T][v_heads*128] output gate         */
+  const void* b;           /* bf16 [batch][T][v_heads]                          */
+  const void* a;           /* bf16 [batch][T][v_heads]                          */
+  const void* conv_w;      /* bf16 [2*k_heads*128 + v_heads*128][4]             */
+  const float* a_log;      /* fp32 [v_heads]                                    */
+  const void* dt_bias;     /* bf16 [v_heads]                                    */
+  const void* norm_w;      /* bf16 [128] gated RMSNorm weight                   */
+  float eps;
+  void* conv_state;        /* bf16 [batch][3][qkv width]                        */
+  float* state;            /* fp32 [batch][v_heads][128][128]                   */
+  float* state_snap;       /* fp32 [batch][T][v_heads][128][128]                */
+  void* out;               /* bf16 [batch][T][v_heads*128]                      */
+  void* scratch;           /* lmx_gdn_scratch_bytes(batch, T, k_heads, v_heads) */
+} lmx_gdn;
+size_t lmx_gdn_scratch_bytes(int batch, int T, int k_heads, int v_heads);
+int lmx_gdn_verify(const lmx_gdn* g, void* stream);
+int lmx_gdn_commit(const lmx_gdn* g, const int32_t* acc, void* stream);
+
+/* MoE router (moe_route, src/common/gated_delta.cpp:973-999; the top-k and
+ * renormalised scores of Qwen3NextSparseMoeBlock, qwen3_next.cpp:452-470):
+ * per row the k largest logits (ties: lower index), in descending order, and
+ * w = softmax over those k (fp32).  k <= 16, E <= 16384. */
+int lmx_moe_route(const void* logits, int rows, int E, int k, int32_t* idx, float* w, void* stream);
+
+/* Routed SwiGLU experts (SwitchGLU + gather_qmm, src/common/switch_layers.cpp:
+ * 200-245, and the score-weighted sum of qwen3_next.cpp:471-478):
+ * y[m] = sum_j w[m][j] * down_e(swiglu(gate_e x_m, up_e x_m)), e = idx[m][j],
+ * over packed affine group-64 expert weights in the MLX SwitchLinear layout:
+ * gate / up [E][I][H*bits/32] (scales, biases [E][I][H/64]), down
+ * [E][H][I*bits/32] ([E][H][I/64]).  act_scratch: bf16 [M][k][I]. */
+typedef struct {
+  const uint32_t* w;
+  const void* scales;
+  const void* biases;
+} lmx_qweights;
+int lmx_moe_experts(const void* x, int M, int H, int I, int E, int k, const int32_t* idx, const float* w,
+                    const lmx_qweights* gate, const lmx_qweights* up, const lmx_qweights* down, int bits,
+                    void* act_scratch, void* y, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Models.  Replaces the ModelContext function table of a loaded Qwen3 /
  * Llama model (include/mlx-lm/common/model_container.h:20-51; graphs
  * src/llm/models/qwen3.cpp:69-220, llama.cpp:203-469).  Weights are synthetic

@@ -595,3 +595,5 @@ extern "C" int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, i
   if (rc) return rc;
   return sdpa_call(q, kv, T, heads, scale, scratch, kNoAllocScratchBytes, out, (cudaStream_t)stream);
 }
+
+#include "gdn_moe_api.cuh"

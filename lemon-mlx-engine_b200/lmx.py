@@ -47,6 +47,11 @@ SIGNATURES = {
     "lmx_tp_comm_open": (I, [P, P]),
     "lmx_tp_comm_free": (I, [P]),
     "lmx_cache_fill_synthetic": (I, [P, I, U64, C.c_uint32]),
+    "lmx_gdn_scratch_bytes": (C.c_size_t, [I, I, I, I]),
+    "lmx_gdn_verify": (I, [P, P]),
+    "lmx_gdn_commit": (I, [P, P, P]),
+    "lmx_moe_route": (I, [P, I, I, I, P, P, P]),
+    "lmx_moe_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, I, P, P, P]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
     "lmx_model_weight": (I, [P, I, I, P, P, P]),
@@ -70,6 +75,18 @@ class KvDesc(C.Structure):
     _fields_ = [("batch", I), ("kv_heads", I), ("head_dim", I), ("capacity", I), ("bits", I),
                 ("k", P), ("v", P), ("k_packed", P), ("v_packed", P), ("k_scales", P),
                 ("k_biases", P), ("v_scales", P), ("v_biases", P), ("lengths", P)]
+
+
+class GdnDesc(C.Structure):
+    """lmx_gdn"""
+    _fields_ = [("batch", I), ("T", I), ("k_heads", I), ("v_heads", I), ("qkv", P), ("z", P), ("b", P),
+                ("a", P), ("conv_w", P), ("a_log", P), ("dt_bias", P), ("norm_w", P), ("eps", F),
+                ("conv_state", P), ("state", P), ("state_snap", P), ("out", P), ("scratch", P)]
+
+
+class QWeights(C.Structure):
+    """lmx_qweights"""
+    _fields_ = [("w", P), ("scales", P), ("biases", P)]
 
 
 class ModelConfig(C.Structure):

@@ -706,6 +706,252 @@ extern "C" int orc_accept_stochastic(const uint16_t* target_logits, const uint16
 }
 
 // ---------------------------------------------------------------------------
+// Hybrid-model ops (configuration 4): the device engine's gdn_moe.cuh in the
+// same canonical orders.  Reference math: Qwen3NextGatedDeltaNet
+// (src/llm/models/qwen3_next.cpp:216-403), gated_delta.cpp:603-650,
+// 885-921, 948-999, 1067-1138; Qwen3NextSparseMoeBlock (qwen3_next.cpp:
+// 452-490), SwitchGLU (src/common/switch_layers.cpp:200-245).
+// ---------------------------------------------------------------------------
+// log(x), x > 0 normal: x = m 2^e, m in [sqrt(1/2), sqrt(2)); log m =
+// 2 atanh((m-1)/(m+1)) by its odd series to u^11; + e ln 2 (split).
+extern "C" float orc_log(float x) {
+  uint32_t bits;
+  std::memcpy(&bits, &x, 4);
+  int e = (int)(bits >> 23) - 127;
+  float m = u2f((bits & 0x7FFFFFu) | 0x3F800000u);
+  if (m > 1.41421356f) {
+    m = m * 0.5f;
+    e += 1;
+  }
+  const float u = (m - 1.0f) / (m + 1.0f);
+  const float u2 = u * u;
+  float p = 0.0909090909f;
+  p = std::fma(p, u2, 0.111111111f);
+  p = std::fma(p, u2, 0.142857143f);
+  p = std::fma(p, u2, 0.2f);
+  p = std::fma(p, u2, 0.333333333f);
+  p = std::fma(p, u2, 1.0f);
+  const float r = (2.0f * u) * p;
+  const float fe = (float)e;
+  return std::fma(fe, 0.693145752f, std::fma(fe, 1.42860677e-06f, r));
+}
+static inline float softplus_f(float x) { return x > 20.0f ? x : orc_log(1.0f + orc_exp(x)); }
+
+namespace {
+const int kGD = 128, kKS = 4;
+}
+
+// Gated DeltaNet verify step (lmx_gdn_verify): reads state / conv_state,
+// writes the state after each token to snap [B][T][Hv][128][128] and the
+// gated-normed output [B][T][Hv*128].
+extern "C" int orc_gdn_verify(int B, int T, int Hk, int Hv, const uint16_t* qkv, const uint16_t* z,
+                              const uint16_t* bb, const uint16_t* aa, const uint16_t* conv_w,
+                              const float* a_log, const uint16_t* dt_bias, const uint16_t* norm_w, float eps,
+                              const uint16_t* conv_state, const float* state, float* snap, uint16_t* out) {
+  if (B < 1 || T < 1 || Hk < 1 || Hv % Hk) return 1;
+  const int CD = 2 * Hk * kGD + Hv * kGD, rep = Hv / Hk;
+  const float wq = bf2f(f2bf(1.0f / kGD)), wk = bf2f(f2bf(0.08838834764831845f));
+  for (int b = 0; b < B; ++b) {
+    // conv + SiLU for every token and channel, q/k norms, v, beta, g
+    std::vector<float> cv((size_t)T * CD), qn((size_t)T * Hk * kGD), kn((size_t)T * Hk * kGD);
+    std::vector<float> beta((size_t)T * Hv), gd((size_t)T * Hv);
+    for (int t = 0; t < T; ++t) {
+      for (int c = 0; c < CD; ++c) {
+        float acc = 0.0f;
+        for (int i = 0; i < kKS; ++i) {
+          const int r = t + i;
+          const float x = r < kKS - 1 ? bf2f(conv_state[((size_t)b * (kKS - 1) + r) * CD + c])
+                                      : bf2f(qkv[((size_t)b * T + (r - (kKS - 1))) * CD + c]);
+          acc = std::fma(bf2f(conv_w[(size_t)c * kKS + i]), x, acc);
+        }
+        const float y = bf2f(f2bf(acc));
+        const float sg = bf2f(f2bf(sigmoid_f(y)));
+        cv[(size_t)t * CD + c] = bf2f(f2bf(y * sg));
+      }
+      for (int s = 0; s < 2 * Hk; ++s) {
+        const float* src = &cv[(size_t)t * CD + s * kGD];
+        const float f = rms_factor(src, kGD, 1e-6f);
+        const float w = s < Hk ? wq : wk;
+        float* dst = s < Hk ? &qn[((size_t)t * Hk + s) * kGD] : &kn[((size_t)t * Hk + s - Hk) * kGD];
+        for (int d = 0; d < kGD; ++d) dst[d] = bf2f(f2bf((src[d] * f) * w));
+      }
+      for (int h = 0; h < Hv; ++h) {
+        const size_t i = ((size_t)b * T + t) * Hv + h;
+        beta[(size_t)t * Hv + h] = bf2f(f2bf(sigmoid_f(bf2f(bb[i]))));
+        const float sp = softplus_f(bf2f(aa[i]) + bf2f(dt_bias[h]));
+        gd[(size_t)t * Hv + h] = bf2f(f2bf(orc_exp(-(orc_exp(a_log[h]) * sp))));
+      }
+    }
+#pragma omp parallel for schedule(static)
+    for (int h = 0; h < Hv; ++h) {
+      const int hk = h / rep;
+      std::vector<float> S((size_t)kGD * kGD);
+      std::memcpy(S.data(), state + (((size_t)b * Hv + h) * kGD) * kGD, S.size() * 4);
+      std::vector<float> y(kGD);
+      for (int t = 0; t < T; ++t) {
+        const float* q = &qn[((size_t)t * Hk + hk) * kGD];
+        const float* k = &kn[((size_t)t * Hk + hk) * kGD];
+        const float g = gd[(size_t)t * Hv + h], be = beta[(size_t)t * Hv + h];
+        for (int dv = 0; dv < kGD; ++dv) {
+          float* row = &S[(size_t)dv * kGD];
+          float part[2];
+          for (int hf = 0; hf < 2; ++hf) {
+            float kv = 0.0f;
+            for (int j = 0; j < 64; ++j) {
+              row[64 * hf + j] = row[64 * hf + j] * g;
+              kv = std::fma(row[64 * hf + j], k[64 * hf + j], kv);
+            }
+            part[hf] = kv;
+          }
+          const float kv = part[0] + part[1];
+          const float v = cv[(size_t)t * CD + 2 * Hk * kGD + h * kGD + dv];
+          const float delta = (v - kv) * be;
+          float yp[2];
+          for (int hf = 0; hf < 2; ++hf) {
+            float a = 0.0f;
+            for (int j = 0; j < 64; ++j) {
+              row[64 * hf + j] = std::fma(delta, k[64 * hf + j], row[64 * hf + j]);
+              a = std::fma(row[64 * hf + j], q[64 * hf + j], a);
+            }
+            yp[hf] = a;
+          }
+          y[dv] = bf2f(f2bf(yp[0] + yp[1]));
+        }
+        std::memcpy(snap + ((((size_t)b * T + t) * Hv + h) * kGD) * kGD, S.data(), S.size() * 4);
+        const float f = rms_factor(y.data(), kGD, eps);
+        for (int dv = 0; dv < kGD; ++dv) {
+          const float nv = bf2f(f2bf((y[dv] * f) * bf2f(norm_w[dv])));
+          const float zv = bf2f(z[(((size_t)b * T + t) * Hv + h) * kGD + dv]);
+          const float sz = bf2f(f2bf(zv * bf2f(f2bf(sigmoid_f(zv)))));
+          out[(((size_t)b * T + t) * Hv + h) * kGD + dv] = f2bf(sz * nv);
+        }
+      }
+    }
+  }
+  return 0;
+}
+
+// lmx_gdn_commit: state[b] = snap[b][acc[b]]; conv_state[b] = the window
+// ending at token acc[b] (in place).
+extern "C" int orc_gdn_commit(int B, int T, int Hk, int Hv, const uint16_t* qkv, const float* snap,
+                              const int32_t* acc, float* state, uint16_t* conv_state) {
+  const int CD = 2 * Hk * kGD + Hv * kGD;
+  for (int b = 0; b < B; ++b) {
+    const int t = std::min(std::max(acc[b], 0), T - 1);
+    std::memcpy(state + ((size_t)b * Hv * kGD) * kGD, snap + (((size_t)b * T + t) * Hv * kGD) * kGD,
+                (size_t)Hv * kGD * kGD * 4);
+    std::vector<uint16_t> win((size_t)(kKS - 1) * CD);
+    for (int r = 0; r < kKS - 1; ++r)
+      for (int c = 0; c < CD; ++c) {
+        const int src = t + 1 + r;
+        win[(size_t)r * CD + c] = src < kKS - 1 ? conv_state[((size_t)b * (kKS - 1) + src) * CD + c]
+                                                : qkv[((size_t)b * T + src - (kKS - 1)) * CD + c];
+      }
+    std::memcpy(conv_state + (size_t)b * (kKS - 1) * CD, win.data(), win.size() * 2);
+  }
+  return 0;
+}
+
+// lmx_moe_route: k largest logits (ties: lower index) in descending order,
+// w_j = exp(l_j - l_0) / sum (slot order).
+extern "C" int orc_moe_route(const uint16_t* logits, int rows, int E, int k, int32_t* idx, float* w) {
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t* l = logits + (size_t)r * E;
+    std::vector<char> taken(E, 0);
+    std::vector<float> lv(k);
+    for (int j = 0; j < k; ++j) {
+      float bv = -INFINITY;
+      int bi = -1;
+      for (int e = 0; e < E; ++e) {
+        const float v = bf2f(l[e]);
+        if (taken[e] || v != v) continue;
+        if (bi < 0 || v > bv) { bv = v; bi = e; }
+      }
+      if (bi >= 0) taken[bi] = 1;
+      lv[j] = bv;
+      idx[(size_t)r * k + j] = bi < 0 ? 0 : bi;
+    }
+    std::vector<float> e0(k);
+    float z = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      e0[j] = orc_exp(lv[j] - lv[0]);
+      z = z + e0[j];
+    }
+    for (int j = 0; j < k; ++j) w[(size_t)r * k + j] = e0[j] / z;
+  }
+  return 0;
+}
+
+namespace {
+// canonical expert dot product (gdn_moe.cuh qd_dot)
+float qd_dot(const uint32_t* wr, const uint16_t* sr, const uint16_t* br, const float* x, int K, int bits) {
+  const int NC = K / 16;
+  float lane[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int c = l; c < NC; c += 32) {
+      float p = 0.0f, xs = 0.0f;
+      for (int j = 0; j < 16; ++j) {
+        const float q = (float)qcode(wr, 16 * c + j, bits);
+        p = std::fma(q, x[16 * c + j], p);
+        xs = xs + x[16 * c + j];
+      }
+      const int g = c >> 2;
+      acc = acc + std::fma(bf2f(sr[g]), p, bf2f(br[g]) * xs);
+    }
+    lane[l] = acc;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    float q[32];
+    for (int l = 0; l < 32; ++l) q[l] = lane[l] + lane[l ^ off];
+    std::memcpy(lane, q, sizeof(lane));
+  }
+  return lane[0];
+}
+}  // namespace
+
+// lmx_moe_experts: y[m] = bf16(fma chain over j of w[m][j] *
+// bf16(down_e . swiglu(bf16(gate_e . x), bf16(up_e . x)))).
+extern "C" int orc_moe_experts(const uint16_t* x, int M, int H, int I, int E, int k, const int32_t* idx,
+                               const float* w, const uint32_t* gw, const uint16_t* gs, const uint16_t* gb,
+                               const uint32_t* uw, const uint16_t* us, const uint16_t* ub, const uint32_t* dw,
+                               const uint16_t* ds, const uint16_t* db, int bits, uint16_t* y) {
+  const size_t wpr_h = (size_t)H * bits / 32, gpr_h = H / 64, wpr_i = (size_t)I * bits / 32, gpr_i = I / 64;
+  std::vector<uint16_t> act((size_t)M * k * I);
+#pragma omp parallel for schedule(dynamic)
+  for (int s = 0; s < M * k; ++s) {
+    const int m = s / k, e = idx[s];
+    if (e < 0 || e >= E) continue;
+    std::vector<float> xf(H);
+    for (int i = 0; i < H; ++i) xf[i] = bf2f(x[(size_t)m * H + i]);
+    for (int r = 0; r < I; ++r) {
+      const size_t row = (size_t)e * I + r;
+      const float g = qd_dot(gw + row * wpr_h, gs + row * gpr_h, gb + row * gpr_h, xf.data(), H, bits);
+      const float u = qd_dot(uw + row * wpr_h, us + row * gpr_h, ub + row * gpr_h, xf.data(), H, bits);
+      act[(size_t)s * I + r] = swiglu1(f2bf(g), f2bf(u));
+    }
+  }
+#pragma omp parallel for schedule(dynamic)
+  for (int m = 0; m < M; ++m) {
+    std::vector<float> af((size_t)k * I);
+    for (size_t i = 0; i < af.size(); ++i) af[i] = bf2f(act[(size_t)m * k * I + i]);
+    for (int r = 0; r < H; ++r) {
+      float acc = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        const int e = idx[(size_t)m * k + j];
+        if (e < 0 || e >= E) continue;
+        const size_t row = (size_t)e * H + r;
+        const float v = bf2f(f2bf(qd_dot(dw + row * wpr_i, ds + row * gpr_i, db + row * gpr_i, &af[(size_t)j * I],
+                                         I, bits)));
+        acc = std::fma(w[(size_t)m * k + j], v, acc);
+      }
+      y[(size_t)m * H + r] = f2bf(acc);
+    }
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
 // Model (Qwen3 / Llama decoder, src/llm/models/qwen3.cpp:69-220,
 // src/llm/models/llama.cpp:203-469) with synthetic weights:
 // linear and embedding weights N(0,0.02) (Irwin-Hall) in bf16, quantized with

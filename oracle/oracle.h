@@ -118,6 +118,19 @@ int orc_model_weight(void* m, int layer, int kind, uint32_t* wq, uint16_t* s, ui
 /* kv_bits: 16 = bf16 cache, 4/8 = affine group-64 quantized cache. */
 void* orc_cache_create(void* model, int n_layers, int batch, int capacity, int kv_bits);
 int orc_cache_fill_synthetic(void* cache, int rows, uint64_t seed, uint32_t tid_base);
+/* Hybrid-model ops (configuration 4), canonical orders of gdn_moe.cuh. */
+float orc_log(float x);
+int orc_gdn_verify(int B, int T, int Hk, int Hv, const uint16_t* qkv, const uint16_t* z, const uint16_t* b,
+                   const uint16_t* a, const uint16_t* conv_w, const float* a_log, const uint16_t* dt_bias,
+                   const uint16_t* norm_w, float eps, const uint16_t* conv_state, const float* state, float* snap,
+                   uint16_t* out);
+int orc_gdn_commit(int B, int T, int Hk, int Hv, const uint16_t* qkv, const float* snap, const int32_t* acc,
+                   float* state, uint16_t* conv_state);
+int orc_moe_route(const uint16_t* logits, int rows, int E, int k, int32_t* idx, float* w);
+int orc_moe_experts(const uint16_t* x, int M, int H, int I, int E, int k, const int32_t* idx, const float* w,
+                    const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,
+                    const uint16_t* us, const uint16_t* ub, const uint32_t* dw, const uint16_t* ds,
+                    const uint16_t* db, int bits, uint16_t* y);
 /* Emulate a tp-rank tensor-parallel split of o_proj / down_proj (partials
  * over column slices summed in fp32 in rank order); 0 = ok. */
 int orc_model_set_tp(void* model, int tp);

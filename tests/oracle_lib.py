@@ -84,6 +84,11 @@ def _declare(L):
         "orc_cache_create": (P, [P, I, I, I, I]),
         "orc_cache_fill_synthetic": (I, [P, I, U64, U32]),
         "orc_model_set_tp": (I, [P, I]),
+        "orc_log": (F, [F]),
+        "orc_gdn_verify": (I, [I, I, I, I, P, P, P, P, P, P, P, P, F, P, P, P, P]),
+        "orc_gdn_commit": (I, [I, I, I, I, P, P, P, P, P]),
+        "orc_moe_route": (I, [P, I, I, I, P, P]),
+        "orc_moe_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, P, P, P, P, I, P]),
         "orc_cache_free": (None, [P]),
         "orc_cache_len": (I, [P, I]),
         "orc_cache_set_position": (None, [P, I, I]),
