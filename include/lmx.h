@@ -165,7 +165,8 @@ int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, int heads, f
  * modifies state or conv_state.  lmx_gdn_commit then keeps the state after
  * token acc[b] of each sequence (MambaCache rollback_spec,
  * include/mlx-lm/common/kv_cache.h:178-288; acc read on the device) and
- * advances conv_state (in place) to the window ending at that token.
+ * advances conv_state (in place) to the window ending at that token;
+ * acc[b] < 0 leaves sequence b unchanged.
  * ------------------------------------------------------------------------- */
 typedef struct {
   int batch, T;            /* sequences, tokens per sequence in this block     */
@@ -209,6 +210,41 @@ typedef struct {
 int lmx_moe_experts(const void* x, int M, int H, int I, int E, int k, const int32_t* idx, const float* w,
                     const lmx_qweights* gate, const lmx_qweights* up, const lmx_qweights* down, int bits,
                     void* act_scratch, void* y, void* stream);
+
+/* Hybrid (Qwen3-Next-style) model and its MTP speculative decoder
+ * (configuration 4): Qwen3NextModel (src/llm/models/qwen3_next.cpp) with
+ * layer l a gated full-attention layer when l % attn_every == attn_every - 1
+ * and a Gated DeltaNet layer otherwise, every layer followed by a sparse MoE
+ * block (top_k of experts + a sigmoid-gated shared expert); one MTP head
+ * (MTPHead, src/llm/models/mtp_head.cpp:146-178: RMSNorm of the embedding
+ * and of the trunk hidden, concat, fc, one attention + MoE decoder layer,
+ * output norm) drafting 2 tokens per step through the shared lm_head, the
+ * step of TokenIterator::mtp_speculative_step (src/common/generate.cpp:
+ * 669-933).  Head dims 128; weights synthetic and seeded (affine group 64). */
+typedef struct {
+  int hidden, layers, attn_every;
+  int heads, kv_heads;            /* gated attention (head_dim 128)        */
+  int lin_k_heads, lin_v_heads;   /* Gated DeltaNet (head dims 128)        */
+  int experts, top_k, expert_inter, shared_inter;
+  int vocab;
+  float rope_theta, eps;
+  int bits;                       /* 4 or 8                                */
+} lmx_hybrid_config;
+int lmx_hybrid_create(const lmx_hybrid_config* cfg, uint64_t seed, void** model);
+int lmx_hybrid_free(void* model);
+/* Trunk forward of a [B, T] token block (host ints) over the state's caches
+ * (attention KV and recurrent states), committing every token; logits
+ * [B, T, vocab] bf16 to logits_host (may be NULL). */
+int lmx_hybrid_state_create(void* model, int batch, int capacity, int kv_bits, int max_tokens_per_forward,
+                            void** state);
+int lmx_hybrid_state_free(void* state);
+int lmx_hybrid_forward(void* model, void* state, const int32_t* tokens_host, int B, int T, void* logits_host);
+/* MTP speculative decoding: greedy, 2 drafts per step (3-token verify). */
+int lmx_hybrid_spec_create(void* model, int batch, int max_tokens, int prompt_len, int kv_bits, void** spec);
+int lmx_hybrid_spec_prefill(void* spec, const int32_t* prompts_host);
+int lmx_hybrid_spec_decode(void* spec, int use_graph, double* seconds);
+int lmx_hybrid_spec_result(void* spec, int32_t* out_host, int64_t* stats_host);
+int lmx_hybrid_spec_free(void* spec);
 
 /* ---------------------------------------------------------------------------
  * Models.  Replaces the ModelContext function table of a loaded Qwen3 /

@@ -48,7 +48,8 @@ struct GdnArgs {
   float eps;
   const bf16_t* conv_state;  // [B][3][CD]
   const float* state;        // [B][Hv][128][128]
-  float* snap;               // [B][T][Hv][128][128]
+  float* snap;               // [B][snap_T][Hv][128][128]: states after the last snap_T tokens
+  int snap_T;                // T (every token) or 1 (only the last, e.g. a prefill chunk)
   bf16_t* out;               // [B][T][Hv*128]
   bf16_t* qn;                // scratch [B][T][Hk][128] normalised q
   bf16_t* kn;                // scratch [B][T][Hk][128] normalised k
@@ -201,8 +202,9 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(GdnArgs a) {
     }
     const float oy = __shfl_xor_sync(0xffffffffu, y, 1);
     y = half ? __fadd_rn(oy, y) : __fadd_rn(y, oy);
-    if (a.snap) {
-      float* sn = a.snap + (((bt * a.Hv + h) * kGdnD + dv) * kGdnD) + 64 * half;
+    const int ts = t - (a.T - a.snap_T);  // snapshot slot of token t
+    if (a.snap && ts >= 0) {
+      float* sn = a.snap + (((((size_t)b * a.snap_T + ts) * a.Hv + h) * kGdnD + dv) * kGdnD) + 64 * half;
 #pragma unroll
       for (int j = 0; j < 64; j += 4) *reinterpret_cast<float4*>(sn + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
     }
@@ -224,16 +226,19 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(GdnArgs a) {
 }
 
 // MambaCache rollback_spec: state[b] = snap[b][acc[b]]; conv_state[b] =
-// the 3 window rows ending at token acc[b] (old state rows, then tokens).
+// the 3 window rows ending at token acc[b] (old state rows, then tokens);
+// acc[b] < 0 leaves sequence b unchanged (a finished sequence).
 // Grid (B, Hv + 1): blocks y < Hv copy one head's state, y == Hv the conv rows.
 __global__ void __launch_bounds__(256) gdn_commit_kernel(GdnArgs a, const int32_t* acc, float* state,
                                                          bf16_t* conv_state_out) {
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x, h = blockIdx.y;
-  const int t = min(max(acc[b], 0), a.T - 1);
+  if (acc[b] < 0) return;
+  const int t = min(acc[b], a.T - 1);
+  const int ts = max(t - (a.T - a.snap_T), 0);  // snapshot slot of token t
   if (h < a.Hv) {
-    const float4* src = reinterpret_cast<const float4*>(a.snap + ((((size_t)b * a.T + t) * a.Hv + h) * kGdnD) * kGdnD);
+    const float4* src = reinterpret_cast<const float4*>(a.snap + ((((size_t)b * a.snap_T + ts) * a.Hv + h) * kGdnD) * kGdnD);
     float4* dst = reinterpret_cast<float4*>(state + (((size_t)b * a.Hv + h) * kGdnD) * kGdnD);
     for (int i = threadIdx.x; i < kGdnD * kGdnD / 4; i += blockDim.x) dst[i] = src[i];
     return;

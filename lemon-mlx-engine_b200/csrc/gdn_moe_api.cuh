@@ -37,6 +37,7 @@ static int gdn_args(const lmx_gdn* g, GdnArgs& a) {
   a.conv_state = (const bf16_t*)g->conv_state;
   a.state = g->state;
   a.snap = g->state_snap;
+  a.snap_T = g->T;
   a.out = (bf16_t*)g->out;
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t bt = (size_t)a.B * a.T;

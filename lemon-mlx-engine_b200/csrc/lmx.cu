@@ -597,3 +597,4 @@ extern "C" int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, i
 }
 
 #include "gdn_moe_api.cuh"
+#include "hybrid.cuh"

@@ -52,6 +52,16 @@ SIGNATURES = {
     "lmx_gdn_commit": (I, [P, P, P]),
     "lmx_moe_route": (I, [P, I, I, I, P, P, P]),
     "lmx_moe_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, I, P, P, P]),
+    "lmx_hybrid_create": (I, [P, U64, P]),
+    "lmx_hybrid_free": (I, [P]),
+    "lmx_hybrid_state_create": (I, [P, I, I, I, I, P]),
+    "lmx_hybrid_state_free": (I, [P]),
+    "lmx_hybrid_forward": (I, [P, P, P, I, I, P]),
+    "lmx_hybrid_spec_create": (I, [P, I, I, I, I, P]),
+    "lmx_hybrid_spec_prefill": (I, [P, P]),
+    "lmx_hybrid_spec_decode": (I, [P, I, P]),
+    "lmx_hybrid_spec_result": (I, [P, P, P]),
+    "lmx_hybrid_spec_free": (I, [P]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
     "lmx_model_weight": (I, [P, I, I, P, P, P]),
@@ -89,6 +99,13 @@ class QWeights(C.Structure):
     _fields_ = [("w", P), ("scales", P), ("biases", P)]
 
 
+class HybridConfig(C.Structure):
+    """lmx_hybrid_config"""
+    _fields_ = [("hidden", I), ("layers", I), ("attn_every", I), ("heads", I), ("kv_heads", I),
+                ("lin_k_heads", I), ("lin_v_heads", I), ("experts", I), ("top_k", I), ("expert_inter", I),
+                ("shared_inter", I), ("vocab", I), ("rope_theta", F), ("eps", F), ("bits", I)]
+
+
 class ModelConfig(C.Structure):
     """lmx_model_config"""
     _fields_ = [("hidden", I), ("layers", I), ("inter", I), ("heads", I), ("kv_heads", I),
@@ -103,6 +120,13 @@ class SpecConfig(C.Structure):
                 ("temperature", F), ("top_p", F), ("seed", U64), ("context_len", I),
                 ("context_seed", U64)]
 
+
+# Qwen3-Next-style hybrid (the unspecified head counts / dims
+# chosen: 16 q / 2 kv attention heads and 16 key / 32 value Gated DeltaNet
+# heads, all of dim 128; RoPE theta 1e7 over the full head).
+QWEN3_NEXT_HYBRID = dict(hidden=2048, layers=48, attn_every=4, heads=16, kv_heads=2, lin_k_heads=16,
+                         lin_v_heads=32, experts=512, top_k=10, expert_inter=512, shared_inter=512,
+                         vocab=151936, rope_theta=1e7, eps=1e-6, bits=4)
 
 # The benchmark configurations' architectures (random-initialised weights).
 QWEN3_0_6B = dict(hidden=1024, layers=28, inter=3072, heads=16, kv_heads=8, head_dim=128,

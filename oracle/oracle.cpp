@@ -837,7 +837,8 @@ extern "C" int orc_gdn_commit(int B, int T, int Hk, int Hv, const uint16_t* qkv,
                               const int32_t* acc, float* state, uint16_t* conv_state) {
   const int CD = 2 * Hk * kGD + Hv * kGD;
   for (int b = 0; b < B; ++b) {
-    const int t = std::min(std::max(acc[b], 0), T - 1);
+    if (acc[b] < 0) continue;  // finished sequence: unchanged
+    const int t = std::min(acc[b], T - 1);
     std::memcpy(state + ((size_t)b * Hv * kGD) * kGD, snap + (((size_t)b * T + t) * Hv * kGD) * kGD,
                 (size_t)Hv * kGD * kGD * 4);
     std::vector<uint16_t> win((size_t)(kKS - 1) * CD);
@@ -1503,6 +1504,399 @@ extern "C" int orc_generate(void* target, const int32_t* prompts, int B, int P, 
     rc = forward_impl(tm, *tc, tm.c.layers, y.data(), B, 1, lg.data(), true);
     if (rc) return rc;
     orc_argmax(lg.data(), B, V, y.data());
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Hybrid (Qwen3-Next-style) model and its MTP speculative loop: the device
+// engine's hybrid.cuh composition, operation for operation (reference:
+// src/llm/models/qwen3_next.cpp:118-490, mtp_head.cpp:146-178,
+// src/common/generate.cpp:669-933).
+// ---------------------------------------------------------------------------
+namespace {
+struct HLayer {
+  bool attn = false;
+  QW q, k, v, qg, o, wqkv, wz, wb, wa, wout, router, eg, eu, ed, sg, su, sd, sgate;
+  std::vector<uint16_t> conv_w, dt_bias;
+  std::vector<float> a_log;
+};
+struct HModel {
+  orc_hybrid_cfg c;
+  std::vector<HLayer> L;
+  HLayer mtp;
+  QW embed, lm_head, mtp_fc;
+  int max_pos = 16384, n_attn = 0, n_gdn = 0, CD = 0;
+  std::vector<float> cos_t, sin_t;
+};
+struct HGdn {
+  std::vector<uint16_t> conv, qkv;  // conv [B][3][CD]; the last forward's inputs [B][T][CD]
+  std::vector<float> state, snap;   // [B][Hv][128][128]; [B][T][Hv][128][128]
+};
+struct HState {
+  int B = 0, cap = 0, T = 0;
+  std::unique_ptr<Cache> kv, mtp_kv;
+  std::vector<HGdn> gdn;
+  std::vector<uint16_t> hid;  // final-normed hidden of the last forward [B*T][H]
+};
+
+std::vector<uint16_t> gen_bf16v(uint64_t seed, uint32_t tid, int64_t n, float std_dev) {
+  std::vector<uint16_t> v((size_t)n);
+  const float C = orc_normal_scale(std_dev);
+  for (int64_t i = 0; i < n; ++i) v[(size_t)i] = normal_bf16(seed, tid, (uint64_t)i, C);
+  return v;
+}
+
+void hqmm(const QW& w, const uint16_t* x, uint16_t* y, int M, int bits) {
+  orc_qmm(x, w.w.data(), w.s.data(), w.b.data(), y, M, w.N, w.K, 64, bits);
+}
+
+void hyb_layer_gen(HModel& m, HLayer& L, int l, bool attn, uint64_t seed) {
+  const orc_hybrid_cfg& c = m.c;
+  const int H = c.hidden, NQ = c.heads * kGD, NK = c.kv_heads * kGD, bits = c.bits;
+  const uint32_t base = (uint32_t)(l + 1) * 64;
+  L.attn = attn;
+  if (attn) {
+    gen_qw(L.q, seed, base + 0, NQ, H, bits, 64);
+    gen_qw(L.k, seed, base + 1, NK, H, bits, 64);
+    gen_qw(L.v, seed, base + 2, NK, H, bits, 64);
+    gen_qw(L.qg, seed, base + 3, NQ, H, bits, 64);
+    gen_qw(L.o, seed, base + 4, H, NQ, bits, 64);
+  } else {
+    const int Z = c.lin_v_heads * kGD;
+    gen_qw(L.wqkv, seed, base + 8, m.CD, H, bits, 64);
+    gen_qw(L.wz, seed, base + 9, Z, H, bits, 64);
+    gen_qw(L.wb, seed, base + 10, c.lin_v_heads, H, bits, 64);
+    gen_qw(L.wa, seed, base + 11, c.lin_v_heads, H, bits, 64);
+    gen_qw(L.wout, seed, base + 12, H, Z, bits, 64);
+    L.conv_w = gen_bf16v(seed, base + 13, (int64_t)m.CD * kKS, 0.3f);
+    L.dt_bias = gen_bf16v(seed, base + 14, c.lin_v_heads, 0.5f);
+    const auto al = gen_bf16v(seed, base + 15, c.lin_v_heads, 0.5f);
+    L.a_log.resize(al.size());
+    for (size_t i = 0; i < al.size(); ++i) L.a_log[i] = bf2f(al[i]);
+  }
+  gen_qw(L.router, seed, base + 16, c.experts, H, bits, 64);
+  gen_qw(L.eg, seed, base + 17, c.experts * c.expert_inter, H, bits, 64);
+  gen_qw(L.eu, seed, base + 18, c.experts * c.expert_inter, H, bits, 64);
+  gen_qw(L.ed, seed, base + 19, c.experts * H, c.expert_inter, bits, 64);
+  gen_qw(L.sg, seed, base + 20, c.shared_inter, H, bits, 64);
+  gen_qw(L.su, seed, base + 21, c.shared_inter, H, bits, 64);
+  gen_qw(L.sd, seed, base + 22, H, c.shared_inter, bits, 64);
+  gen_qw(L.sgate, seed, base + 23, 1, H, bits, 64);
+}
+
+void rms_ones(const uint16_t* x, uint16_t* y, int rows, int dim, float eps) {
+  std::vector<uint16_t> ones(dim, f2bf(1.0f));
+  orc_rms_norm(x, ones.data(), y, rows, dim, eps);
+}
+
+// gated attention of layer L over xn (B x T rows), cache layer li of kc;
+// adds the output to h
+void hyb_attn(HModel& m, Cache& kc, int li, const HLayer& L, const uint16_t* xn, uint16_t* h, int B, int T) {
+  const orc_hybrid_cfg& c = m.c;
+  const int H = c.hidden, Hq = c.heads, Hk = c.kv_heads, D = kGD, R = B * T, NQ = Hq * D, NK = Hk * D;
+  std::vector<uint16_t> q((size_t)R * NQ), k((size_t)R * NK), v((size_t)R * NK), g((size_t)R * NQ),
+      o((size_t)R * NQ), a((size_t)R * H);
+  hqmm(L.q, xn, q.data(), R, c.bits);
+  hqmm(L.k, xn, k.data(), R, c.bits);
+  hqmm(L.v, xn, v.data(), R, c.bits);
+  hqmm(L.qg, xn, g.data(), R, c.bits);
+  rms_ones(q.data(), q.data(), R * Hq, D, c.eps);
+  rms_ones(k.data(), k.data(), R * Hk, D, c.eps);
+  std::vector<int32_t> pos(R);
+  for (int b = 0; b < B; ++b)
+    for (int t = 0; t < T; ++t) pos[b * T + t] = kc.len[b] + t;
+  orc_rope(q.data(), pos.data(), R, Hq, D, m.cos_t.data(), m.sin_t.data());
+  orc_rope(k.data(), pos.data(), R, Hk, D, m.cos_t.data(), m.sin_t.data());
+  const float scale = (float)(1.0 / std::sqrt((double)D));
+  for (int b = 0; b < B; ++b) {
+    for (int t = 0; t < T; ++t)
+      for (int hk = 0; hk < Hk; ++hk) {
+        const size_t row = ((size_t)b * Hk + hk) * kc.cap + (size_t)(kc.len[b] + t);
+        const uint16_t* ks = &k[((size_t)(b * T + t) * Hk + hk) * D];
+        const uint16_t* vs = &v[((size_t)(b * T + t) * Hk + hk) * D];
+        if (kc.bits == 16) {
+          std::memcpy(&kc.k[li][row * D], ks, D * 2);
+          std::memcpy(&kc.v[li][row * D], vs, D * 2);
+        } else {
+          const int WPR = D * kc.bits / 32, gpr = D / 64;
+          for (int gi = 0; gi < gpr; ++gi) {
+            quantize_group(ks + 64 * gi, 64, kc.bits, &kc.kq[li][row * WPR + gi * 64 * kc.bits / 32],
+                           &kc.ks[li][row * gpr + gi], &kc.kb[li][row * gpr + gi]);
+            quantize_group(vs + 64 * gi, 64, kc.bits, &kc.vq[li][row * WPR + gi * 64 * kc.bits / 32],
+                           &kc.vs[li][row * gpr + gi], &kc.vb[li][row * gpr + gi]);
+          }
+        }
+      }
+    std::vector<uint16_t> kd, vd;
+    const uint16_t *kb, *vb;
+    const size_t base = (size_t)b * Hk * kc.cap;
+    if (kc.bits == 16) {
+      kb = &kc.k[li][base * D];
+      vb = &kc.v[li][base * D];
+    } else {
+      const int WPR = D * kc.bits / 32, gpr = D / 64;
+      kd.assign((size_t)Hk * kc.cap * D, 0);
+      vd.assign(kd.size(), 0);
+      for (int hk = 0; hk < Hk; ++hk)
+        for (int j = 0; j < kc.len[b] + T; ++j) {
+          const size_t row = base + (size_t)hk * kc.cap + j;
+          for (int d = 0; d < D; ++d) {
+            const int gi = d / 64;
+            kd[((size_t)hk * kc.cap + j) * D + d] = f2bf(std::fma(bf2f(kc.ks[li][row * gpr + gi]),
+                (float)qcode(&kc.kq[li][row * WPR], d, kc.bits), bf2f(kc.kb[li][row * gpr + gi])));
+            vd[((size_t)hk * kc.cap + j) * D + d] = f2bf(std::fma(bf2f(kc.vs[li][row * gpr + gi]),
+                (float)qcode(&kc.vq[li][row * WPR], d, kc.bits), bf2f(kc.vb[li][row * gpr + gi])));
+          }
+        }
+      kb = kd.data();
+      vb = vd.data();
+    }
+    orc_sdpa(&q[(size_t)b * T * NQ], kb, vb, &o[(size_t)b * T * NQ], T, Hq, Hk, D, kc.cap, kc.len[b], scale);
+  }
+  for (size_t i = 0; i < o.size(); ++i) o[i] = f2bf(bf2f(o[i]) * bf2f(f2bf(sigmoid_f(bf2f(g[i])))));
+  hqmm(L.o, o.data(), a.data(), R, c.bits);
+  orc_add(h, a.data(), h, (int64_t)R * H);
+}
+
+void hyb_moe(HModel& m, const HLayer& L, uint16_t* h, int R) {
+  const orc_hybrid_cfg& c = m.c;
+  const int H = c.hidden;
+  std::vector<uint16_t> xn((size_t)R * H), rl((size_t)R * c.experts), ym((size_t)R * H), g((size_t)R * c.shared_inter),
+      u(g.size()), ys((size_t)R * H), sgl(R);
+  rms_ones(h, xn.data(), R, H, c.eps);
+  hqmm(L.router, xn.data(), rl.data(), R, c.bits);
+  std::vector<int32_t> idx((size_t)R * c.top_k);
+  std::vector<float> w((size_t)R * c.top_k);
+  orc_moe_route(rl.data(), R, c.experts, c.top_k, idx.data(), w.data());
+  orc_moe_experts(xn.data(), R, H, c.expert_inter, c.experts, c.top_k, idx.data(), w.data(), L.eg.w.data(),
+                  L.eg.s.data(), L.eg.b.data(), L.eu.w.data(), L.eu.s.data(), L.eu.b.data(), L.ed.w.data(),
+                  L.ed.s.data(), L.ed.b.data(), c.bits, ym.data());
+  hqmm(L.sg, xn.data(), g.data(), R, c.bits);
+  hqmm(L.su, xn.data(), u.data(), R, c.bits);
+  orc_swiglu(g.data(), u.data(), g.data(), (int64_t)g.size());
+  hqmm(L.sd, g.data(), ys.data(), R, c.bits);
+  hqmm(L.sgate, xn.data(), sgl.data(), R, c.bits);
+  for (int r = 0; r < R; ++r) {
+    const float gs = bf2f(f2bf(sigmoid_f(bf2f(sgl[r]))));
+    for (int i = 0; i < H; ++i) {
+      const size_t j = (size_t)r * H + i;
+      const float t = bf2f(f2bf(gs * bf2f(ys[j])));
+      const float mm = bf2f(f2bf(bf2f(ym[j]) + t));
+      h[j] = f2bf(bf2f(h[j]) + mm);
+    }
+  }
+}
+
+// trunk forward (tokens [B][T]); commit: every GDN layer keeps the state
+// after the last token; else the snapshots stay for hyb_commit.  Leaves the
+// final-normed hidden in s.hid; logits (all rows, or each sequence's last)
+// when non-null.  Advances the attention lengths only when commit.
+void hyb_forward(HModel& m, HState& s, const int32_t* tokens, int B, int T, uint16_t* logits, bool last_only,
+                 bool commit) {
+  const orc_hybrid_cfg& c = m.c;
+  const int H = c.hidden, R = B * T, G = H / 64, Hv = c.lin_v_heads, Z = Hv * kGD;
+  std::vector<uint16_t> h((size_t)R * H), xn((size_t)R * H);
+  for (int r = 0; r < R; ++r) {
+    const int tok = tokens[r];
+    const uint32_t* row = m.embed.w.data() + (size_t)tok * H * c.bits / 32;
+    for (int i = 0; i < H; ++i)
+      h[(size_t)r * H + i] = f2bf(std::fma(bf2f(m.embed.s[(size_t)tok * G + i / 64]), (float)qcode(row, i, c.bits),
+                                           bf2f(m.embed.b[(size_t)tok * G + i / 64])));
+  }
+  int ia = 0, ig = 0;
+  for (int l = 0; l < c.layers; ++l) {
+    const HLayer& L = m.L[l];
+    rms_ones(h.data(), xn.data(), R, H, c.eps);
+    if (L.attn) {
+      hyb_attn(m, *s.kv, ia++, L, xn.data(), h.data(), B, T);
+    } else {
+      HGdn& g = s.gdn[ig++];
+      g.qkv.resize((size_t)R * m.CD);
+      std::vector<uint16_t> z((size_t)R * Z), bb((size_t)R * Hv), aa((size_t)R * Hv), out((size_t)R * Z),
+          a((size_t)R * H), gnorm(kGD, f2bf(1.0f));
+      hqmm(L.wqkv, xn.data(), g.qkv.data(), R, c.bits);
+      hqmm(L.wz, xn.data(), z.data(), R, c.bits);
+      hqmm(L.wb, xn.data(), bb.data(), R, c.bits);
+      hqmm(L.wa, xn.data(), aa.data(), R, c.bits);
+      g.snap.assign((size_t)B * T * Hv * kGD * kGD, 0.0f);
+      orc_gdn_verify(B, T, c.lin_k_heads, Hv, g.qkv.data(), z.data(), bb.data(), aa.data(), L.conv_w.data(),
+                     L.a_log.data(), L.dt_bias.data(), gnorm.data(), c.eps, g.conv.data(), g.state.data(),
+                     g.snap.data(), out.data());
+      if (commit) {
+        std::vector<int32_t> last(B, T - 1);
+        orc_gdn_commit(B, T, c.lin_k_heads, Hv, g.qkv.data(), g.snap.data(), last.data(), g.state.data(),
+                       g.conv.data());
+      }
+      hqmm(L.wout, out.data(), a.data(), R, c.bits);
+      orc_add(h.data(), a.data(), h.data(), (int64_t)R * H);
+    }
+    hyb_moe(m, L, h.data(), R);
+  }
+  s.hid.resize((size_t)R * H);
+  rms_ones(h.data(), s.hid.data(), R, H, c.eps);
+  s.T = T;
+  if (commit && s.kv)
+    for (int b = 0; b < B; ++b) s.kv->len[b] += T;
+  if (!logits) return;
+  if (last_only) {
+    std::vector<uint16_t> hl((size_t)B * H);
+    for (int b = 0; b < B; ++b) std::memcpy(&hl[(size_t)b * H], &s.hid[((size_t)b * T + T - 1) * H], H * 2);
+    hqmm(m.lm_head, hl.data(), logits, B, c.bits);
+  } else {
+    hqmm(m.lm_head, s.hid.data(), logits, R, c.bits);
+  }
+}
+}  // namespace
+
+extern "C" void* orc_hybrid_create(const orc_hybrid_cfg* cfg, uint64_t seed) {
+  auto m = std::make_unique<HModel>();
+  m->c = *cfg;
+  const orc_hybrid_cfg& c = *cfg;
+  if (c.bits != 4 && c.bits != 8) return nullptr;
+  m->CD = 2 * c.lin_k_heads * kGD + c.lin_v_heads * kGD;
+  m->L.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const bool attn = l % c.attn_every == c.attn_every - 1;
+    (attn ? m->n_attn : m->n_gdn)++;
+    hyb_layer_gen(*m, m->L[l], l, attn, seed);
+  }
+  hyb_layer_gen(*m, m->mtp, c.layers, true, seed);
+  gen_qw(m->embed, seed, 1, c.vocab, c.hidden, c.bits, 64);
+  gen_qw(m->lm_head, seed, 2, c.vocab, c.hidden, c.bits, 64);
+  gen_qw(m->mtp_fc, seed, 3, c.hidden, 2 * c.hidden, c.bits, 64);
+  m->cos_t.resize((size_t)m->max_pos * kGD / 2);
+  m->sin_t.resize(m->cos_t.size());
+  orc_rope_table(m->max_pos, kGD, c.rope_theta, m->cos_t.data(), m->sin_t.data());
+  return m.release();
+}
+extern "C" void orc_hybrid_free(void* m) { delete (HModel*)m; }
+
+namespace {
+HState* hyb_state_new(HModel& m, int B, int cap, int kv_bits) {
+  auto s = std::make_unique<HState>();
+  s->B = B;
+  s->cap = cap;
+  Model shape;  // cache geometry
+  shape.c.kv_heads = m.c.kv_heads;
+  shape.c.head_dim = kGD;
+  if (m.n_attn) s->kv.reset((Cache*)orc_cache_create(&shape, m.n_attn, B, cap, kv_bits));
+  s->mtp_kv.reset((Cache*)orc_cache_create(&shape, 1, B, 8, kv_bits));
+  s->gdn.resize(m.n_gdn);
+  for (auto& g : s->gdn) {
+    g.conv.assign((size_t)B * (kKS - 1) * m.CD, 0);
+    g.state.assign((size_t)B * m.c.lin_v_heads * kGD * kGD, 0.0f);
+  }
+  return s.release();
+}
+}  // namespace
+
+extern "C" void* orc_hybrid_state_create(void* mp, int B, int cap, int kv_bits) {
+  return hyb_state_new(*(HModel*)mp, B, cap, kv_bits);
+}
+extern "C" void orc_hybrid_state_free(void* s) { delete (HState*)s; }
+extern "C" int orc_hybrid_forward(void* mp, void* sp, const int32_t* tokens, int B, int T, uint16_t* logits) {
+  HState& s = *(HState*)sp;
+  if (B != s.B) return 1;
+  hyb_forward(*(HModel*)mp, s, tokens, B, T, logits, false, true);
+  return 0;
+}
+
+// MTP speculative decode (greedy, 2 drafts): the device engine's step.
+extern "C" int orc_hybrid_spec_generate(void* mp, const int32_t* prompts, int B, int P, int MT, int kv_bits,
+                                        int32_t* out, int64_t* stats) {
+  HModel& m = *(HModel*)mp;
+  const orc_hybrid_cfg& c = m.c;
+  const int H = c.hidden, V = c.vocab, N = 3;
+  std::unique_ptr<HState> s(hyb_state_new(m, B, P + MT + N + 8, kv_bits));
+  std::vector<uint16_t> lg((size_t)B * N * V);
+  // prefill in 32-token chunks
+  std::vector<int32_t> chunk;
+  for (int t0 = 0; t0 < P; t0 += 32) {
+    const int tn = std::min(32, P - t0);
+    chunk.resize((size_t)B * tn);
+    for (int b = 0; b < B; ++b) std::memcpy(&chunk[(size_t)b * tn], prompts + (size_t)b * P + t0, tn * 4);
+    hyb_forward(m, *s, chunk.data(), B, tn, t0 + tn >= P ? lg.data() : nullptr, true, true);
+  }
+  std::vector<int32_t> vt((size_t)B * N), pred((size_t)B * N), emitted(B, 0), acc(B);
+  std::vector<uint16_t> capt((size_t)B * H), mhid((size_t)B * H);
+  orc_argmax(lg.data(), B, V, pred.data());
+  for (int b = 0; b < B; ++b) {
+    vt[(size_t)b * N] = pred[b];
+    std::memcpy(&capt[(size_t)b * H], &s->hid[((size_t)b * s->T + s->T - 1) * H], H * 2);
+  }
+  int64_t steps = 0, accepted = 0;
+  std::vector<uint16_t> ones(H, f2bf(1.0f));
+  for (int it = 0; it < MT + 1; ++it) {
+    bool all = true;
+    for (int b = 0; b < B; ++b) all = all && emitted[b] >= MT;
+    if (all) break;
+    // MTP drafts d1, d2 (cache reset to 0)
+    for (int b = 0; b < B; ++b) s->mtp_kv->len[b] = 0;
+    for (int i = 1; i < N; ++i) {
+      const uint16_t* hin = i == 1 ? capt.data() : mhid.data();
+      std::vector<uint16_t> e((size_t)B * H), cat((size_t)B * 2 * H), h((size_t)B * H), xn((size_t)B * H),
+          l1((size_t)B * V);
+      const int G = H / 64;
+      for (int b = 0; b < B; ++b) {
+        const int tok = vt[(size_t)b * N + i - 1];
+        const uint32_t* row = m.embed.w.data() + (size_t)tok * H * c.bits / 32;
+        for (int j = 0; j < H; ++j)
+          e[(size_t)b * H + j] = f2bf(std::fma(bf2f(m.embed.s[(size_t)tok * G + j / 64]),
+                                               (float)qcode(row, j, c.bits), bf2f(m.embed.b[(size_t)tok * G + j / 64])));
+      }
+      std::vector<uint16_t> en((size_t)B * H), hn((size_t)B * H);
+      rms_ones(e.data(), en.data(), B, H, c.eps);
+      rms_ones(hin, hn.data(), B, H, c.eps);
+      for (int b = 0; b < B; ++b) {
+        std::memcpy(&cat[(size_t)b * 2 * H], &en[(size_t)b * H], H * 2);
+        std::memcpy(&cat[(size_t)b * 2 * H + H], &hn[(size_t)b * H], H * 2);
+      }
+      hqmm(m.mtp_fc, cat.data(), h.data(), B, c.bits);
+      rms_ones(h.data(), xn.data(), B, H, c.eps);
+      hyb_attn(m, *s->mtp_kv, 0, m.mtp, xn.data(), h.data(), B, 1);
+      hyb_moe(m, m.mtp, h.data(), B);
+      for (int b = 0; b < B; ++b) s->mtp_kv->len[b] += 1;
+      mhid = h;
+      rms_ones(h.data(), xn.data(), B, H, c.eps);
+      hqmm(m.lm_head, xn.data(), l1.data(), B, c.bits);
+      std::vector<int32_t> d(B);
+      orc_argmax(l1.data(), B, V, d.data());
+      for (int b = 0; b < B; ++b) vt[(size_t)b * N + i] = d[b];
+    }
+    // verify
+    hyb_forward(m, *s, vt.data(), B, N, lg.data(), false, false);
+    orc_argmax(lg.data(), B * N, V, pred.data());
+    for (int b = 0; b < B; ++b) {
+      int e = emitted[b];
+      if (e >= MT) {
+        acc[b] = -1;
+        continue;
+      }
+      int a = 0;
+      while (a < N - 1 && pred[(size_t)b * N + a] == vt[(size_t)b * N + a + 1]) ++a;
+      for (int i = 0; i <= a && e < MT; ++i) out[(size_t)b * MT + e++] = vt[(size_t)b * N + i];
+      emitted[b] = e;
+      accepted += a;
+      steps += 1;
+      if (s->kv) s->kv->len[b] += a + 1;
+      vt[(size_t)b * N] = pred[(size_t)b * N + a];
+      acc[b] = a;
+    }
+    for (auto& g : s->gdn)
+      orc_gdn_commit(B, N, c.lin_k_heads, c.lin_v_heads, g.qkv.data(), g.snap.data(), acc.data(), g.state.data(),
+                     g.conv.data());
+    for (int b = 0; b < B; ++b)
+      if (acc[b] >= 0) std::memcpy(&capt[(size_t)b * H], &s->hid[((size_t)b * N + acc[b]) * H], H * 2);
+  }
+  if (stats) {
+    int64_t em = 0;
+    for (int b = 0; b < B; ++b) em += emitted[b];
+    stats[0] = steps;
+    stats[1] = steps * (N - 1);
+    stats[2] = accepted;
+    stats[3] = em;
+    stats[4] = 0;
   }
   return 0;
 }

@@ -131,6 +131,20 @@ int orc_moe_experts(const uint16_t* x, int M, int H, int I, int E, int k, const 
                     const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,
                     const uint16_t* us, const uint16_t* ub, const uint32_t* dw, const uint16_t* ds,
                     const uint16_t* db, int bits, uint16_t* y);
+/* Hybrid (Qwen3-Next-style) model + MTP speculative loop (hybrid.cuh). */
+typedef struct {
+  int hidden, layers, attn_every, heads, kv_heads, lin_k_heads, lin_v_heads;
+  int experts, top_k, expert_inter, shared_inter, vocab;
+  float rope_theta, eps;
+  int bits;
+} orc_hybrid_cfg;
+void* orc_hybrid_create(const orc_hybrid_cfg* cfg, uint64_t seed);
+void orc_hybrid_free(void* model);
+void* orc_hybrid_state_create(void* model, int batch, int capacity, int kv_bits);
+void orc_hybrid_state_free(void* state);
+int orc_hybrid_forward(void* model, void* state, const int32_t* tokens, int B, int T, uint16_t* logits);
+int orc_hybrid_spec_generate(void* model, const int32_t* prompts, int B, int P, int max_tokens, int kv_bits,
+                             int32_t* out, int64_t* stats);
 /* Emulate a tp-rank tensor-parallel split of o_proj / down_proj (partials
  * over column slices summed in fp32 in rank order); 0 = ok. */
 int orc_model_set_tp(void* model, int tp);

@@ -5,6 +5,8 @@ oracle).  Reference formulas: Qwen3NextGatedDeltaNet (src/llm/models/
 qwen3_next.cpp:216-403), gated_delta.cpp:603-650, 885-921, 948-999;
 Qwen3NextSparseMoeBlock (qwen3_next.cpp:452-490), SwitchGLU
 (src/common/switch_layers.cpp:200-245)."""
+import ctypes as C
+
 import numpy as np
 
 import oracle_lib as O
@@ -158,3 +160,33 @@ def reference_experts(c):
             a = g / (1 + np.exp(-g)) * u
             y[m] += c["w"][m, j] * (deq(c["down"], e) @ a)
     return y
+
+
+TINY_HYBRID = dict(hidden=512, layers=4, attn_every=2, heads=4, kv_heads=2, lin_k_heads=2, lin_v_heads=4,
+                   experts=8, top_k=2, expert_inter=512, shared_inter=512, vocab=1000, rope_theta=1e7, eps=1e-6,
+                   bits=4)
+
+
+def oracle_hybrid(cfg, seed):
+    return O.lib().orc_hybrid_create(C.byref(O.HybridCfg(**cfg)), seed)
+
+
+def oracle_hybrid_forward_blocks(o, cfg, B, cap, kv_bits, blocks):
+    st = O.lib().orc_hybrid_state_create(o, B, cap, kv_bits)
+    outs = []
+    for tok in blocks:
+        T = tok.shape[1]
+        lg = np.zeros((B, T, cfg["vocab"]), np.uint16)
+        assert O.lib().orc_hybrid_forward(o, st, O.ptr(np.ascontiguousarray(tok)), B, T, O.ptr(lg)) == 0
+        outs.append(lg)
+    O.lib().orc_hybrid_state_free(st)
+    return outs
+
+
+def oracle_hybrid_spec(o, prompts, MT, kv_bits):
+    B, P = prompts.shape
+    out = np.zeros((B, MT), np.int32)
+    st = np.zeros(5, np.int64)
+    assert O.lib().orc_hybrid_spec_generate(o, O.ptr(np.ascontiguousarray(prompts)), B, P, MT, kv_bits, O.ptr(out),
+                                            O.ptr(st)) == 0
+    return out, st

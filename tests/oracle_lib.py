@@ -45,6 +45,12 @@ class ModelCfg(C.Structure):
                 ("rope_high_freq", F), ("rope_orig_max_pos", F)]
 
 
+class HybridCfg(C.Structure):
+    _fields_ = [("hidden", I), ("layers", I), ("attn_every", I), ("heads", I), ("kv_heads", I),
+                ("lin_k_heads", I), ("lin_v_heads", I), ("experts", I), ("top_k", I), ("expert_inter", I),
+                ("shared_inter", I), ("vocab", I), ("rope_theta", F), ("eps", F), ("bits", I)]
+
+
 class SpecParams(C.Structure):
     _fields_ = [("K", I), ("max_tokens", I), ("temperature", F), ("top_p", F), ("seed", U64),
                 ("draft_layers", I), ("context_len", I), ("context_seed", U64)]
@@ -85,6 +91,12 @@ def _declare(L):
         "orc_cache_fill_synthetic": (I, [P, I, U64, U32]),
         "orc_model_set_tp": (I, [P, I]),
         "orc_log": (F, [F]),
+        "orc_hybrid_create": (P, [C.POINTER(HybridCfg), U64]),
+        "orc_hybrid_free": (None, [P]),
+        "orc_hybrid_state_create": (P, [P, I, I, I]),
+        "orc_hybrid_state_free": (None, [P]),
+        "orc_hybrid_forward": (I, [P, P, P, I, I, P]),
+        "orc_hybrid_spec_generate": (I, [P, P, I, I, I, I, P, P]),
         "orc_gdn_verify": (I, [I, I, I, I, P, P, P, P, P, P, P, P, F, P, P, P, P]),
         "orc_gdn_commit": (I, [I, I, I, I, P, P, P, P, P]),
         "orc_moe_route": (I, [P, I, I, I, P, P]),

@@ -58,3 +58,20 @@ def test_moe_experts_oracle_matches_dequant_matmul(bits):
     ref = H.reference_experts(c)
     # bf16 rounding of gate / up / act / each expert's output
     assert np.abs(got - ref).max() < 2e-2 * np.abs(ref).max() + 1e-2
+
+
+def test_hybrid_oracle_block_equals_token_by_token():
+    # exact mode: a forward over a 6-token block and six single-token
+    # forwards give the same logits (attention cache, Gated DeltaNet state
+    # and conv window carried across calls, MoE per row)
+    O.lib().orc_set_mma_min_m(0)
+    cfg = H.TINY_HYBRID
+    o = H.oracle_hybrid(cfg, 9)
+    tok = np.random.RandomState(2).randint(0, cfg["vocab"], (2, 10)).astype(np.int32)
+    pre = tok[:, :4]
+    blk = H.oracle_hybrid_forward_blocks(o, cfg, 2, 32, 8, [pre, tok[:, 4:]])[1]
+    one = H.oracle_hybrid_forward_blocks(o, cfg, 2, 32, 8, [pre] + [tok[:, i:i + 1] for i in range(4, 10)])[1:]
+    for i in range(6):
+        np.testing.assert_array_equal(blk[:, i], one[i][:, 0])
+    O.lib().orc_hybrid_free(o)
+    O.lib().orc_set_mma_min_m(16)
