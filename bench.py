@@ -62,6 +62,12 @@ WORKLOADS = {
                                            K=5, batch=8, prompt=512, new=512, kv_bits=4,
                                            temperature=0.7, top_p=0.9, cpu_prompt=32, cpu_steps=3, steps=5,
                                            profile="verify_pass_qwen3_8b_k5_bs8.md"),
+    # Qwen3-Next-style hybrid (Gated DeltaNet : gated attention
+    # 3:1, 512 experts top-10 + shared expert) with its MTP head drafting 2
+    # tokens; replicas only (each rank decodes its own 4 sequences).
+    "qwen3-next-mtp2-bs4": dict(arch="QWEN3_NEXT_HYBRID", hybrid=True, K=2, batch=4, prompt=1024, new=128,
+                                kv_bits=16, temperature=0.0, top_p=1.0, steps=2, draft=None,
+                                draft_layers=0, profile="verify_pass_qwen3_next_mtp2_bs4.md"),
     # tensor-parallel over the N GPUs (strong scaling); the draft
     # runs replicated on every rank.  The 8192-token random prefix is an
     # 8160-row synthetic KV context plus a 32-token random prompt.
@@ -249,6 +255,139 @@ def cpu_sample_composed(wl, arch, darch, seed, reps, tokens_per_step):
                 dhead_s=dh, cores=L.orc_threads(), wall_s=time.time() - t0)
 
 
+def cpu_sample_hybrid(wl, arch, seed, reps, tokens_per_step):
+    """Bounded CPU sample of configs[3]: the oracle times a 2-layer model
+    (one Gated DeltaNet + one gated-attention layer, each with its MoE block)
+    of the full widths at the verify shape (B x 3 tokens over the prompt's
+    cache), with and without the lm_head; the oracle's MoE cost is per
+    (token, selected expert), so 16 experts stand in for 512 (the router is
+    timed separately at full width).  A step = 24 x the 2-layer body + head
+    + 2 MTP drafts (each one attention + MoE layer on B rows + head)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    L = O.lib()
+    L.orc_set_mma_min_m(0)
+    B, P = wl["batch"], wl["prompt"]
+    cfg = dict(arch, layers=2, attn_every=2, experts=max(16, arch["top_k"] + 1))
+    t0 = time.time()
+    m = L.orc_hybrid_create(C.byref(O.HybridCfg(**cfg)), seed)
+    rng = np.random.RandomState(seed)
+    st = L.orc_hybrid_state_create(m, B, P + 64, wl["kv_bits"])
+    pre = rng.randint(0, arch["vocab"], (B, 32)).astype(np.int32)
+    L.orc_hybrid_forward(m, st, O.ptr(pre), B, 32, None)
+    lg = np.zeros((B, 3, arch["vocab"]), np.uint16)
+    body, full = [], []
+    for i in range(reps + 1):
+        tok = rng.randint(0, arch["vocab"], (B, 3)).astype(np.int32)
+        a = time.perf_counter()
+        L.orc_hybrid_forward(m, st, O.ptr(tok), B, 3, None)
+        b_ = time.perf_counter()
+        L.orc_hybrid_forward(m, st, O.ptr(tok), B, 3, O.ptr(lg))
+        c_ = time.perf_counter()
+        if i:
+            body.append(b_ - a)
+            full.append(c_ - b_)
+    L.orc_hybrid_state_free(st)
+    L.orc_hybrid_free(m)
+    L.orc_set_mma_min_m(16)
+    t2 = statistics.median(body)
+    head = max(0.0, statistics.median(full) - t2)
+    # the cached context is 32 tokens here, not 1024: attention is a small
+    # share of the per-layer cost (experts and projections dominate)
+    step = (arch["layers"] / 2) * t2 + head + 2 * (t2 / 2 + head)
+    return dict(value=tokens_per_step * B / step, step_s=step, body_s=t2, head_s=head, cores=L.orc_threads(),
+                wall_s=time.time() - t0)
+
+
+def run_hybrid(args, wl, world, rank, local):
+    """configs[3] through the public hybrid API (lmx_hybrid_spec_*)."""
+    lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
+    lmx.call("lmx_set_device", local)
+    arch = getattr(lmx, wl["arch"])
+    B, P, MT = wl["batch"], wl["prompt"], wl["new"]
+    h = C.c_void_p()
+    lmx.call("lmx_hybrid_create", C.byref(lmx.HybridConfig(**arch)), args.seed, C.byref(h))
+    sp = C.c_void_p()
+    lmx.call("lmx_hybrid_spec_create", h, B, MT, P, wl["kv_bits"], C.byref(sp))
+    prompts = np.random.RandomState(args.seed + rank).randint(0, arch["vocab"], (B, P)).astype(np.int32)
+    out = np.zeros((B, MT), np.int32)
+    stats = np.zeros(5, np.int64)
+
+    def one():
+        t0 = time.perf_counter()
+        lmx.call("lmx_hybrid_spec_prefill", sp, prompts.ctypes.data)
+        sec = C.c_double()
+        lmx.call("lmx_hybrid_spec_decode", sp, 1, C.byref(sec))
+        lmx.call("lmx_hybrid_spec_result", sp, out.ctypes.data, stats.ctypes.data)
+        return time.perf_counter() - t0, sec.value, stats.copy()
+
+    for _ in range(args.warmup):
+        one()
+    clocks = Clocks(local)
+    barrier(world)
+    launches0 = lmx.lib().lmx_launch_count()
+    clocks.start()
+    wall, dec, toks, acc, prop, steps, replays = 0.0, 0.0, 0, 0, 0, 0, 0
+    for _ in range(args.steps):
+        w, d, st = one()
+        wall += w
+        dec += d
+        toks += min(int(st[3]), B * MT)
+        steps += int(st[0])
+        prop += int(st[1])
+        acc += int(st[2])
+        replays += int(st[4])
+    barrier(world)
+    ck = clocks.stop()
+    nl = C.c_int64()
+    lmx.call("lmx_hybrid_spec_step_launches", sp, C.byref(nl))
+    gpu_launches = lmx.lib().lmx_launch_count() - launches0 + replays * nl.value
+    vsec, vbytes = C.c_double(), C.c_double()
+    lmx.call("lmx_hybrid_spec_profile", sp, 10, C.byref(vsec), C.byref(vbytes))
+    vsec, vbytes = vsec.value, vbytes.value
+    wall_m, dec_m = reduce(world, [wall, dec], "max")
+    toks_all = int(reduce(world, [float(toks)], "sum")[0])
+    peak, peak_kind = peaks()
+    achieved = vbytes / vsec / 1e9
+    res = {
+        "metric": METRIC, "value": round(toks_all / dec_m, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * wall_m / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "batch": B, "prompt": P, "new_tokens": MT, "kv_bits": wl["kv_bits"],
+                   "weights": "4-bit g64", "draft": "MTP head, 2 tokens per step", "temperature": 0.0,
+                   "parallelism": f"replicas x{world} (independent sequences per rank)",
+                   "l2": f"weights and experts ({vbytes / 1e6:.0f} MB per verify pass) exceed L2; no flush"},
+        "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * MT * 4 + 40},
+        "roofline": {"bound": "hbm", "kernel": f"verify pass ({arch['layers']} layers + lm_head, {B * 3} rows)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_kind, "algorithmic_bytes": vbytes, "verify_pass_us": round(vsec * 1e6, 2),
+                     "traffic": None},
+        "acceptance": {"accepted": acc, "proposed": prop, "rate": round(acc / prop, 4) if prop else None,
+                       "tokens_per_step": round(toks / max(1, steps), 3)},
+        "clocks": ck, "gpu_launches": int(gpu_launches),
+    }
+    if world == 1 and rank == 0 and not args.no_cpu:
+        tps = toks / max(1, steps)
+        r = cpu_sample_hybrid(wl, arch, args.seed, 2, tps)
+        res["cpu_baseline"] = {"value": round(r["value"], 4), "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+                               "sample": cpu_hybrid_sample_text(wl, arch, r, tps)}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    lmx.lib().lmx_hybrid_spec_free(sp)
+    lmx.lib().lmx_hybrid_free(h)
+    return 0
+
+
+def cpu_hybrid_sample_text(wl, arch, r, tps):
+    return (f"oracle/ C++ restatement, {r['cores']} threads: a 2-layer slice (one Gated DeltaNet + one gated "
+            f"attention layer, full widths, 16 experts for the per-token expert cost) at {wl['batch']} x 3 verify "
+            f"rows ({r['body_s'] * 1e3:.0f} ms) x {arch['layers'] // 2} + lm_head ({r['head_s'] * 1e3:.0f} ms) + 2 "
+            f"MTP drafts = {r['step_s']:.2f} s per step at {tps:.3f} tokens per sequence-step "
+            f"({r['wall_s']:.0f} s of CPU sampling)")
+
+
 def cpu_composed_sample_text(wl, arch, r, tps):
     return (f"oracle/ C++ restatement, {r['cores']} threads: one full-size target layer at "
             f"M={wl['batch'] * (wl['K'] + 1)} over a {wl['context'] + wl['prompt']}-row context "
@@ -265,6 +404,22 @@ def run_reference(args, wl, world, rank):
     arch = getattr(lmx, wl["arch"])
     darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     prompts = np.random.RandomState(args.seed).randint(0, arch["vocab"], (wl["batch"], wl["prompt"]))
+    if wl.get("hybrid"):
+        r = cpu_sample_hybrid(wl, arch, args.seed, max(1, args.steps), 1.0)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * r["step_s"], 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "batch": wl["batch"], "prompt": wl["prompt"],
+                       "new_tokens": wl["new"], "kv_bits": wl["kv_bits"]},
+            "cpu_baseline": {"value": round(r["value"], 4), "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+                             "sample": cpu_hybrid_sample_text(wl, arch, r, 1.0)},
+            "e2e": {"value": round(r["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
     if wl.get("tp"):
         # composed sample; a step emits at least one token per sequence (the
         # lower bound is used: no device run here to measure acceptance)
@@ -741,6 +896,8 @@ def main():
     try:
         if args.impl == "reference":
             return run_reference(args, wl, world, rank)
+        if wl.get("hybrid"):
+            return run_hybrid(args, wl, world, rank, local)
         return run_lmx(args, wl, world, rank, local)
     finally:
         if world > 1:

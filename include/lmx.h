@@ -245,6 +245,12 @@ int lmx_hybrid_spec_prefill(void* spec, const int32_t* prompts_host);
 int lmx_hybrid_spec_decode(void* spec, int use_graph, double* seconds);
 int lmx_hybrid_spec_result(void* spec, int32_t* out_host, int64_t* stats_host);
 int lmx_hybrid_spec_free(void* spec);
+/* Measurement hooks: time `iters` verify passes (trunk over 3 tokens,
+ * after a prefill) -> seconds per pass and its algorithmic bytes (the
+ * experts counted from the pass's own routing); kernel launches of one
+ * captured step. */
+int lmx_hybrid_spec_profile(void* spec, int iters, double* seconds, double* bytes);
+int lmx_hybrid_spec_step_launches(void* spec, int64_t* launches);
 
 /* ---------------------------------------------------------------------------
  * Models.  Replaces the ModelContext function table of a loaded Qwen3 /

@@ -311,7 +311,9 @@ static int hyb_state_create(const HybModel& m, int B, int cap, int kv_bits, int 
   if (!rc) rc = ar.alloc(&s->gout, (size_t)R * Z);
   if (!rc) rc = ar.alloc(&s->gscr, gdn_scratch_bytes(B, Tmax, c.lin_k_heads, Hv));
   if (!rc) rc = ar.alloc(&s->rl, (size_t)R * c.experts);
-  if (!rc) rc = ar.alloc(&s->idx, (size_t)R * c.top_k);
+  // routing of every MoE block of the last forward (layers, then the MTP
+  // layer), kept for counting the experts a pass touches
+  if (!rc) rc = ar.alloc(&s->idx, (size_t)(c.layers + 1) * R * c.top_k);
   if (!rc) rc = ar.alloc(&s->wts, (size_t)R * c.top_k);
   if (!rc) rc = ar.alloc(&s->acte, (size_t)R * c.top_k * c.expert_inter);
   if (!rc) rc = ar.alloc(&s->ymoe, (size_t)R * H);
@@ -477,14 +479,15 @@ static int hyb_gdn_commit_all(const HybModel& m, HybState& s, int B, int T, cons
 
 // MoE block of layer L on s.h: xn = rms(h), y = experts + gated shared expert,
 // h += y.
-static int hyb_moe(const HybModel& m, HybState& s, const HybLayer& L, int R, cudaStream_t st) {
+static int hyb_moe(const HybModel& m, HybState& s, const HybLayer& L, int l, int R, cudaStream_t st) {
   const lmx_hybrid_config& c = m.c;
   const int H = c.hidden;
+  int32_t* idx = s.idx + (size_t)l * s.Rmax * c.top_k;
   int rc = launch_rms_norm(s.h, L.post_norm, s.xn, R, H, c.eps, st);
   if (!rc) rc = hyb_qmm(s.xn, &L.router, 1, c.experts, s.rl, c.experts, R, H, c.bits, kPlain, nullptr, st);
   if (!rc)
     rc = cuda_check(lmx_launch(moe_route_kernel, dim3((R + 7) / 8), dim3(256), 0, st, true, (const bf16_t*)s.rl, R,
-                               c.experts, c.top_k, s.idx, s.wts),
+                               c.experts, c.top_k, idx, s.wts),
                     "moe_route");
   if (rc) return rc;
   MoeArgs a;
@@ -494,7 +497,7 @@ static int hyb_moe(const HybModel& m, HybState& s, const HybLayer& L, int R, cud
   a.E = c.experts;
   a.k = c.top_k;
   a.x = s.xn;
-  a.idx = s.idx;
+  a.idx = idx;
   a.w = s.wts;
   a.gw = L.eg.w;
   a.uw = L.eu.w;
@@ -542,7 +545,7 @@ static int hyb_forward(const HybModel& m, HybState& s, const int32_t* tok, int l
     if (rc) break;
     if (L.attn) rc = hyb_attention(m, s, L, s.kv->kv[ia++], B, T, st);
     else rc = hyb_gdn(m, s, L, s.gdn[ig++], B, T, commit_idx ? 1 : T, commit_idx, st);
-    if (!rc) rc = hyb_moe(m, s, L, R, st);
+    if (!rc) rc = hyb_moe(m, s, L, l, R, st);
   }
   if (!rc) rc = launch_rms_norm(s.h, m.final_norm, s.hid, R, H, c.eps, st);
   if (rc || !logits) return rc;
@@ -635,7 +638,7 @@ static int hyb_mtp_draft(HybSpec& sp, int i, const bf16_t* hidden_in, cudaStream
   if (!rc) rc = hyb_qmm(s.cat, &m.mtp_fc, 1, H, s.h, H, B, 2 * H, c.bits, kPlain, nullptr, st);
   if (!rc) rc = launch_rms_norm(s.h, m.mtp.in_norm, s.xn, B, H, c.eps, st);
   if (!rc) rc = hyb_attention(m, s, m.mtp, s.mtp_kv->kv[0], B, 1, st);
-  if (!rc) rc = hyb_moe(m, s, m.mtp, B, st);
+  if (!rc) rc = hyb_moe(m, s, m.mtp, m.c.layers, B, st);
   if (!rc) rc = add_len(s.mtp_kv->len, B, 1, st);
   if (!rc) rc = cuda_check(cudaMemcpyAsync(sp.mtp_hid, s.h, (size_t)B * H * 2, cudaMemcpyDeviceToDevice, st), "mtp hid");
   if (!rc) rc = launch_rms_norm(s.h, m.mtp_norm, s.xn, B, H, c.eps, st);
@@ -813,6 +816,70 @@ static int hyb_spec_decode(HybSpec& sp, int use_graph, double* seconds) {
   return rc;
 }
 
+// Time `iters` verify passes (the trunk over the current [d0, d1, d2], no
+// commit) on the spec's stream after a prefill; bytes = algorithmic bytes of
+// one pass: every layer's projections, router, shared expert and the
+// experts its routing touched (counted from the pass's own routing), the
+// lm_head, KV rows read and written, Gated DeltaNet states read and their
+// 3 snapshots written.
+static double qw_bytes(const QWeight& w, int bits) { return (double)w.N * w.K * bits / 8 + (double)w.N * (w.K / 64) * 4; }
+
+static int hyb_spec_profile(HybSpec& sp, int iters, double* seconds, double* bytes) {
+  if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "hybrid profile before prefill");
+  HybModel& m = *sp.m;
+  HybState& s = *sp.s;
+  const lmx_hybrid_config& c = m.c;
+  const int B = sp.B, R = B * kHybN, bits = c.bits;
+  cudaStream_t st = sp.st;
+  auto once = [&]() { return hyb_forward(m, s, sp.vt, kHybN, 0, B, kHybN, s.logits, false, nullptr, st); };
+  int rc = once();
+  if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "profile");
+  if (rc) return rc;
+  std::vector<int32_t> idx((size_t)c.layers * s.Rmax * c.top_k);
+  rc = cuda_check(cudaMemcpy(idx.data(), s.idx, idx.size() * 4, cudaMemcpyDeviceToHost), "idx");
+  std::vector<int> lens(B, 0);
+  if (!rc && s.kv) rc = cuda_check(cudaMemcpy(lens.data(), s.kv->len, B * 4, cudaMemcpyDeviceToHost), "len");
+  if (rc) return rc;
+  double by = qw_bytes(m.lm_head, bits) + (double)R * c.hidden * 2;
+  const double per_expert = qw_bytes(m.L[0].eg, bits) / c.experts * 2 + qw_bytes(m.L[0].ed, bits) / c.experts;
+  for (int l = 0; l < c.layers; ++l) {
+    const HybLayer& L = m.L[l];
+    for (const QWeight* q : {&L.q, &L.k, &L.v, &L.qg, &L.o, &L.wqkv, &L.wz, &L.wb, &L.wa, &L.wout, &L.router, &L.sg,
+                             &L.su, &L.sd, &L.sgate})
+      if (q->w) by += qw_bytes(*q, bits);
+    std::vector<char> seen(c.experts, 0);
+    int uniq = 0;
+    for (int r = 0; r < R * c.top_k; ++r) {
+      const int e = idx[(size_t)l * s.Rmax * c.top_k + r];
+      if (e >= 0 && e < c.experts && !seen[e]) { seen[e] = 1; ++uniq; }
+    }
+    by += uniq * per_expert;
+    if (L.attn) {
+      const double row = (double)c.kv_heads * kHeadDim * (s.kv->bits == 16 ? 2.0 : s.kv->bits / 8.0 + 4.0 / 64) * 2;
+      for (int b = 0; b < B; ++b) by += row * (lens[b] + kHybN);
+    } else {
+      by += (double)B * c.lin_v_heads * kGdnD * kGdnD * 4 * (1 + kHybN);
+    }
+  }
+  for (int i = 0; i < 2 && !rc; ++i) rc = once();
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, st);
+  nvtxRangePushA("lmx_verify_pass");
+  for (int i = 0; i < iters && !rc; ++i) rc = once();
+  nvtxRangePop();
+  cudaEventRecord(e1, st);
+  if (!rc) rc = cuda_check(cudaEventSynchronize(e1), "profile");
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (seconds) *seconds = ms * 1e-3 / (iters > 0 ? iters : 1);
+  if (bytes) *bytes = by;
+  return rc;
+}
+
 struct HybStateHandle {
   HybModel* m = nullptr;
   std::unique_ptr<HybState> s;
@@ -932,4 +999,18 @@ extern "C" int lmx_hybrid_spec_result(void* spec, int32_t* out_host, int64_t* st
 extern "C" int lmx_hybrid_spec_free(void* spec) {
   delete (HybSpec*)spec;
   return LMX_OK;
+}
+
+extern "C" int lmx_hybrid_spec_profile(void* spec, int iters, double* seconds, double* bytes) {
+  if (!spec) return set_error(LMX_ERR_INVALID, "hybrid_spec_profile: null argument");
+  return hyb_spec_profile(*(HybSpec*)spec, iters, seconds, bytes);
+}
+
+extern "C" int lmx_hybrid_spec_step_launches(void* spec, int64_t* launches) {
+  HybSpec* sp = (HybSpec*)spec;
+  if (!sp || !launches || !sp->graph) return set_error(LMX_ERR_INVALID, "hybrid_spec_step_launches: no graph yet");
+  size_t nodes = 0;
+  int rc = cuda_check(cudaGraphGetNodes(sp->graph, nullptr, &nodes), "graph nodes");
+  *launches = (int64_t)nodes;
+  return rc;
 }

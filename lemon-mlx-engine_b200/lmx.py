@@ -62,6 +62,8 @@ SIGNATURES = {
     "lmx_hybrid_spec_decode": (I, [P, I, P]),
     "lmx_hybrid_spec_result": (I, [P, P, P]),
     "lmx_hybrid_spec_free": (I, [P]),
+    "lmx_hybrid_spec_profile": (I, [P, I, P, P]),
+    "lmx_hybrid_spec_step_launches": (I, [P, P]),
     "lmx_model_view": (I, [P, I, P]),
     "lmx_model_free": (I, [P]),
     "lmx_model_weight": (I, [P, I, I, P, P, P]),
