@@ -304,6 +304,8 @@ def run_hybrid(args, wl, world, rank, local):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", local)
     arch = getattr(lmx, wl["arch"])
+    if args.layers:
+        arch = dict(arch, layers=args.layers)
     B, P, MT = wl["batch"], wl["prompt"], wl["new"]
     h = C.c_void_p()
     lmx.call("lmx_hybrid_create", C.byref(lmx.HybridConfig(**arch)), args.seed, C.byref(h))
@@ -321,6 +323,15 @@ def run_hybrid(args, wl, world, rank, local):
         lmx.call("lmx_hybrid_spec_result", sp, out.ctypes.data, stats.ctypes.data)
         return time.perf_counter() - t0, sec.value, stats.copy()
 
+    if args.profile_verify:
+        # prefill only, then N verify passes inside the NVTX range lmx_verify_pass
+        lmx.call("lmx_hybrid_spec_prefill", sp, prompts.ctypes.data)
+        vs, vb = C.c_double(), C.c_double()
+        lmx.call("lmx_hybrid_spec_profile", sp, args.profile_verify, C.byref(vs), C.byref(vb))
+        print(json.dumps({"verify_pass_us": round(vs.value * 1e6, 2), "bytes": vb.value}), flush=True)
+        lmx.lib().lmx_hybrid_spec_free(sp)
+        lmx.lib().lmx_hybrid_free(h)
+        return 0
     for _ in range(args.warmup):
         one()
     clocks = Clocks(local)
