@@ -608,7 +608,17 @@ def run_lmx(args, wl, world, rank, local):
 
 
 QMM_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
-QMM_MS = [1, 2, 5, 8, 16, 32]
+QMM_MS = [1, 2, 4, 5, 8, 12, 16, 32]
+
+
+def qmm_path(lmx, M):
+    """Which K1 kernel takes M rows under the library's current thresholds."""
+    mma, tcg = lmx.lib().lmx_mma_min_m(), lmx.lib().lmx_gemv_tc_min_m()
+    if mma > 0 and M >= mma:
+        return "tcgen05"
+    if mma > 0 and tcg > 0 and tcg <= M <= 16:
+        return "mma.sync"
+    return "gemv"
 
 
 def qmm_time(lmx, N, K, M, bits, seed=2026):
@@ -656,7 +666,7 @@ def qmm_time(lmx, N, K, M, bits, seed=2026):
     del g
     byts = wbytes + N * (K // 64) * 4 + M * K * 2 + M * N * 2
     return dict(N=N, K=K, M=M, bits=bits, us=round(t * 1e6, 2), GBs=round(byts / t / 1e9, 1),
-                path="tcgen05" if M >= lmx.lib().lmx_mma_min_m() > 0 else "gemv")
+                path=qmm_path(lmx, M))
 
 
 def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):

@@ -61,6 +61,15 @@ int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
 int lmx_set_mma_min_m(int m);
 int lmx_mma_min_m(void);
 
+/* Smallest M routed to the small-batch tensor-core GEMV (mma.sync with the
+ * weights dequantized into register fragments; default 4) for M below the
+ * tcgen05 threshold; 0 = off.  Only in tensor-core mode: with
+ * lmx_set_mma_min_m(0) every M runs the canonical GEMV order whatever this
+ * is.  Results are within the tensor-core tolerance.  Process-wide; no
+ * reference counterpart. */
+int lmx_set_gemv_tc_min_m(int m);
+int lmx_gemv_tc_min_m(void);
+
 /* mx::fast::rms_norm(x, w, eps) over the last axis (e.g. qwen3.cpp:78,145).
  * x, y [rows, dim] bf16 (may alias), w [dim] bf16. */
 int lmx_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,

@@ -15,6 +15,7 @@
 #include "qmm_mma.cuh"
 #include "attn.cuh"
 #include "attn_mma.cuh"
+#include "qmv_tc.cuh"
 #include "engine_kernels.cuh"
 #include "sample.cuh"
 #include "tp.cuh"
@@ -255,8 +256,12 @@ static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
 // K1 tensor-core path (M >= the threshold, default 16; 0 disables it)
 // ---------------------------------------------------------------------------
 static int g_mma_min_m = 16;
+static int g_tcg_min_m = 4;
 int qmm_mma_min_m() { return g_mma_min_m; }
 bool qmm_uses_mma(int M) { return g_mma_min_m > 0 && M >= g_mma_min_m; }
+// the small-batch tensor-core GEMV (qmv_tc.cuh): M in [g_tcg_min_m, the
+// tcgen05 threshold), tensor-core mode only (off in exact mode)
+bool qmm_uses_tcg(int M) { return g_mma_min_m > 0 && g_tcg_min_m > 0 && M >= g_tcg_min_m && M < g_mma_min_m && M <= 16; }
 
 // Activation map: bf16 [M][ldx], box {64, box_h}, 128-byte swizzle (the UMMA
 // K-major canonical layout).  Encoded per launch: activation buffers vary.
@@ -403,6 +408,54 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
   return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmm_mma_kernel<BITS>, mp, a)), "qmm_mma: launch");
 }
 
+template <int BITS>
+static int launch_tcg_t(const QmmArgs& a, cudaStream_t st) {
+  int tiles = 0;
+  if (a.mode == QMM_SWIGLU) {
+    tiles = (a.N + kTcgRows - 1) / kTcgRows;
+  } else {
+    for (int i = 0; i < a.nmat; ++i) tiles += (a.mat[i].rows + kTcgRows - 1) / kTcgRows;
+  }
+  // split K over a cluster while the tiles fill fewer than two waves of
+  // 148 SMs and every warp keeps at least two groups
+  const int G = a.K / 64;
+  int ks = 1;
+  while (ks < 4 && tiles * ks < 2 * 148 && G >= 8 * 2 * (2 * ks)) ks *= 2;
+  // the (scale, bias) table: rows of the tile x (groups of one rank + 1) words
+  const size_t smem = (size_t)(a.mode == QMM_SWIGLU ? 2 * kTcgRows : kTcgRows) * ((G + ks - 1) / ks + 1) * 4;
+  static size_t smem_set[2][64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (smem > 32 * 1024 && smem > smem_set[a.M > 8][d & 63]) {
+    const void* fn = a.M <= 8 ? (const void*)qmv_tc_kernel<BITS, 1> : (const void*)qmv_tc_kernel<BITS, 2>;
+    int rc = cuda_check(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                        "qmv_tc: set smem");
+    if (rc) return rc;
+    smem_set[a.M > 8][d & 63] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * ks);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (ks > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = ks;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  if (a.M <= 8)
+    return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_tc_kernel<BITS, 1>, a, ks)), "qmv_tc: launch");
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_tc_kernel<BITS, 2>, a, ks)), "qmv_tc: launch");
+}
+
 int launch_qmm(const QmmCall& c, cudaStream_t st) {
   if (c.M == 0 || c.N == 0) return LMX_OK;
   if (c.M < 0 || c.N < 0 || c.K <= 0 || c.K % 64)
@@ -438,6 +491,7 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
   a.mode = c.mode;
   a.err = device_error_word();
   if (!c.norm_w && qmm_uses_mma(c.M)) return c.bits == 4 ? launch_mma_t<4>(a, st) : launch_mma_t<8>(a, st);
+  if (!c.norm_w && qmm_uses_tcg(c.M)) return c.bits == 4 ? launch_tcg_t<4>(a, st) : launch_tcg_t<8>(a, st);
   return c.bits == 4 ? launch_qmv_bits<4>(a, st) : launch_qmv_bits<8>(a, st);
 }
 
@@ -501,6 +555,14 @@ extern "C" int lmx_set_mma_min_m(int m) {
   return LMX_OK;
 }
 extern "C" int lmx_mma_min_m(void) { return g_mma_min_m; }
+
+extern "C" int lmx_set_gemv_tc_min_m(int m) {
+  if (m < 0 || m > 16) return set_error(LMX_ERR_INVALID, "gemv_tc_min_m %d (0 = off, at most 16)", m);
+  g_tcg_min_m = m;
+  return LMX_OK;
+}
+
+extern "C" int lmx_gemv_tc_min_m(void) { return g_tcg_min_m; }
 
 extern "C" int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                                     const void* biases, void* y, int M, int N, int K, int group_size,

@@ -47,6 +47,7 @@ unsigned* device_error_word();
 int launch_qmm(const QmmCall& c, cudaStream_t st);
 // Tensor-core path for M >= the threshold (un-normalised x only).
 bool qmm_uses_mma(int M);
+bool qmm_uses_tcg(int M);
 int qmm_mma_min_m();
 int launch_rms_norm(const bf16_t* x, const bf16_t* w, bf16_t* y, int rows, int dim, float eps,
                     cudaStream_t st);

@@ -33,6 +33,8 @@ SIGNATURES = {
     "lmx_set_mma_min_m": (I, [I]),
     "lmx_launch_count": (C.c_longlong, []),
     "lmx_mma_min_m": (I, []),
+    "lmx_set_gemv_tc_min_m": (I, [I]),
+    "lmx_gemv_tc_min_m": (I, []),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
     "lmx_sample": (I, [P, I, I, F, F, P, P, P]),
