@@ -6,8 +6,8 @@
 // fp32 accumulate).
 //
 // One CTA of 16 warps per (sequence, KV head, row tile of <= 64 rows,
-// split): the split covers `cpc` chunks of 128 keys, processed with an
-// online softmax:
+// split): the split covers cpc = ceil(chunks / nsplit) of the 128-key chunks
+// the tile reaches at the current cache length, with an online softmax:
 //   stage K, V chunk -> bf16 smem (dequantized on the way, rows past the
 //   visible range zero-filled).  Affine (4/8-bit) caches: the packed rows of
 //   the next chunk stream into a two-stage raw ring by cp.async.bulk (one
@@ -144,10 +144,10 @@ LMX_DEV void sdpa_stage_raw(int jn, const uint8_t* raw, const uint32_t (&sb)[2 *
 }
 
 // MT = m16 row tiles (rows padded to 16*MT <= 64).  a.tiles row tiles of
-// 16*MT rows, a.nsplit splits of cpc chunks; partials [b][kvh][tile][split]
+// 16*MT rows, a.nsplit splits of the reached chunks; partials [b][kvh][tile][split]
 // [kAttnMmaRows][kPartStride], counters [b][kvh][tile].
 template <int MT, int BITS>
-__global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a, int cpc) {
+__global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
   constexpr int MP = 16 * MT;
   constexpr size_t RAW = sdpa_raw_stage<BITS>(), RB = (size_t)kHeadDim * BITS / 8;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a, i
   const int off = a.kv.len[b];
   const int jmax = off + (r0 + nr - 1) / G + 1;
   const int nchunks = (jmax + kAttnChunk - 1) / kAttnChunk;
+  const int cpc = (nchunks + a.nsplit - 1) / a.nsplit;  // this block's chunks, evenly over the splits
   const int tile_splits = (nchunks + cpc - 1) / cpc;
   if (split >= tile_splits) return;
   const int c_begin = split * cpc, c_end = min(nchunks, c_begin + cpc);

@@ -47,20 +47,49 @@ static int launch_sdpa_t(const SdpaArgs& a, int B, cudaStream_t st) {
 static constexpr int kSdpaLongCache = 2048;  // cache rows from which every block takes the tensor-core SDPA
 
 // Tensor-core SDPA geometry (attn_mma.cuh): row tiles of 16*MT <= 64 rows,
-// splits of cpc 128-key chunks, about 4 CTAs per SM over the capacity.
+// nsplit key splits per (sequence, KV head, tile), as many as one wave of
+// resident CTAs holds (at most one per 128-key chunk of the capacity).  The
+// kernel divides the chunks a block actually reaches (the cache length on
+// the device) evenly over the splits, so a graph captured once stays
+// balanced as the caches grow.
 struct SdpaMmaPlan {
-  int MT = 1, tiles = 1, nsplit = 1, cpc = 1;
+  int MT = 1, tiles = 1, nsplit = 1;
 };
-static SdpaMmaPlan sdpa_mma_plan(int B, int Hk, int rows, int cap) {
+template <int MT, int BITS>
+static int sdpa_mma_occupancy() {
+  static int occ[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  if (!occ[d & 63]) {
+    int n = 0;
+    if (cudaFuncSetAttribute(sdpa_mma_kernel<MT, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sdpa_mma_smem<MT, BITS>()) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, sdpa_mma_kernel<MT, BITS>, kAttnThreads,
+                                                      sdpa_mma_smem<MT, BITS>()) != cudaSuccess ||
+        n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    occ[d & 63] = n;
+  }
+  return occ[d & 63];
+}
+template <int MT>
+static int sdpa_mma_occupancy_t(int bits) {
+  return bits == 8 ? sdpa_mma_occupancy<MT, 8>() : (bits == 4 ? sdpa_mma_occupancy<MT, 4>()
+                                                               : sdpa_mma_occupancy<MT, 16>());
+}
+static SdpaMmaPlan sdpa_mma_plan(int B, int Hk, int rows, int cap, int bits) {
   SdpaMmaPlan p;
   const int r = rows < kAttnMmaRows ? rows : kAttnMmaRows;
   p.MT = (r + 15) / 16;
   p.tiles = (rows + 16 * p.MT - 1) / (16 * p.MT);
+  const int occ = p.MT == 1 ? sdpa_mma_occupancy_t<1>(bits)
+                            : (p.MT == 2 ? sdpa_mma_occupancy_t<2>(bits)
+                                         : (p.MT == 3 ? sdpa_mma_occupancy_t<3>(bits) : sdpa_mma_occupancy_t<4>(bits)));
   const int chunks = (cap + kAttnChunk - 1) / kAttnChunk;
   const int base = B * Hk * p.tiles;
-  const int want = std::max(1, (4 * device_sms() + base - 1) / base);
-  p.cpc = std::max(1, (chunks + want - 1) / want);
-  p.nsplit = (chunks + p.cpc - 1) / p.cpc;
+  p.nsplit = std::max(1, std::min(chunks, occ * device_sms() / std::max(1, base)));
   return p;
 }
 
@@ -75,7 +104,7 @@ static void sdpa_scratch_need(int B, int Tmax, int G, int Hk, int cap, size_t& p
 }
 
 template <int MT, int BITS>
-static int launch_sdpa_mma_tb(const SdpaArgs& a, int B, int cpc, cudaStream_t st) {
+static int launch_sdpa_mma_tb(const SdpaArgs& a, int B, cudaStream_t st) {
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
@@ -87,14 +116,14 @@ static int launch_sdpa_mma_tb(const SdpaArgs& a, int B, int cpc, cudaStream_t st
     attr_set[d & 63] = true;
   }
   return cuda_check(lmx_launch(sdpa_mma_kernel<MT, BITS>, dim3(a.nsplit * a.tiles, a.kv.Hk, B), dim3(kAttnThreads),
-                               sdpa_mma_smem<MT, BITS>(), st, true, a, cpc),
+                               sdpa_mma_smem<MT, BITS>(), st, true, a),
                     "sdpa_mma: launch");
 }
 template <int MT>
-static int launch_sdpa_mma_t(const SdpaArgs& a, int B, int cpc, cudaStream_t st) {
-  if (a.kv.bits == 8) return launch_sdpa_mma_tb<MT, 8>(a, B, cpc, st);
-  if (a.kv.bits == 4) return launch_sdpa_mma_tb<MT, 4>(a, B, cpc, st);
-  return launch_sdpa_mma_tb<MT, 16>(a, B, cpc, st);
+static int launch_sdpa_mma_t(const SdpaArgs& a, int B, cudaStream_t st) {
+  if (a.kv.bits == 8) return launch_sdpa_mma_tb<MT, 8>(a, B, st);
+  if (a.kv.bits == 4) return launch_sdpa_mma_tb<MT, 4>(a, B, st);
+  return launch_sdpa_mma_tb<MT, 16>(a, B, st);
 }
 
 static int launch_sdpa(const SdpaArgs& a_in, int B, cudaStream_t st) {
@@ -105,7 +134,7 @@ static int launch_sdpa(const SdpaArgs& a_in, int B, cudaStream_t st) {
   // kernel's per-split loads
   if (qmm_uses_mma(rows) || (qmm_mma_min_m() > 0 && a_in.kv.cap >= kSdpaLongCache)) {
     SdpaArgs a = a_in;
-    const SdpaMmaPlan p = sdpa_mma_plan(B, a.kv.Hk, rows, a.kv.cap);
+    const SdpaMmaPlan p = sdpa_mma_plan(B, a.kv.Hk, rows, a.kv.cap, a.kv.bits);
     a.err = device_error_word();
     a.tiles = p.tiles;
     a.nsplit = p.nsplit;
@@ -113,10 +142,10 @@ static int launch_sdpa(const SdpaArgs& a_in, int B, cudaStream_t st) {
         (size_t)B * a.kv.Hk * p.tiles > a.n_counters)
       return set_error(LMX_ERR_INVALID, "sdpa: scratch too small for the tensor-core path");
     switch (p.MT) {
-      case 1: return launch_sdpa_mma_t<1>(a, B, p.cpc, st);
-      case 2: return launch_sdpa_mma_t<2>(a, B, p.cpc, st);
-      case 3: return launch_sdpa_mma_t<3>(a, B, p.cpc, st);
-      default: return launch_sdpa_mma_t<4>(a, B, p.cpc, st);
+      case 1: return launch_sdpa_mma_t<1>(a, B, st);
+      case 2: return launch_sdpa_mma_t<2>(a, B, st);
+      case 3: return launch_sdpa_mma_t<3>(a, B, st);
+      default: return launch_sdpa_mma_t<4>(a, B, st);
     }
   }
   const SdpaArgs& a = a_in;

@@ -371,13 +371,6 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
   a.ldy = q.ldy;
   a.res = q.res;
   a.err = q.err;
-  // split K over a cluster until the grid covers the SMs (>= 2 chunks per CTA)
-  const int nk = q.K / kMmaK, target = device_sms() * sh.per_sm, base = ntiles * sh.mtiles;
-  int ks = target / (base > 0 ? base : 1);
-  if (ks > kMmaMaxSplit) ks = kMmaMaxSplit;
-  if (ks > nk / 2) ks = nk / 2;
-  if (ks < 1) ks = 1;
-  a.ks = ks;
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
@@ -387,6 +380,22 @@ static int launch_mma_t(const QmmArgs& q, cudaStream_t st) {
     if (rc) return rc;
     attr_set[d & 63] = true;
   }
+  // split-K factor: the largest (up to 8, >= 2 chunks per CTA) whose grid
+  // fits one wave of two CTAs per SM (each CTA's pipeline is latency-bound,
+  // so a second resident CTA adds throughput) on the SMs whole clusters can
+  // reach: clusters are placed within a GPC, and a grid of 6-CTA clusters was
+  // seen to reach 142 of 148 SMs, so 4% of the SMs are held back
+  const int nk = q.K / kMmaK, base = ntiles * sh.mtiles;
+  const int slots = sh.per_sm * (device_sms() * 96 / 100);
+  int ks = 1;
+  for (int k = kMmaMaxSplit; k >= 2; --k) {
+    if (k > nk / 2) continue;
+    if (base * k <= slots) {
+      ks = k;
+      break;
+    }
+  }
+  a.ks = ks;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ntiles * ks, sh.mtiles);
   cfg.blockDim = dim3(kMmaThreads);
@@ -501,7 +510,7 @@ int launch_rms_norm(const bf16_t* x, const bf16_t* w, bf16_t* y, int rows, int d
   if (!x || !w || !y || rows < 0 || dim <= 0 || (dim & 7) || ((uintptr_t)x & 15) || ((uintptr_t)w & 15) ||
       ((uintptr_t)y & 15))
     return set_error(LMX_ERR_INVALID, "rms_norm: bad arguments (16-byte aligned rows, dim %% 8 == 0)");
-  return cuda_check(lmx_launch(rms_norm_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, true, x, w, y,
+  return cuda_check(lmx_launch(rms_norm_kernel, dim3(rows), dim3(256), 0, st, true, x, w, y,
                                rows, dim, eps),
                     "rms_norm: launch");
 }

@@ -37,30 +37,64 @@ LMX_DEV float rms_factor_warp(const bf16_t* x, int dim, float eps, int lane) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(p, (float)dim), eps)));
 }
 
-// RMSNorm (mx::fast::rms_norm, e.g. src/llm/models/qwen3.cpp:78,145): one warp
-// per row, factor as above, y = bf16((x * r) * w).
+// RMSNorm (mx::fast::rms_norm, e.g. src/llm/models/qwen3.cpp:78,145): one
+// CTA per row.  Warp 0 forms the factor as above while every thread loads its
+// chunks of x and w (chunk c = threadIdx.x + 256 i); after the barrier (which
+// also makes in-place use safe: all of x is read before any y is written)
+// each thread writes y = bf16((x * r) * w) for its chunks.
+static constexpr int kNormChunks = 4;  // chunks per thread held in registers (dim <= 8192)
+
+LMX_DEV uint4 rms_apply8(const uint4& xv, const uint4& wv, float f) {
+  const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bf16_t lo = f2bf(__fmul_rn(__fmul_rn(lo_bf(xa[k]), f), lo_bf(wa[k])));
+    const bf16_t hi = f2bf(__fmul_rn(__fmul_rn(hi_bf(xa[k]), f), hi_bf(wa[k])));
+    o[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16_t* x, const bf16_t* w, bf16_t* y,
                                                        int rows, int dim, float eps) {
+  __shared__ float s_f;
   grid_wait();
   grid_launch_dependents();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int tid = threadIdx.x, lane = tid & 31, row = blockIdx.x;
   if (row >= rows) return;
   const bf16_t* xr = x + (size_t)row * dim;
-  const float f = rms_factor_warp(xr, dim, eps, lane);
   bf16_t* yr = y + (size_t)row * dim;
-  for (int c = lane; c < (dim >> 3); c += 32) {
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + 8 * c);
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * c);
-    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
-    uint32_t o[4];
+  const int nch = dim >> 3;
+  uint4 xv[kNormChunks], wv[kNormChunks];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const bf16_t lo = f2bf(__fmul_rn(__fmul_rn(lo_bf(xa[k]), f), lo_bf(wa[k])));
-      const bf16_t hi = f2bf(__fmul_rn(__fmul_rn(hi_bf(xa[k]), f), hi_bf(wa[k])));
-      o[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+  for (int i = 0; i < kNormChunks; ++i) {
+    const int c = tid + 256 * i;
+    if (c < nch) {
+      xv[i] = *reinterpret_cast<const uint4*>(xr + 8 * c);
+      wv[i] = *reinterpret_cast<const uint4*>(w + 8 * c);
     }
-    *reinterpret_cast<uint4*>(yr + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (tid < 32) {
+    const float f = rms_factor_warp(xr, dim, eps, lane);
+    if (lane == 0) s_f = f;
+  }
+  __syncthreads();
+  const float f = s_f;
+  if (nch <= 256 * kNormChunks) {
+#pragma unroll
+    for (int i = 0; i < kNormChunks; ++i) {
+      const int c = tid + 256 * i;
+      if (c < nch) *reinterpret_cast<uint4*>(yr + 8 * c) = rms_apply8(xv[i], wv[i], f);
+    }
+  } else {
+    // rows longer than the register tile: x may equal y, so every thread
+    // first holds its values (the loop writes only chunks it has read)
+    for (int c = tid; c < nch; c += 256) {
+      const uint4 a = *reinterpret_cast<const uint4*>(xr + 8 * c);
+      const uint4 b = *reinterpret_cast<const uint4*>(w + 8 * c);
+      *reinterpret_cast<uint4*>(yr + 8 * c) = rms_apply8(a, b, f);
+    }
   }
 }
 

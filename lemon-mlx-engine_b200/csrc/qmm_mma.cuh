@@ -371,11 +371,25 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
     uint32_t pph = 0;  // parity of the pfull phase of stage sp
     int s = 0;
     uint32_t aph = 0;  // parity of the mdone phase that frees A stage s
+    // one step (kMmaStep chunks) at a time: every wait and shared-memory load
+    // of the step first, then dequantization and TMEM stores chunk by chunk
+    // (the loads of the second chunk overlap the first one's work)
     for (int t = 0; t < nsteps && ok; ++t) {
       const int cnt = min(kMmaStep, nloc - kMmaStep * t);
-      for (int u = 0; u < cnt; ++u) {
+      if (t >= NA && !warp_wait(&mdone[s], aph, a.err, 0x66u)) {
+        ok = false;
+        break;
+      }
+      uint32_t wv[kMmaStep][BITS];  // this thread's 32 k of row rr per chunk (4 or 8 words)
+      bf16_t scu[kMmaStep], biu[kMmaStep];
+      int spu[kMmaStep];
+      bool endu[kMmaStep];
+#pragma unroll
+      for (int u = 0; u < kMmaStep; ++u) {
+        endu[u] = false;
+        spu[u] = sp;
+        if (u >= cnt || !ok) continue;
         const int j = kMmaStep * t + u, kc = kc0 + j, c = j % CH;
-        bf16_t sc, bi;
         if (vec) {
           if (j > 0 && (kc & 7) == 0) {
             cs = ns;
@@ -386,57 +400,57 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
             }
           }
           const int g = kc & 7, sh = 16 * (g & 1);
-          sc = (bf16_t)(u4_word(cs, g >> 1) >> sh);
-          bi = (bf16_t)(u4_word(cb, g >> 1) >> sh);
+          scu[u] = (bf16_t)(u4_word(cs, g >> 1) >> sh);
+          biu[u] = (bf16_t)(u4_word(cb, g >> 1) >> sh);
         } else {
-          sc = srow[kc];
-          bi = brow[kc];
+          scu[u] = srow[kc];
+          biu[u] = brow[kc];
         }
         if (c == 0 && !warp_wait(&pfull[sp], pph, a.err, 0x65u)) {
           ok = false;
-          break;
+          continue;
         }
-        // this thread's 32 k of row rr: 16-byte units 2c+h (4-bit) or 4c+2h, 4c+2h+1 (8-bit)
+        // 16-byte units 2c+h (4-bit) or 4c+2h, 4c+2h+1 (8-bit) of the packed row
         const uint8_t* pst = prow0 + sp * PBYTES;
-        uint32_t wv[BITS];  // 4 or 8 words
 #pragma unroll
         for (int i = 0; i < BITS / 4; ++i) {
           const int un = (BITS == 4) ? (2 * c + h) : (4 * c + 2 * h + i);
           const uint4 p = *reinterpret_cast<const uint4*>(pst + ((un ^ sw) << 4));
-          wv[4 * i] = p.x;
-          wv[4 * i + 1] = p.y;
-          wv[4 * i + 2] = p.z;
-          wv[4 * i + 3] = p.w;
+          wv[u][4 * i] = p.x;
+          wv[u][4 * i + 1] = p.y;
+          wv[u][4 * i + 2] = p.z;
+          wv[u][4 * i + 3] = p.w;
         }
+        endu[u] = c == CH - 1 || j == nloc - 1;
+        if (endu[u] && ++sp == NP) {
+          sp = 0;
+          pph ^= 1u;
+        }
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < kMmaStep; ++u) {
+        if (u >= cnt) continue;
         uint32_t o[16];
         if (BITS == 4) {
-          if (!rvalid) sc = bi = 0;
+          const bf16_t sc = rvalid ? scu[u] : (bf16_t)0, bi = rvalid ? biu[u] : (bf16_t)0;
           const uint32_t s2 = (uint32_t)sc | ((uint32_t)sc << 16), b2 = (uint32_t)bi | ((uint32_t)bi << 16);
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) deq8_b4(wv[cc], s2, b2, &o[4 * cc]);
+          for (int cc = 0; cc < 4; ++cc) deq8_b4(wv[u][cc], s2, b2, &o[4 * cc]);
         } else {
-          const float sf = rvalid ? bf2f(sc) : 0.0f, bf = rvalid ? bf2f(bi) : 0.0f;
+          const float sf = rvalid ? bf2f(scu[u]) : 0.0f, bf = rvalid ? bf2f(biu[u]) : 0.0f;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) deq8_b8(wv[2 * cc], wv[2 * cc + 1], sf, bf, &o[4 * cc]);
-        }
-        // after the packed stage's last chunk has been consumed (its loads are
-        // complete) it may be refilled; an arrive issued right after the loads
-        // could let the TMA overwrite words still in flight
-        if (c == CH - 1 || j == nloc - 1) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pfree[sp]);
-          if (++sp == NP) {
-            sp = 0;
-            pph ^= 1u;
-          }
-        }
-        if (u == 0 && t >= NA && !warp_wait(&mdone[s], aph, a.err, 0x66u)) {
-          ok = false;
-          break;
+          for (int cc = 0; cc < 4; ++cc) deq8_b8(wv[u][2 * cc], wv[u][2 * cc + 1], sf, bf, &o[4 * cc]);
         }
         tmem_st16(tlane + tmem_a + (uint32_t)(64 * s + 32 * u + 16 * h), o);
       }
-      if (!ok) break;
+      // a packed stage whose last chunk has been consumed (its loads are
+      // complete: their values are used above) may be refilled; an arrive
+      // right after the loads could let the TMA overwrite words in flight
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < kMmaStep; ++u)
+        if (u < cnt && endu[u] && lane == 0) mbar_arrive(&pfree[spu[u]]);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -468,30 +482,54 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
   else __syncthreads();
   grid_wait();
   if (*s_fail == 0) {
+    // four consecutive rows of one token per thread: the ranks' float4s are
+    // requested four at a time before any is added (the remote reads
+    // overlap), and the partial tiles are summed in rank order
     const int rows_out = swiglu ? kMmaRows / 2 : kMmaRows;
     const int mcount = min(a.Mpad, a.M - m0);
-    const int total = mcount * rows_out;
+    const int total = mcount * rows_out / 4;
     const int per = (total + ks - 1) / ks;
     const int i0 = rank * per, i1 = min(total, i0 + per);
     for (int idx = i0 + (int)threadIdx.x; idx < i1; idx += kMmaThreads) {
-      const int m = idx / rows_out, r2 = idx % rows_out;
-      float acc = 0.0f, acc2 = 0.0f;
-      for (int k = 0; k < ks; ++k) {
-        const float* rb = ks > 1 ? cluster.map_shared_rank(red, k) : red;
-        acc = __fadd_rn(acc, rb[m * kMmaRows + r2]);
-        if (swiglu) acc2 = __fadd_rn(acc2, rb[m * kMmaRows + 64 + r2]);
+      const int m = (4 * idx) / rows_out, r2 = (4 * idx) % rows_out;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int k0 = 0; k0 < kMmaMaxSplit; k0 += 4) {
+        float4 v[4], v2[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k0 + k < ks) {
+            const float* rb = ks > 1 ? cluster.map_shared_rank(red, k0 + k) : red;
+            v[k] = *reinterpret_cast<const float4*>(rb + m * kMmaRows + r2);
+            if (swiglu) v2[k] = *reinterpret_cast<const float4*>(rb + m * kMmaRows + 64 + r2);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k0 + k < ks) {
+            acc[0] = __fadd_rn(acc[0], v[k].x), acc[1] = __fadd_rn(acc[1], v[k].y);
+            acc[2] = __fadd_rn(acc[2], v[k].z), acc[3] = __fadd_rn(acc[3], v[k].w);
+            if (swiglu) {
+              acc2[0] = __fadd_rn(acc2[0], v2[k].x), acc2[1] = __fadd_rn(acc2[1], v2[k].y);
+              acc2[2] = __fadd_rn(acc2[2], v2[k].z), acc2[3] = __fadd_rn(acc2[3], v2[k].w);
+            }
+          }
+        }
       }
       const size_t orow = (size_t)(m0 + m) * a.ldy;
-      if (swiglu) {
-        const int col = row0 + r2;
-        if (col < a.N) a.y[orow + col] = swiglu_c(f2bf(acc), f2bf(acc2));
-      } else {
-        const int row = row0 + r2;
-        if (row < mma_mat(a, mi).rows) {
-          const size_t o = orow + a.cstart[mi] + row;
-          bf16_t yv = f2bf(acc);
-          if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[o])));
-          a.y[o] = yv;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (swiglu) {
+          const int col = row0 + r2 + e;
+          if (col < a.N) a.y[orow + col] = swiglu_c(f2bf(acc[e]), f2bf(acc2[e]));
+        } else {
+          const int row = row0 + r2 + e;
+          if (row < mma_mat(a, mi).rows) {
+            const size_t o = orow + a.cstart[mi] + row;
+            bf16_t yv = f2bf(acc[e]);
+            if (a.mode == QMM_RESID) yv = f2bf(__fadd_rn(bf2f(yv), bf2f(a.res[o])));
+            a.y[o] = yv;
+          }
         }
       }
     }
