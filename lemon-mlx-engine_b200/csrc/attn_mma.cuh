@@ -88,17 +88,30 @@ constexpr size_t sdpa_mma_smem() {
 }
 
 // Scales / biases of this thread's items of one chunk (rows >= jn: 0), as
-// bf16 pairs: sb[i] = (scale, bias) of K, sb[items + i] of V.
-LMX_DEV void sdpa_load_scales(const KvDesc& kv, size_t row0, int jn, int tid, uint32_t (&sb)[2 * kAttnItems]) {
+// loaded: sr[4i .. 4i+3] = K scale, K bias, V scale, V bias of item i.  Nothing
+// here uses the values, so the loads stay in flight until sdpa_pack_scales
+// (a chunk later in the loop).
+LMX_DEV void sdpa_load_scales(const KvDesc& kv, size_t row0, int jn, int tid, uint32_t (&sr)[4 * kAttnItems]) {
 #pragma unroll
   for (int i = 0; i < kAttnItems; ++i) {
     const int e = tid + kAttnThreads * i, j = e >> 3, g = (e & 7) >> 2;
-    sb[i] = sb[kAttnItems + i] = 0u;
+    sr[4 * i] = sr[4 * i + 1] = sr[4 * i + 2] = sr[4 * i + 3] = 0u;
     if (j < jn) {
       const size_t r = (row0 + j) * 2 + g;
-      sb[i] = (uint32_t)__ldg(kv.ks + r) | ((uint32_t)__ldg(kv.kb + r) << 16);
-      sb[kAttnItems + i] = (uint32_t)__ldg(kv.vs + r) | ((uint32_t)__ldg(kv.vb + r) << 16);
+      sr[4 * i] = __ldg(kv.ks + r);
+      sr[4 * i + 1] = __ldg(kv.kb + r);
+      sr[4 * i + 2] = __ldg(kv.vs + r);
+      sr[4 * i + 3] = __ldg(kv.vb + r);
     }
+  }
+}
+
+// -> bf16 pairs: sb[i] = (scale, bias) of K, sb[items + i] of V.
+LMX_DEV void sdpa_pack_scales(const uint32_t (&sr)[4 * kAttnItems], uint32_t (&sb)[2 * kAttnItems]) {
+#pragma unroll
+  for (int i = 0; i < kAttnItems; ++i) {
+    sb[i] = sr[4 * i] | (sr[4 * i + 1] << 16);
+    sb[kAttnItems + i] = sr[4 * i + 2] | (sr[4 * i + 3] << 16);
   }
 }
 
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
     bulk_g2s(dst, reinterpret_cast<const uint8_t*>(a.kv.kq) + (kvrow + j0) * RB, bytes, bar);
     bulk_g2s(dst + kAttnChunk * RB, reinterpret_cast<const uint8_t*>(a.kv.vq) + (kvrow + j0) * RB, bytes, bar);
   };
-  uint32_t sb[2 * kAttnItems];
+  uint32_t sb[2 * kAttnItems], sr[4 * kAttnItems];
   if (BITS != 16) {
     if (tid == 0) {
       mbar_init(&full[0], 1);
@@ -199,7 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       issue(c_begin);
     }
-    sdpa_load_scales(a.kv, kvrow + (size_t)c_begin * kAttnChunk, chunk_rows(c_begin), tid, sb);
+    sdpa_load_scales(a.kv, kvrow + (size_t)c_begin * kAttnChunk, chunk_rows(c_begin), tid, sr);
   }
   if (tid == 0) s_fail = 0;
 
@@ -243,15 +256,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
       }
     } else {
       if (tid == 0 && ch + 1 < c_end) issue(ch + 1);  // its stage was freed by the sync above
-      uint32_t sb_next[2 * kAttnItems];
-      if (ch + 1 < c_end) sdpa_load_scales(a.kv, kvrow + j0 + kAttnChunk, chunk_rows(ch + 1), tid, sb_next);
+      // this chunk's scales (loaded a chunk ago), then the next chunk's loads
+      sdpa_pack_scales(sr, sb);
+      if (ch + 1 < c_end) sdpa_load_scales(a.kv, kvrow + j0 + kAttnChunk, chunk_rows(ch + 1), tid, sr);
       const int k = ch - c_begin;
       if (!mbar_wait_bounded(&full[k & 1], (uint32_t)((k >> 1) & 1), a.err, 0x42u)) s_fail = 1;
       sdpa_stage_raw<BITS>(jn, raw + (size_t)(k & 1) * RAW, sb, Ks, Vs, tid);
-      if (ch + 1 < c_end) {
-#pragma unroll
-        for (int i = 0; i < 2 * kAttnItems; ++i) sb[i] = sb_next[i];
-      }
     }
     __syncthreads();
     if (s_fail) break;
