@@ -233,11 +233,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
     alpha[tid] = 1.0f;  // padding rows keep it
   }
   const float sl2 = __fmul_rn(a.scale, 1.4426950408889634f);  // scale * log2(e)
-  float o[MT][4];
+  // P V split: warp w owns head dims [16 (w % 8), +16) (two n8 tiles) over
+  // the keys [64 (w / 8), +64) of each chunk, so a warp reads half of P; the
+  // two key halves' partial outputs are added after the last chunk
+  const int kh = warp >> 3, ds = warp & 7;
+  float o[MT][2][4];
 #pragma unroll
   for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) o[mi][e] = 0.0f;
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mi][nt][e] = 0.0f;
 
   int ch = c_begin;
   for (; ch < c_end; ++ch) {
@@ -342,32 +348,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
     }
     __syncthreads();
 
-    // O = O * alpha + P V: warp w owns head dims [8w, 8w+8); one transposed
-    // x4 load covers two k16 steps (32 keys)
+    // O = O * alpha + P V over this warp's key half; one transposed x4 load
+    // covers two k16 steps (32 keys) of 8 head dims
     {
       const bf16_t* P = reinterpret_cast<const bf16_t*>(S);
 #pragma unroll
       for (int mi = 0; mi < MT; ++mi) {
         const float fa = alpha[mi * 16 + (lane >> 2)], fb = alpha[mi * 16 + (lane >> 2) + 8];
-        o[mi][0] = __fmul_rn(o[mi][0], fa);
-        o[mi][1] = __fmul_rn(o[mi][1], fa);
-        o[mi][2] = __fmul_rn(o[mi][2], fb);
-        o[mi][3] = __fmul_rn(o[mi][3], fb);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          o[mi][nt][0] = __fmul_rn(o[mi][nt][0], fa);
+          o[mi][nt][1] = __fmul_rn(o[mi][nt][1], fa);
+          o[mi][nt][2] = __fmul_rn(o[mi][nt][2], fb);
+          o[mi][nt][3] = __fmul_rn(o[mi][nt][3], fb);
+        }
       }
 #pragma unroll
-      for (int kk = 0; kk < kAttnChunk / 32; ++kk) {
-        uint32_t bf[4];
-        ldsm_x4_t(bf, Vs + (kk * 32 + (lane & 7) + (lane >> 3) * 8) * kAttnKP + 8 * warp);
+      for (int kk = 0; kk < 2; ++kk) {
+        const int kb = 64 * kh + 32 * kk;
+        uint32_t bf[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          ldsm_x4_t(bf[nt], Vs + (kb + (lane & 7) + (lane >> 3) * 8) * kAttnKP + 16 * ds + 8 * nt);
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int mi = 0; mi < MT; ++mi) {
             uint32_t af[4];
-            const bf16_t* prow = P + (mi * 16 + (lane & 15)) * (2 * kAttnSP) + kk * 32 + h * 16 + (lane >> 4) * 8;
+            const bf16_t* prow = P + (mi * 16 + (lane & 15)) * (2 * kAttnSP) + kb + h * 16 + (lane >> 4) * 8;
             ldsm_x4(af, prow + kAttnChunk);  // lo terms first: the smaller addend
-            mma_16816(o[mi], af, bf[2 * h], bf[2 * h + 1]);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) mma_16816(o[mi][nt], af, bf[nt][2 * h], bf[nt][2 * h + 1]);
             ldsm_x4(af, prow);
-            mma_16816(o[mi], af, bf[2 * h], bf[2 * h + 1]);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) mma_16816(o[mi][nt], af, bf[nt][2 * h], bf[nt][2 * h + 1]);
           }
       }
     }
@@ -380,23 +394,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
     return;
   }
 
+  // the key halves' partial outputs: half 1 parks its tile in S (free now,
+  // MP x 128 fp32 <= MP x kAttnSP), half 0 adds it
+  float* Op = S;
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int row = mi * 16 + (lane >> 2), d = 16 * ds + 8 * nt + 2 * (lane & 3);
+      if (kh == 1) {
+        *reinterpret_cast<float2*>(Op + row * kHeadDim + d) = make_float2(o[mi][nt][0], o[mi][nt][1]);
+        *reinterpret_cast<float2*>(Op + (row + 8) * kHeadDim + d) = make_float2(o[mi][nt][2], o[mi][nt][3]);
+      }
+    }
+  __syncthreads();
   float* part = a.part + ((((size_t)b * a.kv.Hk + kvh) * a.tiles + tile) * a.nsplit + split) *
                              (size_t)kAttnMmaRows * kPartStride;
   if (tid < nr) {
     part[tid * kPartStride + 0] = m_run[tid];
     part[tid * kPartStride + 1] = l_run[tid];
   }
+  if (kh == 0) {
 #pragma unroll
-  for (int mi = 0; mi < MT; ++mi) {
-    const int row = mi * 16 + (lane >> 2), d = 8 * warp + 2 * (lane & 3);
-    if (row < nr) {
-      part[row * kPartStride + 2 + d] = o[mi][0];
-      part[row * kPartStride + 3 + d] = o[mi][1];
-    }
-    if (row + 8 < nr) {
-      part[(row + 8) * kPartStride + 2 + d] = o[mi][2];
-      part[(row + 8) * kPartStride + 3 + d] = o[mi][3];
-    }
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int row = mi * 16 + (lane >> 2), d = 16 * ds + 8 * nt + 2 * (lane & 3);
+        const float2 u = *reinterpret_cast<const float2*>(Op + row * kHeadDim + d);
+        const float2 w = *reinterpret_cast<const float2*>(Op + (row + 8) * kHeadDim + d);
+        if (row < nr) {
+          part[row * kPartStride + 2 + d] = __fadd_rn(o[mi][nt][0], u.x);
+          part[row * kPartStride + 3 + d] = __fadd_rn(o[mi][nt][1], u.y);
+        }
+        if (row + 8 < nr) {
+          part[(row + 8) * kPartStride + 2 + d] = __fadd_rn(o[mi][nt][2], w.x);
+          part[(row + 8) * kPartStride + 3 + d] = __fadd_rn(o[mi][nt][3], w.y);
+        }
+      }
   }
 
   __threadfence();
