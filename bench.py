@@ -669,6 +669,16 @@ def qmm_time(lmx, N, K, M, bits, seed=2026):
                 path=qmm_path(lmx, M))
 
 
+SDPA_LONG_CACHE = 2048  # caches of at least this many rows take the tensor-core kernel
+
+
+def sdpa_path(lmx, rows, cap):
+    """Which K2 kernel runs for `rows` query rows per KV head over a cache of
+    `cap` rows under the library's current tensor-core threshold."""
+    mma = lmx.lib().lmx_mma_min_m()
+    return "tensor-core" if mma > 0 and (rows >= mma or cap >= SDPA_LONG_CACHE) else "cuda-core"
+
+
 def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):
     """Device time of one lmx_sdpa_decode launch over an affine (4/8-bit) or
     bf16 cache with every sequence at length cap - T (uniform random codes,
@@ -737,7 +747,7 @@ def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):
     byts = 2 * B * Hk * cap * row_bytes + 2 * B * T * Hq * D * 2  # every row is visible (lengths cap - T)
     G = Hq // Hk
     return dict(B=B, T=T, Hq=Hq, Hk=Hk, cap=cap, bits=bits, us=round(t * 1e6, 2), GBs=round(byts / t / 1e9, 1),
-                path="tensor-core" if G * T >= lmx.lib().lmx_mma_min_m() > 0 else "cuda-core")
+                path=sdpa_path(lmx, G * T, cap))
 
 
 def _graph_time(run, reps=5):
