@@ -27,3 +27,19 @@ def test_version_and_error_text(lmx):
     # an invalid call fails with a status, not an exception or a crash
     rc = L.lmx_quantized_matmul(None, None, None, None, None, 1, 8, 64, 32, 4, None)
     assert rc == 2 and b"group_size" in L.lmx_last_error()
+
+
+def test_tensor_core_thresholds_host_side(lmx):
+    # the process-wide path switches are host state: settable and validated
+    # without a GPU; restored to their defaults afterwards
+    L = lmx.lib()
+    assert L.lmx_mma_min_m() == 16 and L.lmx_gemv_tc_min_m() == 4
+    try:
+        assert L.lmx_set_gemv_tc_min_m(17) != 0 and b"gemv_tc_min_m" in L.lmx_last_error()
+        assert L.lmx_set_gemv_tc_min_m(-1) != 0
+        assert L.lmx_set_gemv_tc_min_m(0) == 0 and L.lmx_gemv_tc_min_m() == 0
+        assert L.lmx_set_gemv_tc_min_m(8) == 0 and L.lmx_gemv_tc_min_m() == 8
+        assert L.lmx_set_mma_min_m(0) == 0 and L.lmx_mma_min_m() == 0
+    finally:
+        L.lmx_set_gemv_tc_min_m(4)
+        L.lmx_set_mma_min_m(16)
