@@ -183,14 +183,20 @@ def cpu_sample(wl, prompts, lmx_cfg, draft_cfg, seed, steps, warmup):
         return L.orc_model_create(C.byref(O.ModelCfg(**cfg)), sd)
 
     L.orc_set_mma_min_m(0)
+    L.orc_set_threads(0)  # every host core, whatever OMP_NUM_THREADS the launcher exported
     t0 = time.time()
     model = create(lmx_cfg, seed)
     dmodel = create(draft_cfg, seed + 1) if draft_cfg else None
     setup = time.time() - t0
+    # cpu_prompt: the sample prefills only the last cpu_prompt prompt tokens
+    # through the model; the rows before them are a seeded synthetic KV
+    # context, so the timed decode reads a cache of the workload's length
+    cp = wl["cpu_prompt"] or prompts.shape[1]
+    ctx = prompts.shape[1] - cp
     prm = O.SpecParams(K=wl["K"], max_tokens=wl["new"], temperature=wl["temperature"],
-                       top_p=wl["top_p"], seed=seed, draft_layers=wl["draft_layers"])
-    p = np.ascontiguousarray(prompts if not wl["cpu_prompt"] else prompts[:, :wl["cpu_prompt"]],
-                             dtype=np.int32)
+                       top_p=wl["top_p"], seed=seed, draft_layers=wl["draft_layers"],
+                       context_len=ctx, context_seed=seed)
+    p = np.ascontiguousarray(prompts[:, prompts.shape[1] - cp:], dtype=np.int32)
     ss = L.orc_spec_session(model, dmodel, O.ptr(p), p.shape[0], p.shape[1], prm, wl["kv_bits"])
     st = np.zeros(5, np.int64)
     L.orc_spec_session_step(ss, warmup)
@@ -206,7 +212,15 @@ def cpu_sample(wl, prompts, lmx_cfg, draft_cfg, seed, steps, warmup):
         L.orc_model_free(dmodel)
     L.orc_set_mma_min_m(16)
     return dict(value=tokens / dt if dt > 0 else 0.0, tokens=tokens, seconds=dt, spec_steps=n,
-                cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup, prompt=p.shape[1])
+                cores=L.orc_threads(), prefill_s=st[4] * 1e-9, setup_s=setup, prompt=p.shape[1], context=ctx)
+
+
+def cpu_sample_text(r, steps):
+    pre = (f"a {r['context']}-row synthetic KV context + a {r['prompt']}-token prompt prefill (untimed) in place "
+           f"of the {r['context'] + r['prompt']}-token prompt" if r["context"] else
+           f"an untimed {r['prompt']}-token prefill")
+    return (f"{steps} speculative steps ({r['tokens']} tokens) of the workload's decode after {pre}; "
+            f"oracle/ C++ restatement, canonical order, {r['cores']} threads")
 
 
 def cpu_sample_composed(wl, arch, darch, seed, reps, tokens_per_step):
@@ -221,6 +235,7 @@ def cpu_sample_composed(wl, arch, darch, seed, reps, tokens_per_step):
     import oracle_lib as O
     L = O.lib()
     L.orc_set_mma_min_m(0)
+    L.orc_set_threads(0)  # every host core, whatever OMP_NUM_THREADS the launcher exported
     B, K, ctx = wl["batch"], wl["K"], wl.get("context", 0) + wl["prompt"]
     rng = np.random.RandomState(seed)
 
@@ -267,6 +282,7 @@ def cpu_sample_hybrid(wl, arch, seed, reps, tokens_per_step):
     import oracle_lib as O
     L = O.lib()
     L.orc_set_mma_min_m(0)
+    L.orc_set_threads(0)  # every host core, whatever OMP_NUM_THREADS the launcher exported
     B, P = wl["batch"], wl["prompt"]
     cfg = dict(arch, layers=2, attn_every=2, experts=max(16, arch["top_k"] + 1))
     t0 = time.time()
@@ -462,9 +478,7 @@ def run_reference(args, wl, world, rank):
                    "prompt": wl["prompt"], "new_tokens": wl["new"], "kv_bits": wl["kv_bits"]},
         "cpu_baseline": {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
                          "kind": "port",
-                         "sample": f"{args.steps} speculative steps ({r['tokens']} tokens) of the "
-                                   f"workload's decode after an untimed {r['prompt']}-token "
-                                   f"prefill, oracle/ C++ restatement, {r['cores']} threads"},
+                         "sample": cpu_sample_text(r, args.steps)},
         "e2e": {"value": round(r["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -480,19 +494,28 @@ def run_lmx(args, wl, world, rank, local):
         arch = dict(arch, layers=args.layers)
     darch = getattr(lmx, wl["draft"]) if wl["draft"] else None
     tp = bool(wl.get("tp"))
-    B, P, ctx = wl["batch"], wl["prompt"], wl.get("context", 0)
+    B_all, P, ctx = wl["batch"], wl["prompt"], wl.get("context", 0)
+    # data parallel: the workload's B sequences are split over
+    # the ranks (rank r decodes global sequences [b0, b1)), total work fixed;
+    # --replicas (or a batch smaller than the world) gives every rank its own
+    # B sequences instead (weak scaling)
+    split = not tp and world > 1 and not args.replicas and B_all >= world
+    b0, b1 = (rank * B_all // world, (rank + 1) * B_all // world) if split else (0, B_all)
+    B = b1 - b0
     comm = None
     if tp and world > 1:  # one shard per rank; handles exchanged over the process group
         comm = lmx.TpComm.from_process_group(max_rows=B * 32, max_hidden=arch["hidden"])
     target = lmx.Model(arch, args.seed, comm=comm)
     # separate draft model (seed + 1) or the target's first layers (self-draft)
     draft = lmx.Model(darch, args.seed + 1) if darch else None
-    # data parallel: each rank its own sequences; tensor parallel: the same
-    prompts = np.random.RandomState(args.seed + (0 if tp else rank)).randint(
-        0, arch["vocab"], (B, P)).astype(np.int32)
+    # one seeded prompt array for the whole job (split: this rank's slice of
+    # it; tensor parallel: all of it on every rank); replicas: per-rank seeds
+    replicas = not tp and world > 1 and not split
+    prompts = np.random.RandomState(args.seed + (rank if replicas else 0)).randint(
+        0, arch["vocab"], (B_all, P)).astype(np.int32)[b0:b1]
     sd = lmx.SpecDecoder(target, draft, wl["draft_layers"], B, wl["K"], wl["new"], P,
                          kv_bits=wl["kv_bits"], temperature=wl["temperature"], top_p=wl["top_p"],
-                         seed=args.seed, context_len=ctx, context_seed=args.seed)
+                         seed=args.seed, context_len=ctx, context_seed=args.seed, seq_base=b0)
 
     if args.profile_verify or args.profile_draft:
         # prefill only (KV cache at the prompt length), then N verify passes
@@ -541,10 +564,20 @@ def run_lmx(args, wl, world, rank, local):
     # verify-pass and lm_head rooflines (CUDA events on the decoder's stream)
     vsec, vbytes = sd.profile(0, 20)
     hsec, hbytes = sd.profile(3, 20)
+    dsec, dbytes = sd.profile(1, 20)
+    step_launches = sd.step_launches()
     L = arch["layers"]
     wall_m, dec_m = reduce(world, [wall, dec], "max")
     # tensor parallel: every rank emits the same tokens
     toks_all = toks if tp else int(reduce(world, [float(toks)], "sum")[0])
+    if tp:
+        par, scaling = f"tp{world} (target sharded, draft replicated)", "strong"
+    elif split:
+        par, scaling = f"dp{world} ({B_all} sequences split over {world} ranks, {B} on rank {rank})", "strong"
+    elif world > 1:
+        par, scaling = f"replicas x{world} (each rank its own {B} sequences)", "weak"
+    else:
+        par, scaling = "dp1", "strong"
     peak, peak_kind = peaks()
     traffic = None
     try:
@@ -559,14 +592,13 @@ def run_lmx(args, wl, world, rank, local):
         "metric": METRIC, "value": round(toks_all / dec_m, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * wall_m / args.steps, 3), "higher_is_better": True,
-        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "batch": B, "K": wl["K"], "prompt": P,
+        "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "batch": B_all, "K": wl["K"], "prompt": P,
                    "new_tokens": wl["new"], "kv_bits": wl["kv_bits"], "weights": "4-bit g64",
                    "context": ctx + P,
                    "draft": wl["draft"] or f"target's first {wl['draft_layers']} layers",
                    "temperature": wl["temperature"], "top_p": wl["top_p"],
-                   "parallelism": (f"tp{world} (target sharded, draft replicated)" if tp
-                                   else f"dp{world} (independent sequences per rank)"),
+                   "parallelism": par,
                    "l2": f"weights ({vbytes / 1e6:.0f} MB per verify pass) exceed L2; no flush"},
         "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * wl["new"] * 4 + 40},
@@ -578,6 +610,15 @@ def run_lmx(args, wl, world, rank, local):
                      "algorithmic_bytes": vbytes, "verify_pass_us": round(vsec * 1e6, 2),
                      "traffic": traffic},
         f"lm_head_m{B}": {"us": round(hsec * 1e6, 2), "GBs": round(hbytes / hsec / 1e9, 1)},
+        # one draft token (draft forward over B rows incl. its lm_head) and the
+        # split of one speculative step (decode time / graph replays): verify
+        # pass + K draft tokens + the rest (sampling, acceptance, bookkeeping)
+        "draft_token": {"us": round(dsec * 1e6, 2), "GBs": round(dbytes / dsec / 1e9, 1),
+                        "frac": round(dbytes / dsec / 1e9 / peak, 4), "bytes": dbytes},
+        "step": {"ms": round(1e3 * dec / max(1, replays), 3), "verify_ms": round(1e3 * vsec, 3),
+                 "draft_ms": round(1e3 * wl["K"] * dsec, 3),
+                 "other_ms": round(1e3 * (dec / max(1, replays) - vsec - wl["K"] * dsec), 3),
+                 "launches": int(step_launches)},
         "acceptance": {"accepted": acc, "proposed": prop,
                        "rate": round(acc / prop, 4) if prop else None,
                        "tokens_per_step": round(toks / max(1, steps), 3)},
@@ -592,9 +633,7 @@ def run_lmx(args, wl, world, rank, local):
         r = cpu_sample(wl, prompts, arch, darch, args.seed, args.cpu_steps, 1)
         res["cpu_baseline"] = {"value": round(r["value"], 3), "unit": "tokens/s", "cores": r["cores"],
                                "kind": "port",
-                               "sample": f"{args.cpu_steps} speculative steps ({r['tokens']} tokens) "
-                                         f"of the same decode after an untimed {r['prompt']}-token "
-                                         "prefill (oracle/ C++ restatement, canonical order)"}
+                               "sample": cpu_sample_text(r, args.cpu_steps)}
     if rank == 0:
         print(json.dumps(res), flush=True)
     sd.close()
@@ -879,6 +918,9 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None,
                     help="speculative steps in the CPU sample (default: 6, or the workload's own)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1 without tensor parallelism: every rank decodes the workload's whole batch "
+                         "(weak scaling) instead of its share of one batch")
     ap.add_argument("--profile-verify", type=int, default=0,
                     help="only prefill the workload and run N verify passes inside the NVTX "
                          "range lmx_verify_pass (for ncu --nvtx-include)")

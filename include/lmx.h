@@ -313,6 +313,28 @@ int lmx_tp_comm_create(int rank, int size, int max_rows, int max_hidden, void** 
 int lmx_tp_comm_handle(void* comm, void* handle_out);
 int lmx_tp_comm_open(void* comm, const void* handles);  /* size x LMX_TP_HANDLE_BYTES */
 int lmx_tp_comm_free(void* comm);  /* after every model that uses it */
+/* Bytes of a communicator's device block.  A caller that maps its peers'
+ * memory itself (its own IPC or virtual-memory mapping) attaches each peer's
+ * block by a pointer this process can address instead of opening handles;
+ * the comm is open once every peer is attached or opened.  Blocks are
+ * 256-byte aligned. */
+size_t lmx_tp_comm_block_bytes(void* comm);
+int lmx_tp_comm_attach(void* comm, int peer, void* peer_block);
+/* The all-reduce after o_proj / down_proj as one op (the north star's NCCL
+ * all-reduce over NVLink, here fused): h[r] = bf16(h[r] + bf16(sum over
+ * ranks of partial_p[r])), the sum in fp32 in rank order; xn[r] =
+ * rms_norm(h[r]) * norm_w (mx::fast::rms_norm).  partial [rows][hidden]
+ * bf16 is this rank's share; it is staged into the comm's current slot
+ * unless it already is that slot (lmx_tp_comm_partial, so a producer can
+ * write there directly).  Every rank must call it in the same order.  A peer
+ * that does not arrive within 2 s makes the kernel give up: h and xn are left
+ * unchanged and the device error word (lmx_device_error) reads 0x71.  The
+ * peers' flags are then out of step with this rank's: free and re-create the
+ * communicator on every rank before the next exchange.  The reference runs
+ * on one device and has no counterpart. */
+int lmx_tp_comm_partial(void* comm, void** partial);
+int lmx_tp_allreduce_rmsnorm(void* comm, const void* partial, int rows, int hidden, void* h, const void* norm_w,
+                             float eps, void* xn, void* stream);
 int lmx_model_create_tp(const lmx_model_config* cfg, uint64_t seed, void* comm, void** model);
 
 /* ---------------------------------------------------------------------------
@@ -361,6 +383,11 @@ typedef struct {
    * random-token prefix; lmx_cache_fill_synthetic).  0: none.            */
   int context_len;
   uint64_t context_seed;
+  /* Global id of this decoder's sequence 0: the uniform draws of sequence b
+   * are keyed by seq_base + b, so a batch split across ranks (each rank its
+   * slice, seq_base = the slice's first global index) draws exactly what one
+   * decoder over the whole batch would.  0 for a single decoder.          */
+  int seq_base;
 } lmx_spec_config;
 
 /* draft may be NULL (self-draft: the first draft_layers of target). */

@@ -386,13 +386,14 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   for (int e = tid; e < nr * kHeadDim; e += 256) {
     const int rr = e / kHeadDim, d = e % kHeadDim;
     float M = -INFINITY;
-    for (int s = 0; s < tile_splits; ++s) M = fmaxf(M, pbase[((size_t)s * kRowTile + rr) * kPartStride]);
+    // other CTAs' partials: L2 loads (__ldcg), never a possibly stale L1 line
+    for (int s = 0; s < tile_splits; ++s) M = fmaxf(M, __ldcg(pbase + ((size_t)s * kRowTile + rr) * kPartStride));
     float L = 0.0f, O = 0.0f;
     for (int s = 0; s < tile_splits; ++s) {
       const float* ps = pbase + ((size_t)s * kRowTile + rr) * kPartStride;
-      const float w = exp_c(__fsub_rn(ps[0], M));
-      L = __fmaf_rn(w, ps[1], L);
-      O = __fmaf_rn(w, ps[2 + d], O);
+      const float w = exp_c(__fsub_rn(__ldcg(ps), M));
+      L = __fmaf_rn(w, __ldcg(ps + 1), L);
+      O = __fmaf_rn(w, __ldcg(ps + 2 + d), O);
     }
     const int r = r0 + rr, t = r / G, g = r % G;
     a.out[((size_t)b * a.T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + g) * kHeadDim + d] =

@@ -219,9 +219,12 @@ struct Arena {
 struct TpComm {
   int n = 1, rank = 0, max_rows = 0, max_hidden = 0;
   void* block = nullptr;  // local, from cudaMalloc (exportable)
+  size_t block_bytes = 0;
   uint32_t* epoch = nullptr;
-  void* peer[kTpMaxRanks] = {};
+  void* peer[kTpMaxRanks] = {};      // opened through IPC handles (closed here)
+  bool attached[kTpMaxRanks] = {};   // attached by pointer (the caller's mapping)
   bool opened = false;
+  int sel = 0;  // partial slot of the next exchange: alternates over every exchange on the comm
   TpPeers t;
   ~TpComm() {
     for (int p = 0; p < kTpMaxRanks; ++p)
@@ -246,6 +249,7 @@ static int tp_comm_create(int rank, int n, int max_rows, int max_hidden, TpComm*
   c->t.pairs_off = 2 * c->t.slot_bytes;
   c->t.flags_off = c->t.pairs_off + up((size_t)max_rows * 8);
   const size_t bytes = c->t.flags_off + up((size_t)kTpSlots * kTpMaxRanks * 4);
+  c->block_bytes = bytes;
   int rc = cuda_check(cudaMalloc(&c->block, bytes), "tp_comm: block");
   if (!rc) rc = cuda_check(cudaMemset(c->block, 0, bytes), "tp_comm: zero");
   if (!rc) rc = cuda_check(cudaMalloc(&c->epoch, (size_t)kTpSlots * 4), "tp_comm: epoch");
@@ -263,7 +267,7 @@ static int tp_comm_create(int rank, int n, int max_rows, int max_hidden, TpComm*
 static int tp_comm_open(TpComm& c, const void* handles) {
   if (c.opened) return set_error(LMX_ERR_INVALID, "tp_comm: already open");
   for (int p = 0; p < c.n; ++p) {
-    if (p == c.rank) continue;
+    if (p == c.rank || c.attached[p]) continue;
     cudaIpcMemHandle_t hd;
     std::memcpy(&hd, (const uint8_t*)handles + (size_t)p * sizeof(cudaIpcMemHandle_t), sizeof(hd));
     int rc = cuda_check(cudaIpcOpenMemHandle(&c.peer[p], hd, cudaIpcMemLazyEnablePeerAccess),
@@ -272,6 +276,21 @@ static int tp_comm_open(TpComm& c, const void* handles) {
     c.t.base[p] = (uint8_t*)c.peer[p];
   }
   c.opened = true;
+  return LMX_OK;
+}
+
+// Attach peer `p`'s block by a device pointer this process can already
+// address (a mapping the caller made itself).  The comm is open once every
+// peer is attached or opened.
+static int tp_comm_attach(TpComm& c, int p, void* block) {
+  if (c.opened) return set_error(LMX_ERR_INVALID, "tp_comm: already open");
+  if (p < 0 || p >= c.n || p == c.rank || !block || ((uintptr_t)block & 255))
+    return set_error(LMX_ERR_INVALID, "tp_comm_attach: bad peer %d or unaligned block", p);
+  c.t.base[p] = (uint8_t*)block;
+  c.attached[p] = true;
+  bool all = true;
+  for (int q = 0; q < c.n; ++q) all = all && (q == c.rank || c.attached[q] || c.peer[q]);
+  c.opened = all;
   return LMX_OK;
 }
 
@@ -643,7 +662,8 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
                       "embed");
   if (rc) return rc;
   const float scale = (float)(1.0 / std::sqrt((double)kHeadDim));
-  int sel = 0;  // tp partial slot, alternating per exchange
+  int dummy_sel = 0;
+  int& sel = tp ? m.comm->sel : dummy_sel;  // tp partial slot, alternating per exchange on the comm
   for (int l = 0; l < n_layers && !rc; ++l) {
     const Layer& L = m.L[l];
     QmmCall qc;
@@ -848,6 +868,7 @@ static StochParams stoch_params(const Spec& sp) {
   p.temperature = sp.cfg.temperature;
   p.top_p = sp.cfg.top_p;
   p.seed = sp.cfg.seed;
+  p.seq_base = (uint32_t)sp.cfg.seq_base;
   return p;
 }
 
@@ -890,7 +911,7 @@ static int spec_step(Spec& sp) {
 namespace lmx {
 
 static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
-  if (cfg.batch < 1 || cfg.K < 1 || cfg.max_tokens < 1 || cfg.prompt_len < 2)
+  if (cfg.batch < 1 || cfg.K < 1 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
   if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
     return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
@@ -1090,6 +1111,42 @@ extern "C" int lmx_tp_comm_open(void* comm, const void* handles) {
 extern "C" int lmx_tp_comm_free(void* comm) {
   delete (TpComm*)comm;
   return LMX_OK;
+}
+
+extern "C" size_t lmx_tp_comm_block_bytes(void* comm) { return comm ? ((TpComm*)comm)->block_bytes : 0; }
+
+extern "C" int lmx_tp_comm_attach(void* comm, int peer, void* peer_block) {
+  TpComm* c = (TpComm*)comm;
+  if (!c) return set_error(LMX_ERR_INVALID, "tp_comm_attach: null comm");
+  return tp_comm_attach(*c, peer, peer_block);
+}
+
+extern "C" int lmx_tp_comm_partial(void* comm, void** partial) {
+  TpComm* c = (TpComm*)comm;
+  if (!c || !partial) return set_error(LMX_ERR_INVALID, "tp_comm_partial: null argument");
+  *partial = tp_slot(*c, c->sel);
+  return LMX_OK;
+}
+
+extern "C" int lmx_tp_allreduce_rmsnorm(void* comm, const void* partial, int rows, int hidden, void* h,
+                                        const void* norm_w, float eps, void* xn, void* stream) {
+  TpComm* c = (TpComm*)comm;
+  if (!c || !h || !norm_w || !xn || rows < 1 || hidden < 8 || hidden % 8)
+    return set_error(LMX_ERR_INVALID, "tp_allreduce_rmsnorm: bad arguments");
+  if (!c->opened) return set_error(LMX_ERR_INVALID, "tp_allreduce_rmsnorm: comm not open");
+  if (rows > c->max_rows || hidden > c->max_hidden)
+    return set_error(LMX_ERR_INVALID, "tp_allreduce_rmsnorm: %dx%d exceeds the comm", rows, hidden);
+  cudaStream_t st = (cudaStream_t)stream;
+  bf16_t* slot = tp_slot(*c, c->sel);
+  int rc = LMX_OK;
+  if (partial && partial != slot)
+    rc = cuda_check(cudaMemcpyAsync(slot, partial, (size_t)rows * hidden * 2, cudaMemcpyDeviceToDevice, st),
+                    "tp_allreduce_rmsnorm: stage partial");
+  if (!rc)
+    rc = launch_tp_allreduce_norm(*c, c->sel, rows, hidden, (bf16_t*)h, (const bf16_t*)norm_w, eps, (bf16_t*)xn,
+                                  st);
+  if (!rc) c->sel ^= 1;
+  return rc;
 }
 
 extern "C" int lmx_model_view(void* model, int n_layers, void** view) {

@@ -1,6 +1,6 @@
 // lmx_internal.h -- host-side launch API shared by the library's translation
-// units (kernels in lmx.cu, the speculative engine in engine.cu).  Not part of
-// the public C ABI.
+// parts (the kernels and C ABI in lmx.cu, the speculative engine in
+// engine.cuh, the hybrid model in hybrid.cuh).  Not part of the public C ABI.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -454,6 +454,7 @@ LMX_DEV int residual_draw_dev(const bf16_t* lp, const Dist& P, const bf16_t* lq,
 struct StochParams {
   float temperature, top_p;
   uint64_t seed;
+  uint32_t seq_base = 0;  // global id of row 0: uniforms are keyed by global sequence
 };
 
 // Cluster launch of a sampling kernel over `rows` rows, with programmatic
@@ -492,7 +493,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_rows_kernel(const bf16_t*
   const bf16_t* l = logits + (size_t)b * ld;
   Dist D;
   make_dist_dev(l, V, sp.temperature, sp.top_p, D, c, sm);
-  const int t = draw_dev(l, D, uniform24(sp.seed, b, step, slot, stream), c, sm);
+  const int t = draw_dev(l, D, uniform24(sp.seed, sp.seq_base + b, step, slot, stream), c, sm);
   if (cl_lead(c)) out[b] = t;
   cl_sync();
 }
@@ -515,7 +516,7 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(const bf16_t
   const bf16_t* l = qlog + ((size_t)b * s.K + i) * V;
   Dist D;
   make_dist_dev(l, V, sp.temperature, sp.top_p, D, c, sm);
-  const int tok = draw_dev(l, D, uniform24(sp.seed, b, (uint32_t)s.ustep[b], i, 0), c, sm);
+  const int tok = draw_dev(l, D, uniform24(sp.seed, sp.seq_base + b, (uint32_t)s.ustep[b], i, 0), c, sm);
   if (cl_lead(c)) {
     s.drafts[b * s.K + i] = tok;
     if (s.emitted[b] < s.max_tokens) s.dlen[b] += adv;
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_stochastic_kernel(const b
     cl_sync();
     return;
   }
-  const uint32_t uf = uniform24(sp.seed, b, step, 0, 2);
+  const uint32_t uf = uniform24(sp.seed, sp.seq_base + b, step, 0, 2);
   int acc = K, next = -1;
   for (int i = 0; i < K; ++i) {
     const bf16_t* lp = tlog + ((size_t)b * (K + 1) + i) * V;
@@ -556,7 +557,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_stochastic_kernel(const b
     make_dist_dev(lq, V, sp.temperature, sp.top_p, Q, c, sm);
     const int d = s.drafts[b * K + i];
     const uint64_t pd = kept_weight_of(lp, P, d, c, sm), qd = kept_weight_of(lq, Q, d, c, sm);
-    const uint32_t ua = uniform24(sp.seed, b, step, i, 1);
+    const uint32_t ua = uniform24(sp.seed, sp.seq_base + b, step, i, 1);
     if ((u128)ua * qd * P.Zk < (((u128)pd * Q.Zk) << 24)) continue;
     acc = i;
     next = residual_draw_dev(lp, P, lq, Q, uf, c, sm);

@@ -48,6 +48,10 @@ SIGNATURES = {
     "lmx_tp_comm_handle": (I, [P, P]),
     "lmx_tp_comm_open": (I, [P, P]),
     "lmx_tp_comm_free": (I, [P]),
+    "lmx_tp_comm_block_bytes": (C.c_size_t, [P]),
+    "lmx_tp_comm_attach": (I, [P, I, P]),
+    "lmx_tp_comm_partial": (I, [P, P]),
+    "lmx_tp_allreduce_rmsnorm": (I, [P, P, I, I, P, P, F, P, P]),
     "lmx_cache_fill_synthetic": (I, [P, I, U64, C.c_uint32]),
     "lmx_gdn_scratch_bytes": (C.c_size_t, [I, I, I, I]),
     "lmx_gdn_verify": (I, [P, P]),
@@ -122,7 +126,7 @@ class SpecConfig(C.Structure):
     """lmx_spec_config"""
     _fields_ = [("batch", I), ("K", I), ("max_tokens", I), ("prompt_len", I), ("kv_bits", I),
                 ("temperature", F), ("top_p", F), ("seed", U64), ("context_len", I),
-                ("context_seed", U64)]
+                ("context_seed", U64), ("seq_base", I)]
 
 
 # configs[3]: Qwen3-Next-style hybrid (the unspecified head counts / dims
@@ -245,9 +249,9 @@ class SpecDecoder:
 
     def __init__(self, target: Model, draft, draft_layers: int, batch: int, K: int,
                  max_tokens: int, prompt_len: int, kv_bits=16, temperature=0.0, top_p=1.0,
-                 seed=0, context_len=0, context_seed=0):
+                 seed=0, context_len=0, context_seed=0, seq_base=0):
         self.cfg = SpecConfig(batch, K, max_tokens, prompt_len, kv_bits, temperature, top_p, seed,
-                              context_len, context_seed)
+                              context_len, context_seed, seq_base)
         h = C.c_void_p()
         call("lmx_spec_create", target.h, draft.h if draft is not None else None, draft_layers,
              C.byref(self.cfg), C.byref(h))

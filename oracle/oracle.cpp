@@ -1908,3 +1908,17 @@ extern "C" int orc_threads(void) {
   return 1;
 #endif
 }
+
+/* Set the OpenMP thread count of every later oracle call (n <= 0: one per
+ * online host core).  Launchers such as torch.distributed.run export
+ * OMP_NUM_THREADS=1, which would leave the CPU baseline single-threaded. */
+extern "C" int orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n <= 0) n = omp_get_num_procs();
+  omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}

@@ -181,6 +181,8 @@ int orc_spec_session_step(void* session, int n_steps);
 void orc_spec_session_result(void* session, int32_t* out, int64_t* stats);
 void orc_spec_session_free(void* session);
 int orc_threads(void);
+/* OpenMP threads for later calls (n <= 0: every online host core); returns the count. */
+int orc_set_threads(int n);
 /* Plain (non-speculative) greedy decode, same emission contract. */
 int orc_generate(void* target, const int32_t* prompts, int B, int P, int max_tokens,
                  int kv_bits, int32_t* out);

@@ -1,7 +1,7 @@
 """Generate golden vectors from the reference's own Python functions.
 
-Run in a container where the reference tree is mounted (its path is given by
---ref, default /root/reference).  It imports
+Run where the reference tree is mounted; its root directory is the required
+--ref argument.  It imports
 
   debug_numerical_trace.py : dequantize_4bit_affine, rms_norm, quantized_matmul_4bit
   debug_layer0_reference.py: dequantize_weight (4- and 8-bit)
@@ -32,7 +32,7 @@ def bf16_round(f32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root directory of the reference tree")
     ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "golden.npz"))
     a = ap.parse_args()
     trace = load(os.path.join(a.ref, "debug_numerical_trace.py"), "ref_trace")

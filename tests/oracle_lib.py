@@ -108,6 +108,7 @@ def _declare(L):
         "orc_spec_generate": (I, [P, P, P, I, I, C.POINTER(SpecParams), I, P, P]),
         "orc_generate": (I, [P, P, I, I, I, I, P]),
         "orc_threads": (I, []),
+        "orc_set_threads": (I, [I]),
         "orc_spec_session": (P, [P, P, P, I, I, C.POINTER(SpecParams), I]),
         "orc_spec_session_step": (I, [P, I]),
         "orc_spec_session_result": (None, [P, P, P]),

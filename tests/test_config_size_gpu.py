@@ -1,0 +1,195 @@
+"""Parity at the benchmark configurations' own sizes (not toy models).
+
+Config 1: the full Qwen3-0.6B architecture (28 layers,
+hidden 1024, 16 q / 8 kv heads, FFN 3072, vocab 151936, tied 4-bit
+embedding), a 128-token prompt (four 32-token prefill chunks), a 2-layer
+self-draft with K = 4 and 256 greedy tokens over a bf16 KV cache.
+
+The oracle's reference stream is established teacher-forced: one exact-mode
+oracle forward over prompt + stream gives the logits at every generated
+position, and a greedy stream s is the oracle's greedy stream exactly when
+s[i] == argmax(oracle logits at position i) for every i (by induction over
+i, the contexts are then identical).  Greedy speculative decoding emits the
+target's greedy stream (src/common/generate.cpp:800-823 accepts a draft only
+where it equals the target's argmax), so this pins the speculative stream
+to the reference's greedy decode of the same model and prompt.
+
+Tensor-core mode (the benchmarked default) is pinned the way a non-bit-exact
+path can be: teacher-forced logits within 2e-2 + one bf16 ulp of the exact
+oracle at all 256 positions, and the tensor-core speculative stream equal to
+the oracle's up to its first divergence, where the oracle's top-2 logit gap
+must be a near-tie (at most twice the logit tolerance).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+
+pytestmark = pytest.mark.gpu
+
+SEED = 2026
+P, K, MT, CHUNK = 128, 4, 256, 32
+
+
+def oracle_cfg(cfg):
+    d = dict(cfg)
+    d["group"] = d.pop("group_size")
+    return O.ModelCfg(**d)
+
+
+def tol(ref_f32):
+    """The logit contract: 2e-2 max-abs plus one bf16 ulp of the logit."""
+    return 2e-2 + np.abs(ref_f32) * 2.0 ** -7
+
+
+def oracle_teacher_forced(o, cfg, tokens, first, n_layers=None):
+    """Exact-mode oracle logits (f32) at positions first .. len(tokens)-1 of
+    one sequence, forwarded in 32-token chunks."""
+    L = n_layers or cfg["layers"]
+    V = cfg["vocab"]
+    oc = O.lib().orc_cache_create(o, L, 1, len(tokens) + 8, 16)
+    out = []
+    for t0 in range(0, len(tokens), CHUNK):
+        blk = np.ascontiguousarray(tokens[t0:t0 + CHUNK], np.int32)[None]
+        T = blk.shape[1]
+        lg = np.zeros((1, T, V), np.uint16)
+        assert O.lib().orc_forward(o, oc, L, O.ptr(blk), 1, T, O.ptr(lg)) == 0
+        for t in range(T):
+            if t0 + t >= first:
+                out.append(lg[0, t])
+    O.lib().orc_cache_free(oc)
+    return O.bf16_to_f32(np.stack(out))
+
+
+def first_max(row):
+    return int(np.argmax(row))  # numpy returns the first maximum, as mx::argmax
+
+
+@pytest.fixture(scope="module")
+def c1(lmx, cuda):
+    cfg = dict(lmx.QWEN3_0_6B)
+    g = lmx.Model(cfg, SEED)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), SEED)
+    prompts = np.random.RandomState(SEED).randint(0, cfg["vocab"], (1, P)).astype(np.int32)
+    state = {}
+    yield cfg, g, o, prompts, state
+    g.close()
+    O.lib().orc_model_free(o)
+
+
+def spec_stream(lmx, g, prompts):
+    sd = lmx.SpecDecoder(g, None, 2, 1, K, MT, P, kv_bits=16)
+    sd.prefill(prompts)
+    sd.decode(use_graph=True)
+    out, st = sd.result()
+    sd.close()
+    return out[0], st
+
+
+def test_config1_exact_stream_is_reference_greedy(lmx, c1, mma_threshold):
+    """Exact mode: the GPU's speculative stream is the oracle's greedy stream,
+    token for token, at the config-1 size (multi-chunk prefill included)."""
+    cfg, g, o, prompts, state = c1
+    mma_threshold(0)
+    s, st = spec_stream(lmx, g, prompts)
+    assert st["emitted"] >= MT
+    ref = oracle_teacher_forced(o, cfg, np.concatenate([prompts[0], s[:-1]]), P - 1)
+    assert ref.shape == (MT, cfg["vocab"])
+    greedy = np.array([first_max(r) for r in ref])
+    bad = np.nonzero(greedy != s)[0]
+    assert bad.size == 0, f"first divergence at {bad[0]}: GPU {s[bad[0]]}, oracle {greedy[bad[0]]}"
+    state["stream"], state["ref"] = s, ref
+
+
+def test_config1_tensor_core_teacher_forced_and_stream(lmx, c1, mma_threshold):
+    """Tensor-core mode (default thresholds: tcgen05 for the 32-token prefill
+    chunks, the small-batch tensor-core GEMV for the 5-token verify blocks,
+    the CUDA-core GEMV for single draft tokens)."""
+    cfg, g, o, prompts, state = c1
+    if "stream" not in state:
+        pytest.skip("needs the exact-mode stream of the previous test")
+    s, ref = state["stream"], state["ref"]
+    V = cfg["vocab"]
+    mma_threshold(16)
+    # teacher-forced: the prompt in 32-token chunks, then the oracle's stream
+    # in (K+1)-token verify blocks, as the speculative loop feeds them
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, cfg["layers"], 1, P + MT + 16, 16, CHUNK, C.byref(gc))
+    got = []
+    for t0 in range(0, P, CHUNK):
+        blk = np.ascontiguousarray(prompts[:, t0:t0 + CHUNK])
+        lg = np.zeros((1, blk.shape[1], V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, cfg["layers"], blk.ctypes.data, 1, blk.shape[1], lg.ctypes.data)
+    got.append(lg[0, -1])
+    for t0 in range(0, MT - 1, K + 1):
+        blk = np.ascontiguousarray(s[t0:min(t0 + K + 1, MT - 1)], np.int32)[None]
+        lg = np.zeros((1, blk.shape[1], V), np.uint16)
+        lmx.call("lmx_forward", g.h, gc, cfg["layers"], blk.ctypes.data, 1, blk.shape[1], lg.ctypes.data)
+        got.extend(lg[0])
+    lmx.call("lmx_cache_free", gc)
+    got = O.bf16_to_f32(np.stack(got))
+    assert got.shape == ref.shape
+    diff = np.abs(got - ref)
+    over = diff > tol(ref)
+    assert not over.any(), (f"{int(over.sum())} of {over.size} logits beyond 2e-2 + ulp, "
+                            f"max |diff| {diff.max():.4g}")
+    # argmax flips under teacher forcing: near-ties only
+    top = ref.max(axis=1)
+    for i in np.nonzero(got.argmax(axis=1) != s)[0]:
+        j = first_max(got[i])
+        assert top[i] - ref[i, j] <= 2 * tol(top[i]), f"position {i}: gap {top[i] - ref[i, j]:.4g}"
+    # the benchmarked speculative loop itself
+    s_tc, _ = spec_stream(lmx, g, prompts)
+    div = np.nonzero(s_tc != s)[0]
+    if div.size:
+        p = int(div[0])
+        gap = float(ref[p, s[p]] - ref[p, s_tc[p]])
+        print(f"tensor-core stream: first divergence at token {p} of {MT}, oracle top-2 gap {gap:.4g}")
+        assert gap <= 2 * tol(ref[p, s[p]]), f"divergence at {p} is not a near-tie (gap {gap:.4g})"
+    else:
+        print(f"tensor-core stream identical to the oracle's for all {MT} tokens")
+
+
+def test_config3_width_verify_block_tensor_core(lmx, cuda, mma_threshold):
+    """A 4-layer slice of the Qwen3-8B target at full width (hidden 4096,
+    32 q / 8 kv heads, FFN 12288, vocab 151936, untied 4-bit lm_head) with
+    config 3's batch: 8 sequences, a 12-token exact-mode prefill, then
+    6-token verify blocks (M = 48: tcgen05) and a single-token block (M = 8:
+    small-batch tensor-core GEMV); logits within 2e-2 + ulp of the exact
+    oracle, which computes the same blocks in the canonical order."""
+    cfg = dict(lmx.QWEN3_8B, layers=4)
+    B, V, L = 8, cfg["vocab"], cfg["layers"]
+    g = lmx.Model(cfg, SEED)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), SEED)
+    gc = C.c_void_p()
+    lmx.call("lmx_cache_create", g.h, L, B, 96, 16, 32, C.byref(gc))
+    oc = O.lib().orc_cache_create(o, L, B, 96, 16)
+    rng = np.random.RandomState(3)
+    try:
+        for i, T in enumerate((12, 6, 6, 1, 6)):
+            mma_threshold(0 if i == 0 else 16)
+            O.lib().orc_set_mma_min_m(0)  # the oracle stays on the exact order
+            tok = rng.randint(0, V, (B, T)).astype(np.int32)
+            gl = np.zeros((B, T, V), np.uint16)
+            ol = np.zeros((B, T, V), np.uint16)
+            lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+            assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+            gf, of = O.bf16_to_f32(gl), O.bf16_to_f32(ol)
+            if i == 0:
+                np.testing.assert_array_equal(gl, ol)
+                continue
+            diff = np.abs(gf - of)
+            over = diff > tol(of)
+            assert not over.any(), f"block {i}: {int(over.sum())} logits beyond 2e-2 + ulp, max {diff.max():.4g}"
+            if i == 2:  # roll the sequences back by different amounts
+                for b in range(B):
+                    pos = 12 + 6 + (b % 6)
+                    lmx.call("lmx_cache_set_position", gc, b, pos)
+                    O.lib().orc_cache_set_position(oc, b, pos)
+    finally:
+        lmx.call("lmx_cache_free", gc)
+        O.lib().orc_cache_free(oc)
+        g.close()
+        O.lib().orc_model_free(o)
