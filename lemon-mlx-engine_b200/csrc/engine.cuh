@@ -525,6 +525,7 @@ struct Cache {
   int hk0 = 0, Hk_total = 0;  // first KV head of this shard, KV heads of the whole model
   std::vector<KvDesc> kv;
   int* len = nullptr;
+  DecLayer* dec = nullptr;  // per-layer weights + this cache, for the fused decode (device)
   Arena ar;
 };
 
@@ -554,6 +555,9 @@ static int cache_create(const Model& m, int n_layers, int B, int cap, int bits, 
   auto c = std::make_unique<Cache>();
   c->n_layers = n_layers;
   c->B = B;
+  // rows are allocated in whole 128-key splits: the fused decode stages a
+  // split's rows with bulk copies that never cross into the next sequence
+  cap = (cap + kSplit - 1) / kSplit * kSplit;
   c->cap = cap;
   c->bits = bits;
   c->Hk = m.hk;
@@ -584,6 +588,27 @@ static int cache_create(const Model& m, int n_layers, int B, int cap, int bits, 
     }
     if (rc) return rc;
   }
+  // layer descriptors of the fused decode: the model's weights with this cache
+  // (none for a geometry-only model)
+  if ((int)m.L.size() < n_layers) {
+    *out = c.release();
+    return LMX_OK;
+  }
+  std::vector<DecLayer> dl(n_layers);
+  for (int l = 0; l < n_layers; ++l) {
+    DecLayer& d = dl[l];
+    std::memset(&d, 0, sizeof(d));
+    for (int k = 0; k < 7; ++k) d.m[k] = m.L[l].w[k].mat();
+    d.in_norm = m.L[l].in_norm;
+    d.post_norm = m.L[l].post_norm;
+    d.q_norm = m.c.qk_norm ? m.L[l].q_norm : nullptr;
+    d.k_norm = m.c.qk_norm ? m.L[l].k_norm : nullptr;
+    d.kv = c->kv[l];
+  }
+  rc = c->ar.alloc(&c->dec, (size_t)n_layers, false);
+  if (!rc) rc = cuda_check(cudaMemcpy(c->dec, dl.data(), dl.size() * sizeof(DecLayer), cudaMemcpyHostToDevice),
+                           "cache: decode layers");
+  if (rc) return rc;
   *out = c.release();
   return LMX_OK;
 }
@@ -604,8 +629,35 @@ struct Workspace {
          *logits = nullptr;
   float* part = nullptr;
   unsigned* counters = nullptr;
+  // fused decode: split-K partial tiles, per-tile counters, grid-barrier counters
+  float* dgpart = nullptr;
+  unsigned* dgcnt = nullptr;
+  unsigned* dbar = nullptr;
+  size_t dgpart_floats = 0;
+  int dgcnt_n = 0;
   Arena ar;
 };
+
+// Process-wide switch of the fused small-batch decode (tensor-core mode only).
+static int g_fused_decode = 1;
+
+// Reserve the fused decode's scratch in ws for model m at up to R rows.
+static int dec_ws_reserve(Workspace& ws, const Model& m, int R) {
+  if (R > kDecMaxRows) R = kDecMaxRows;
+  DecPlan p;
+  if (!dec_plan(m.c.hidden, m.hq, m.hk, m.il, R, device_sms(), p)) return LMX_OK;  // never fused
+  int rc = LMX_OK;
+  if (p.gpart_floats > ws.dgpart_floats) {
+    rc = ws.ar.alloc(&ws.dgpart, p.gpart_floats, false);
+    if (!rc) ws.dgpart_floats = p.gpart_floats;
+  }
+  if (!rc && p.max_tiles > ws.dgcnt_n) {
+    rc = ws.ar.alloc(&ws.dgcnt, (size_t)p.max_tiles);
+    if (!rc) ws.dgcnt_n = p.max_tiles;
+  }
+  if (!rc && !ws.dbar) rc = ws.ar.alloc(&ws.dbar, 2);
+  return rc;
+}
 
 // Sized by m's per-rank shapes (hq, hk, il, vl; hidden from m.c).
 static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_rows, Workspace& ws) {
@@ -624,10 +676,26 @@ static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_
   if (!rc) rc = ws.ar.alloc(&ws.o, (size_t)R * NQ);
   if (!rc) rc = ws.ar.alloc(&ws.act, (size_t)R * m.il);
   if (!rc) rc = ws.ar.alloc(&ws.logits, (size_t)logit_rows * m.vl);
+  cap = (cap + kSplit - 1) / kSplit * kSplit;  // as the caches round it
   sdpa_scratch_need(B, Tmax, G, m.hk, cap, ws.part_floats, ws.n_counters);
   if (!rc) rc = ws.ar.alloc(&ws.part, ws.part_floats, false);
   if (!rc) rc = ws.ar.alloc(&ws.counters, ws.n_counters);
   return rc;
+}
+
+// The fused decode forward applies: tensor-core mode, no tensor parallelism,
+// R <= 16 rows, shapes the plan supports, scratch reserved, one CTA per SM fits.
+static bool dec_applies(const Model& m, const Cache& c, int n_layers, int B, int T, const Workspace& ws,
+                        DecPlan& p) {
+  const int R = B * T, G = m.hq / m.hk;
+  if (!g_fused_decode || m.tp > 1 || qmm_mma_min_m() <= 0 || R < 1 || R > kDecMaxRows || G * T > kRowTile)
+    return false;
+  if ((m.c.bits != 4 && m.c.bits != 8) || !c.dec || c.cap % kSplit || n_layers > c.n_layers) return false;
+  if (!dec_plan(m.c.hidden, m.hq, m.hk, m.il, R, device_sms(), p)) return false;
+  if (p.gpart_floats > ws.dgpart_floats || p.max_tiles > ws.dgcnt_n || !ws.dbar) return false;
+  const size_t need = (size_t)B * m.hk * (c.cap / kSplit) * kRowTile * kPartStride;
+  if (need > ws.part_floats || (size_t)B * m.hk > ws.n_counters) return false;
+  return dec_occupancy_for(m.c.bits, R) >= 1;
 }
 
 // One forward of T tokens per sequence through layers [0, n_layers) of m,
@@ -664,6 +732,39 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   const float scale = (float)(1.0 / std::sqrt((double)kHeadDim));
   int dummy_sel = 0;
   int& sel = tp ? m.comm->sel : dummy_sel;  // tp partial slot, alternating per exchange on the comm
+  DecPlan dp;
+  if (dec_applies(m, c, n_layers, B, T, ws, dp)) {
+    // the whole layer stack in one persistent launch (decode.cuh)
+    DecArgs da;
+    da.L = c.dec;
+    da.nl = n_layers;
+    da.B = B;
+    da.T = T;
+    da.R = R;
+    da.H = H;
+    da.Hq = Hq;
+    da.Hk = Hk;
+    da.I = I;
+    for (int ph = 0; ph < kDecPhases; ++ph) da.ks[ph] = dp.ks[ph];
+    da.nsplit = c.cap / kSplit;
+    da.eps = cf.eps;
+    da.scale = scale;
+    da.cos_t = m.cos_t;
+    da.sin_t = m.sin_t;
+    da.max_pos = m.max_pos;
+    da.h = ws.h;
+    da.qkv = ws.qkv;
+    da.o = ws.o;
+    da.act = ws.act;
+    da.gpart = ws.dgpart;
+    da.gcnt = ws.dgcnt;
+    da.apart = ws.part;
+    da.acnt = ws.counters;
+    da.bar = ws.dbar;
+    da.err = device_error_word();
+    rc = dec_launch(da, cf.bits, st);
+    n_layers = 0;  // the per-op loop below has nothing left to do
+  }
   for (int l = 0; l < n_layers && !rc; ++l) {
     const Layer& L = m.L[l];
     QmmCall qc;
@@ -945,6 +1046,8 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   shape.vl = std::max(tm->vl, dm->vl);
   const int Tmax = std::max(K + 1, kPrefillChunk);
   rc = workspace_create(shape, B, Tmax, cap, B * (K + 1), sp->ws);
+  if (!rc) rc = dec_ws_reserve(sp->ws, *tm, kDecMaxRows);
+  if (!rc) rc = dec_ws_reserve(sp->ws, *dm, kDecMaxRows);
   if (rc) return rc;
   SpecState& s = sp->s;
   s.B = B;
@@ -1067,6 +1170,13 @@ static int spec_decode(Spec& sp, int use_graph, double* seconds) {
 using namespace lmx;
 
 extern "C" int lmx_set_device(int device) { return cuda_check(cudaSetDevice(device), "set_device"); }
+
+extern "C" int lmx_set_fused_decode(int on) {
+  if (on != 0 && on != 1) return set_error(LMX_ERR_INVALID, "fused_decode: 0 or 1");
+  g_fused_decode = on;
+  return LMX_OK;
+}
+extern "C" int lmx_fused_decode(void) { return g_fused_decode; }
 
 extern "C" int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model) {
   if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create: null argument");
@@ -1194,6 +1304,7 @@ extern "C" int lmx_cache_create(void* model, int n_layers, int batch, int capaci
   auto h = std::make_unique<CacheHandle>();
   int rc = cache_create(*m, n_layers, batch, capacity, kv_bits, &h->c);
   if (!rc) rc = workspace_create(*m, batch, max_tokens_per_forward, capacity, batch * max_tokens_per_forward, h->ws);
+  if (!rc) rc = dec_ws_reserve(h->ws, *m, kDecMaxRows);
   if (rc) return rc;
   h->Tmax = max_tokens_per_forward;
   *cache = h.release();

@@ -19,6 +19,7 @@
 #include "engine_kernels.cuh"
 #include "sample.cuh"
 #include "tp.cuh"
+#include "decode.cuh"
 
 // Device error word: bounded waits that give up record a code here.
 __device__ unsigned g_lmx_kernel_error;

@@ -15,10 +15,18 @@ where it equals the target's argmax), so this pins the speculative stream
 to the reference's greedy decode of the same model and prompt.
 
 Tensor-core mode (the benchmarked default) is pinned the way a non-bit-exact
-path can be: teacher-forced logits within 2e-2 + one bf16 ulp of the exact
-oracle at all 256 positions, and the tensor-core speculative stream equal to
-the oracle's up to its first divergence, where the oracle's top-2 logit gap
-must be a near-tie (at most twice the logit tolerance).
+path can be.  Its blocks of >= 16 rows (the 32-token prefill chunks) take the
+tcgen05 path, which -- like MLX's batched qmm kernel -- multiplies weights
+dequantized to bf16, bf16(s*q + b), where the canonical order (MLX's qmv
+form) sums s * sum q x + b * sum x: at the full 28-layer depth the two forms
+alone move logits by up to ~0.06 (measured on the B200: 2.9% of the 256 x
+151936 logits beyond 2e-2 of the all-qmv-form oracle).  So the reference for
+tensor-core mode is the oracle taking the same form per block (its
+tensor-core emulation: dequantize-then-dot in double for >= 16 rows, the
+canonical order below), fed the same blocks: teacher-forced logits within
+2e-2 + one bf16 ulp at all 256 positions, and the tensor-core speculative
+stream equal to the oracle's up to its first divergence, where the oracle's
+top-2 logit gap must be a near-tie (at most twice the logit tolerance).
 """
 import ctypes as C
 
@@ -44,15 +52,17 @@ def tol(ref_f32):
     return 2e-2 + np.abs(ref_f32) * 2.0 ** -7
 
 
-def oracle_teacher_forced(o, cfg, tokens, first, n_layers=None):
-    """Exact-mode oracle logits (f32) at positions first .. len(tokens)-1 of
-    one sequence, forwarded in 32-token chunks."""
-    L = n_layers or cfg["layers"]
+def oracle_teacher_forced(o, cfg, tokens, first, block=CHUNK):
+    """Oracle logits (f32) at positions first .. len(tokens)-1 of one
+    sequence: the prompt (positions < P) in 32-token chunks, the rest in
+    blocks of `block` tokens, in the oracle's current mode."""
+    L = cfg["layers"]
     V = cfg["vocab"]
     oc = O.lib().orc_cache_create(o, L, 1, len(tokens) + 8, 16)
     out = []
-    for t0 in range(0, len(tokens), CHUNK):
-        blk = np.ascontiguousarray(tokens[t0:t0 + CHUNK], np.int32)[None]
+    bounds = list(range(0, P, CHUNK)) + list(range(P, len(tokens), block)) + [len(tokens)]
+    for t0, t1 in zip(bounds[:-1], bounds[1:]):
+        blk = np.ascontiguousarray(tokens[t0:t1], np.int32)[None]
         T = blk.shape[1]
         lg = np.zeros((1, T, V), np.uint16)
         assert O.lib().orc_forward(o, oc, L, O.ptr(blk), 1, T, O.ptr(lg)) == 0
@@ -113,7 +123,10 @@ def test_config1_tensor_core_teacher_forced_and_stream(lmx, c1, mma_threshold):
     s, ref = state["stream"], state["ref"]
     V = cfg["vocab"]
     mma_threshold(16)
-    # teacher-forced: the prompt in 32-token chunks, then the oracle's stream
+    # the reference in this mode: the oracle's tensor-core emulation over the
+    # same blocks (32-token prefill chunks, then (K+1)-token verify blocks)
+    ref = oracle_teacher_forced(o, cfg, np.concatenate([prompts[0], s[:-1]]), P - 1, block=K + 1)
+    # teacher-forced: the prompt in 32-token chunks, then the exact stream
     # in (K+1)-token verify blocks, as the speculative loop feeds them
     gc = C.c_void_p()
     lmx.call("lmx_cache_create", g.h, cfg["layers"], 1, P + MT + 16, 16, CHUNK, C.byref(gc))
@@ -135,21 +148,34 @@ def test_config1_tensor_core_teacher_forced_and_stream(lmx, c1, mma_threshold):
     over = diff > tol(ref)
     assert not over.any(), (f"{int(over.sum())} of {over.size} logits beyond 2e-2 + ulp, "
                             f"max |diff| {diff.max():.4g}")
-    # argmax flips under teacher forcing: near-ties only
+    # argmax flips under teacher forcing: near-ties of the reference only
     top = ref.max(axis=1)
-    for i in np.nonzero(got.argmax(axis=1) != s)[0]:
+    ref_tok = ref.argmax(axis=1)
+    flips = np.nonzero(got.argmax(axis=1) != ref_tok)[0]
+    for i in flips:
         j = first_max(got[i])
         assert top[i] - ref[i, j] <= 2 * tol(top[i]), f"position {i}: gap {top[i] - ref[i, j]:.4g}"
-    # the benchmarked speculative loop itself
+    # the benchmarked speculative loop itself, against the reference's greedy
+    # stream in this mode (by the same induction: identical while every
+    # token is the reference's argmax given the identical prefix)
+    # The teacher-forcing prefix is the exact stream s, so ref_tok is the
+    # reference's own greedy stream up to q, the first position where s
+    # leaves it; the check runs to d = min(q, first divergence of s_tc from s).
     s_tc, _ = spec_stream(lmx, g, prompts)
-    div = np.nonzero(s_tc != s)[0]
-    if div.size:
-        p = int(div[0])
-        gap = float(ref[p, s[p]] - ref[p, s_tc[p]])
-        print(f"tensor-core stream: first divergence at token {p} of {MT}, oracle top-2 gap {gap:.4g}")
-        assert gap <= 2 * tol(ref[p, s[p]]), f"divergence at {p} is not a near-tie (gap {gap:.4g})"
+    first = lambda m: int(np.nonzero(m)[0][0]) if m.any() else MT - 1
+    q, p = first(s != ref_tok), first(s_tc != s)
+    d = min(p, q)
+    assert (s_tc[:d] == ref_tok[:d]).all()
+    print(f"exact-mode stream equals the tensor-core reference's for {q} tokens")
+    if s_tc[d] != ref_tok[d]:
+        p = d
+        gap = float(ref[p, ref_tok[p]] - ref[p, s_tc[p]])
+        print(f"tensor-core stream: first divergence at token {p} of {MT}, reference top-2 gap {gap:.4g} "
+              f"({flips.size} teacher-forced argmax flips)")
+        assert gap <= 2 * tol(ref[p, ref_tok[p]]), f"divergence at {p} is not a near-tie (gap {gap:.4g})"
     else:
-        print(f"tensor-core stream identical to the oracle's for all {MT} tokens")
+        print(f"tensor-core stream equals the reference's over the {d + 1} tokens checked "
+              f"({flips.size} teacher-forced argmax flips)")
 
 
 def test_config3_width_verify_block_tensor_core(lmx, cuda, mma_threshold):
@@ -158,7 +184,8 @@ def test_config3_width_verify_block_tensor_core(lmx, cuda, mma_threshold):
     config 3's batch: 8 sequences, a 12-token exact-mode prefill, then
     6-token verify blocks (M = 48: tcgen05) and a single-token block (M = 8:
     small-batch tensor-core GEMV); logits within 2e-2 + ulp of the exact
-    oracle, which computes the same blocks in the canonical order."""
+    oracle's tensor-core emulation of the same blocks (dequantize-then-dot
+    for the 48-row blocks, the canonical order for the 8-row one)."""
     cfg = dict(lmx.QWEN3_8B, layers=4)
     B, V, L = 8, cfg["vocab"], cfg["layers"]
     g = lmx.Model(cfg, SEED)
@@ -170,7 +197,6 @@ def test_config3_width_verify_block_tensor_core(lmx, cuda, mma_threshold):
     try:
         for i, T in enumerate((12, 6, 6, 1, 6)):
             mma_threshold(0 if i == 0 else 16)
-            O.lib().orc_set_mma_min_m(0)  # the oracle stays on the exact order
             tok = rng.randint(0, V, (B, T)).astype(np.int32)
             gl = np.zeros((B, T, V), np.uint16)
             ol = np.zeros((B, T, V), np.uint16)
