@@ -70,13 +70,14 @@ int lmx_mma_min_m(void);
 int lmx_set_gemv_tc_min_m(int m);
 int lmx_gemv_tc_min_m(void);
 
-/* The fused small-batch decode forward (default on): in tensor-core mode a
- * model forward of at most 16 token rows (B*T) runs its whole decoder stack
- * as one persistent kernel (one CTA per SM, grid barriers between the
- * dependent phases, weights and cached rows streamed ahead into shared
- * memory) instead of eight kernels per layer.  Results are within the
- * tensor-core tolerance; exact mode never uses it.  Process-wide; no
- * reference counterpart. */
+/* The fused small-batch decode forward (default off): in tensor-core mode a
+ * model forward of at most 16 token rows (B*T, at most 8 query rows per KV
+ * head) runs its whole decoder stack as one persistent kernel (one CTA per
+ * SM, grid barriers between the dependent phases, weights streamed ahead into
+ * shared memory) instead of eight kernels per layer.  Results are within the
+ * tensor-core tolerance; exact mode never uses it.  Off by default because
+ * the per-op kernels are faster today.  Process-wide; no reference
+ * counterpart. */
 int lmx_set_fused_decode(int on);
 int lmx_fused_decode(void);
 

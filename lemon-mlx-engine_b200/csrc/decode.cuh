@@ -8,19 +8,19 @@
 // ramp and memory latency, not by HBM.  Here one CTA per SM walks the same
 // ops as five phases per layer separated by grid barriers:
 //   A  q|k|v GEMV of rms_norm(h)                       -> qkv
-//   B  attention: per (sequence, KV head, 128-key split) q norm + RoPE, the
-//      new K/V rows that fall in the split (norm, RoPE, quantize, append to
-//      the cache), the split's softmax partial; the last split of a
-//      (sequence, KV head) to finish combines them                -> o
+//   B  attention: one CTA per (sequence, KV head): q norm + RoPE, the new
+//      K/V rows (norm, RoPE, quantize, append to the cache), the 128-key
+//      splits over its warps, their partials combined in order    -> o
 //   C  o_proj GEMV + residual                           -> h
 //   D  gate|up GEMV of rms_norm(h) + SwiGLU             -> act
 //   E  down GEMV + residual                             -> h
-// A producer warp per CTA streams each work item's bytes (packed weight rows
-// with their scales / biases, or the split's cached K/V rows) into a ring in
-// shared memory with cp.async.bulk (no multicast), completion on one
-// mbarrier per item.  Weights and cached rows do not depend on the previous
-// phase, so the producer runs ahead across the grid barriers and the HBM
-// stream does not wait for them.  Sixteen consumer warps compute.
+// A producer warp per CTA streams each GEMV work item's bytes (packed weight
+// rows with their scales / biases) into a ring in shared memory with
+// cp.async.bulk (no multicast), completion on one mbarrier per item.
+// Weights do not depend on the previous phase, so the producer runs ahead
+// across the grid barriers and the HBM stream does not wait for them.  The
+// attention phase reads the cached rows with coalesced loads, each lane its
+// own keys (scores) or dims (P V).  Sixteen consumer warps compute.
 //
 // Numerics.  GEMV: MLX's qmv form per 64-k group, e = s * sum q x + b * sum x,
 // with the codes exact on the tensor cores (mma.sync.m16n8k16, swap-AB:
@@ -60,8 +60,9 @@ static constexpr int kDecRedP = kDecMaxRows + 1;           // float pitch of the
 // union region: GEMV (x rows + per-warp partial tiles) or attention staging
 static constexpr size_t kDecXBytes = (size_t)kDecMaxRows * kDecXP * 2;
 static constexpr size_t kDecRedBytes = (size_t)kDecWarps * 32 * kDecRedP * 4;
-static constexpr size_t kDecAttnBytes = (size_t)kSplit * kKPitch * 2 + (size_t)kSplit * kHeadDim * 2 +
-                                        (size_t)kRowTile * kHeadDim * 4 * 2;
+static constexpr int kDecAttnRows = 8;  // query rows per KV head (G*T) the attention phase takes
+static constexpr size_t kDecAttnBytes = (size_t)kDecAttnRows * kHeadDim * 4 + (size_t)2 * 8 * kHeadDim * 2 +
+                                        (size_t)kDecWarps * kDecAttnRows * kSplit * 4;
 static constexpr size_t kDecUnion = kDecXBytes + kDecRedBytes > kDecAttnBytes ? kDecXBytes + kDecRedBytes
                                                                               : kDecAttnBytes;
 static constexpr size_t kDecSmem = kDecRing + kDecUnion;
@@ -76,7 +77,7 @@ struct DecArgs {
   const DecLayer* L;
   int nl, B, T, R, H, Hq, Hk, I;
   int ks[kDecPhases];  // k-slices per tile of the GEMV phases (index = phase)
-  int nsplit;          // 128-key splits per (sequence, KV head) in the item space
+  int nsplit;          // 128-key splits of the capacity (stride of the partials)
   float eps, scale;
   const float *cos_t, *sin_t;
   int max_pos;
@@ -106,19 +107,9 @@ LMX_DEV DecGemv dec_gemv(const DecArgs& a, int ph) {
   return g;
 }
 
-LMX_DEV int dec_items(const DecArgs& a, int ph) {
-  if (ph == 1) return a.B * a.Hk * a.nsplit;
+LMX_DEV int dec_items(const DecArgs& a, int ph) {  // GEMV phases (0, 2, 3, 4)
   const DecGemv g = dec_gemv(a, ph);
   return g.tiles * g.ks;
-}
-
-// An attention item is empty when its split lies past the sequence's keys.
-LMX_DEV bool dec_attn_empty(const DecArgs& a, const DecLayer& L, int it, int& b, int& kvh, int& sp, int& len) {
-  b = it / (a.Hk * a.nsplit);
-  kvh = (it / a.nsplit) % a.Hk;
-  sp = it % a.nsplit;
-  len = __ldcg(L.kv.len + b);
-  return sp * kSplit >= len + a.T;
 }
 
 // Weight row `r` (0 .. nrows-1) of tile `tile`: matrix and row within it.
@@ -145,13 +136,6 @@ LMX_DEV int dec_wpitch(int kslice, int bits) { return bits == 4 ? kslice / 2 + 3
 LMX_DEV int dec_spitch(int kslice) { return kslice / 32 + 16; }
 LMX_DEV uint32_t dec_gemv_bytes(const DecGemv& g, int bits) {
   return (uint32_t)(g.nrows * (dec_wpitch(g.kslice, bits) + 2 * dec_spitch(g.kslice)));
-}
-
-// Attention item staging: the split's cached rows as stored (codes or bf16),
-// K then V, then the four scale / bias arrays [128][2] bf16.
-LMX_DEV uint32_t dec_kv_rowbytes(int bits) { return bits == 16 ? 256u : (uint32_t)(kHeadDim * bits / 8); }
-LMX_DEV uint32_t dec_attn_bytes(int bits) {
-  return 2u * kSplit * dec_kv_rowbytes(bits) + (bits == 16 ? 0u : 4u * kSplit * 4u);
 }
 
 struct DecCtl {
@@ -320,33 +304,6 @@ LMX_DEV void dec_append(const KvDesc& kv, bool is_k, size_t row, int lane, const
   deq = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Chunk c (d = 8c .. 8c+7) of staged row j as bf16: kv_chunk8's arithmetic
-// over the staged copy.
-LMX_DEV uint4 dec_kv_chunk8(const uint8_t* st, int bits, bool is_k, int j, int c) {
-  const uint32_t rb = dec_kv_rowbytes(bits);
-  const uint8_t* rows = st + (is_k ? 0 : kSplit * rb);
-  if (bits == 16) return *reinterpret_cast<const uint4*>(rows + (size_t)j * rb + c * 16);
-  const bf16_t* sbv = reinterpret_cast<const bf16_t*>(st + 2 * kSplit * rb) + (is_k ? 0 : 4 * kSplit);
-  const float s = bf2f(sbv[j * 2 + c / 8]);
-  const float b = bf2f(sbv[2 * kSplit + j * 2 + c / 8]);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(rows + (size_t)j * rb);
-  uint32_t q[8];
-  if (bits == 4) {
-    const uint32_t x = w[c];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[e] = (x >> (4 * e)) & 0xFu;
-  } else {
-    const uint32_t x0 = w[2 * c], x1 = w[2 * c + 1];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) { q[e] = (x0 >> (8 * e)) & 0xFFu; q[4 + e] = (x1 >> (8 * e)) & 0xFFu; }
-  }
-  uint32_t o[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e)
-    o[e] = (uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e], b)) | ((uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e + 1], b)) << 16);
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
 // ---- producer (warp kDecWarps) ------------------------------------------------
 // Walks this CTA's items in consumer order and issues their bulk copies: lane
 // 0 reserves the slot and the ring bytes and arms the slot's mbarrier with the
@@ -355,30 +312,16 @@ template <int BITS>
 LMX_DEV void dec_producer(const DecArgs& a, DecCtl& c, uint8_t* ring) {
   const int lane = threadIdx.x & 31;
   int n = 0;
-  bool waited = false, stop = false;
+  bool stop = false;
   for (int l = 0; l < a.nl && !stop; ++l) {
     const DecLayer& L = a.L[l];
     for (int ph = 0; ph < kDecPhases && !stop; ++ph) {
+      if (ph == 1) continue;  // the attention phase reads the cache directly
       const int items = dec_items(a, ph);
       for (int it = blockIdx.x; it < items && !stop; it += gridDim.x) {
-        uint32_t bytes = 0, tx = 0;
-        int b = 0, kvh = 0, sp = 0, len = 0, nold = 0;
-        DecGemv g = {};
-        if (ph == 1) {
-          if (!waited) {  // cached rows and lengths come from earlier kernels
-            grid_wait();
-            waited = true;
-          }
-          if (dec_attn_empty(a, L, it, b, kvh, sp, len)) continue;
-          nold = min(kSplit, max(0, len - sp * kSplit));
-          bytes = dec_attn_bytes(L.kv.bits);
-          if (nold > 0)
-            tx = 2u * nold * dec_kv_rowbytes(L.kv.bits) + (L.kv.bits == 16 ? 0u : 4u * ((nold + 3) & ~3) * 4u);
-        } else {
-          g = dec_gemv(a, ph);
-          bytes = dec_gemv_bytes(g, BITS);
-          tx = (uint32_t)g.nrows * (uint32_t)(g.kslice * BITS / 8 + 2 * (g.kslice / 32));
-        }
+        const DecGemv g = dec_gemv(a, ph);
+        const uint32_t bytes = dec_gemv_bytes(g, BITS);
+        const uint32_t tx = (uint32_t)g.nrows * (uint32_t)(g.kslice * BITS / 8 + 2 * (g.kslice / 32));
         const int slot = n % kDecSlots;
         int ok = 1;
         if (lane == 0) {
@@ -389,7 +332,10 @@ LMX_DEV void dec_producer(const DecArgs& a, DecCtl& c, uint8_t* ring) {
             if ((pos % kDecRing) + bytes > kDecRing) pos += kDecRing - pos % kDecRing;
             const int done = *(volatile int*)&c.done_items;
             const unsigned long long tail = *(volatile unsigned long long*)&c.tail;
-            if (done > n - kDecSlots && pos + bytes - tail <= kDecRing) break;
+            // free when the item's bytes stay clear of the unconsumed items
+            // [tail, head); a drained ring (tail == head) takes any placement,
+            // including one after skipping the ring's end
+            if (done > n - kDecSlots && (tail == c.head || pos + bytes - tail <= kDecRing)) break;
             if (*(volatile int*)&c.abort_) { ok = 0; break; }
             __nanosleep(64);
             if (global_ns() - t0 > 4000000000ull) {
@@ -410,26 +356,7 @@ LMX_DEV void dec_producer(const DecArgs& a, DecCtl& c, uint8_t* ring) {
         if (!ok) { stop = true; break; }
         __syncwarp();
         uint8_t* dst = ring + *(volatile uint32_t*)&c.off[slot];
-        if (ph == 1) {
-          const KvDesc& kv = L.kv;
-          const uint32_t rb = dec_kv_rowbytes(kv.bits);
-          const size_t row0 = ((size_t)b * kv.Hk + kvh) * kv.cap + (size_t)sp * kSplit;
-          const uint32_t rows4 = (uint32_t)((nold + 3) & ~3);
-          if (nold > 0) {
-            if (lane == 0) {
-              const void* src = kv.bits == 16 ? (const void*)(kv.k + row0 * kHeadDim)
-                                              : (const void*)(kv.kq + row0 * (kHeadDim * kv.bits / 32));
-              bulk_g2s(dst, src, (uint32_t)nold * rb, &c.full[slot]);
-            } else if (lane == 1) {
-              const void* src = kv.bits == 16 ? (const void*)(kv.v + row0 * kHeadDim)
-                                              : (const void*)(kv.vq + row0 * (kHeadDim * kv.bits / 32));
-              bulk_g2s(dst + kSplit * rb, src, (uint32_t)nold * rb, &c.full[slot]);
-            } else if (lane >= 2 && lane < 6 && kv.bits != 16) {
-              const bf16_t* src = lane == 2 ? kv.ks : (lane == 3 ? kv.kb : (lane == 4 ? kv.vs : kv.vb));
-              bulk_g2s(dst + 2 * kSplit * rb + (lane - 2) * kSplit * 4, src + row0 * 2, rows4 * 4u, &c.full[slot]);
-            }
-          }
-        } else {
+        {
           const int tile = it / g.ks, k0 = (it % g.ks) * g.kslice;
           const int wp = dec_wpitch(g.kslice, BITS), spb = dec_spitch(g.kslice), G64 = g.K / 64;
           for (int r = lane; r < g.nrows; r += 32) {
@@ -447,7 +374,6 @@ LMX_DEV void dec_producer(const DecArgs& a, DecCtl& c, uint8_t* ring) {
       }
     }
   }
-  if (!waited) grid_wait();
   if (lane == 0) {
     c.issued = n;
     __threadfence_block();
@@ -629,164 +555,198 @@ LMX_DEV void dec_gemv_item(const DecArgs& a, const DecLayer& L, DecCtl& c, int p
   }
 }
 
-// ---- consumer: one attention item (canonical split SDPA, sdpa_split_kernel) --
-LMX_DEV void dec_attn_item(const DecArgs& a, const DecLayer& L, DecCtl& c, int b, int kvh, int sp, int len,
-                           const uint8_t* st, uint8_t* U) {
+// ---- consumer: the attention of one (sequence, KV head) ---------------------
+// The canonical split SDPA (sdpa_split_kernel's order) with the splits of 128
+// keys spread over the CTA's warps: warp w takes splits w, w + 16, ...; lane l
+// scores keys l, l+32, l+64, l+96 of a split (each an fma chain over d
+// ascending, K dequantized on the fly from the cached codes as kv_chunk8),
+// the warp forms the split's max / exp / lane-ordered sum, then lane l
+// accumulates o[d] for d = 4l .. 4l+3 as fma chains over the split's keys
+// ascending.  Split partials (m, l, o) go to global scratch and are combined
+// in split order by the CTA -- no cross-CTA hand-off.  The block's new K / V
+// rows are prepared (norm, RoPE, quantize), appended to the cache and kept in
+// shared memory as the values a cache read returns.  NR >= G*T query rows.
+static constexpr int kDecSP = kSplit;  // keys per split
+LMX_DEV float dec_deq(float s, uint32_t q, float b) { return bf2f(f2bf(__fmaf_rn(s, (float)q, b))); }
+
+template <int NR>
+LMX_DEV void dec_attn_seq(const DecArgs& a, const DecLayer& L, int b, int kvh, uint8_t* U) {
   const KvDesc& kv = L.kv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = a.Hq / a.Hk, T = a.T, nr = G * T;
-  const int j0 = sp * kSplit, jmax = len + T, jn = min(kSplit, jmax - j0), jn4 = (jn + 3) & ~3;
-  const int nold = min(kSplit, max(0, len - j0));
-  const int tile_splits = (jmax + kSplit - 1) / kSplit;
-  bf16_t* Ks = reinterpret_cast<bf16_t*>(U);
-  bf16_t* Vs = Ks + kSplit * kKPitch;
-  float* Qs = reinterpret_cast<float*>(Vs + kSplit * kHeadDim);
-  float* S = Qs + kRowTile * kHeadDim;
+  const int len = __ldcg(kv.len + b), jmax = len + T;
+  const int nsp = (jmax + kDecSP - 1) / kDecSP;
+  float* Qs = reinterpret_cast<float*>(U);                          // [NR][128]
+  bf16_t* Nk = reinterpret_cast<bf16_t*>(Qs + NR * kHeadDim);       // [8][128] new K rows
+  bf16_t* Nv = Nk + 8 * kHeadDim;                                   // [8][128] new V rows
+  float* S = reinterpret_cast<float*>(Nv + 8 * kHeadDim) + warp * NR * kDecSP;  // this warp's [NR][128]
   if (jmax > kv.cap || jmax > a.max_pos) {  // the block does not fit the cache: report, write nothing
     if (tid == 0) atomicExch(a.err, 0x41u);
     return;
   }
-  // (a) query rows: q norm + RoPE, scaled (row rr = t*G + g)
-  for (int rr = warp; rr < nr; rr += kDecWarps) {
-    const int t = rr / G, gq = rr % G;
+  // (a) query rows (q norm + RoPE, scaled) and the new K / V rows
+  for (int task = warp; task < nr + 2 * T; task += kDecWarps) {
     float x[8];
-    dec_prep_head(a, L, b * T + t, kvh * G + gq, len + t, lane, x);
-    if (lane < 16)
+    if (task < nr) {
+      const int t = task / G, gq = task % G;
+      dec_prep_head(a, L, b * T + t, kvh * G + gq, len + t, lane, x);
+      if (lane < 16)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) Qs[rr * kHeadDim + 8 * lane + e] = __fmul_rn(x[e], a.scale);
+        for (int e = 0; e < 8; ++e) Qs[task * kHeadDim + 8 * lane + e] = __fmul_rn(x[e], a.scale);
+    } else {
+      const int u = task - nr, t = u >> 1;
+      const bool is_k = (u & 1) == 0;
+      dec_prep_head(a, L, b * T + t, is_k ? a.Hq + kvh : a.Hq + a.Hk + kvh, len + t, lane, x);
+      uint4 deq = make_uint4(0, 0, 0, 0);
+      dec_append(kv, is_k, ((size_t)b * kv.Hk + kvh) * kv.cap + len + t, lane, x, deq);
+      if (lane < 16) *reinterpret_cast<uint4*>((is_k ? Nk : Nv) + t * kHeadDim + 8 * lane) = deq;
+    }
   }
-  // (b) the block's new K / V rows that fall in this split: appended here
-  for (int task = warp; task < 2 * T; task += kDecWarps) {
-    const int t = task >> 1, pos = len + t;
-    const bool is_k = (task & 1) == 0;
-    if (pos < j0 || pos >= j0 + kSplit) continue;
-    float x[8];
-    dec_prep_head(a, L, b * T + t, is_k ? a.Hq + kvh : a.Hq + a.Hk + kvh, pos, lane, x);
-    uint4 deq = make_uint4(0, 0, 0, 0);
-    dec_append(kv, is_k, ((size_t)b * kv.Hk + kvh) * kv.cap + pos, lane, x, deq);
-    if (lane < 16)
-      *reinterpret_cast<uint4*>((is_k ? Ks + (pos - j0) * kKPitch : Vs + (pos - j0) * kHeadDim) + 8 * lane) = deq;
-  }
-  // (c) cached rows from the staged copy; V rows jn .. jn4-1 zero
-  for (int e = tid; e < nold * 16; e += kDecCons) {
-    const int j = e >> 4, ch = e & 15;
-    *reinterpret_cast<uint4*>(Ks + j * kKPitch + ch * 8) = dec_kv_chunk8(st, kv.bits, true, j, ch);
-    *reinterpret_cast<uint4*>(Vs + j * kHeadDim + ch * 8) = dec_kv_chunk8(st, kv.bits, false, j, ch);
-  }
-  for (int e = tid; e < (jn4 - jn) * 16; e += kDecCons)
-    *reinterpret_cast<uint4*>(Vs + (jn + (e >> 4)) * kHeadDim + (e & 15) * 8) = make_uint4(0, 0, 0, 0);
+  for (int e = tid; e < (NR - nr) * kHeadDim; e += kDecCons) Qs[nr * kHeadDim + e] = 0.0f;
   dec_sync();
-  // (d) scores: thread (key j, row class rp); rows rp, rp + 4, ...
-  {
-    const int j = tid & (kSplit - 1), rp = tid >> 7;
-    if (j < jn) {
-      float acc[8];
+  const size_t base = ((size_t)b * kv.Hk + kvh) * kv.cap;
+  const int bits = kv.bits;
+  float* part = a.apart + ((size_t)b * a.Hk + kvh) * a.nsplit * (size_t)kRowTile * kPartStride;
+  for (int sp = warp; sp < nsp; sp += kDecWarps) {
+    const int j0 = sp * kDecSP, jn = min(kDecSP, jmax - j0);
+    // scores
+#pragma unroll 1
+    for (int k = 0; k < 4; ++k) {
+      const int j = lane + 32 * k;
+      if (j >= jn) break;
+      const int row = j0 + j;
+      float acc[NR];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-      const bf16_t* kr = Ks + j * kKPitch;
+      for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+      if (row >= len) {  // a new row of this block
+        const bf16_t* kr = Nk + (row - len) * kHeadDim;
+#pragma unroll 4
+        for (int d = 0; d < kHeadDim; ++d) {
+          const float kv_ = bf2f(kr[d]);
+#pragma unroll
+          for (int r = 0; r < NR; ++r) acc[r] = __fmaf_rn(Qs[r * kHeadDim + d], kv_, acc[r]);
+        }
+      } else if (bits == 16) {
+        const uint4* kr = reinterpret_cast<const uint4*>(kv.k + (base + row) * kHeadDim);
 #pragma unroll 2
-      for (int dc = 0; dc < kHeadDim / 8; ++dc) {
-        const uint4 kw = *reinterpret_cast<const uint4*>(kr + dc * 8);
-        const float k8[8] = {lo_bf(kw.x), hi_bf(kw.x), lo_bf(kw.y), hi_bf(kw.y),
-                             lo_bf(kw.z), hi_bf(kw.z), lo_bf(kw.w), hi_bf(kw.w)};
+        for (int c8 = 0; c8 < kHeadDim / 8; ++c8) {
+          const uint4 w = kr[c8];
+          const float k8[8] = {lo_bf(w.x), hi_bf(w.x), lo_bf(w.y), hi_bf(w.y),
+                               lo_bf(w.z), hi_bf(w.z), lo_bf(w.w), hi_bf(w.w)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = rp + 4 * i;
-          if (rr < nr) {
-            const float4 qa = *reinterpret_cast<const float4*>(Qs + rr * kHeadDim + dc * 8);
-            const float4 qb = *reinterpret_cast<const float4*>(Qs + rr * kHeadDim + dc * 8 + 4);
-            float x = acc[i];
-            x = __fmaf_rn(qa.x, k8[0], x);
-            x = __fmaf_rn(qa.y, k8[1], x);
-            x = __fmaf_rn(qa.z, k8[2], x);
-            x = __fmaf_rn(qa.w, k8[3], x);
-            x = __fmaf_rn(qb.x, k8[4], x);
-            x = __fmaf_rn(qb.y, k8[5], x);
-            x = __fmaf_rn(qb.z, k8[6], x);
-            x = __fmaf_rn(qb.w, k8[7], x);
-            acc[i] = x;
+          for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int r = 0; r < NR; ++r) acc[r] = __fmaf_rn(Qs[r * kHeadDim + 8 * c8 + e], k8[e], acc[r]);
+        }
+      } else {
+        const uint32_t* kr = kv.kq + (base + row) * (kHeadDim * bits / 32);
+#pragma unroll 1
+        for (int g = 0; g < 2; ++g) {
+          const float s = bf2f(kv.ks[(base + row) * 2 + g]), bb = bf2f(kv.kb[(base + row) * 2 + g]);
+          const int nw = 64 * bits / 32;  // words of one 64-d group
+#pragma unroll 2
+          for (int wi = 0; wi < nw; ++wi) {
+            const uint32_t w = kr[g * nw + wi];
+            const int per = 32 / bits;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (e >= per) break;
+              const float kv_ = dec_deq(s, (w >> (bits * e)) & ((1u << bits) - 1u), bb);
+              const int d = 64 * g + wi * per + e;
+#pragma unroll
+              for (int r = 0; r < NR; ++r) acc[r] = __fmaf_rn(Qs[r * kHeadDim + d], kv_, acc[r]);
+            }
           }
         }
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (rp + 4 * i < nr) S[(rp + 4 * i) * kSplit + j] = acc[i];
+      for (int r = 0; r < NR; ++r) S[r * kDecSP + j] = acc[r];
     }
-  }
-  dec_sync();
-  float* pb = a.apart + (((size_t)b * a.Hk + kvh) * a.nsplit + sp) * (size_t)kRowTile * kPartStride;
-  // (e) per-row split softmax: warp per row
-  for (int rr = warp; rr < nr; rr += kDecWarps) {
-    const int t = rr / G;
-    const int vis = min(jn, len + t + 1 - j0);
-    float m = -INFINITY;
+    __syncwarp();
+    // split softmax per row (canonical: lane l owns keys l + 32k)
+    for (int r = 0; r < nr; ++r) {
+      const int t = r / G;
+      const int vis = min(jn, len + t + 1 - j0);
+      float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < kSplit / 32; ++k) {
-      const int j = lane + 32 * k;
-      if (j < vis) m = fmaxf(m, S[rr * kSplit + j]);
-    }
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float lp = 0.0f;
+      for (int k = 0; k < 4; ++k) {
+        const int j = lane + 32 * k;
+        if (j < vis) m = fmaxf(m, S[r * kDecSP + j]);
+      }
+      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float lp = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kSplit / 32; ++k) {
-      const int j = lane + 32 * k;
-      float p = 0.0f;
-      if (j < vis) p = exp_c(__fsub_rn(S[rr * kSplit + j], m));
-      S[rr * kSplit + j] = p;
-      lp = __fadd_rn(lp, p);
-    }
-    lp = warp_sum_xor(lp, 16, 1);
-    if (lane == 0) {
-      pb[rr * kPartStride + 0] = m;
-      pb[rr * kPartStride + 1] = lp;
-    }
-  }
-  dec_sync();
-  // (f) o[d] of the split: fma chains over keys ascending (V rows past jn are
-  // zero and their p is zero)
-  {
-    const int d = tid & (kHeadDim - 1), rp = tid >> 7;
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll 2
-    for (int j = 0; j < jn4; j += 4) {
-      const float v0 = bf2f(Vs[j * kHeadDim + d]), v1 = bf2f(Vs[(j + 1) * kHeadDim + d]);
-      const float v2 = bf2f(Vs[(j + 2) * kHeadDim + d]), v3 = bf2f(Vs[(j + 3) * kHeadDim + d]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int rr = rp + 4 * i;
-        if (rr < nr) {
-          const float4 p4 = *reinterpret_cast<const float4*>(S + rr * kSplit + j);
-          float x = acc[i];
-          x = __fmaf_rn(p4.x, v0, x);
-          x = __fmaf_rn(p4.y, v1, x);
-          x = __fmaf_rn(p4.z, v2, x);
-          x = __fmaf_rn(p4.w, v3, x);
-          acc[i] = x;
-        }
+      for (int k = 0; k < 4; ++k) {
+        const int j = lane + 32 * k;
+        float p = 0.0f;
+        if (j < vis) p = exp_c(__fsub_rn(S[r * kDecSP + j], m));
+        S[r * kDecSP + j] = p;
+        lp = __fadd_rn(lp, p);
+      }
+      lp = warp_sum_xor(lp, 16, 1);
+      if (lane == 0) {
+        float* pb = part + ((size_t)sp * kRowTile + r) * kPartStride;
+        pb[0] = m;
+        pb[1] = lp;
       }
     }
+    __syncwarp();
+    // o[d], d = 4 lane .. 4 lane + 3: fma chains over the split's keys ascending
+    float o[NR][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (rp + 4 * i < nr) pb[(rp + 4 * i) * kPartStride + 2 + d] = acc[i];
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[r][e] = 0.0f;
+    const int g = lane >> 4;
+#pragma unroll 2
+    for (int j = 0; j < jn; ++j) {
+      const int row = j0 + j;
+      float v[4];
+      if (row >= len) {
+        const uint2 w = *reinterpret_cast<const uint2*>(Nv + (row - len) * kHeadDim + 4 * lane);
+        v[0] = lo_bf(w.x), v[1] = hi_bf(w.x), v[2] = lo_bf(w.y), v[3] = hi_bf(w.y);
+      } else if (bits == 16) {
+        const uint2 w = *reinterpret_cast<const uint2*>(kv.v + (base + row) * kHeadDim + 4 * lane);
+        v[0] = lo_bf(w.x), v[1] = hi_bf(w.x), v[2] = lo_bf(w.y), v[3] = hi_bf(w.y);
+      } else {
+        const float s = bf2f(kv.vs[(base + row) * 2 + g]), bb = bf2f(kv.vb[(base + row) * 2 + g]);
+        const uint32_t* vr = kv.vq + (base + row) * (kHeadDim * bits / 32);
+        if (bits == 4) {
+          const uint32_t w = vr[lane >> 1] >> ((lane & 1) * 16);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = dec_deq(s, (w >> (4 * e)) & 0xFu, bb);
+        } else {
+          const uint32_t w = vr[lane];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = dec_deq(s, (w >> (8 * e)) & 0xFFu, bb);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const float p = S[r * kDecSP + j];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[r][e] = __fmaf_rn(p, v[e], o[r][e]);
+      }
+    }
+    // (rows of kPartStride = 130 floats: the o[] part is 8-byte aligned)
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      if (r < nr) {
+        float2* po = reinterpret_cast<float2*>(part + ((size_t)sp * kRowTile + r) * kPartStride + 2 + 4 * lane);
+        po[0] = make_float2(o[r][0], o[r][1]);
+        po[1] = make_float2(o[r][2], o[r][3]);
+      }
+    __syncwarp();
   }
-  // (g) the last split of (b, kvh) to finish combines the splits in order
-  __threadfence();
   dec_sync();
-  unsigned* ctr = a.acnt + (size_t)b * a.Hk + kvh;
-  if (tid == 0) c.is_last = atomicAdd(ctr, 1u) + 1u == (unsigned)tile_splits;
-  dec_sync();
-  if (!c.is_last) return;
-  __threadfence();
-  const float* pbase = a.apart + ((size_t)b * a.Hk + kvh) * a.nsplit * (size_t)kRowTile * kPartStride;
+  // combine the splits in order (canonical), this CTA's own partials
   for (int e = tid; e < nr * kHeadDim; e += kDecCons) {
     const int rr = e / kHeadDim, d = e % kHeadDim;
     float M = -INFINITY;
-    for (int s = 0; s < tile_splits; ++s) M = fmaxf(M, __ldcg(pbase + ((size_t)s * kRowTile + rr) * kPartStride));
+    for (int s = 0; s < nsp; ++s) M = fmaxf(M, __ldcg(part + ((size_t)s * kRowTile + rr) * kPartStride));
     float Lsum = 0.0f, O = 0.0f;
-    for (int s = 0; s < tile_splits; ++s) {
-      const float* ps = pbase + ((size_t)s * kRowTile + rr) * kPartStride;
+    for (int s = 0; s < nsp; ++s) {
+      const float* ps = part + ((size_t)s * kRowTile + rr) * kPartStride;
       const float w = exp_c(__fsub_rn(__ldcg(ps), M));
       Lsum = __fmaf_rn(w, __ldcg(ps + 1), Lsum);
       O = __fmaf_rn(w, __ldcg(ps + 2 + d), O);
@@ -794,7 +754,6 @@ LMX_DEV void dec_attn_item(const DecArgs& a, const DecLayer& L, DecCtl& c, int b
     const int t = rr / G, gq = rr % G;
     a.o[((size_t)b * T + t) * a.Hq * kHeadDim + (size_t)(kvh * G + gq) * kHeadDim + d] = f2bf(__fdiv_rn(O, Lsum));
   }
-  if (tid == 0) *ctr = 0u;
 }
 
 // ---- the kernel ----------------------------------------------------------------
@@ -834,17 +793,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fwd_kernel(DecArgs a) {
         dec_sync();
       }
       int xk0 = -1;
-      const int items = dec_items(a, ph);
+      if (ph == 1) {  // attention: one (sequence, KV head) per CTA, no staged bytes
+        const int nr = (a.Hq / a.Hk) * a.T;
+        for (int it = blockIdx.x; it < a.B * a.Hk; it += gridDim.x) {
+          if (nr <= 2) dec_attn_seq<2>(a, L, it / a.Hk, it % a.Hk, U);
+          else if (nr <= 4) dec_attn_seq<4>(a, L, it / a.Hk, it % a.Hk, U);
+          else dec_attn_seq<8>(a, L, it / a.Hk, it % a.Hk, U);
+          dec_sync();
+        }
+      }
+      const int items = ph == 1 ? 0 : dec_items(a, ph);
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        int b = 0, kvh = 0, sp = 0, len = 0;
-        if (ph == 1 && dec_attn_empty(a, L, it, b, kvh, sp, len)) continue;
         const int slot = n % kDecSlots;
         if (!mbar_wait_bounded(&c.full[slot], (uint32_t)((n / kDecSlots) & 1), a.err, 0x74u)) c.abort_ = 1;
         dec_sync();
         if (*(volatile int*)&c.abort_) { ok = false; break; }
         const uint8_t* st = ring + c.off[slot];
-        if (ph == 1) dec_attn_item(a, L, c, b, kvh, sp, len, st, U);
-        else if (NT == 1) dec_gemv_item<BITS, 1>(a, L, c, ph, it, st, U, xk0);
+        if (NT == 1) dec_gemv_item<BITS, 1>(a, L, c, ph, it, st, U, xk0);
         else dec_gemv_item<BITS, 2>(a, L, c, ph, it, st, U, xk0);
         dec_sync();  // every consumer is done with the stage (and with U)
         if (tid == 0) {

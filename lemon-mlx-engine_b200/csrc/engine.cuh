@@ -639,7 +639,11 @@ struct Workspace {
 };
 
 // Process-wide switch of the fused small-batch decode (tensor-core mode only).
-static int g_fused_decode = 1;
+// Off by default: measured on the B200 it is slower than the per-op kernels
+// (a Qwen3-0.6B draft token at B = 8 over a 900-row 4-bit cache: 4.3 ms fused
+// against 2.3 ms; each phase is bound by its ~2-4 us of per-item latency and
+// ~3 us grid barriers, not by HBM).
+static int g_fused_decode = 0;
 
 // Reserve the fused decode's scratch in ws for model m at up to R rows.
 static int dec_ws_reserve(Workspace& ws, const Model& m, int R) {
@@ -688,7 +692,7 @@ static int workspace_create(const Model& m, int B, int Tmax, int cap, int logit_
 static bool dec_applies(const Model& m, const Cache& c, int n_layers, int B, int T, const Workspace& ws,
                         DecPlan& p) {
   const int R = B * T, G = m.hq / m.hk;
-  if (!g_fused_decode || m.tp > 1 || qmm_mma_min_m() <= 0 || R < 1 || R > kDecMaxRows || G * T > kRowTile)
+  if (!g_fused_decode || m.tp > 1 || qmm_mma_min_m() <= 0 || R < 1 || R > kDecMaxRows || G * T > kDecAttnRows)
     return false;
   if ((m.c.bits != 4 && m.c.bits != 8) || !c.dec || c.cap % kSplit || n_layers > c.n_layers) return false;
   if (!dec_plan(m.c.hidden, m.hq, m.hk, m.il, R, device_sms(), p)) return false;

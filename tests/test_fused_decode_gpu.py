@@ -31,12 +31,19 @@ def within(got, ref, what, kv_bits):
     g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
     diff = np.abs(g - r)
     lim = 2e-2 + np.abs(r) * 2.0 ** -7
-    if kv_bits == 4:  # a 4-bit cache code can flip on a one-ulp K/V difference (see test_engine_gpu)
-        over = int((diff > 2 * lim).sum())
-        assert over <= 5e-4 * diff.size and not (diff > 1e-1 + lim).any(), \
-            f"{what}: {over} logits beyond 4e-2, max |diff| {diff.max():.4g}"
+    if kv_bits != 16:
+        # a quantized cache code can flip on a one-ulp K/V difference and move
+        # every logit of the rows that read it (see test_engine_gpu): bounded
+        # by 1e-1 per logit
+        assert not (diff > 1e-1 + lim).any(), f"{what}: max |diff| {diff.max():.4g}"
         return
     assert not (diff > lim).any(), f"{what}: {int((diff > lim).sum())} beyond 2e-2 + ulp, max {diff.max():.4g}"
+
+
+@pytest.fixture(autouse=True)
+def fused_off_after(lmx):
+    yield
+    lmx.call("lmx_set_fused_decode", 0)
 
 
 @pytest.fixture(scope="module")
@@ -58,7 +65,7 @@ def models(lmx, cuda):
 def test_fused_decode_blocks_match_oracle(lmx, models, mma_threshold, bits, kv_bits, B):
     cfg, g, o = models[bits]
     L, V = cfg["layers"], cfg["vocab"]
-    assert lmx.lib().lmx_fused_decode() == 1
+    lmx.call("lmx_set_fused_decode", 1)
     mma_threshold(16)
     gc = C.c_void_p()
     cap = 400
@@ -120,7 +127,6 @@ def test_fused_decode_deterministic_and_switchable(lmx, models, mma_threshold):
         lmx.call("lmx_forward", g.h, gc, L, blk.ctypes.data, B, 1, gl.ctypes.data)
         lmx.call("lmx_cache_free", gc)
         outs.append(gl)
-    lmx.call("lmx_set_fused_decode", 1)
     np.testing.assert_array_equal(outs[0], outs[1])  # deterministic
     # the per-op path (small-batch tensor-core GEMV) agrees within tolerance
     within(outs[0], outs[2], "fused vs per-op", 4)
