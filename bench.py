@@ -708,14 +708,11 @@ def qmm_time(lmx, N, K, M, bits, seed=2026):
                 path=qmm_path(lmx, M))
 
 
-SDPA_LONG_CACHE = 2048  # caches of at least this many rows take the tensor-core kernel
-
-
 def sdpa_path(lmx, rows, cap):
     """Which K2 kernel runs for `rows` query rows per KV head over a cache of
-    `cap` rows under the library's current tensor-core threshold."""
-    mma = lmx.lib().lmx_mma_min_m()
-    return "tensor-core" if mma > 0 and (rows >= mma or cap >= SDPA_LONG_CACHE) else "cuda-core"
+    `cap` rows under the library's current thresholds."""
+    mma, long_cache = lmx.lib().lmx_mma_min_m(), lmx.lib().lmx_sdpa_tc_min_cache()
+    return "tensor-core" if mma > 0 and (rows >= mma or (long_cache > 0 and cap >= long_cache)) else "cuda-core"
 
 
 def sdpa_time(lmx, B, T, Hq, Hk, cap, bits, seed=2026):
@@ -937,6 +934,8 @@ def main():
                                               "12,2048,512,512,10,4)")
     ap.add_argument("--gdn", default="", help="op-level Gated DeltaNet verify + commit B,T,Hk,Hv (configuration 4: "
                                               "4,3,16,32)")
+    ap.add_argument("--sdpa-tc-min-cache", type=int, default=-1,
+                    help="with --sdpa: set lmx_set_sdpa_tc_min_cache first (0: by row count only)")
     ap.add_argument("--sdpa", default="", help="one op-level attention shape B,T,Hq,Hk,cap,bits (e.g. "
                                                "16,5,64,8,8300,8 = one Llama-3-70B verify layer)")
     args = ap.parse_args()
@@ -955,6 +954,8 @@ def main():
     if args.sdpa:
         lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
         lmx.call("lmx_set_device", 0)
+        if args.sdpa_tc_min_cache >= 0:
+            lmx.call("lmx_set_sdpa_tc_min_cache", args.sdpa_tc_min_cache)
         B, T, Hq, Hk, cap, bits = [int(v) for v in args.sdpa.split(",")]
         print(json.dumps(sdpa_time(lmx, B, T, Hq, Hk, cap, bits)), flush=True)
         return 0

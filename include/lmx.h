@@ -81,6 +81,16 @@ int lmx_gemv_tc_min_m(void);
 int lmx_set_fused_decode(int on);
 int lmx_fused_decode(void);
 
+/* Cache capacity (rows) from which, in tensor-core mode, every attention
+ * block takes the tensor-core SDPA -- also single-token decode, whose few
+ * query rows per KV head would otherwise take the CUDA-core kernel (default
+ * 1: every block); 0 = only blocks of at least the tensor-core threshold's
+ * rows per KV head.  Results
+ * are within the tensor-core tolerance.  Process-wide; no reference
+ * counterpart. */
+int lmx_set_sdpa_tc_min_cache(int rows);
+int lmx_sdpa_tc_min_cache(void);
+
 /* mx::fast::rms_norm(x, w, eps) over the last axis (e.g. qwen3.cpp:78,145).
  * x, y [rows, dim] bf16 (may alias), w [dim] bf16. */
 int lmx_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,

@@ -44,7 +44,13 @@ static int launch_sdpa_t(const SdpaArgs& a, int B, cudaStream_t st) {
                     "sdpa: launch");
 }
 
-static constexpr int kSdpaLongCache = 2048;  // cache rows from which every block takes the tensor-core SDPA
+// Cache rows from which every block (also a single decode token) takes the
+// tensor-core SDPA in tensor-core mode; process-wide, lmx_set_sdpa_tc_min_cache.
+// Default 1 (every block): measured on the B200 the tensor-core kernel is the
+// faster one for single-token decode at every capacity tried (8 sequences,
+// 16 q / 8 kv heads, 4-bit cache: 9.8 us vs 16.4 us at 130 rows, 23.2 vs
+// 51.9 us at 1030, 33.1 vs 88.7 us at 1800).
+static int g_sdpa_long_cache = 1;
 
 // Tensor-core SDPA geometry (attn_mma.cuh): row tiles of 16*MT <= 64 rows,
 // nsplit key splits per (sequence, KV head, tile), as many as one wave of
@@ -132,7 +138,7 @@ static int launch_sdpa(const SdpaArgs& a_in, int B, cudaStream_t st) {
   // rows per KV head (verify), and any block over a long cache, where its
   // bulk-copy pipeline streams the cache far faster than the canonical
   // kernel's per-split loads
-  if (qmm_uses_mma(rows) || (qmm_mma_min_m() > 0 && a_in.kv.cap >= kSdpaLongCache)) {
+  if (qmm_uses_mma(rows) || (qmm_mma_min_m() > 0 && g_sdpa_long_cache > 0 && a_in.kv.cap >= g_sdpa_long_cache)) {
     SdpaArgs a = a_in;
     const SdpaMmaPlan p = sdpa_mma_plan(B, a.kv.Hk, rows, a.kv.cap, a.kv.bits);
     a.err = device_error_word();
@@ -1181,6 +1187,13 @@ extern "C" int lmx_set_fused_decode(int on) {
   return LMX_OK;
 }
 extern "C" int lmx_fused_decode(void) { return g_fused_decode; }
+
+extern "C" int lmx_set_sdpa_tc_min_cache(int rows) {
+  if (rows < 0) return set_error(LMX_ERR_INVALID, "sdpa_tc_min_cache: rows >= 0 (0 = only by row count)");
+  g_sdpa_long_cache = rows;
+  return LMX_OK;
+}
+extern "C" int lmx_sdpa_tc_min_cache(void) { return g_sdpa_long_cache; }
 
 extern "C" int lmx_model_create(const lmx_model_config* cfg, uint64_t seed, void** model) {
   if (!cfg || !model) return set_error(LMX_ERR_INVALID, "model_create: null argument");

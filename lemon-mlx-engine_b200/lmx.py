@@ -37,6 +37,8 @@ SIGNATURES = {
     "lmx_gemv_tc_min_m": (I, []),
     "lmx_set_fused_decode": (I, [I]),
     "lmx_fused_decode": (I, []),
+    "lmx_set_sdpa_tc_min_cache": (I, [I]),
+    "lmx_sdpa_tc_min_cache": (I, []),
     "lmx_rms_norm": (I, [P, P, P, I, I, F, P]),
     "lmx_argmax": (I, [P, I, I, P, P]),
     "lmx_sample": (I, [P, I, I, F, F, P, P, P]),

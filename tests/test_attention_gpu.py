@@ -108,12 +108,13 @@ def test_sdpa_decode_rejects_small_scratch(lmx, cuda):
 @pytest.mark.parametrize("bits", [16, 8, 4])
 @pytest.mark.parametrize("T,Hq,Hk,cap", [(5, 64, 8, 8300), (6, 32, 8, 1100), (40, 4, 2, 420),
                                          (2, 16, 2, 300), (5, 8, 1, 700), (1, 32, 8, 2100),
-                                         (1, 16, 8, 3000)])
+                                         (1, 16, 8, 3000), (1, 16, 8, 300)])
 def test_sdpa_tensor_core_within_tolerance(lmx, cuda, mma_threshold, bits, T, Hq, Hk, cap):
     # G*T query rows per KV head: 40 (Llama-3-70B verify, 8k cache), 24
     # (Qwen3-8B verify), 80 (two row tiles), 16 (one m16 tile), 40 with a
-    # single KV head; and single-token decode (4 and 2 rows) over caches of
-    # >= 2048 rows, which also take the tensor-core kernel.  Tolerance: the
+    # single KV head; and single-token decode (4 and 2 rows) over long and
+    # short caches, which in tensor-core mode take the tensor-core kernel
+    # too (lmx_set_sdpa_tc_min_cache, default every block).  Tolerance: the
     # products accumulate in the tensor core's order, exponentials come from
     # the hardware ex2 and p keeps ~16 bits -> at most a few bf16 ulps.
     mma_threshold(16)

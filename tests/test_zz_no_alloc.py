@@ -21,13 +21,14 @@ def _dev(cuda, a):
     return cuda.from_numpy(np.ascontiguousarray(a.view(view) if view else a)).cuda()
 
 
-# (bits, T, Hq, cap): the first three take the CUDA-core kernel (at most 12
-# query rows per KV head over short caches); the last two the tensor-core
-# kernel -- 40 rows per KV head (8 q heads per KV head x 5 verify tokens),
-# and a single-token decode over a cache of more than 2048 rows.
-@pytest.mark.parametrize("bits,T,Hq,cap", [(16, 5, 16, 300), (8, 1, 16, 300), (4, 6, 16, 300),
-                                           (8, 5, 64, 300), (4, 1, 16, 2304)])
-def test_noalloc_matches_caller_scratch_entry(lmx, cuda, bits, T, Hq, cap):
+# (bits, T, Hq, cap, exact): the first three in exact mode take the CUDA-core
+# kernel; the last two in tensor-core mode the tensor-core kernel -- 40 rows
+# per KV head (8 q heads per KV head x 5 verify tokens), and a single-token
+# decode over a cache of more than 2048 rows.
+@pytest.mark.parametrize("bits,T,Hq,cap,exact", [(16, 5, 16, 300, 1), (8, 1, 16, 300, 1), (4, 6, 16, 300, 1),
+                                                 (8, 5, 64, 300, 0), (4, 1, 16, 2304, 0)])
+def test_noalloc_matches_caller_scratch_entry(lmx, cuda, mma_threshold, bits, T, Hq, cap, exact):
+    mma_threshold(0 if exact else 16)
     rng = np.random.RandomState(7 + bits + T)
     B, Hk = 2, 8
     lens = np.array([17, cap - T], np.int32)
