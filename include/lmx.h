@@ -392,7 +392,8 @@ int lmx_forward(void* model, void* cache, int n_layers, const int32_t* tokens_ho
  * ------------------------------------------------------------------------- */
 typedef struct {
   int batch;        /* independent sequences decoded together            */
-  int K;            /* draft tokens per step (reference n_draft_tokens-1) */
+  int K;            /* draft tokens per step (reference n_draft_tokens-1);
+                     * 0: plain decoding, one token per step, no draft   */
   int max_tokens;   /* tokens emitted per sequence                       */
   int prompt_len;
   int kv_bits;      /* 16, 8 or 4                                        */
@@ -423,6 +424,46 @@ int lmx_spec_decode(void* spec, int use_graph, double* seconds);
  * (graph replays, including those after every sequence finished). */
 int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_host);
 int lmx_spec_free(void* spec);
+
+/* TokenIterator::next() (src/common/generate.cpp:968-1045, include/mlx-lm/
+ * common/generate.h:236-330) after lmx_spec_prefill: the next token of every
+ * sequence, in the reference's emission order (d0 first, then the accepted
+ * drafts; the correction / bonus token is the next step's d0).  A speculative
+ * step runs (one graph replay) only when a sequence that has not reached
+ * max_tokens has no token left; with K = 0 in lmx_spec_config the step is
+ * one plain decode step, the reference's fallback when no draft is available
+ * (generate.cpp:671-686).  tokens_host[b] = -1 once sequence b has produced
+ * max_tokens tokens; *n_live counts the other sequences (0: the reference's
+ * nullopt).  EOS is the caller's to check, as in the reference. */
+int lmx_spec_next(void* spec, int32_t* tokens_host, int* n_live);
+
+/* GenerateCompletionInfo (include/mlx-lm/common/generate.h:170-199), per
+ * sequence; times in seconds. */
+typedef struct {
+  int prompt_token_count;
+  int generation_token_count;
+  double prompt_time;
+  double generation_time;
+  int mtp_draft_tokens_proposed;
+  int mtp_draft_tokens_accepted;
+  int mtp_speculative_steps;
+} lmx_completion_info;
+/* GenerateCancelPredicate (generate.h:218-228): nonzero aborts. */
+typedef int (*lmx_cancel_fn)(void* user);
+/* The per-token callback of generate(): nonzero stops sequence `seq`
+ * (GenerateDisposition::stop). */
+typedef int (*lmx_token_fn)(void* user, int seq, int32_t token);
+/* generate() (src/common/generate.cpp:1061-1125): prefill prompts_host
+ * [batch, prompt_len], then lmx_spec_next until every sequence has stopped.
+ * should_cancel (may be NULL) is polled before every step; a token in
+ * eos_ids ends its sequence and is neither counted nor passed to on_token;
+ * on_token (may be NULL) returning nonzero ends its sequence.  info [batch]
+ * (may be NULL): prompt_time = the prefill's wall time, generation_time from
+ * the sequence's first token to its end (the reference restarts its clock
+ * at the first token). */
+int lmx_spec_generate(void* spec, const int32_t* prompts_host, const int32_t* eos_ids, int n_eos,
+                      lmx_cancel_fn should_cancel, void* cancel_user, lmx_token_fn on_token, void* token_user,
+                      lmx_completion_info* info);
 /* Measurement hooks (no reference counterpart; used by bench.py): time one
  * piece of the step on the decoder's stream with CUDA events, `iters` launches
  * after decode.  what: 0 verify pass, 1 one draft token, 2 lm_head at

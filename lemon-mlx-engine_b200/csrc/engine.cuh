@@ -6,6 +6,7 @@
 // cache is rolled back to p+acc+1.  Everything per step stays on the device
 // and one step is captured as a CUDA graph.
 #pragma once
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -967,6 +968,10 @@ struct Spec {
   cudaGraphExec_t exec = nullptr;
   bool prefilled = false;
   int64_t replays = 0;  // graph replays (steps enqueued) of the last decode
+  // per-token iteration (lmx_spec_next): tokens read so far per sequence,
+  // the device counts and stream mirrored after the last step
+  std::vector<int> it_rp, it_em;
+  std::vector<int32_t> it_buf;
   ~Spec() {
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
@@ -1022,7 +1027,7 @@ static int spec_step(Spec& sp) {
 namespace lmx {
 
 static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
-  if (cfg.batch < 1 || cfg.K < 1 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
+  if (cfg.batch < 1 || cfg.K < 0 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
   if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
     return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
@@ -1041,7 +1046,8 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   int rc = cache_create(*tm, tm->n_layers, B, cap, cfg.kv_bits, &tc);
   if (rc) return rc;
   sp->tc.reset(tc);
-  rc = cache_create(*dm, dl, B, cap, cfg.kv_bits, &dc);
+  // K = 0 is plain (non-speculative) decoding: the draft never runs
+  rc = cache_create(*dm, K > 0 ? dl : 1, B, cap, cfg.kv_bits, &dc);
   if (rc) return rc;
   sp->dc.reset(dc);
   // one workspace serves both models: every dimension is the larger of the
@@ -1109,36 +1115,44 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
                     "prefill sample");
   else if (!rc)
     rc = model_argmax(*sp.tm, sp.ws.logits, B, sp.tm->vl, sp.yprefill, st);
-  if (!rc) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
+  if (!rc && sp.cfg.K > 0) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
   if (!rc)
     rc = cuda_check(lmx_launch(prefill_done_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
                                (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill, sp.cfg.context_len),
                     "prefill_done");
   if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "prefill");
   if (!rc) sp.prefilled = true;
+  sp.it_rp.assign(B, 0);
+  sp.it_em.assign(B, 0);
+  sp.it_buf.assign((size_t)B * sp.cfg.max_tokens, 0);
   return rc;
 }
 
 // Decode until every sequence has max_tokens: one captured graph per step.
+// Capture one speculative step as a CUDA graph (once per decoder).
+static int spec_capture(Spec& sp) {
+  if (sp.exec) return LMX_OK;
+  cudaStream_t st = sp.st;
+  int rc = cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "capture begin");
+  if (rc) return rc;
+  int rc2 = spec_step(sp);
+  cudaGraph_t g = nullptr;
+  rc = cuda_check(cudaStreamEndCapture(st, &g), "capture end");
+  if (rc2) {
+    if (g) cudaGraphDestroy(g);
+    return rc2;
+  }
+  if (rc) return rc;
+  sp.graph = g;
+  return cuda_check(cudaGraphInstantiate(&sp.exec, g, 0), "graph instantiate");
+}
+
 static int spec_decode(Spec& sp, int use_graph, double* seconds) {
   if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "spec: decode before prefill");
   cudaStream_t st = sp.st;
   int rc = LMX_OK;
-  if (use_graph && !sp.exec) {
-    rc = cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "capture begin");
-    if (rc) return rc;
-    int rc2 = spec_step(sp);
-    cudaGraph_t g = nullptr;
-    rc = cuda_check(cudaStreamEndCapture(st, &g), "capture end");
-    if (rc2) {
-      if (g) cudaGraphDestroy(g);
-      return rc2;
-    }
-    if (rc) return rc;
-    sp.graph = g;
-    rc = cuda_check(cudaGraphInstantiate(&sp.exec, g, 0), "graph instantiate");
-    if (rc) return rc;
-  }
+  if (use_graph) rc = spec_capture(sp);
+  if (rc) return rc;
   const int B = sp.cfg.batch, MT = sp.cfg.max_tokens;
   std::vector<int> em(B);
   cudaEvent_t e0, e1;
@@ -1170,6 +1184,124 @@ static int spec_decode(Spec& sp, int use_graph, double* seconds) {
     if (code) rc = set_error(LMX_ERR_CUDA, "kernel reported error 0x%x", code);
   }
   return rc;
+}
+
+// TokenIterator::next() (src/common/generate.cpp:968-1045): the next token of
+// every sequence in emission order (d0 first, then the accepted drafts; the
+// correction / bonus token is the next step's d0).  One speculative step (one
+// graph replay; K = 0: one plain decode step, generate.cpp:671-686) runs only
+// when a sequence that has not reached max_tokens has no token left to read.
+// tok[b] = -1 once sequence b has given all max_tokens; *n_live counts the
+// others (0 is the reference's nullopt).
+static int spec_next(Spec& sp, int32_t* tok, int* n_live) {
+  if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "spec_next: before prefill");
+  const int B = sp.cfg.batch, MT = sp.cfg.max_tokens;
+  int rc = spec_capture(sp);
+  bool need = false;
+  for (int b = 0; b < B; ++b) need = need || (sp.it_rp[b] < MT && sp.it_rp[b] >= sp.it_em[b]);
+  if (!rc && need) {
+    rc = cuda_check(cudaGraphLaunch(sp.exec, sp.st), "graph launch");
+    ++sp.replays;
+    if (!rc)
+      rc = cuda_check(cudaMemcpyAsync(sp.it_em.data(), sp.s.emitted, (size_t)B * 4, cudaMemcpyDeviceToHost, sp.st),
+                      "emitted");
+    if (!rc)
+      rc = cuda_check(cudaMemcpyAsync(sp.it_buf.data(), sp.s.out, sp.it_buf.size() * 4, cudaMemcpyDeviceToHost,
+                                      sp.st),
+                      "stream");
+    if (!rc) rc = cuda_check(cudaStreamSynchronize(sp.st), "spec_next");
+    if (!rc) {
+      unsigned code = 0;
+      cudaMemcpyFromSymbol(&code, g_lmx_kernel_error, sizeof(code));
+      if (code) rc = set_error(LMX_ERR_CUDA, "kernel reported error 0x%x", code);
+    }
+  }
+  if (rc) return rc;
+  int live = 0;
+  for (int b = 0; b < B; ++b) {
+    if (sp.it_rp[b] < std::min(sp.it_em[b], MT)) {
+      tok[b] = sp.it_buf[(size_t)b * MT + sp.it_rp[b]++];
+      ++live;
+    } else {
+      tok[b] = -1;
+    }
+  }
+  *n_live = live;
+  return LMX_OK;
+}
+
+// generate() (src/common/generate.cpp:1061-1125) per sequence: prefill the
+// prompts, then tokens from spec_next until every sequence has stopped.  The
+// cancellation predicate is polled before every step (generate.h:218-228);
+// a token in eos_ids ends its sequence without being counted or passed on;
+// on_token returning nonzero ends its sequence after it (GenerateDisposition::
+// stop).  Timings as GenerateCompletionInfo (generate.h:170-199): prompt_time
+// the prefill's wall time, generation_time from a sequence's first token to
+// its end (the reference restarts its clock at the first token).
+static int spec_generate(Spec& sp, const int32_t* prompts, const int32_t* eos, int n_eos, lmx_cancel_fn cancel,
+                         void* cancel_user, lmx_token_fn on_token, void* token_user, lmx_completion_info* info) {
+  using clk = std::chrono::steady_clock;
+  const int B = sp.cfg.batch;
+  const auto t0 = clk::now();
+  int rc = spec_prefill(sp, prompts);
+  if (rc) return rc;
+  const double prompt_s = std::chrono::duration<double>(clk::now() - t0).count();
+  std::vector<int> count(B, 0);
+  std::vector<char> done(B, 0), started(B, 0);
+  std::vector<clk::time_point> first(B, clk::now()), end(B, clk::now());
+  std::vector<int32_t> tok(B);
+  for (;;) {
+    if (cancel && cancel(cancel_user)) break;
+    int live = 0;
+    rc = spec_next(sp, tok.data(), &live);
+    if (rc) return rc;
+    if (!live) break;
+    bool any = false;
+    for (int b = 0; b < B; ++b) {
+      if (done[b] || tok[b] < 0) continue;
+      if (!started[b]) {
+        started[b] = 1;
+        first[b] = clk::now();
+      }
+      bool is_eos = false;
+      for (int i = 0; i < n_eos && !is_eos; ++i) is_eos = eos[i] == tok[b];
+      if (is_eos) {
+        done[b] = 1;
+        end[b] = clk::now();
+        continue;
+      }
+      ++count[b];
+      if (on_token && on_token(token_user, b, tok[b])) {
+        done[b] = 1;
+        end[b] = clk::now();
+        continue;
+      }
+      any = true;
+    }
+    bool all = true;
+    for (int b = 0; b < B; ++b) all = all && (done[b] || sp.it_rp[b] >= sp.cfg.max_tokens);
+    if (all || !any) {
+      bool pending = false;  // a sequence may still have tokens to read
+      for (int b = 0; b < B; ++b) pending = pending || (!done[b] && sp.it_rp[b] < sp.cfg.max_tokens);
+      if (!pending) break;
+    }
+  }
+  std::vector<int> steps(B), acc(B);
+  rc = cuda_check(cudaMemcpy(steps.data(), sp.s.steps, (size_t)B * 4, cudaMemcpyDeviceToHost), "stats");
+  if (!rc) rc = cuda_check(cudaMemcpy(acc.data(), sp.s.accepted, (size_t)B * 4, cudaMemcpyDeviceToHost), "stats");
+  if (rc) return rc;
+  const auto now = clk::now();
+  for (int b = 0; b < B && info; ++b) {
+    lmx_completion_info& f = info[b];
+    f.prompt_token_count = sp.cfg.prompt_len;
+    f.generation_token_count = count[b];
+    f.prompt_time = prompt_s;
+    f.generation_time = started[b] ? std::chrono::duration<double>((done[b] ? end[b] : now) - first[b]).count() : 0.0;
+    f.mtp_draft_tokens_proposed = steps[b] * sp.cfg.K;
+    f.mtp_draft_tokens_accepted = acc[b];
+    f.mtp_speculative_steps = steps[b];
+  }
+  return LMX_OK;
 }
 
 }  // namespace lmx
@@ -1423,6 +1555,20 @@ extern "C" int lmx_spec_result(void* spec, int32_t* out_host, int64_t* stats_hos
   return rc;
 }
 
+extern "C" int lmx_spec_next(void* spec, int32_t* tokens_host, int* n_live) {
+  if (!spec || !tokens_host || !n_live) return set_error(LMX_ERR_INVALID, "spec_next: null argument");
+  return spec_next(*(Spec*)spec, tokens_host, n_live);
+}
+
+extern "C" int lmx_spec_generate(void* spec, const int32_t* prompts_host, const int32_t* eos_ids, int n_eos,
+                                 lmx_cancel_fn should_cancel, void* cancel_user, lmx_token_fn on_token,
+                                 void* token_user, lmx_completion_info* info) {
+  if (!spec || !prompts_host || n_eos < 0 || (n_eos > 0 && !eos_ids))
+    return set_error(LMX_ERR_INVALID, "spec_generate: bad arguments");
+  return spec_generate(*(Spec*)spec, prompts_host, eos_ids, n_eos, should_cancel, cancel_user, on_token, token_user,
+                       info);
+}
+
 extern "C" int lmx_spec_free(void* spec) {
   delete (Spec*)spec;
   return LMX_OK;
@@ -1456,6 +1602,7 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     if (head) s += qmm_bytes(m.head(), bits, M);
     return s;
   };
+  if (what == 1 && K == 0) return set_error(LMX_ERR_INVALID, "profile: no draft (K = 0)");
   if (what == 0) by = model_bytes(*sp.tm, sp.tm->n_layers, B * (K + 1), tl, K + 1, true);
   else if (what == 1) by = model_bytes(*sp.dm, sp.dl, B, dl, 1, true);
   else if (what == 2) by = qmm_bytes(sp.tm->head(), bits, B * (K + 1));

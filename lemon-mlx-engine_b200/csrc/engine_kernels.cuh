@@ -205,6 +205,7 @@ LMX_DEV void commit_step(const SpecState& s, int b, int acc, int next) {
   s.steps[b] += 1;
   s.tok2[2 * b] = acc > 0 ? d[acc - 1] : y;
   s.tok2[2 * b + 1] = next;
+  s.vt[b * (s.K + 1)] = next;  // the next verify input starts with it (K = 0: it is the whole input)
   s.tlen[b] = p + acc + 1;
   s.dlen[b] = p + acc;
 }
@@ -241,6 +242,7 @@ __global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, 
   if (b >= s.B) return;
   s.tok2[2 * b] = prompts[(size_t)b * P + P - 1];
   s.tok2[2 * b + 1] = y[b];
+  s.vt[b * (s.K + 1)] = y[b];
   s.tlen[b] = ctx + P;
   s.dlen[b] = ctx + P - 1;
   s.emitted[b] = 0;

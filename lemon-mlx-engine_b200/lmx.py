@@ -87,6 +87,8 @@ SIGNATURES = {
     "lmx_spec_decode": (I, [P, I, P]),
     "lmx_spec_result": (I, [P, P, P]),
     "lmx_spec_free": (I, [P]),
+    "lmx_spec_next": (I, [P, P, P]),
+    "lmx_spec_generate": (I, [P, P, P, I, P, P, P, P, P]),
     "lmx_spec_profile": (I, [P, I, I, P, P]),
     "lmx_spec_step_launches": (I, [P, P]),
 }
@@ -247,6 +249,17 @@ class Model:
             pass
 
 
+class CompletionInfo(C.Structure):
+    """lmx_completion_info (GenerateCompletionInfo)"""
+    _fields_ = [("prompt_token_count", I), ("generation_token_count", I), ("prompt_time", C.c_double),
+                ("generation_time", C.c_double), ("mtp_draft_tokens_proposed", I),
+                ("mtp_draft_tokens_accepted", I), ("mtp_speculative_steps", I)]
+
+
+CANCEL_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
+TOKEN_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int32)
+
+
 class SpecDecoder:
     """Speculative decoder over a target and a draft (or self-draft) model:
     the reference's generate()/TokenIterator emission contract."""
@@ -281,6 +294,29 @@ class SpecDecoder:
              st.ctypes.data_as(C.c_void_p))
         return out, dict(steps=int(st[0]), proposed=int(st[1]), accepted=int(st[2]),
                          emitted=int(st[3]), replays=int(st[4]))
+
+    def next(self):
+        """TokenIterator::next(): the next token of every sequence (-1 once a
+        sequence has produced max_tokens), or None when none is left."""
+        import numpy as np
+        out = np.zeros(self.cfg.batch, np.int32)
+        live = C.c_int(0)
+        call("lmx_spec_next", self.h, out.ctypes.data_as(C.c_void_p), C.byref(live))
+        return out if live.value else None
+
+    def generate(self, prompts, eos=(), should_cancel=None, on_token=None):
+        """generate(): prefill, then tokens until every sequence stops (EOS,
+        on_token returning True, max_tokens) or should_cancel() returns True.
+        Returns the per-sequence CompletionInfo list."""
+        import numpy as np
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        e = np.ascontiguousarray(list(eos), dtype=np.int32)
+        cf = CANCEL_FN(lambda _u: 1 if should_cancel() else 0) if should_cancel else CANCEL_FN()
+        tf = TOKEN_FN(lambda _u, b, t: 1 if on_token(b, t) else 0) if on_token else TOKEN_FN()
+        info = (CompletionInfo * self.cfg.batch)()
+        call("lmx_spec_generate", self.h, p.ctypes.data_as(C.c_void_p),
+             e.ctypes.data_as(C.c_void_p) if e.size else None, int(e.size), cf, None, tf, None, info)
+        return list(info)
 
     def profile(self, what, iters=20):
         sec, by = C.c_double(0.0), C.c_double(0.0)

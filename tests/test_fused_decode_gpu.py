@@ -28,16 +28,19 @@ def oracle_cfg(cfg):
 
 
 def within(got, ref, what, kv_bits):
+    # 3 layers of Qwen3-0.6B widths after a prefill whose 40-row chunks take
+    # the tcgen05 path: the accumulation-order drift against the oracle's
+    # emulation reaches ~0.03 (measured), so the bound is 4e-2 + ulp
     g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
     diff = np.abs(g - r)
-    lim = 2e-2 + np.abs(r) * 2.0 ** -7
+    lim = 4e-2 + np.abs(r) * 2.0 ** -7
     if kv_bits != 16:
         # a quantized cache code can flip on a one-ulp K/V difference and move
         # every logit of the rows that read it (see test_engine_gpu): bounded
         # by 1e-1 per logit
         assert not (diff > 1e-1 + lim).any(), f"{what}: max |diff| {diff.max():.4g}"
         return
-    assert not (diff > lim).any(), f"{what}: {int((diff > lim).sum())} beyond 2e-2 + ulp, max {diff.max():.4g}"
+    assert not (diff > lim).any(), f"{what}: {int((diff > lim).sum())} beyond 4e-2 + ulp, max {diff.max():.4g}"
 
 
 @pytest.fixture(autouse=True)
