@@ -159,6 +159,21 @@ typedef struct {
   int32_t* lengths;         /* [batch] rows cached before the current block    */
 } lmx_kv;
 
+/* KV append (KVCacheSimple::update_impl, src/common/kv_cache.cpp:34-110;
+ * QuantizedKVCache::update_impl + quantize_kv, :271-298, :243-269): rows
+ * k_new / v_new bf16 [batch][kv_heads][T][128] (the reference's update
+ * layout; keys already normed and roped) go to rows lengths[b] .. +T-1 of
+ * each sequence -- quantized on append for a 4/8-bit cache with the rule
+ * scale = bf16((max-min)/(2^bits-1)), bias = bf16(min), q = rint((x-bias)/
+ * scale) per group of 64 -- and every length advances by T (on the device).
+ * A block past the capacity is written nowhere and sets the device error
+ * word to 0x42 (lmx_device_error). */
+int lmx_kv_append(const lmx_kv* kv, const void* k_new, const void* v_new, int T, void* stream);
+/* KVCache::set_position (kv_cache.cpp:135-142, :301-377): roll sequence seq
+ * back to pos rows (no-op when pos >= its length); on the device, in stream
+ * order. */
+int lmx_kv_set_position(const lmx_kv* kv, int seq, int pos, void* stream);
+
 /* Scratch bytes lmx_sdpa_decode needs for this shape (split partials and
  * per-tile counters).  The scratch must be zero-filled before its first use;
  * every call leaves it ready for the next. */
@@ -370,6 +385,13 @@ int lmx_cache_free(void* cache);
  * back to `pos` rows (no-op if pos >= its length). */
 int lmx_cache_set_position(void* cache, int seq, int pos);
 int lmx_cache_len(void* cache, int seq, int* len);
+/* Layer `layer` of an engine cache as an lmx_kv descriptor: device pointers
+ * into the cache itself (KVCacheSimple::state(), include/mlx-lm/common/
+ * kv_cache.h:81-87), for lmx_sdpa_decode, lmx_kv_append and
+ * lmx_kv_set_position or for reading the rows.  Valid until the cache is
+ * freed; capacity may exceed the one requested (rows are allocated in whole
+ * 128-key splits). */
+int lmx_cache_kv(void* cache, int layer, lmx_kv* out);
 /* Synthetic context: rows [0, rows) of every layer's K and V hold seeded
  * N(0,1) values (Philox normal, tensor id tid_base + 2*layer + (0 K, 1 V),
  * element ((b*kv_heads + head)*rows + row)*128 + d over the whole model's KV
@@ -410,6 +432,14 @@ typedef struct {
    * slice, seq_base = the slice's first global index) draws exactly what one
    * decoder over the whole batch would.  0 for a single decoder.          */
   int seq_base;
+  /* REF_KV_PAD_QUIRK (4/8-bit caches): reproduce the reference's
+   * maybe_quantize_kv_cache (src/common/kv_cache.cpp:391-413) -- the prompt
+   * is prefilled with a bf16 cache, then the whole reference allocation
+   * (max(first 512-token chunk, 256) rows, doubled as the prompt grows;
+   * zero rows past the prompt included) is quantized and decoding continues
+   * at that offset.  0: the intended semantics (rows quantized on append,
+   * the offset counts tokens).                                             */
+  int kv_quirk;
 } lmx_spec_config;
 
 /* draft may be NULL (self-draft: the first draft_layers of target). */

@@ -1026,6 +1026,23 @@ static int spec_step(Spec& sp) {
 
 namespace lmx {
 
+// The reference's KVCacheSimple allocation after prefilling n tokens: the
+// prompt in chunks of 512 while more than 512 remain, then the rest
+// (include/mlx-lm/llm/llm_model.h:18-60); first allocation max(chunk, 256)
+// rows, then max(2 alloc, offset + chunk) when a chunk does not fit
+// (src/common/kv_cache.cpp:34-110, include/mlx-lm/common/kv_cache.h:43).
+static int kv_quirk_alloc(int n) {
+  int alloc = 0, off = 0, rem = n;
+  while (rem > 0) {
+    const int c = rem > 512 ? 512 : rem;
+    if (alloc == 0) alloc = std::max(c, 256);
+    else if (off + c > alloc) alloc = std::max(2 * alloc, off + c);
+    off += c;
+    rem -= c;
+  }
+  return alloc;
+}
+
 static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
   if (cfg.batch < 1 || cfg.K < 0 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
@@ -1041,7 +1058,8 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   sp->cfg = cfg;
   const int B = cfg.batch, K = cfg.K, P = cfg.prompt_len;
   if (cfg.context_len < 0) return set_error(LMX_ERR_INVALID, "spec: context_len < 0");
-  const int cap = cfg.context_len + P + cfg.max_tokens + K + 8;
+  const bool quirk = cfg.kv_quirk && cfg.kv_bits != 16;
+  const int cap = (quirk ? kv_quirk_alloc(cfg.context_len + P) : cfg.context_len + P) + cfg.max_tokens + K + 8;
   Cache *tc = nullptr, *dc = nullptr;
   int rc = cache_create(*tm, tm->n_layers, B, cap, cfg.kv_bits, &tc);
   if (rc) return rc;
@@ -1096,6 +1114,36 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
 
 static constexpr uint32_t kCtxTidTarget = 0x40000000u, kCtxTidDraft = 0x50000000u;
 
+// Quantize rows [0, rows) of a bf16 cache layer into a 4/8-bit one (the
+// append rule): one warp per (sequence, KV head, row, K or V).
+__global__ void kv_quirk_convert_kernel(KvDesc src, KvDesc dst, int rows) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)src.B * src.Hk * rows * 2) return;
+  const bool is_v = (w & 1) != 0;
+  const int64_t r = w >> 1, bh = r / rows;
+  const int j = (int)(r % rows);
+  float x[8];
+  if (lane < 16) unpack8(*reinterpret_cast<const uint4*>((is_v ? src.v : src.k) + ((size_t)bh * src.cap + j) * kHeadDim + 8 * lane), x);
+  else
+    for (int e = 0; e < 8; ++e) x[e] = 0.0f;
+  uint4 deq;
+  dec_append(dst, !is_v, (size_t)bh * dst.cap + j, lane, x, deq);
+}
+
+// Prefill for the KV pad quirk: the prompt into bf16 copies of both caches,
+// then the reference allocation quantized into the real caches.
+static int quirk_convert(Cache& src, Cache& dst, int rows, cudaStream_t st) {
+  if (rows > dst.cap || rows > src.cap) return set_error(LMX_ERR_CAPACITY, "kv quirk: %d rows > capacity", rows);
+  const int64_t threads = (int64_t)src.B * src.Hk * rows * 2 * 32;
+  for (int l = 0; l < dst.n_layers; ++l) {
+    kv_quirk_convert_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(src.kv[l], dst.kv[l], rows);
+    int rc = cuda_check(cudaGetLastError(), "kv quirk convert");
+    if (rc) return rc;
+  }
+  return LMX_OK;
+}
+
 // Prefill (TokenIterator::prepare, src/common/generate.cpp:508-549): the
 // target runs the prompt and its argmax at the last position is d0 of the
 // first step; the draft runs prompt[0, P-1) (its first step re-runs P-1).
@@ -1104,10 +1152,24 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
   cudaStream_t st = sp.st;
   int rc = cuda_check(cudaMemcpyAsync(sp.prompts, prompts_host, (size_t)B * P * 4, cudaMemcpyHostToDevice, st),
                       "prompts");
+  const int ctx = sp.cfg.context_len;
+  const bool quirk = sp.cfg.kv_quirk && sp.cfg.kv_bits != 16;
+  const int tl = quirk ? kv_quirk_alloc(ctx + P) : ctx + P, dl = quirk ? kv_quirk_alloc(ctx + P - 1) : ctx + P - 1;
+  // the KV pad quirk prefills into bf16 copies of the caches
+  std::unique_ptr<Cache> tq, dq;
+  if (!rc && quirk) {
+    Cache *a = nullptr, *b = nullptr;
+    rc = cache_create(*sp.tm, sp.tc->n_layers, B, sp.tc->cap, 16, &a);
+    tq.reset(a);
+    if (!rc) rc = cache_create(*sp.dm, sp.dc->n_layers, B, sp.dc->cap, 16, &b);
+    dq.reset(b);
+  }
+  Cache& tpre = quirk ? *tq : *sp.tc;
+  Cache& dpre = quirk ? *dq : *sp.dc;
   // the synthetic context (if any) precedes the prompt in both caches
-  if (!rc) rc = cache_fill_synthetic(*sp.tc, sp.cfg.context_len, sp.cfg.context_seed, kCtxTidTarget, st);
-  if (!rc) rc = cache_fill_synthetic(*sp.dc, sp.cfg.context_len, sp.cfg.context_seed, kCtxTidDraft, st);
-  if (!rc) rc = forward_chunked(*sp.tm, *sp.tc, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
+  if (!rc) rc = cache_fill_synthetic(tpre, ctx, sp.cfg.context_seed, kCtxTidTarget, st);
+  if (!rc) rc = cache_fill_synthetic(dpre, ctx, sp.cfg.context_seed, kCtxTidDraft, st);
+  if (!rc) rc = forward_chunked(*sp.tm, tpre, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
   if (!rc && sp.cfg.temperature > 0.0f)
     rc = cuda_check(samp_launch(sample_rows_kernel, B, st,
                                (const bf16_t*)sp.ws.logits, sp.tm->c.vocab, sp.tm->c.vocab, stoch_params(sp),
@@ -1115,10 +1177,15 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
                     "prefill sample");
   else if (!rc)
     rc = model_argmax(*sp.tm, sp.ws.logits, B, sp.tm->vl, sp.yprefill, st);
-  if (!rc && sp.cfg.K > 0) rc = forward_chunked(*sp.dm, *sp.dc, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
+  if (!rc && sp.cfg.K > 0) rc = forward_chunked(*sp.dm, dpre, sp.dl, sp.prompts, P, P - 1, B, sp.ws, nullptr, st);
+  if (!rc && quirk) {
+    rc = quirk_convert(*tq, *sp.tc, tl, st);
+    if (!rc) rc = quirk_convert(*dq, *sp.dc, dl, st);
+    if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "kv quirk");  // the bf16 copies go now
+  }
   if (!rc)
     rc = cuda_check(lmx_launch(prefill_done_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
-                               (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill, sp.cfg.context_len),
+                               (const int32_t*)sp.prompts, P, (const int32_t*)sp.yprefill, tl, dl),
                     "prefill_done");
   if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "prefill");
   if (!rc) sp.prefilled = true;
@@ -1748,6 +1815,97 @@ static int sdpa_call(const void* q, const lmx_kv* kv, int T, int heads, float sc
   return launch_sdpa(sa, d.B, st);
 }
 }  // namespace lmx
+
+namespace lmx {
+// KV append over a caller-described cache: k_new / v_new bf16
+// [batch][kv_heads][T][128] (the reference's update layout), row t of
+// sequence b written at lengths[b] + t (quantized on append for 4/8-bit);
+// one warp per (sequence, KV head, token, K or V).  A block past the
+// capacity sets the device error word 0x42 and writes nothing.
+__global__ void kv_append_kernel(KvDesc kv, const bf16_t* kn, const bf16_t* vn, int T, unsigned* err) {
+  grid_wait();
+  grid_launch_dependents();
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)kv.B * kv.Hk * T * 2) return;
+  const bool is_v = (w & 1) != 0;
+  const int64_t r = w >> 1;  // ((b * Hk + h) * T + t)
+  const int t = (int)(r % T);
+  const int64_t bh = r / T;
+  const int b = (int)(bh / kv.Hk);
+  const int pos = kv.len[b] + t;
+  if (kv.len[b] + T > kv.cap) {
+    if (lane == 0 && t == 0) atomicExch(err, 0x42u);
+    return;
+  }
+  float x[8];
+  if (lane < 16) unpack8(*reinterpret_cast<const uint4*>((is_v ? vn : kn) + (size_t)r * kHeadDim + 8 * lane), x);
+  else
+    for (int e = 0; e < 8; ++e) x[e] = 0.0f;
+  uint4 deq;
+  dec_append(kv, !is_v, (size_t)bh * kv.cap + pos, lane, x, deq);
+}
+
+__global__ void kv_advance_kernel(int* len, int B, int T, int cap) {
+  grid_wait();
+  grid_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B && len[b] + T <= cap) len[b] += T;  // a refused block leaves the length
+}
+
+__global__ void kv_set_position_kernel(int* len, int seq, int pos) {
+  grid_wait();
+  grid_launch_dependents();
+  if (threadIdx.x == 0 && pos < len[seq]) len[seq] = pos;
+}
+}  // namespace lmx
+
+extern "C" int lmx_cache_kv(void* cache, int layer, lmx_kv* out) {
+  CacheHandle* h = (CacheHandle*)cache;
+  if (!h || !out || layer < 0 || layer >= h->c->n_layers) return set_error(LMX_ERR_INVALID, "cache_kv: bad arguments");
+  const KvDesc& d = h->c->kv[layer];
+  std::memset(out, 0, sizeof(*out));
+  out->batch = d.B;
+  out->kv_heads = d.Hk;
+  out->head_dim = kHeadDim;
+  out->capacity = d.cap;
+  out->bits = d.bits;
+  out->k = d.k;
+  out->v = d.v;
+  out->k_packed = d.kq;
+  out->v_packed = d.vq;
+  out->k_scales = d.ks;
+  out->k_biases = d.kb;
+  out->v_scales = d.vs;
+  out->v_biases = d.vb;
+  out->lengths = d.len;
+  return LMX_OK;
+}
+
+extern "C" int lmx_kv_append(const lmx_kv* kv, const void* k_new, const void* v_new, int T, void* stream) {
+  KvDesc d;
+  int rc = kv_from_c(kv, d);
+  if (rc) return rc;
+  if (!k_new || !v_new || T < 1 || ((uintptr_t)k_new & 15) || ((uintptr_t)v_new & 15))
+    return set_error(LMX_ERR_INVALID, "kv_append: bad block (16-byte aligned bf16 [batch][kv_heads][T][128])");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t threads = (int64_t)d.B * d.Hk * T * 2 * 32;
+  rc = cuda_check(lmx_launch(kv_append_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, true, d,
+                             (const bf16_t*)k_new, (const bf16_t*)v_new, T, device_error_word()),
+                  "kv_append");
+  if (!rc)
+    rc = cuda_check(lmx_launch(kv_advance_kernel, dim3((d.B + 127) / 128), dim3(128), 0, st, true, d.len, d.B, T, d.cap),
+                    "kv_append: lengths");
+  return rc;
+}
+
+extern "C" int lmx_kv_set_position(const lmx_kv* kv, int seq, int pos, void* stream) {
+  if (!kv || !kv->lengths || seq < 0 || seq >= kv->batch || pos < 0)
+    return set_error(LMX_ERR_INVALID, "kv_set_position: bad arguments");
+  return cuda_check(lmx_launch(kv_set_position_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, true,
+                               (int*)kv->lengths, seq, pos),
+                    "kv_set_position");
+}
 
 extern "C" size_t lmx_sdpa_scratch_bytes(int batch, int T, int heads, int kv_heads, int capacity) {
   if (batch < 1 || T < 1 || heads < 1 || kv_heads < 1 || capacity < 1 || heads % kv_heads) return 0;

@@ -232,10 +232,12 @@ __global__ void accept_greedy_kernel(SpecState s) {
   commit_step(s, b, acc, pr[acc]);
 }
 
-// Prefill bookkeeping: y = argmax of the last prompt position (already in
-// pred[b*(K+1)]), tok2 = (prompt[P-1], y), lengths ctx+P and ctx+P-1 (ctx:
-// synthetic context rows before the prompt).
-__global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, const int32_t* y, int ctx) {
+// Prefill bookkeeping: y = the first token from the last prompt position,
+// tok2 = (prompt[P-1], y), the target / draft cache lengths (ctx+P and
+// ctx+P-1, ctx synthetic context rows before the prompt; with the KV pad
+// quirk, the reference allocations).
+__global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, const int32_t* y, int tlen,
+                                    int dlen) {
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -243,8 +245,8 @@ __global__ void prefill_done_kernel(SpecState s, const int32_t* prompts, int P, 
   s.tok2[2 * b] = prompts[(size_t)b * P + P - 1];
   s.tok2[2 * b + 1] = y[b];
   s.vt[b * (s.K + 1)] = y[b];
-  s.tlen[b] = ctx + P;
-  s.dlen[b] = ctx + P - 1;
+  s.tlen[b] = tlen;
+  s.dlen[b] = dlen;
   s.emitted[b] = 0;
   s.accepted[b] = 0;
   s.steps[b] = 0;

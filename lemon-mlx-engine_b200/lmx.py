@@ -46,6 +46,9 @@ SIGNATURES = {
     "lmx_sdpa_scratch_bytes": (C.c_size_t, [I, I, I, I, I]),
     "lmx_sdpa_decode": (I, [P, P, I, I, F, P, C.c_size_t, P, P]),
     "lmx_sdpa_decode_noalloc": (I, [P, P, I, I, F, P, P]),
+    "lmx_kv_append": (I, [P, P, P, I, P]),
+    "lmx_kv_set_position": (I, [P, I, I, P]),
+    "lmx_cache_kv": (I, [P, I, P]),
     "lmx_model_create": (I, [P, U64, P]),
     "lmx_model_create_tp": (I, [P, U64, P, P]),
     "lmx_tp_comm_create": (I, [I, I, I, I, P]),
@@ -132,7 +135,7 @@ class SpecConfig(C.Structure):
     """lmx_spec_config"""
     _fields_ = [("batch", I), ("K", I), ("max_tokens", I), ("prompt_len", I), ("kv_bits", I),
                 ("temperature", F), ("top_p", F), ("seed", U64), ("context_len", I),
-                ("context_seed", U64), ("seq_base", I)]
+                ("context_seed", U64), ("seq_base", I), ("kv_quirk", I)]
 
 
 # configs[3]: Qwen3-Next-style hybrid (the unspecified head counts / dims
@@ -266,9 +269,9 @@ class SpecDecoder:
 
     def __init__(self, target: Model, draft, draft_layers: int, batch: int, K: int,
                  max_tokens: int, prompt_len: int, kv_bits=16, temperature=0.0, top_p=1.0,
-                 seed=0, context_len=0, context_seed=0, seq_base=0):
+                 seed=0, context_len=0, context_seed=0, seq_base=0, kv_quirk=0):
         self.cfg = SpecConfig(batch, K, max_tokens, prompt_len, kv_bits, temperature, top_p, seed,
-                              context_len, context_seed, seq_base)
+                              context_len, context_seed, seq_base, kv_quirk)
         h = C.c_void_p()
         call("lmx_spec_create", target.h, draft.h if draft is not None else None, draft_layers,
              C.byref(self.cfg), C.byref(h))

@@ -1264,6 +1264,46 @@ static int forward_impl(Model& m, Cache& c, int n_layers, const int32_t* tokens,
 // prefill chunking), so that every quantized matmul sees the same M on both
 // sides and takes the same path; logits of each sequence's last token.
 static constexpr int kPrefillChunk = 32;
+// REF_KV_PAD_QUIRK (the reference's maybe_quantize_kv_cache, src/common/
+// kv_cache.cpp:391-413): the prompt is prefilled into a bf16 KVCacheSimple,
+// whose first allocation is max(first chunk, 256) rows and which grows to
+// max(2 alloc, offset + n) when a chunk does not fit (kv_cache.cpp:34-110,
+// include/mlx-lm/common/kv_cache.h:43); the prompt goes in chunks of 512
+// while more than 512 remain, then the rest (llm_model.h:18-60).  After the
+// prompt the WHOLE allocation -- zero rows past the prompt included -- is
+// quantized and the cache offset becomes the allocation length.
+static int g_kv_quirk = 0;
+extern "C" void orc_set_kv_quirk(int on) { g_kv_quirk = on ? 1 : 0; }
+extern "C" int orc_kv_quirk_alloc(int n) {
+  int alloc = 0, off = 0, rem = n;
+  while (rem > 0) {
+    const int c = rem > 512 ? 512 : rem;
+    if (alloc == 0) alloc = std::max(c, 256);
+    else if (off + c > alloc) alloc = std::max(2 * alloc, off + c);
+    off += c;
+    rem -= c;
+  }
+  return alloc;
+}
+// Quantize rows [0, rows) of every layer of the bf16 cache `src` into the
+// quantized cache `dst` (same geometry) and set every length to rows.
+static void quirk_convert(const Cache& src, Cache& dst, int rows) {
+  const int D = src.D, WPR = D * dst.bits / 32, gpr = D / 64;
+  for (int l = 0; l < dst.L; ++l)
+    for (int b = 0; b < dst.B; ++b)
+      for (int hk = 0; hk < dst.Hk; ++hk)
+        for (int j = 0; j < rows; ++j) {
+          const size_t rs = ((size_t)b * src.Hk + hk) * src.cap + j, rd = ((size_t)b * dst.Hk + hk) * dst.cap + j;
+          for (int gi = 0; gi < gpr; ++gi) {
+            quantize_group(&src.k[l][rs * D + 64 * gi], 64, dst.bits, &dst.kq[l][rd * WPR + gi * 64 * dst.bits / 32],
+                           &dst.ks[l][rd * gpr + gi], &dst.kb[l][rd * gpr + gi]);
+            quantize_group(&src.v[l][rs * D + 64 * gi], 64, dst.bits, &dst.vq[l][rd * WPR + gi * 64 * dst.bits / 32],
+                           &dst.vs[l][rd * gpr + gi], &dst.vb[l][rd * gpr + gi]);
+          }
+        }
+  for (int b = 0; b < dst.B; ++b) dst.len[b] = rows;
+}
+
 static int prefill_chunked(Model& m, Cache& c, int n_layers, const int32_t* tokens, int ld, int B, int T,
                            uint16_t* last_logits) {
   std::vector<int32_t> chunk;
@@ -1326,19 +1366,29 @@ extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prom
   const int K = ss->K, V = ss->V, dl = ss->dl;
   if (K < 1 || dl < 1 || dl > dm.c.layers || P < 2 || dm.c.vocab != V) return nullptr;
   if (prm->context_len < 0) return nullptr;
-  const int cap = prm->context_len + P + ss->MT + K + 8;
+  const int ctx = prm->context_len;
+  const bool quirk = g_kv_quirk && kv_bits != 16;
+  const int at = quirk ? orc_kv_quirk_alloc(ctx + P) : ctx + P, ad = quirk ? orc_kv_quirk_alloc(ctx + P - 1) : ctx + P;
+  const int cap = std::max(at, ad) + ss->MT + K + 8;
   ss->tc.reset((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, kv_bits));
   ss->dc.reset((Cache*)orc_cache_create(&dm, dl, B, cap, kv_bits));
   if (!ss->tc || !ss->dc) return nullptr;
+  // quirk: the prompt goes into bf16 caches first (converted below)
+  std::unique_ptr<Cache> tq, dq;
+  if (quirk) {
+    tq.reset((Cache*)orc_cache_create(&tm, tm.c.layers, B, cap, 16));
+    dq.reset((Cache*)orc_cache_create(&dm, dl, B, cap, 16));
+  }
+  Cache& tpre = quirk ? *tq : *ss->tc;
+  Cache& dpre = quirk ? *dq : *ss->dc;
   // the synthetic context precedes the prompt in both caches (tensor ids as
   // the device engine: target 0x40000000, draft 0x50000000)
-  if (prm->context_len > 0 &&
-      (orc_cache_fill_synthetic(ss->tc.get(), prm->context_len, prm->context_seed, 0x40000000u) ||
-       orc_cache_fill_synthetic(ss->dc.get(), prm->context_len, prm->context_seed, 0x50000000u)))
+  if (ctx > 0 && (orc_cache_fill_synthetic(&tpre, ctx, prm->context_seed, 0x40000000u) ||
+                  orc_cache_fill_synthetic(&dpre, ctx, prm->context_seed, 0x50000000u)))
     return nullptr;
   const auto t0 = std::chrono::steady_clock::now();
   std::vector<uint16_t> lg((size_t)B * V);
-  if (prefill_chunked(tm, *ss->tc, tm.c.layers, prompts, P, B, P, lg.data())) return nullptr;
+  if (prefill_chunked(tm, tpre, tm.c.layers, prompts, P, B, P, lg.data())) return nullptr;
   ss->y.resize(B);
   ss->last.resize(B);
   std::vector<int32_t> pp((size_t)B * (P - 1));
@@ -1349,7 +1399,11 @@ extern "C" void* orc_spec_session(void* target, void* draft, const int32_t* prom
     ss->last[b] = prompts[(size_t)b * P + P - 1];
     std::memcpy(&pp[(size_t)b * (P - 1)], &prompts[(size_t)b * P], (P - 1) * 4);
   }
-  if (prefill_chunked(dm, *ss->dc, dl, pp.data(), P - 1, B, P - 1, nullptr)) return nullptr;
+  if (prefill_chunked(dm, dpre, dl, pp.data(), P - 1, B, P - 1, nullptr)) return nullptr;
+  if (quirk) {
+    quirk_convert(*tq, *ss->tc, at);
+    quirk_convert(*dq, *ss->dc, ad);
+  }
   ss->prefill_ns =
       std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
   ss->emitted.assign(B, 0);

@@ -183,6 +183,13 @@ void orc_spec_session_free(void* session);
 int orc_threads(void);
 /* OpenMP threads for later calls (n <= 0: every online host core); returns the count. */
 int orc_set_threads(int n);
+/* REF_KV_PAD_QUIRK mode for quantized KV caches (the reference's
+ * maybe_quantize_kv_cache): the prompt is prefilled into a bf16 cache, then
+ * the whole reference allocation (orc_kv_quirk_alloc rows, zero rows past the
+ * prompt included) is quantized and decoding continues at that offset.  Off:
+ * the intended semantics (rows quantized on append, offset = tokens). */
+void orc_set_kv_quirk(int on);
+int orc_kv_quirk_alloc(int n_tokens);
 /* Plain (non-speculative) greedy decode, same emission contract. */
 int orc_generate(void* target, const int32_t* prompts, int B, int P, int max_tokens,
                  int kv_bits, int32_t* out);

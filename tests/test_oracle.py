@@ -232,3 +232,13 @@ def test_set_position_rollback_is_exact(tiny_model):
     L.orc_forward(tiny_model, cache, TINY["layers"], O.ptr(extra), 1, 3, O.ptr(ly))
     np.testing.assert_array_equal(lx, ly)
     L.orc_cache_free(cache)
+
+
+def test_kv_quirk_allocation_rule():
+    # the reference's KVCacheSimple allocation after a prompt of n tokens
+    # (512-token chunks while more remain; first allocation max(chunk, 256);
+    # doubling when a chunk does not fit): kv_cache.cpp:34-110, llm_model.h:18-60
+    L = O.lib()
+    for n, want in [(1, 256), (40, 256), (255, 256), (256, 256), (257, 257), (300, 300), (512, 512),
+                    (513, 1024), (600, 1024), (1100, 2048), (8192, 8192)]:
+        assert L.orc_kv_quirk_alloc(n) == want, (n, L.orc_kv_quirk_alloc(n), want)
