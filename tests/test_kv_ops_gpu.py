@@ -73,11 +73,14 @@ def test_kv_append_and_set_position(lmx, cuda, bits):
     assert list(lens) == [2 * T, 2 * T - 3]
     for b in range(B):
         for h in range(Hk):
+            # sequence 1 was rolled back by 3 rows: the second block
+            # overwrote the first block's last 3 rows
             starts = [0, T if b == 0 else T - 3]
-            for (kn, vn), r0 in zip(blocks, starts):
+            counts = [T if b == 0 else T - 3, T]
+            for (kn, vn), r0, cnt in zip(blocks, starts, counts):
                 for which, src in (("k", kn), ("v", vn)):
-                    got = rows_of(kv, which, b, h, r0, T)
-                    x = np.ascontiguousarray(src[b, h])
+                    got = rows_of(kv, which, b, h, r0, cnt)
+                    x = np.ascontiguousarray(src[b, h, :cnt])
                     if bits == 16:
                         np.testing.assert_array_equal(got, x)
                     else:
