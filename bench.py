@@ -323,11 +323,20 @@ def run_hybrid(args, wl, world, rank, local):
     if args.layers:
         arch = dict(arch, layers=args.layers)
     B, P, MT = wl["batch"], wl["prompt"], wl["new"]
+    # N > 1: expert parallelism (every rank decodes the same B sequences with
+    # its 1/N of the experts; strong scaling); --replicas: independent copies
+    ep = world > 1 and not args.replicas
+    comm = None
     h = C.c_void_p()
-    lmx.call("lmx_hybrid_create", C.byref(lmx.HybridConfig(**arch)), args.seed, C.byref(h))
+    if ep:
+        comm = lmx.TpComm.from_process_group(max_rows=B * 32 * arch["top_k"], max_hidden=arch["hidden"])
+        lmx.call("lmx_hybrid_create_ep", C.byref(lmx.HybridConfig(**arch)), args.seed, comm.h, C.byref(h))
+    else:
+        lmx.call("lmx_hybrid_create", C.byref(lmx.HybridConfig(**arch)), args.seed, C.byref(h))
     sp = C.c_void_p()
     lmx.call("lmx_hybrid_spec_create", h, B, MT, P, wl["kv_bits"], C.byref(sp))
-    prompts = np.random.RandomState(args.seed + rank).randint(0, arch["vocab"], (B, P)).astype(np.int32)
+    prompts = np.random.RandomState(args.seed + (rank if world > 1 and not ep else 0)).randint(
+        0, arch["vocab"], (B, P)).astype(np.int32)
     out = np.zeros((B, MT), np.int32)
     stats = np.zeros(5, np.int64)
 
@@ -347,6 +356,9 @@ def run_hybrid(args, wl, world, rank, local):
         print(json.dumps({"verify_pass_us": round(vs.value * 1e6, 2), "bytes": vb.value}), flush=True)
         lmx.lib().lmx_hybrid_spec_free(sp)
         lmx.lib().lmx_hybrid_free(h)
+        if comm is not None:
+            barrier(world)
+            comm.close()
         return 0
     for _ in range(args.warmup):
         one()
@@ -373,21 +385,25 @@ def run_hybrid(args, wl, world, rank, local):
     lmx.call("lmx_hybrid_spec_profile", sp, 10, C.byref(vsec), C.byref(vbytes))
     vsec, vbytes = vsec.value, vbytes.value
     wall_m, dec_m = reduce(world, [wall, dec], "max")
-    toks_all = int(reduce(world, [float(toks)], "sum")[0])
+    # expert parallelism: every rank emits the same tokens
+    toks_all = toks if ep else int(reduce(world, [float(toks)], "sum")[0])
     peak, peak_kind = peaks()
     achieved = vbytes / vsec / 1e9
+    par = (f"ep{world} (experts sharded, {arch['experts'] // world} per rank; the rest replicated)" if ep
+           else (f"replicas x{world} (independent sequences per rank)" if world > 1 else "1 GPU"))
     res = {
         "metric": METRIC, "value": round(toks_all / dec_m, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * wall_m / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong" if ep else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": args.workload, "batch": B, "prompt": P, "new_tokens": MT, "kv_bits": wl["kv_bits"],
                    "weights": "4-bit g64", "draft": "MTP head, 2 tokens per step", "temperature": 0.0,
-                   "parallelism": f"replicas x{world} (independent sequences per rank)",
+                   "parallelism": par,
                    "l2": f"weights and experts ({vbytes / 1e6:.0f} MB per verify pass) exceed L2; no flush"},
         "e2e": {"value": round(toks_all / wall_m, 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": B * P * 4, "d2h_bytes_per_step": B * MT * 4 + 40},
-        "roofline": {"bound": "hbm", "kernel": f"verify pass ({arch['layers']} layers + lm_head, {B * 3} rows)",
+        "roofline": {"bound": "hbm", "kernel": f"verify pass ({arch['layers']} layers + lm_head, {B * 3} rows"
+                                               + (f", per rank of ep{world})" if ep else ")"),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": peak_kind, "algorithmic_bytes": vbytes, "verify_pass_us": round(vsec * 1e6, 2),
                      "traffic": None},
@@ -404,6 +420,9 @@ def run_hybrid(args, wl, world, rank, local):
         print(json.dumps(res), flush=True)
     lmx.lib().lmx_hybrid_spec_free(sp)
     lmx.lib().lmx_hybrid_free(h)
+    if comm is not None:
+        barrier(world)
+        comm.close()
     return 0
 
 

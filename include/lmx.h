@@ -276,6 +276,21 @@ typedef struct {
   int bits;                       /* 4 or 8                                */
 } lmx_hybrid_config;
 int lmx_hybrid_create(const lmx_hybrid_config* cfg, uint64_t seed, void** model);
+/* Expert parallelism across the GPUs of one node (configuration 4): this
+ * rank holds experts [rank*E/n, (rank+1)*E/n) of every MoE block (the same
+ * seeded values as the unsharded model); attention, Gated DeltaNet, router,
+ * shared expert, embedding, lm_head and the MTP head's other weights are
+ * replicated.  Per MoE block every rank runs the gate|up / down of the slots
+ * whose expert it holds and writes their outputs into its communicator
+ * block; after a bounded barrier every rank combines the k slots of each row
+ * in slot order, pulling each slot from its owner over NVLink -- the
+ * single-GPU arithmetic, so streams are identical for every rank count.  The
+ * communicator (lmx_tp_comm_create, opened on every rank) needs max_rows >=
+ * rows per forward x top_k and max_hidden >= hidden.  Every rank must issue
+ * the same calls in the same order.  The reference runs on one device and
+ * has no counterpart (its SwitchGLU / gather_qmm: src/common/
+ * switch_layers.cpp:79-245). */
+int lmx_hybrid_create_ep(const lmx_hybrid_config* cfg, uint64_t seed, void* comm, void** model);
 int lmx_hybrid_free(void* model);
 /* Trunk forward of a [B, T] token block (host ints) over the state's caches
  * (attention KV and recurrent states), committing every token; logits

@@ -345,16 +345,23 @@ struct MoeArgs {
   bf16_t* act;           // [M][k][I]
   bf16_t* y;             // [M][H]
   unsigned* err;         // device error word (expert index out of range)
+  // expert parallelism: this rank holds experts [e_lo, e_hi) (the weight
+  // pointers start at expert e_lo) and writes each owned slot's down output
+  // bf16 [M][k][H] to slot_out instead of combining (ep_combine_kernel)
+  int e_lo = 0, e_hi = 1 << 30;
+  bf16_t* slot_out = nullptr;
 };
 
-// Expert of slot s, or -1 (and the error word set) when out of range.
+// Local expert of slot s (index into this rank's weights), or -1 when it is
+// another rank's expert or out of range (the error word set).
 LMX_DEV int moe_expert(const MoeArgs& a, size_t s) {
   const int e = a.idx[s];
   if (e < 0 || e >= a.E) {
     if (a.err) atomicExch(a.err, 0x81u);
     return -1;
   }
-  return e;
+  if (e < a.e_lo || e >= a.e_hi) return -1;
+  return e - a.e_lo;
 }
 
 // gate / up: CTA = (slot m*k+j, block of 64 expert rows); warp per row pair
@@ -403,11 +410,15 @@ __global__ void __launch_bounds__(256) moe_down_kernel(MoeArgs a) {
       const int e = moe_expert(a, (size_t)m * a.k + j);
       if (e < 0) continue;
       const size_t row = (size_t)e * a.H + r;
-      const float v = bf2f(f2bf(qd_dot<BITS>(a.dw + row * wpr, a.ds + row * gpr, a.db + row * gpr,
-                                             mx_smem + (size_t)j * a.I, a.I, lane)));
-      acc = __fmaf_rn(a.w[(size_t)m * a.k + j], v, acc);
+      const bf16_t v = f2bf(qd_dot<BITS>(a.dw + row * wpr, a.ds + row * gpr, a.db + row * gpr,
+                                         mx_smem + (size_t)j * a.I, a.I, lane));
+      if (a.slot_out) {
+        if (lane == 0) a.slot_out[((size_t)m * a.k + j) * a.H + r] = v;
+      } else {
+        acc = __fmaf_rn(a.w[(size_t)m * a.k + j], bf2f(v), acc);
+      }
     }
-    if (lane == 0) a.y[(size_t)m * a.H + r] = f2bf(acc);
+    if (lane == 0 && !a.slot_out) a.y[(size_t)m * a.H + r] = f2bf(acc);
   }
 }
 

@@ -109,6 +109,11 @@ struct HybModel {
   float *cos_t = nullptr, *sin_t = nullptr;
   int max_pos = 16384;
   int n_attn = 0, n_gdn = 0;
+  // expert parallelism: this rank's experts [e_lo, e_lo + per) of every MoE
+  // block (router, shared expert, attention / GDN, heads replicated); comm
+  // not owned
+  int ep = 1, ep_rank = 0, per = 0, e_lo = 0;
+  TpComm* comm = nullptr;
   Arena ar;
   int CD() const { return 2 * c.lin_k_heads * kGdnD + c.lin_v_heads * kGdnD; }
 };
@@ -174,9 +179,13 @@ static int hyb_layer_create(HybModel& m, int l, bool attn, uint64_t seed, cudaSt
     if (!rc) rc = fill_ones(ar, &L.gnorm, kGdnD, st);
   }
   gq(L.router, 16, c.experts, H);
-  gq(L.eg, 17, c.experts * c.expert_inter, H);
-  gq(L.eu, 18, c.experts * c.expert_inter, H);
-  gq(L.ed, 19, c.experts * H, c.expert_inter);
+  // this rank's experts as row blocks of the stacked expert matrices, with
+  // their full-matrix element indices (the same values as unsharded)
+  const int per = m.per, e0 = m.e_lo;
+  if (!rc) rc = gen_qweight(ar, L.eg, seed, base + 17, per * c.expert_inter, H, c.bits, st, (int64_t)e0 * c.expert_inter, 0, H);
+  if (!rc) rc = gen_qweight(ar, L.eu, seed, base + 18, per * c.expert_inter, H, c.bits, st, (int64_t)e0 * c.expert_inter, 0, H);
+  if (!rc)
+    rc = gen_qweight(ar, L.ed, seed, base + 19, per * H, c.expert_inter, c.bits, st, (int64_t)e0 * H, 0, c.expert_inter);
   gq(L.sg, 20, c.shared_inter, H);
   gq(L.su, 21, c.shared_inter, H);
   gq(L.sd, 22, H, c.shared_inter);
@@ -186,14 +195,25 @@ static int hyb_layer_create(HybModel& m, int l, bool attn, uint64_t seed, cudaSt
   return rc;
 }
 
-static int hyb_create(const lmx_hybrid_config& c, uint64_t seed, HybModel** out) {
+static int hyb_create(const lmx_hybrid_config& c, uint64_t seed, TpComm* comm, HybModel** out) {
   if ((c.bits != 4 && c.bits != 8) || c.hidden % 512 || c.layers < 1 || c.attn_every < 1 || c.heads < 1 ||
       c.kv_heads < 1 || c.heads % c.kv_heads || c.lin_k_heads < 1 || c.lin_v_heads % c.lin_k_heads ||
       c.experts < 1 || c.top_k < 1 || c.top_k > 16 || c.top_k > c.experts || c.expert_inter % 512 ||
       c.shared_inter % 512 || c.vocab < 1 || c.experts > 16384)
     return set_error(LMX_ERR_UNSUPPORTED, "hybrid config not supported (hidden / FFNs %% 512, top_k <= 16, 4/8-bit)");
+  const int ep = comm ? comm->n : 1;
+  if (ep > 1) {
+    if (!comm->opened) return set_error(LMX_ERR_INVALID, "hybrid_create: ep comm not opened");
+    if (c.experts % ep || c.hidden > comm->max_hidden)
+      return set_error(LMX_ERR_UNSUPPORTED, "hybrid_create: experts %% ep == 0 and hidden <= comm max_hidden needed");
+  }
   auto m = std::make_unique<HybModel>();
   m->c = c;
+  m->ep = ep;
+  m->ep_rank = comm ? comm->rank : 0;
+  m->per = c.experts / ep;
+  m->e_lo = m->ep_rank * m->per;
+  m->comm = ep > 1 ? comm : nullptr;
   m->L.resize(c.layers);
   cudaStream_t st = 0;
   int rc = LMX_OK;
@@ -511,7 +531,23 @@ static int hyb_moe(const HybModel& m, HybState& s, const HybLayer& L, int l, int
   a.act = s.acte;
   a.y = s.ymoe;
   a.err = device_error_word();
+  if (m.ep > 1) {  // this rank's experts, then the exchange-combine across ranks
+    TpComm& cm = *m.comm;
+    if ((int64_t)R * c.top_k > cm.max_rows || H > cm.max_hidden)
+      return set_error(LMX_ERR_INVALID, "hybrid ep: %d x %d slot rows exceed the comm", R, c.top_k);
+    a.e_lo = m.e_lo;
+    a.e_hi = m.e_lo + m.per;
+    a.slot_out = tp_slot(cm, cm.sel);
+  }
   rc = c.bits == 4 ? launch_moe_t<4>(a, st) : launch_moe_t<8>(a, st);
+  if (!rc && m.ep > 1) {
+    TpComm& cm = *m.comm;
+    const int grid = R < kTpArCtas ? R : kTpArCtas;
+    rc = cuda_check(lmx_launch(ep_combine_kernel, dim3(grid), dim3(256), 0, st, true, cm.t, cm.sel, R, c.top_k, H,
+                               (const int32_t*)idx, (const float*)s.wts, m.per, s.ymoe, device_error_word()),
+                    "ep_combine");
+    cm.sel ^= 1;
+  }
   const QWeight gu[2] = {L.sg, L.su};
   if (!rc) rc = hyb_qmm(s.xn, gu, 2, c.shared_inter, s.acts, c.shared_inter, R, H, c.bits, kSwiglu, nullptr, st);
   if (!rc) rc = hyb_qmm(s.acts, &L.sd, 1, H, s.ysh, H, R, c.shared_inter, c.bits, kPlain, nullptr, st);
@@ -841,7 +877,8 @@ static int hyb_spec_profile(HybSpec& sp, int iters, double* seconds, double* byt
   if (!rc && s.kv) rc = cuda_check(cudaMemcpy(lens.data(), s.kv->len, B * 4, cudaMemcpyDeviceToHost), "len");
   if (rc) return rc;
   double by = qw_bytes(m.lm_head, bits) + (double)R * c.hidden * 2;
-  const double per_expert = qw_bytes(m.L[0].eg, bits) / c.experts * 2 + qw_bytes(m.L[0].ed, bits) / c.experts;
+  // (expert parallelism: this rank's experts only)
+  const double per_expert = qw_bytes(m.L[0].eg, bits) / m.per * 2 + qw_bytes(m.L[0].ed, bits) / m.per;
   for (int l = 0; l < c.layers; ++l) {
     const HybLayer& L = m.L[l];
     for (const QWeight* q : {&L.q, &L.k, &L.v, &L.qg, &L.o, &L.wqkv, &L.wz, &L.wb, &L.wa, &L.wout, &L.router, &L.sg,
@@ -851,7 +888,7 @@ static int hyb_spec_profile(HybSpec& sp, int iters, double* seconds, double* byt
     int uniq = 0;
     for (int r = 0; r < R * c.top_k; ++r) {
       const int e = idx[(size_t)l * s.Rmax * c.top_k + r];
-      if (e >= 0 && e < c.experts && !seen[e]) { seen[e] = 1; ++uniq; }
+      if (e >= m.e_lo && e < m.e_lo + m.per && !seen[e]) { seen[e] = 1; ++uniq; }
     }
     by += uniq * per_expert;
     if (L.attn) {
@@ -893,7 +930,15 @@ using namespace lmx;
 extern "C" int lmx_hybrid_create(const lmx_hybrid_config* cfg, uint64_t seed, void** model) {
   if (!cfg || !model) return set_error(LMX_ERR_INVALID, "hybrid_create: null argument");
   HybModel* m = nullptr;
-  int rc = hyb_create(*cfg, seed, &m);
+  int rc = hyb_create(*cfg, seed, nullptr, &m);
+  if (!rc) *model = m;
+  return rc;
+}
+
+extern "C" int lmx_hybrid_create_ep(const lmx_hybrid_config* cfg, uint64_t seed, void* comm, void** model) {
+  if (!cfg || !model) return set_error(LMX_ERR_INVALID, "hybrid_create_ep: null argument");
+  HybModel* m = nullptr;
+  int rc = hyb_create(*cfg, seed, (TpComm*)comm, &m);
   if (!rc) *model = m;
   return rc;
 }

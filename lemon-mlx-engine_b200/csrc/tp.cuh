@@ -230,4 +230,41 @@ __global__ void __launch_bounds__(1024) tp_argmax_exchange_kernel(TpPeers t, int
   }
 }
 
+// Expert parallelism: the combine of the routed experts across ranks.  Rank
+// p wrote the bf16 down output of every slot whose expert it holds (experts
+// [p*per, (p+1)*per)) into its partial slot `sel` as [M][k][H]; after the
+// barrier every rank forms y[m] = bf16(fma chain over slots j in order of
+// w[m][j] * v[m][j]), pulling v from the slot's owner over NVLink -- the
+// single-GPU moe_down_kernel's order, so every rank and every rank count
+// computes the same bits.  One CTA per row (rows strided), 8 outputs per
+// thread, 16-byte L2 loads.
+__global__ void __launch_bounds__(256) ep_combine_kernel(TpPeers t, int sel, int M, int k, int H, const int32_t* idx,
+                                                         const float* w, int per, bf16_t* y, unsigned* err) {
+  __shared__ int s_ok;
+  grid_wait();
+  if (threadIdx.x == 0) s_ok = tp_barrier(t, blockIdx.x, err) ? 1 : 0;
+  __syncthreads();
+  grid_launch_dependents();
+  if (!s_ok) return;
+  const size_t soff = (size_t)sel * t.slot_bytes;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        const int ex = idx[(size_t)m * k + j];
+        const int owner = min(max(ex, 0) / per, t.n - 1);
+        const uint4 v = ld_cg16(t.base[owner] + soff + (((size_t)m * k + j) * H + 8 * c) * sizeof(bf16_t));
+        float x[8];
+        unpack8(v, x);
+        const float wj = w[(size_t)m * k + j];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(wj, x[e], acc[e]);
+      }
+      *reinterpret_cast<uint4*>(y + (size_t)m * H + 8 * c) = pack8(acc);
+    }
+  }
+}
+
 }  // namespace lmx

@@ -66,6 +66,7 @@ SIGNATURES = {
     "lmx_moe_route": (I, [P, I, I, I, P, P, P]),
     "lmx_moe_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, I, P, P, P]),
     "lmx_hybrid_create": (I, [P, U64, P]),
+    "lmx_hybrid_create_ep": (I, [P, U64, P, P]),
     "lmx_hybrid_free": (I, [P]),
     "lmx_hybrid_state_create": (I, [P, I, I, I, I, P]),
     "lmx_hybrid_state_free": (I, [P]),
