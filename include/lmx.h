@@ -204,8 +204,8 @@ int lmx_sdpa_decode_noalloc(const void* q, const lmx_kv* kv, int T, int heads, f
  * (src/common/gated_delta.cpp:885-921), q/k RMSNorm, beta / g
  * (gated_delta.cpp:603-633), gated_delta_update_seq with per-token states
  * (gated_delta.cpp:1067-1138), gated RMSNorm (gated_delta.cpp:948-971).
- * Head dims 128.  The recurrent state is fp32 [B][Hv][128 (v)][128 (k)] (the
- * reference keeps it in bf16).  lmx_gdn_verify reads state / conv_state and
+ * Head dims 128.  The recurrent state is fp32 [B][Hv][128 (v)][128 (k)]
+ * holding bf16-rounded values between blocks (lmx_set_gdn_state_bf16).  lmx_gdn_verify reads state / conv_state and
  * writes the state after every token (state_snap) and the output; it never
  * modifies state or conv_state.  lmx_gdn_commit then keeps the state after
  * token acc[b] of each sequence (MambaCache rollback_spec,
@@ -232,6 +232,14 @@ typedef struct {
   void* scratch;           /* lmx_gdn_scratch_bytes(batch, T, k_heads, v_heads) */
 } lmx_gdn;
 size_t lmx_gdn_scratch_bytes(int batch, int T, int k_heads, int v_heads);
+/* Recurrent-state precision between blocks (process-wide, default 1): the
+ * reference keeps the state in fp32 while it runs a block of tokens and
+ * stores the per-token states and the block's final state as bf16
+ * (src/common/gated_delta.cpp:93, :162-172); with 1 the snapshots (and so
+ * every committed state) are rounded to bf16 the same way, the state
+ * arrays staying fp32 holding bf16 values; 0 keeps full fp32 states. */
+int lmx_set_gdn_state_bf16(int on);
+int lmx_gdn_state_bf16(void);
 int lmx_gdn_verify(const lmx_gdn* g, void* stream);
 int lmx_gdn_commit(const lmx_gdn* g, const int32_t* acc, void* stream);
 

@@ -35,6 +35,10 @@ namespace lmx {
 static constexpr int kGdnD = 128;  // Dk = Dv
 static constexpr int kGdnKS = 4;   // conv kernel
 
+// Process-wide: Gated DeltaNet state snapshots (and hence committed states)
+// rounded to bf16 as the reference stores them (1, default) or kept fp32 (0).
+static int g_gdn_state_bf16 = 1;
+
 struct GdnArgs {
   int B, T, Hk, Hv;
   const bf16_t* qkv;      // [B][T][CD], CD = 2*Hk*128 + Hv*128
@@ -50,6 +54,7 @@ struct GdnArgs {
   const float* state;        // [B][Hv][128][128]
   float* snap;               // [B][snap_T][Hv][128][128]: states after the last snap_T tokens
   int snap_T;                // T (every token) or 1 (only the last, e.g. a prefill chunk)
+  int state_bf16 = 1;        // snapshots rounded to bf16, as the reference stores its states
   bf16_t* out;               // [B][T][Hv*128]
   bf16_t* qn;                // scratch [B][T][Hk][128] normalised q
   bf16_t* kn;                // scratch [B][T][Hk][128] normalised k
@@ -205,8 +210,20 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(GdnArgs a) {
     const int ts = t - (a.T - a.snap_T);  // snapshot slot of token t
     if (a.snap && ts >= 0) {
       float* sn = a.snap + (((((size_t)b * a.snap_T + ts) * a.Hv + h) * kGdnD + dv) * kGdnD) + 64 * half;
+      // the reference keeps the state in fp32 within a block and stores it
+      // (the per-token states and the block's final state) as bf16
+      // (src/common/gated_delta.cpp:93, :162-172): state_bf16 rounds the
+      // snapshots the same way; the running state stays fp32
+      if (a.state_bf16) {
 #pragma unroll
-      for (int j = 0; j < 64; j += 4) *reinterpret_cast<float4*>(sn + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+        for (int j = 0; j < 64; j += 4)
+          *reinterpret_cast<float4*>(sn + j) = make_float4(bf2f(f2bf(S[j])), bf2f(f2bf(S[j + 1])),
+                                                           bf2f(f2bf(S[j + 2])), bf2f(f2bf(S[j + 3])));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; j += 4)
+          *reinterpret_cast<float4*>(sn + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+      }
     }
     // gated RMSNorm of the head's y (bf16), canonical warp factor
     if (!half) yb[dv] = f2bf(y);

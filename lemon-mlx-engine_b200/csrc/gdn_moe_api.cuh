@@ -38,6 +38,7 @@ static int gdn_args(const lmx_gdn* g, GdnArgs& a) {
   a.state = g->state;
   a.snap = g->state_snap;
   a.snap_T = g->T;
+  a.state_bf16 = g_gdn_state_bf16;
   a.out = (bf16_t*)g->out;
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t bt = (size_t)a.B * a.T;
@@ -85,6 +86,13 @@ extern "C" int lmx_gdn_commit(const lmx_gdn* g, const int32_t* acc, void* stream
                                acc, g->state, (bf16_t*)g->conv_state),
                     "gdn_commit: launch");
 }
+
+extern "C" int lmx_set_gdn_state_bf16(int on) {
+  if (on != 0 && on != 1) return lmx::set_error(LMX_ERR_INVALID, "gdn_state_bf16: 0 or 1");
+  lmx::g_gdn_state_bf16 = on;
+  return LMX_OK;
+}
+extern "C" int lmx_gdn_state_bf16(void) { return lmx::g_gdn_state_bf16; }
 
 extern "C" int lmx_moe_route(const void* logits, int rows, int E, int k, int32_t* idx, float* w, void* stream) {
   using namespace lmx;

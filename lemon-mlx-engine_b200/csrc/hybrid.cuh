@@ -435,6 +435,7 @@ static int hyb_gdn(const HybModel& m, HybState& s, const HybLayer& L, HybGdnLaye
   if (!rc) rc = hyb_qmm(s.xn, &L.wa, 1, Hv, s.ga, Hv, R, H, c.bits, kPlain, nullptr, st);
   if (rc) return rc;
   GdnArgs a;
+  a.state_bf16 = g_gdn_state_bf16;
   a.B = B;
   a.T = T;
   a.Hk = c.lin_k_heads;
@@ -482,6 +483,8 @@ static int hyb_gdn_commit_all(const HybModel& m, HybState& s, int B, int T, cons
   for (size_t i = 0; i < s.gdn.size() && !rc; ++i) {
     HybGdnLayer& g = s.gdn[i];
     GdnArgs a;
+    a.state_bf16 = g_gdn_state_bf16;
+  a.state_bf16 = g_gdn_state_bf16;
     std::memset(&a, 0, sizeof(a));
     a.B = B;
     a.T = T;

@@ -61,6 +61,8 @@ SIGNATURES = {
     "lmx_tp_allreduce_rmsnorm": (I, [P, P, I, I, P, P, F, P, P]),
     "lmx_cache_fill_synthetic": (I, [P, I, U64, C.c_uint32]),
     "lmx_gdn_scratch_bytes": (C.c_size_t, [I, I, I, I]),
+    "lmx_set_gdn_state_bf16": (I, [I]),
+    "lmx_gdn_state_bf16": (I, []),
     "lmx_gdn_verify": (I, [P, P]),
     "lmx_gdn_commit": (I, [P, P, P]),
     "lmx_moe_route": (I, [P, I, I, I, P, P, P]),

@@ -744,6 +744,9 @@ const int kGD = 128, kKS = 4;
 // Gated DeltaNet verify step (lmx_gdn_verify): reads state / conv_state,
 // writes the state after each token to snap [B][T][Hv][128][128] and the
 // gated-normed output [B][T][Hv*128].
+static int g_gdn_state_bf16 = 1;
+extern "C" void orc_set_gdn_state_bf16(int on) { g_gdn_state_bf16 = on ? 1 : 0; }
+
 extern "C" int orc_gdn_verify(int B, int T, int Hk, int Hv, const uint16_t* qkv, const uint16_t* z,
                               const uint16_t* bb, const uint16_t* aa, const uint16_t* conv_w,
                               const float* a_log, const uint16_t* dt_bias, const uint16_t* norm_w, float eps,
@@ -817,7 +820,15 @@ extern "C" int orc_gdn_verify(int B, int T, int Hk, int Hv, const uint16_t* qkv,
           }
           y[dv] = bf2f(f2bf(yp[0] + yp[1]));
         }
-        std::memcpy(snap + ((((size_t)b * T + t) * Hv + h) * kGD) * kGD, S.data(), S.size() * 4);
+        {
+          // the reference stores its per-token / final states as bf16
+          // (gated_delta.cpp:93, :162-172); the running state stays fp32
+          float* sn = snap + ((((size_t)b * T + t) * Hv + h) * kGD) * kGD;
+          if (g_gdn_state_bf16)
+            for (size_t i = 0; i < S.size(); ++i) sn[i] = bf2f(f2bf(S[i]));
+          else
+            std::memcpy(sn, S.data(), S.size() * 4);
+        }
         const float f = rms_factor(y.data(), kGD, eps);
         for (int dv = 0; dv < kGD; ++dv) {
           const float nv = bf2f(f2bf((y[dv] * f) * bf2f(norm_w[dv])));

@@ -183,6 +183,9 @@ void orc_spec_session_free(void* session);
 int orc_threads(void);
 /* OpenMP threads for later calls (n <= 0: every online host core); returns the count. */
 int orc_set_threads(int n);
+/* Gated DeltaNet state snapshots rounded to bf16 as the reference stores
+ * them (1, default) or kept fp32 (0); the device's lmx_set_gdn_state_bf16. */
+void orc_set_gdn_state_bf16(int on);
 /* REF_KV_PAD_QUIRK mode for quantized KV caches (the reference's
  * maybe_quantize_kv_cache): the prompt is prefilled into a bf16 cache, then
  * the whole reference allocation (orc_kv_quirk_alloc rows, zero rows past the

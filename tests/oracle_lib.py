@@ -109,6 +109,7 @@ def _declare(L):
         "orc_generate": (I, [P, P, I, I, I, I, P]),
         "orc_threads": (I, []),
         "orc_set_threads": (I, [I]),
+        "orc_set_gdn_state_bf16": (None, [I]),
         "orc_set_kv_quirk": (None, [I]),
         "orc_kv_quirk_alloc": (I, [I]),
         "orc_spec_session": (P, [P, P, P, I, I, C.POINTER(SpecParams), I]),

@@ -38,8 +38,19 @@ def gdn_device(lmx, cuda, c):
     return g, d
 
 
+@pytest.fixture(params=[1, 0], ids=["bf16-state", "fp32-state"])
+def state_mode(request, lmx):
+    # the reference's bf16 states between blocks (default) and fp32 states,
+    # set alike on the library and the oracle
+    lmx.call("lmx_set_gdn_state_bf16", request.param)
+    O.lib().orc_set_gdn_state_bf16(request.param)
+    yield request.param
+    lmx.call("lmx_set_gdn_state_bf16", 1)
+    O.lib().orc_set_gdn_state_bf16(1)
+
+
 @pytest.mark.parametrize("B,T,Hk,Hv", [(2, 3, 2, 4), (4, 3, 16, 32), (3, 1, 1, 2)])
-def test_gdn_verify_and_commit_bit_exact(lmx, cuda, B, T, Hk, Hv):
+def test_gdn_verify_and_commit_bit_exact(lmx, cuda, state_mode, B, T, Hk, Hv):
     # (4, 3, 16, 32): configuration 4's GDN layer (batch 4, 3 verify tokens,
     # 16 key / 32 value heads of 128)
     c = H.gdn_case(B * 10 + Hv, B=B, T=T, Hk=Hk, Hv=Hv)
