@@ -27,7 +27,8 @@ typedef enum {
   LMX_ERR_UNSUPPORTED = 2,  /* valid for the reference, not implemented   */
   LMX_ERR_CUDA = 3,         /* CUDA runtime error (see lmx_last_error)    */
   LMX_ERR_OOM = 4,          /* device allocation failed (setup calls only) */
-  LMX_ERR_CAPACITY = 5      /* KV cache capacity exceeded                 */
+  LMX_ERR_CAPACITY = 5,     /* KV cache capacity exceeded                 */
+  LMX_ERR_IO = 6            /* checkpoint file missing / malformed         */
 } lmx_status;
 
 /* Human-readable text of the last error on this thread. */
@@ -347,6 +348,42 @@ int lmx_model_free(void* model);
 /* Copy one packed weight to host memory (kind: 0 q,1 k,2 v,3 o,4 gate,5 up,
  * 6 down,7 embed,8 lm_head).  For a tensor-parallel shard: the shard. */
 int lmx_model_weight(void* model, int layer, int kind, void* w_host, void* s_host, void* b_host);
+
+/* ---------------------------------------------------------------------------
+ * Checkpoints: MLX-format model directories (load_llm_from_directory,
+ * src/llm/llm_factory.cpp:272-290; load_safetensors_from_directory,
+ * src/common/safetensors.cpp:23-75; register_quantized_weights,
+ * src/common/quantize_utils.cpp:14-104).  A directory holds config.json and
+ * model.safetensors, or the shards named by model.safetensors.index.json
+ * (else every *.safetensors in it).  Qwen3 (model_type "qwen3") and Llama
+ * ("llama", "mistral", with Llama-3 rope scaling); linear layers and the
+ * embedding MLX affine-quantized at 4 or 8 bits, group 64, with per-layer
+ * overrides from config.json's "quantization" object ({"bits", "group_size"}
+ * keyed by the layer prefix, e.g. "model.layers.3.mlp.down_proj"); q/k/v of a
+ * layer share their bits, as do gate/up.  Norms and scales may be BF16, F16 or
+ * F32 (rounded to bf16).  lm_head.weight is ignored when the embeddings are
+ * tied.  A missing tensor, a shape that disagrees with config.json or an
+ * unquantized linear layer fails with LMX_ERR_IO / LMX_ERR_UNSUPPORTED.
+ * ------------------------------------------------------------------------- */
+/* config.json (path: the file or its directory) -> cfg (bits / group_size:
+ * the default quantization) and up to max_eos EOS ids (n_eos: how many the
+ * file lists).  Host only: needs no GPU. */
+int lmx_model_config_load(const char* path, lmx_model_config* cfg, int32_t* eos_ids, int max_eos, int* n_eos);
+/* The quantization config.json gives the layer `prefix` (quantization_for,
+ * include/mlx-lm/common/base_config.h:47-54).  Host only. */
+int lmx_model_quant_for(const char* path, const char* prefix, int* bits, int* group_size);
+/* One safetensors header entry: dtype string (<= 15 chars), shape, absolute
+ * data offset in the file.  Host only. */
+int lmx_safetensors_tensor(const char* file, const char* name, char* dtype, int64_t* shape, int max_dims, int* ndim,
+                           uint64_t* data_offset);
+int lmx_model_load(const char* dir, void** model);
+/* This rank's tensor-parallel shard of a checkpoint (lmx_model_create_tp's
+ * split); only the shard's blocks are copied to the device. */
+int lmx_model_load_tp(const char* dir, void* comm, void** model);
+/* Write config.json + model.safetensors (MLX names, U32 packed weights, BF16
+ * scales / biases / norms); per-layer overrides for weights whose bits differ
+ * from the model's.  A tp 1, full-depth model. */
+int lmx_model_save(void* model, const char* dir);
 
 /* ---------------------------------------------------------------------------
  * Tensor parallelism across the GPUs of one node (one process per GPU).  The

@@ -362,6 +362,7 @@ struct QWeight {
   bf16_t* s = nullptr;
   bf16_t* b = nullptr;
   int N = 0, K = 0;
+  int bits = 4;  // this weight's quantization (a checkpoint may override it per layer)
   QMat mat() const {
     QMat m;
     m.w = w;
@@ -392,6 +393,7 @@ struct Model {
   TpComm* comm = nullptr;
   int hq = 0, hk = 0, il = 0, vl = 0;
   QWeight head_tp;  // vocab rows [tp_rank*vl, +vl) of the lm_head (tp > 1)
+  bool uniform_bits = true;  // every weight at c.bits (the fused decode kernel's precondition)
   const QWeight& head() const { return tp > 1 ? head_tp : (c.tied ? embed : lm_head); }
 };
 
@@ -401,6 +403,7 @@ static int gen_qweight(Arena& ar, QWeight& q, uint64_t seed, uint32_t tid, int N
                        cudaStream_t st, int64_t row0 = 0, int64_t col0 = 0, int64_t Kfull = 0) {
   q.N = N;
   q.K = K;
+  q.bits = bits;
   int rc = ar.alloc(&q.w, (size_t)N * K * bits / 32, false);
   if (!rc) rc = ar.alloc(&q.s, (size_t)N * (K / 64), false);
   if (!rc) rc = ar.alloc(&q.b, (size_t)N * (K / 64), false);
@@ -419,13 +422,40 @@ static int fill_ones(Arena& ar, bf16_t** p, int n, cudaStream_t st) {
   return cuda_check(cudaGetLastError(), "fill");
 }
 
+// Where model_build takes its tensors from: the seeded generator below or
+// a checkpoint (loader.cuh).  qweight fills rows [row0, row0+N) x columns
+// [col0, col0+K) of the named [Nfull, Kfull] linear weight (tid: the seeded
+// tensor id); norm fills n values of the named vector.
+struct WeightSource {
+  virtual ~WeightSource() = default;
+  virtual int qweight(Arena& ar, QWeight& q, uint32_t tid, const std::string& name, int N, int K, int64_t row0,
+                      int64_t col0, int64_t Nfull, int64_t Kfull, cudaStream_t st) = 0;
+  virtual int norm(Arena& ar, bf16_t** p, const std::string& name, int n, cudaStream_t st) = 0;
+};
+
+// Synthetic weights: N(0, 0.02) quantized at the config's bits; norms ones.
+struct SeededSource : WeightSource {
+  uint64_t seed;
+  int bits;
+  SeededSource(uint64_t s, int b) : seed(s), bits(b) {}
+  int qweight(Arena& ar, QWeight& q, uint32_t tid, const std::string&, int N, int K, int64_t row0, int64_t col0,
+              int64_t, int64_t Kfull, cudaStream_t st) override {
+    return gen_qweight(ar, q, seed, tid, N, K, bits, st, row0, col0, Kfull);
+  }
+  int norm(Arena& ar, bf16_t** p, const std::string&, int n, cudaStream_t st) override {
+    return fill_ones(ar, p, n, st);
+  }
+};
+
 // comm == nullptr (or a size-1 comm): the whole model.  Otherwise this
 // rank's tensor-parallel shard (Megatron split, tp.cuh): q/k/v by heads,
 // gate/up by FFN rows, o/down by the matching input columns, the lm_head by
 // vocabulary rows (a view into the packed embedding when tied); embedding
 // table and norms are replicated.  Every shard holds exactly the values of
-// its block of the unsharded weights.
-static int model_create(const lmx_model_config& c, uint64_t seed, TpComm* comm, Model** out) {
+// its block of the unsharded weights.  Tensor names are the MLX checkpoint's
+// (Qwen3Model / LlamaModel::weight_map, src/llm/models/qwen3.cpp:100-160,
+// :236-241).
+static int model_build(const lmx_model_config& c, WeightSource& src, TpComm* comm, Model** out) {
   if (c.group_size != 64 || (c.bits != 4 && c.bits != 8) || c.head_dim != kHeadDim ||
       c.hidden % 512 || c.heads % c.kv_heads || c.layers < 1 || c.vocab < 1)
     return set_error(LMX_ERR_UNSUPPORTED, "model config not supported (head_dim 128, hidden %% 512 == 0, group 64, 4/8-bit)");
@@ -452,39 +482,50 @@ static int model_create(const lmx_model_config& c, uint64_t seed, TpComm* comm, 
   const int H = c.hidden, D = c.head_dim, I = c.inter, NQ = c.heads * D, NK = c.kv_heads * D;
   const int nq = m->hq * D, nk = m->hk * D, il = m->il;
   cudaStream_t st = 0;
+  static const char* const kProj[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                                       "mlp.gate_proj",    "mlp.up_proj",      "mlp.down_proj"};
   m->L.resize(c.layers);
   for (int l = 0; l < c.layers; ++l) {
-    // {rows, cols, row0, col0, full width}
-    const int64_t shp[7][5] = {{nq, H, (int64_t)r * nq, 0, H},  {nk, H, (int64_t)r * nk, 0, H},
-                               {nk, H, (int64_t)r * nk, 0, H},  {H, nq, 0, (int64_t)r * nq, NQ},
-                               {il, H, (int64_t)r * il, 0, H},  {il, H, (int64_t)r * il, 0, H},
-                               {H, il, 0, (int64_t)r * il, I}};
-    (void)NK;
+    const std::string pre = "model.layers." + std::to_string(l) + ".";
+    // {rows, cols, row0, col0, full rows, full width}
+    const int64_t shp[7][6] = {{nq, H, (int64_t)r * nq, 0, NQ, H},  {nk, H, (int64_t)r * nk, 0, NK, H},
+                               {nk, H, (int64_t)r * nk, 0, NK, H},  {H, nq, 0, (int64_t)r * nq, H, NQ},
+                               {il, H, (int64_t)r * il, 0, I, H},   {il, H, (int64_t)r * il, 0, I, H},
+                               {H, il, 0, (int64_t)r * il, H, I}};
     for (int k = 0; k < 7; ++k) {
-      int rc = gen_qweight(ar, m->L[l].w[k], seed, (uint32_t)((l + 1) * 16 + k), (int)shp[k][0], (int)shp[k][1],
-                           c.bits, st, shp[k][2], shp[k][3], shp[k][4]);
+      int rc = src.qweight(ar, m->L[l].w[k], (uint32_t)((l + 1) * 16 + k), pre + kProj[k], (int)shp[k][0],
+                           (int)shp[k][1], shp[k][2], shp[k][3], shp[k][4], shp[k][5], st);
       if (rc) return rc;
     }
-    int rc = fill_ones(ar, &m->L[l].in_norm, H, st);
-    if (!rc) rc = fill_ones(ar, &m->L[l].post_norm, H, st);
-    if (!rc) rc = fill_ones(ar, &m->L[l].q_norm, D, st);
-    if (!rc) rc = fill_ones(ar, &m->L[l].k_norm, D, st);
+    const Layer& Ly = m->L[l];
+    if (Ly.w[0].bits != Ly.w[1].bits || Ly.w[0].bits != Ly.w[2].bits || Ly.w[4].bits != Ly.w[5].bits)
+      return set_error(LMX_ERR_UNSUPPORTED,
+                       "layer %d: q/k/v (and gate/up) run as one fused GEMM and must share their bits", l);
+    int rc = src.norm(ar, &m->L[l].in_norm, pre + "input_layernorm.weight", H, st);
+    if (!rc) rc = src.norm(ar, &m->L[l].post_norm, pre + "post_attention_layernorm.weight", H, st);
+    if (!rc && c.qk_norm) rc = src.norm(ar, &m->L[l].q_norm, pre + "self_attn.q_norm.weight", D, st);
+    if (!rc && c.qk_norm) rc = src.norm(ar, &m->L[l].k_norm, pre + "self_attn.k_norm.weight", D, st);
     if (rc) return rc;
   }
-  int rc = gen_qweight(ar, m->embed, seed, 1, c.vocab, H, c.bits, st);
+  int rc = src.qweight(ar, m->embed, 1, "model.embed_tokens", c.vocab, H, 0, 0, c.vocab, H, st);
   if (!rc && !c.tied) {
-    if (tp == 1) rc = gen_qweight(ar, m->lm_head, seed, 2, c.vocab, H, c.bits, st);
-    else rc = gen_qweight(ar, m->head_tp, seed, 2, m->vl, H, c.bits, st, (int64_t)r * m->vl, 0, H);
+    if (tp == 1) rc = src.qweight(ar, m->lm_head, 2, "lm_head", c.vocab, H, 0, 0, c.vocab, H, st);
+    else rc = src.qweight(ar, m->head_tp, 2, "lm_head", m->vl, H, (int64_t)r * m->vl, 0, c.vocab, H, st);
   } else if (!rc && tp > 1) {  // vocab rows of the tied table
     QWeight& v = m->head_tp;
     v.N = m->vl;
     v.K = H;
-    v.w = m->embed.w + (size_t)r * m->vl * (H * c.bits / 32);
+    v.bits = m->embed.bits;
+    v.w = m->embed.w + (size_t)r * m->vl * (H * v.bits / 32);
     v.s = m->embed.s + (size_t)r * m->vl * (H / 64);
     v.b = m->embed.b + (size_t)r * m->vl * (H / 64);
   }
-  if (!rc) rc = fill_ones(ar, &m->final_norm, H, st);
+  if (!rc) rc = src.norm(ar, &m->final_norm, "model.norm.weight", H, st);
   if (rc) return rc;
+  m->uniform_bits = true;
+  for (const Layer& Ly : m->L)
+    for (const QWeight& q : Ly.w) m->uniform_bits = m->uniform_bits && q.bits == c.bits;
+  m->uniform_bits = m->uniform_bits && m->embed.bits == c.bits && m->head().bits == c.bits;
   // RoPE table: period_i = base^(2i/D) (with the Llama-3 frequency scaling of
   // LlamaDynamicNTKScalingRoPE::compute_freqs, src/llm/models/llama.cpp:122-183,
   // when rope_factor > 1), theta = pos / period (double), fp32 cos/sin
@@ -521,6 +562,11 @@ static int model_create(const lmx_model_config& c, uint64_t seed, TpComm* comm, 
   if (rc) return rc;
   *out = m.release();
   return LMX_OK;
+}
+
+static int model_create(const lmx_model_config& c, uint64_t seed, TpComm* comm, Model** out) {
+  SeededSource src(seed, c.bits);
+  return model_build(c, src, comm, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -701,7 +747,8 @@ static bool dec_applies(const Model& m, const Cache& c, int n_layers, int B, int
   const int R = B * T, G = m.hq / m.hk;
   if (!g_fused_decode || m.tp > 1 || qmm_mma_min_m() <= 0 || R < 1 || R > kDecMaxRows || G * T > kDecAttnRows)
     return false;
-  if ((m.c.bits != 4 && m.c.bits != 8) || !c.dec || c.cap % kSplit || n_layers > c.n_layers) return false;
+  if ((m.c.bits != 4 && m.c.bits != 8) || !m.uniform_bits || !c.dec || c.cap % kSplit || n_layers > c.n_layers)
+    return false;
   if (!dec_plan(m.c.hidden, m.hq, m.hk, m.il, R, device_sms(), p)) return false;
   if (p.gpart_floats > ws.dgpart_floats || p.max_tiles > ws.dgcnt_n || !ws.dbar) return false;
   const size_t need = (size_t)B * m.hk * (c.cap / kSplit) * kRowTile * kPartStride;
@@ -737,7 +784,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   const bool fuse = !tp && R <= kQmmMaxNormRows && !qmm_uses_mma(R) && !qmm_uses_tcg(R);
   int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
                                  (const uint32_t*)m.embed.w, (const bf16_t*)m.embed.s,
-                                 (const bf16_t*)m.embed.b, H, cf.bits, ws.h, R),
+                                 (const bf16_t*)m.embed.b, H, m.embed.bits, ws.h, R),
                       "embed");
   if (rc) return rc;
   const float scale = (float)(1.0 / std::sqrt((double)kHeadDim));
@@ -797,7 +844,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     qc.ldy = qc.N;
     qc.M = R;
     qc.K = H;
-    qc.bits = cf.bits;
+    qc.bits = L.w[0].bits;
     if (!rc) rc = launch_qmm(qc, st);
 
     PrepArgs pa;
@@ -841,7 +888,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     oc.ldy = H;
     oc.M = R;
     oc.K = NQ;
-    oc.bits = cf.bits;
+    oc.bits = L.w[3].bits;
     if (tp) {
       oc.y = tp_slot(*m.comm, sel);
       oc.mode = kPlain;
@@ -872,7 +919,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     gc.ldy = I;
     gc.M = R;
     gc.K = H;
-    gc.bits = cf.bits;
+    gc.bits = L.w[4].bits;
     gc.mode = kSwiglu;
     if (!rc) rc = launch_qmm(gc, st);
 
@@ -883,7 +930,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     dc.ldy = H;
     dc.M = R;
     dc.K = I;
-    dc.bits = cf.bits;
+    dc.bits = L.w[6].bits;
     if (tp) {
       dc.y = tp_slot(*m.comm, sel);
       dc.mode = kPlain;
@@ -920,7 +967,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   hc.ldy = logits_ld ? logits_ld : m.vl;
   hc.M = M;
   hc.K = H;
-  hc.bits = cf.bits;
+  hc.bits = m.head().bits;
   return launch_qmm(hc, st);
 }
 
@@ -1046,8 +1093,7 @@ static int kv_quirk_alloc(int n) {
 static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg, Spec** out) {
   if (cfg.batch < 1 || cfg.K < 0 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
-  if (dm->c.vocab != tm->c.vocab || dm->c.bits != tm->c.bits)
-    return set_error(LMX_ERR_INVALID, "spec: draft and target must share vocab and bits");
+  if (dm->c.vocab != tm->c.vocab) return set_error(LMX_ERR_INVALID, "spec: draft and target must share the vocabulary");
   if (dm->tp > 1) return set_error(LMX_ERR_UNSUPPORTED, "spec: the draft runs replicated (tp 1) on every rank");
   if (tm->tp > 1 && cfg.temperature > 0.0f)
     return set_error(LMX_ERR_UNSUPPORTED, "spec: a tensor-parallel target decodes greedily (temperature 0)");
@@ -1499,7 +1545,7 @@ extern "C" int lmx_model_weight(void* model, int layer, int kind, void* w_host, 
   else if (kind == 8) q = &m->head();
   else if (layer >= 0 && layer < (int)m->L.size() && kind >= 0 && kind < 7) q = &m->L[layer].w[kind];
   if (!q) return set_error(LMX_ERR_INVALID, "model_weight: bad layer/kind");
-  const size_t nw = (size_t)q->N * q->K * m->c.bits / 32, ng = (size_t)q->N * (q->K / 64);
+  const size_t nw = (size_t)q->N * q->K * q->bits / 32, ng = (size_t)q->N * (q->K / 64);
   int rc = cuda_check(cudaMemcpy(w_host, q->w, nw * 4, cudaMemcpyDeviceToHost), "copy w");
   if (!rc) rc = cuda_check(cudaMemcpy(s_host, q->s, ng * 2, cudaMemcpyDeviceToHost), "copy s");
   if (!rc) rc = cuda_check(cudaMemcpy(b_host, q->b, ng * 2, cudaMemcpyDeviceToHost), "copy b");
@@ -1643,7 +1689,8 @@ extern "C" int lmx_spec_free(void* spec) {
 
 namespace lmx {
 // Algorithmic HBM bytes of one quantized matrix read plus its activations.
-static double qmm_bytes(const QWeight& w, int bits, int M) {
+static double qmm_bytes(const QWeight& w, int M) {
+  const int bits = w.bits;
   return (double)w.N * w.K * bits / 8 + (double)w.N * (w.K / 64) * 4 + (double)M * w.K * 2 + (double)M * w.N * 2;
 }
 
@@ -1653,7 +1700,7 @@ static double qmm_bytes(const QWeight& w, int bits, int M) {
 // M = B(K+1), 3 lm_head at M = B.  bytes = algorithmic bytes per launch.
 static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* bytes) {
   if (!sp.prefilled) return set_error(LMX_ERR_INVALID, "profile before prefill");
-  const int B = sp.cfg.batch, K = sp.cfg.K, bits = sp.tm->c.bits;
+  const int B = sp.cfg.batch, K = sp.cfg.K;
   cudaStream_t st = sp.st;
   std::vector<int> tl(B), dl(B);
   int rc = cuda_check(cudaMemcpy(tl.data(), sp.tc->len, B * 4, cudaMemcpyDeviceToHost), "len");
@@ -1663,17 +1710,17 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
   auto model_bytes = [&](const Model& m, int nl, int M, const std::vector<int>& lens, int T, bool head) {
     double s = 0;
     for (int l = 0; l < nl; ++l)
-      for (int k = 0; k < 7; ++k) s += qmm_bytes(m.L[l].w[k], bits, M);
+      for (int k = 0; k < 7; ++k) s += qmm_bytes(m.L[l].w[k], M);
     for (int b = 0; b < B; ++b)  // K and V rows read by attention, new rows written
       s += (double)nl * 2 * m.hk * (lens[b] + T) * kHeadDim * (sp.cfg.kv_bits == 16 ? 2.0 : sp.cfg.kv_bits / 8.0 + 4.0 / 64);
-    if (head) s += qmm_bytes(m.head(), bits, M);
+    if (head) s += qmm_bytes(m.head(), M);
     return s;
   };
   if (what == 1 && K == 0) return set_error(LMX_ERR_INVALID, "profile: no draft (K = 0)");
   if (what == 0) by = model_bytes(*sp.tm, sp.tm->n_layers, B * (K + 1), tl, K + 1, true);
   else if (what == 1) by = model_bytes(*sp.dm, sp.dl, B, dl, 1, true);
-  else if (what == 2) by = qmm_bytes(sp.tm->head(), bits, B * (K + 1));
-  else if (what == 3) by = qmm_bytes(sp.tm->head(), bits, B);
+  else if (what == 2) by = qmm_bytes(sp.tm->head(), B * (K + 1));
+  else if (what == 3) by = qmm_bytes(sp.tm->head(), B);
   else return set_error(LMX_ERR_INVALID, "profile: what=%d", what);
   auto once = [&]() -> int {
     if (what == 0)
@@ -1696,7 +1743,7 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     hc.y = sp.ws.logits;
     hc.ldy = sp.tm->vl;
     hc.K = sp.tm->c.hidden;
-    hc.bits = bits;
+    hc.bits = sp.tm->head().bits;
     return launch_qmm(hc, st);
   };
   for (int i = 0; i < 3 && !rc; ++i) rc = once();

@@ -605,6 +605,7 @@ extern "C" int lmx_argmax(const void* logits, int rows, int V, int32_t* out, voi
   return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
 }
 #include "engine.cuh"
+#include "loader.cuh"
 
 // ---------------------------------------------------------------------------
 // Attention for callers that cannot allocate device memory: a host framework

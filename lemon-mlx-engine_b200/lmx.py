@@ -51,6 +51,12 @@ SIGNATURES = {
     "lmx_cache_kv": (I, [P, I, P]),
     "lmx_model_create": (I, [P, U64, P]),
     "lmx_model_create_tp": (I, [P, U64, P, P]),
+    "lmx_model_config_load": (I, [C.c_char_p, P, P, I, P]),
+    "lmx_model_quant_for": (I, [C.c_char_p, C.c_char_p, P, P]),
+    "lmx_safetensors_tensor": (I, [C.c_char_p, C.c_char_p, C.c_char_p, P, I, P, P]),
+    "lmx_model_load": (I, [C.c_char_p, P]),
+    "lmx_model_load_tp": (I, [C.c_char_p, P, P]),
+    "lmx_model_save": (I, [P, C.c_char_p]),
     "lmx_tp_comm_create": (I, [I, I, I, I, P]),
     "lmx_tp_comm_handle": (I, [P, P]),
     "lmx_tp_comm_open": (I, [P, P]),
@@ -237,6 +243,23 @@ class Model:
             call("lmx_model_create", C.byref(ModelConfig(**cfg)), seed, C.byref(h))
         self.h = h
 
+    @classmethod
+    def load(cls, path: str, comm=None):
+        """An MLX-format checkpoint directory (config.json + safetensors);
+        with a TpComm of size > 1, this rank's shard."""
+        cfg = config_load(path)[0]
+        h = C.c_void_p()
+        if comm is not None:
+            call("lmx_model_load_tp", os.fsencode(path), comm.h, C.byref(h))
+        else:
+            call("lmx_model_load", os.fsencode(path), C.byref(h))
+        m = cls(cfg, 0, _handle=h)
+        m._comm = comm
+        return m
+
+    def save(self, path: str):
+        call("lmx_model_save", self.h, os.fsencode(path))
+
     def view(self, n_layers):
         h = C.c_void_p()
         call("lmx_model_view", self.h, n_layers, C.byref(h))
@@ -253,6 +276,15 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+def config_load(path: str):
+    """config.json (file or directory) -> (lmx_model_config as a dict, EOS ids)."""
+    c = ModelConfig()
+    eos = (C.c_int32 * 16)()
+    n = C.c_int()
+    call("lmx_model_config_load", os.fsencode(path), C.byref(c), eos, 16, C.byref(n))
+    return {f: getattr(c, f) for f, _ in ModelConfig._fields_}, list(eos[:min(n.value, 16)])
 
 
 class CompletionInfo(C.Structure):

@@ -974,6 +974,7 @@ extern "C" int orc_moe_experts(const uint16_t* x, int M, int H, int I, int E, in
 namespace {
 struct QW {
   int N = 0, K = 0;
+  int bits = 4;  // per weight: a checkpoint's per-layer override may differ from the model's
   std::vector<uint32_t> w;
   std::vector<uint16_t> s, b;
 };
@@ -1003,6 +1004,7 @@ struct Cache {
 void gen_qw(QW& q, uint64_t seed, uint32_t tid, int N, int K, int bits, int group) {
   q.N = N;
   q.K = K;
+  q.bits = bits;
   std::vector<uint16_t> tmp((size_t)N * K);
   orc_gen_normal_bf16(seed, tid, 0.02f, (int64_t)tmp.size(), tmp.data());
   q.w.resize((size_t)N * K * bits / 32);
@@ -1012,7 +1014,7 @@ void gen_qw(QW& q, uint64_t seed, uint32_t tid, int N, int K, int bits, int grou
 }
 
 void qmm(const Model& m, const QW& w, const uint16_t* x, uint16_t* y, int M) {
-  orc_qmm(x, w.w.data(), w.s.data(), w.b.data(), y, M, w.N, w.K, m.group, m.bits);
+  orc_qmm(x, w.w.data(), w.s.data(), w.b.data(), y, M, w.N, w.K, m.group, w.bits);
 }
 
 // h = h + x W^T for the row-split projections (o_proj, down_proj).  With
@@ -1028,7 +1030,7 @@ void qmm_resid(const Model& m, const QW& w, const uint16_t* x, uint16_t* h, int 
     orc_add(h, a.data(), h, (int64_t)M * N);
     return;
   }
-  const int Ks = K / tp, G = K / 64, Gs = Ks / 64, WPR = K * m.bits / 32, WPRs = Ks * m.bits / 32;
+  const int Ks = K / tp, G = K / 64, Gs = Ks / 64, WPR = K * w.bits / 32, WPRs = Ks * w.bits / 32;
   std::vector<float> sum((size_t)M * N);
   std::vector<uint16_t> xs((size_t)M * Ks), ss((size_t)N * Gs), bs((size_t)N * Gs);
   std::vector<uint32_t> ws((size_t)N * WPRs);
@@ -1039,7 +1041,7 @@ void qmm_resid(const Model& m, const QW& w, const uint16_t* x, uint16_t* h, int 
       std::memcpy(&ss[(size_t)n * Gs], &w.s[(size_t)n * G + (size_t)r * Gs], Gs * 2);
       std::memcpy(&bs[(size_t)n * Gs], &w.b[(size_t)n * G + (size_t)r * Gs], Gs * 2);
     }
-    orc_qmm(xs.data(), ws.data(), ss.data(), bs.data(), a.data(), M, N, Ks, m.group, m.bits);
+    orc_qmm(xs.data(), ws.data(), ss.data(), bs.data(), a.data(), M, N, Ks, m.group, w.bits);
     for (size_t i = 0; i < sum.size(); ++i) sum[i] = r == 0 ? bf2f(a[i]) : sum[i] + bf2f(a[i]);
   }
   for (size_t i = 0; i < sum.size(); ++i) h[i] = f2bf(bf2f(f2bf(sum[i])) + bf2f(h[i]));
@@ -1084,6 +1086,40 @@ extern "C" void* orc_model_create(const orc_model_cfg* cfg, uint64_t seed) {
 }
 
 extern "C" void orc_model_free(void* m) { delete (Model*)m; }
+
+// Install a checkpoint's tensors (test infrastructure: the tests read the
+// safetensors file themselves and hand the arrays over).  kind as
+// orc_model_weight; N x K is the weight's own shape, which must match the
+// model's for that slot.
+extern "C" int orc_model_set_weight(void* mp, int layer, int kind, int bits, const uint32_t* wq, const uint16_t* s,
+                                    const uint16_t* b) {
+  Model& m = *(Model*)mp;
+  QW* q = nullptr;
+  if (kind == 7) q = &m.embed;
+  else if (kind == 8 && !m.c.tied) q = &m.lm_head;
+  else if (layer >= 0 && layer < (int)m.L.size() && kind >= 0 && kind < 7) q = &m.L[layer].w[kind];
+  if (!q || (bits != 4 && bits != 8)) return 1;
+  q->bits = bits;
+  q->w.assign(wq, wq + (size_t)q->N * q->K * bits / 32);
+  q->s.assign(s, s + (size_t)q->N * (q->K / 64));
+  q->b.assign(b, b + (size_t)q->N * (q->K / 64));
+  return 0;
+}
+
+// which: 0 input_layernorm, 1 post_attention_layernorm, 2 q_norm, 3 k_norm
+// (of `layer`), 4 the final norm.
+extern "C" int orc_model_set_norm(void* mp, int layer, int which, const uint16_t* v) {
+  Model& m = *(Model*)mp;
+  std::vector<uint16_t>* dst = nullptr;
+  if (which == 4) dst = &m.final_norm;
+  else if (layer >= 0 && layer < (int)m.L.size()) {
+    Layer& L = m.L[layer];
+    dst = which == 0 ? &L.in_norm : which == 1 ? &L.post_norm : which == 2 ? &L.q_norm : which == 3 ? &L.k_norm : nullptr;
+  }
+  if (!dst) return 1;
+  std::copy(v, v + dst->size(), dst->begin());
+  return 0;
+}
 
 extern "C" int orc_model_weight(void* mp, int layer, int kind, uint32_t* wq, uint16_t* s,
                                 uint16_t* b) {
@@ -1178,10 +1214,10 @@ static int forward_impl(Model& m, Cache& c, int n_layers, const int32_t* tokens,
   // embedding lookup = dequantized row of the packed table
   for (int r = 0; r < R; ++r) {
     const int tok = tokens[r];
-    const uint32_t* row = m.embed.w.data() + (size_t)tok * H * m.bits / 32;
+    const uint32_t* row = m.embed.w.data() + (size_t)tok * H * m.embed.bits / 32;
     for (int i = 0; i < H; ++i) {
       float s = bf2f(m.embed.s[(size_t)tok * G + i / 64]), bb = bf2f(m.embed.b[(size_t)tok * G + i / 64]);
-      h[(size_t)r * H + i] = f2bf(std::fma(s, (float)qcode(row, i, m.bits), bb));
+      h[(size_t)r * H + i] = f2bf(std::fma(s, (float)qcode(row, i, m.embed.bits), bb));
     }
   }
   std::vector<int32_t> pos(R);

@@ -114,6 +114,11 @@ void orc_model_free(void* m);
 /* Copy a generated weight out (for bit-exactness checks vs the GPU generator).
  * kind: 0 q,1 k,2 v,3 o,4 gate,5 up,6 down,7 embed,8 lm_head. */
 int orc_model_weight(void* m, int layer, int kind, uint32_t* wq, uint16_t* s, uint16_t* b);
+/* Install a checkpoint's weight at `bits` (its own quantization) / a norm
+ * vector (which: 0 input, 1 post-attention, 2 q, 3 k of `layer`; 4 final). */
+int orc_model_set_weight(void* m, int layer, int kind, int bits, const uint32_t* wq, const uint16_t* s,
+                         const uint16_t* b);
+int orc_model_set_norm(void* m, int layer, int which, const uint16_t* v);
 
 /* kv_bits: 16 = bf16 cache, 4/8 = affine group-64 quantized cache. */
 void* orc_cache_create(void* model, int n_layers, int batch, int capacity, int kv_bits);

@@ -87,6 +87,8 @@ def _declare(L):
         "orc_model_create": (P, [C.POINTER(ModelCfg), U64]),
         "orc_model_free": (None, [P]),
         "orc_model_weight": (I, [P, I, I, P, P, P]),
+        "orc_model_set_weight": (I, [P, I, I, I, P, P, P]),
+        "orc_model_set_norm": (I, [P, I, I, P]),
         "orc_cache_create": (P, [P, I, I, I, I]),
         "orc_cache_fill_synthetic": (I, [P, I, U64, U32]),
         "orc_model_set_tp": (I, [P, I]),

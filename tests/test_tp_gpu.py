@@ -11,6 +11,7 @@ import sys
 import numpy as np
 import pytest
 
+import checkpoint_io as CK
 import oracle_lib as O
 import tp_worker as W
 
@@ -37,14 +38,32 @@ def free_port():
 def tp2_result(cuda, tmp_path_factory):
     if cuda.cuda.device_count() < 2:
         pytest.skip("tensor-parallel test needs 2 GPUs")
-    out = str(tmp_path_factory.mktemp("tp") / "tp2.npz")
+    tmp = tmp_path_factory.mktemp("tp")
+    out = str(tmp / "tp2.npz")
+    ckpt = str(tmp / "ckpt")
+    make_tp_checkpoint(ckpt)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", f"--master-port={free_port()}",
-           os.path.join(HERE, "tp_worker.py"), "--out", out]
+           os.path.join(HERE, "tp_worker.py"), "--out", out, "--ckpt", ckpt]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, f"tp worker failed:\n{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
-    return dict(np.load(out))
+    res = dict(np.load(out))
+    res["ckpt"] = ckpt
+    return res
+
+
+# Qwen3-style 4-bit checkpoint with 8-bit overrides on a row-split (o_proj),
+# a column-split (gate/up) layer and the vocab-split lm_head
+CKPT_CFG = dict(W.TARGET, qk_norm=1, group=64, rope_factor=0.0, rope_low_freq=0.0, rope_high_freq=0.0,
+                rope_orig_max_pos=0.0)
+del CKPT_CFG["group_size"]
+CKPT_OVER = {"model.layers.0.self_attn.o_proj": 8, "model.layers.1.mlp.gate_proj": 8,
+             "model.layers.1.mlp.up_proj": 8, "lm_head": 8}
+
+
+def make_tp_checkpoint(d):
+    CK.make_checkpoint(d, CKPT_CFG, 77, overrides=CKPT_OVER)
 
 
 def oracle_forward_logits(tp, mma):
@@ -97,3 +116,24 @@ def test_tp2_greedy_stream_matches_oracle(tp2_result):
     assert rc == 0
     np.testing.assert_array_equal(tp2_result["stream"], out)
     assert int(tp2_result["accepted"]) == st[2]
+
+
+def test_tp2_checkpoint_shards_bit_exact(tp2_result):
+    # each rank copied only its block of every tensor; together they give
+    # the oracle's tensor-parallel emulation of the whole checkpoint
+    O.lib().orc_set_mma_min_m(0)
+    cfg, o = CK.oracle_from_checkpoint(tp2_result["ckpt"])
+    assert O.lib().orc_model_set_tp(o, 2) == 0
+    oc = O.lib().orc_cache_create(o, cfg["layers"], W.B, 128, 16)
+    try:
+        for i, tok in enumerate(W.forward_tokens()):
+            T = tok.shape[1]
+            ol = np.zeros((W.B, T, cfg["vocab"]), np.uint16)
+            assert O.lib().orc_forward(o, oc, cfg["layers"], O.ptr(tok), W.B, T, O.ptr(ol)) == 0
+            got = tp2_result[f"ckpt_logits_{i}"]
+            bad = np.argwhere(got != ol)
+            assert bad.size == 0, f"block {i}: {len(bad)} mismatching logits, first {bad[:3].tolist()}"
+    finally:
+        O.lib().orc_cache_free(oc)
+        O.lib().orc_model_free(o)
+        O.lib().orc_set_mma_min_m(16)

@@ -7,6 +7,7 @@ Every rank builds its shard of the same seeded models and runs
     tensor-core threshold, and
   * a greedy speculative session: Llama-style target (tensor-parallel) with a
     replicated draft, 8-bit KV, a synthetic context before the prompt;
+  * with --ckpt, forwards of a checkpoint loaded as tensor-parallel shards;
 and rank 0 writes everything to --out (.npz) for the parent to compare with
 the oracle's tensor-parallel emulation.  Every rank must produce the same
 stream; the worker checks that itself.
@@ -57,6 +58,7 @@ def gather_concat(x, axis):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
+    ap.add_argument("--ckpt", default="", help="checkpoint directory to load as tp shards")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -81,6 +83,21 @@ def main():
             res[f"logits_mma{mma}_{i}"] = gather_concat(lg, 2)
         lmx.call("lmx_cache_free", gc)
     m.close()
+
+    # a mixed-precision checkpoint loaded as this rank's shard, exact mode
+    if args.ckpt:
+        lmx.call("lmx_set_mma_min_m", 0)
+        m = lmx.Model.load(args.ckpt, comm=comm)
+        c = m.cfg
+        gc = C.c_void_p()
+        lmx.call("lmx_cache_create", m.h, c["layers"], B, 128, 16, 8, C.byref(gc))
+        for i, tok in enumerate(forward_tokens()):
+            T = tok.shape[1]
+            lg = np.zeros((B, T, c["vocab"] // world), np.uint16)
+            lmx.call("lmx_forward", m.h, gc, c["layers"], tok.ctypes.data, B, T, lg.ctypes.data)
+            res[f"ckpt_logits_{i}"] = gather_concat(lg, 2)
+        lmx.call("lmx_cache_free", gc)
+        m.close()
 
     # greedy speculative session, exact mode
     lmx.call("lmx_set_mma_min_m", 0)
