@@ -70,6 +70,13 @@ int lmx_mma_min_m(void);
  * reference counterpart. */
 int lmx_set_gemv_tc_min_m(int m);
 int lmx_gemv_tc_min_m(void);
+/* Matrices with at least this many 16-row tiles (default 1024: an lm_head)
+ * run the small-batch tensor-core GEMV with one warp per tile over the whole
+ * K instead of eight warps splitting K; 0 = never.  Same math, groups summed
+ * by one warp (within the same tolerance).  Process-wide; no reference
+ * counterpart. */
+int lmx_set_gemv_tc_rows_min_tiles(int t);
+int lmx_gemv_tc_rows_min_tiles(void);
 
 /* The fused small-batch decode forward (default off): in tensor-core mode a
  * model forward of at most 16 token rows (B*T, at most 8 query rows per KV

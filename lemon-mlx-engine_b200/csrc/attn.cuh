@@ -197,21 +197,40 @@ static constexpr int kPartStride = kHeadDim + 2;  // m, l, o[128]
 
 // Dequantize (or copy) 8 consecutive K/V values d = 8c..8c+7 of one cache
 // row into packed bf16 (bf16(fma(s, q, b)) for the affine cache).
-LMX_DEV uint4 kv_chunk8(const KvDesc& kv, bool is_k, size_t row, int c) {
-  if (kv.bits == 16)
-    return *reinterpret_cast<const uint4*>((is_k ? kv.k : kv.v) + row * kHeadDim + c * 8);
-  const float s = bf2f((is_k ? kv.ks : kv.vs)[row * 2 + c / 8]);
-  const float b = bf2f((is_k ? kv.kb : kv.vb)[row * 2 + c / 8]);
-  const uint32_t* w = (is_k ? kv.kq : kv.vq) + row * (kHeadDim * kv.bits / 32);
-  uint32_t q[8];
+// Chunk c (8 values) of a K or V row in two halves, so a caller can issue
+// every load of a tile before converting any of it: kv_raw8 loads the raw
+// words (bf16: the 8 values; 4 / 8-bit: the packed word(s) and the group's
+// scale | bias << 16), kv_cvt8 dequantizes them, bf16(fma(s, q, b)).
+LMX_DEV void kv_raw8(const KvDesc& kv, bool is_k, size_t row, int c, uint4& w, uint32_t& sb) {
+  if (kv.bits == 16) {
+    w = *reinterpret_cast<const uint4*>((is_k ? kv.k : kv.v) + row * kHeadDim + c * 8);
+    sb = 0u;
+    return;
+  }
+  sb = (uint32_t)(is_k ? kv.ks : kv.vs)[row * 2 + c / 8] | ((uint32_t)(is_k ? kv.kb : kv.vb)[row * 2 + c / 8] << 16);
+  const uint32_t* p = (is_k ? kv.kq : kv.vq) + row * (kHeadDim * kv.bits / 32);
+  w = make_uint4(0u, 0u, 0u, 0u);
   if (kv.bits == 4) {
-    const uint32_t x = w[c];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[e] = (x >> (4 * e)) & 0xFu;
+    w.x = p[c];
   } else {
-    const uint32_t x0 = w[2 * c], x1 = w[2 * c + 1];
+    w.x = p[2 * c];
+    w.y = p[2 * c + 1];
+  }
+}
+
+LMX_DEV uint4 kv_cvt8(int bits, const uint4& w, uint32_t sb) {
+  if (bits == 16) return w;
+  const float s = __uint_as_float(sb << 16), b = __uint_as_float(sb & 0xffff0000u);
+  uint32_t q[8];
+  if (bits == 4) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) { q[e] = (x0 >> (8 * e)) & 0xFFu; q[4 + e] = (x1 >> (8 * e)) & 0xFFu; }
+    for (int e = 0; e < 8; ++e) q[e] = (w.x >> (4 * e)) & 0xFu;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      q[e] = (w.x >> (8 * e)) & 0xFFu;
+      q[4 + e] = (w.y >> (8 * e)) & 0xFFu;
+    }
   }
   uint32_t o[4];
 #pragma unroll
@@ -219,6 +238,13 @@ LMX_DEV uint4 kv_chunk8(const KvDesc& kv, bool is_k, size_t row, int c) {
     o[e] = (uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e], b)) |
            ((uint32_t)f2bf(__fmaf_rn(s, (float)q[2 * e + 1], b)) << 16);
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+LMX_DEV uint4 kv_chunk8(const KvDesc& kv, bool is_k, size_t row, int c) {
+  uint4 w;
+  uint32_t sb;
+  kv_raw8(kv, is_k, row, c, w, sb);
+  return kv_cvt8(kv.bits, w, sb);
 }
 
 static constexpr int kKPitch = kHeadDim + 8;  // bf16 elements per staged K row (16 B pad)
@@ -252,16 +278,34 @@ __global__ void __launch_bounds__(256) sdpa_split_kernel(SdpaArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t kvrow0 = ((size_t)b * a.kv.Hk + kvh) * a.kv.cap + j0;
 
-  // stage K, V rows [0, jn) as bf16 (16-byte chunks), zero V rows [jn, jn4)
-  for (int e = tid; e < jn4 * 16; e += 256) {
-    const int j = e >> 4, c = e & 15;
-    uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
+  // stage K, V rows [0, jn) as bf16 (16-byte chunks), zero V rows [jn, jn4):
+  // every raw load of the tile first (one memory round trip), then the
+  // conversions and shared-memory stores
+  constexpr int kStageIters = kSplit * 16 / 256;
+  uint4 kw[kStageIters], vw[kStageIters];
+  uint32_t ksb[kStageIters], vsb[kStageIters];
+#pragma unroll
+  for (int i = 0; i < kStageIters; ++i) {
+    const int e = tid + 256 * i, j = e >> 4, c = e & 15;
+    kw[i] = vw[i] = make_uint4(0u, 0u, 0u, 0u);
+    ksb[i] = vsb[i] = 0u;
     if (j < jn) {
-      kc = kv_chunk8(a.kv, true, kvrow0 + j, c);
-      vc = kv_chunk8(a.kv, false, kvrow0 + j, c);
+      kv_raw8(a.kv, true, kvrow0 + j, c, kw[i], ksb[i]);
+      kv_raw8(a.kv, false, kvrow0 + j, c, vw[i], vsb[i]);
     }
-    *reinterpret_cast<uint4*>(Ks + j * kKPitch + c * 8) = kc;
-    *reinterpret_cast<uint4*>(Vs + j * kHeadDim + c * 8) = vc;
+  }
+#pragma unroll
+  for (int i = 0; i < kStageIters; ++i) {
+    const int e = tid + 256 * i, j = e >> 4, c = e & 15;
+    if (j < jn4) {
+      uint4 kc = make_uint4(0u, 0u, 0u, 0u), vc = kc;
+      if (j < jn) {
+        kc = kv_cvt8(a.kv.bits, kw[i], ksb[i]);
+        vc = kv_cvt8(a.kv.bits, vw[i], vsb[i]);
+      }
+      *reinterpret_cast<uint4*>(Ks + j * kKPitch + c * 8) = kc;
+      *reinterpret_cast<uint4*>(Vs + j * kHeadDim + c * 8) = vc;
+    }
   }
   for (int e = tid; e < nr * kHeadDim; e += 256) {
     const int rr = e / kHeadDim, d = e % kHeadDim;

@@ -781,7 +781,9 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
     return set_error(LMX_ERR_INVALID, "forward: attention scratch too small");
   if (tp && (R > m.comm->max_rows || H > m.comm->max_hidden))
     return set_error(LMX_ERR_INVALID, "forward: %d rows exceed the tp comm", R);
-  const bool fuse = !tp && R <= kQmmMaxNormRows && !qmm_uses_mma(R) && !qmm_uses_tcg(R);
+  // the input / post-attention RMSNorm fused into the GEMV prologue (both
+  // GEMV paths; the tcgen05 path takes normalised rows through TMA)
+  const bool fuse = !tp && R <= kQmmMaxNormRows && !qmm_uses_mma(R);
   int rc = cuda_check(lmx_launch(embed_kernel, dim3(R), dim3(256), 0, st, true, tok, T, tok_ld, tok_off,
                                  (const uint32_t*)m.embed.w, (const bf16_t*)m.embed.s,
                                  (const bf16_t*)m.embed.b, H, m.embed.bits, ws.h, R),
@@ -951,7 +953,7 @@ static int forward(const Model& m, Cache& c, int n_layers, const int32_t* tok, i
   const bf16_t* src = ws.h;
   if (tp) {
     src = ws.xn;  // final-normed by the last all-reduce
-  } else if (M > kQmmMaxNormRows || qmm_uses_mma(M) || qmm_uses_tcg(M)) {
+  } else if (M > kQmmMaxNormRows || qmm_uses_mma(M)) {
     rc = launch_rms_norm(ws.h, m.final_norm, ws.xn, R, H, cf.eps, st);
     if (rc) return rc;
     src = ws.xn;
@@ -1730,7 +1732,7 @@ static int spec_profile(Spec& sp, int what, int iters, double* seconds, double* 
     QmmCall hc;
     hc.M = what == 2 ? B * (K + 1) : B;
     hc.x = sp.ws.h;
-    if (qmm_uses_mma(hc.M) || qmm_uses_tcg(hc.M)) {  // the tensor-core paths take normalised rows
+    if (qmm_uses_mma(hc.M)) {  // the tcgen05 path takes normalised rows
       const int r2 = launch_rms_norm(sp.ws.h, sp.tm->final_norm, sp.ws.xn, hc.M, sp.tm->c.hidden, sp.tm->c.eps, st);
       if (r2) return r2;
       hc.x = sp.ws.xn;

@@ -258,6 +258,9 @@ static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 static int g_mma_min_m = 16;
 static int g_tcg_min_m = 4;
+// matrices of at least this many 16-row tiles take the warp-per-tile form
+// of the small-batch GEMV (qmv_tc_rows_kernel); 0 = never
+static int g_tcg_rows_min_tiles = 1024;
 int qmm_mma_min_m() { return g_mma_min_m; }
 bool qmm_uses_mma(int M) { return g_mma_min_m > 0 && M >= g_mma_min_m; }
 // the small-batch tensor-core GEMV (qmv_tc.cuh): M in [g_tcg_min_m, the
@@ -426,11 +429,27 @@ static int launch_tcg_t(const QmmArgs& a, cudaStream_t st) {
   } else {
     for (int i = 0; i < a.nmat; ++i) tiles += (a.mat[i].rows + kTcgRows - 1) / kTcgRows;
   }
-  // split K over a cluster while the tiles fill fewer than two waves of
-  // 148 SMs and every warp keeps at least two groups
-  const int G = a.K / 64;
+  // many tiles (PLAIN / RESID): one warp per tile over the full K
+  if (a.mode != QMM_SWIGLU && tiles >= g_tcg_rows_min_tiles && g_tcg_rows_min_tiles > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((tiles + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (a.M <= 8)
+      return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_tc_rows_kernel<BITS, 1>, a)), "qmv_tc_rows: launch");
+    return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_tc_rows_kernel<BITS, 2>, a)), "qmv_tc_rows: launch");
+  }
+  // split K over a cluster while the tiles fill at most two waves of 148
+  // SMs and every warp keeps at least one group: at these sizes a CTA's time
+  // is its chain of dependent loads, so more CTAs with fewer groups each win
+  const int G = a.K / 64, nslice = a.mode == QMM_SWIGLU ? 4 : 8;
   int ks = 1;
-  while (ks < 4 && tiles * ks < 2 * 148 && G >= 8 * 2 * (2 * ks)) ks *= 2;
+  while (ks < 4 && tiles * (2 * ks) <= 2 * 148 && G >= nslice * (2 * ks)) ks *= 2;
   // the (scale, bias) table: rows of the tile x (groups of one rank + 1) words
   const size_t smem = (size_t)(a.mode == QMM_SWIGLU ? 2 * kTcgRows : kTcgRows) * ((G + ks - 1) / ks + 1) * 4;
   static size_t smem_set[2][64] = {};
@@ -501,7 +520,7 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
   a.mode = c.mode;
   a.err = device_error_word();
   if (!c.norm_w && qmm_uses_mma(c.M)) return c.bits == 4 ? launch_mma_t<4>(a, st) : launch_mma_t<8>(a, st);
-  if (!c.norm_w && qmm_uses_tcg(c.M)) return c.bits == 4 ? launch_tcg_t<4>(a, st) : launch_tcg_t<8>(a, st);
+  if (qmm_uses_tcg(c.M)) return c.bits == 4 ? launch_tcg_t<4>(a, st) : launch_tcg_t<8>(a, st);
   return c.bits == 4 ? launch_qmv_bits<4>(a, st) : launch_qmv_bits<8>(a, st);
 }
 
@@ -573,6 +592,14 @@ extern "C" int lmx_set_gemv_tc_min_m(int m) {
 }
 
 extern "C" int lmx_gemv_tc_min_m(void) { return g_tcg_min_m; }
+
+extern "C" int lmx_set_gemv_tc_rows_min_tiles(int t) {
+  if (t < 0) return set_error(LMX_ERR_INVALID, "gemv_tc_rows_min_tiles %d", t);
+  g_tcg_rows_min_tiles = t;
+  return LMX_OK;
+}
+
+extern "C" int lmx_gemv_tc_rows_min_tiles(void) { return g_tcg_rows_min_tiles; }
 
 extern "C" int lmx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                                     const void* biases, void* y, int M, int N, int K, int group_size,

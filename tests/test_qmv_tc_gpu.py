@@ -102,3 +102,68 @@ def test_gemv_tc_threshold_validation(lmx, gemv_tc):
     assert lmx.lib().lmx_set_gemv_tc_min_m(-1) != 0
     gemv_tc(6)
     assert lmx.lib().lmx_gemv_tc_min_m() == 6
+
+
+@pytest.fixture
+def rows_tiles(lmx):
+    def set_(t):
+        lmx.call("lmx_set_gemv_tc_rows_min_tiles", t)
+
+    yield set_
+    set_(1024)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [4, 8, 13])
+@pytest.mark.parametrize("N,K", [(1000, 1024), (4096, 4096), (520, 4160), (20000, 1024)])
+def test_qmv_tc_rows_within_tolerance(lmx, cuda, mma_threshold, gemv_tc, rows_tiles, bits, M, N, K):
+    # the warp-per-tile form (forced for every matrix here; by default for
+    # >= 1024 tiles, e.g. the 20000-row case): same bound as the split form
+    mma_threshold(16)
+    gemv_tc(4)
+    rows_tiles(1)
+    wq, s, b = O.gen_sweep_weights(21 + N, 5 + K, N, K, bits)
+    x = O.gen_normal_bf16(9 + M, K, 1.0, M * K).reshape(M, K)
+    got = run_qmm(lmx, cuda, x, wq, s, b, bits, N, K)
+    exact = check_close(got, O.qmm(x, wq, s, b, bits), x, magnitudes(wq, s, b, N, K, bits))
+    assert exact > 0.9, f"only {exact:.3f} of outputs equal the canonical GEMV's"
+
+
+def test_qmv_tc_rows_in_the_decoder(lmx, cuda, mma_threshold, gemv_tc, rows_tiles):
+    # every PLAIN / RESID GEMV of a decoder through the warp-per-tile form
+    # (q|k|v and the lm_head with the fused RMSNorm, o_proj / down_proj with
+    # the residual add): logits within the engine's tensor-core tolerance of
+    # the oracle, and of the split form
+    import ctypes as C
+    from test_engine_gpu import TINY, assert_logits_close, oracle_cfg
+    mma_threshold(16)
+    gemv_tc(4)
+    cfg = dict(TINY, tied=0)
+    g = lmx.Model(cfg, 99)
+    o = O.lib().orc_model_create(C.byref(oracle_cfg(cfg)), 99)
+    L, V, B = cfg["layers"], cfg["vocab"], 4
+    rng = np.random.RandomState(3)
+    pre = rng.randint(0, V, (B, 12)).astype(np.int32)
+    outs = []
+    try:
+        for t in (1, 1024):
+            rows_tiles(t)
+            gc = C.c_void_p()
+            lmx.call("lmx_cache_create", g.h, L, B, 64, 16, 12, C.byref(gc))
+            oc = O.lib().orc_cache_create(o, L, B, 64, 16)
+            for T in (3, 1, 2):  # M = 12, 4, 8: every block on the small-batch GEMV
+                tok = pre[:, :T].copy()
+                gl = np.zeros((B, T, V), np.uint16)
+                ol = np.zeros((B, T, V), np.uint16)
+                lmx.call("lmx_forward", g.h, gc, L, tok.ctypes.data, B, T, gl.ctypes.data)
+                assert O.lib().orc_forward(o, oc, L, O.ptr(tok), B, T, O.ptr(ol)) == 0
+                assert_logits_close(gl, ol, f"rows_min_tiles {t}, T={T}")
+                outs.append(gl)
+            lmx.call("lmx_cache_free", gc)
+            O.lib().orc_cache_free(oc)
+        for a, b in zip(outs[:3], outs[3:]):
+            assert_logits_close(a, b, "warp-per-tile vs split form")
+    finally:
+        g.close()
+        O.lib().orc_model_free(o)
+    assert lmx.lib().lmx_set_gemv_tc_rows_min_tiles(-1) != 0
