@@ -508,6 +508,8 @@ def run_reference(args, wl, world, rank):
 def run_lmx(args, wl, world, rank, local):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", local)
+    if args.sdpa_tc_min_cache >= 0:
+        lmx.call("lmx_set_sdpa_tc_min_cache", args.sdpa_tc_min_cache)
     arch = getattr(lmx, wl["arch"])
     if args.layers:
         arch = dict(arch, layers=args.layers)
@@ -631,7 +633,9 @@ def run_lmx(args, wl, world, rank, local):
         f"lm_head_m{B}": {"us": round(hsec * 1e6, 2), "GBs": round(hbytes / hsec / 1e9, 1)},
         # one draft token (draft forward over B rows incl. its lm_head) and the
         # split of one speculative step (decode time / graph replays): verify
-        # pass + K draft tokens + the rest (sampling, acceptance, bookkeeping)
+        # pass + K draft tokens + the rest (sampling, acceptance, bookkeeping);
+        # verify pass and draft token are timed as CUDA-graph replays, as the
+        # decode runs them
         "draft_token": {"us": round(dsec * 1e6, 2), "GBs": round(dbytes / dsec / 1e9, 1),
                         "frac": round(dbytes / dsec / 1e9 / peak, 4), "bytes": dbytes},
         "step": {"ms": round(1e3 * dec / max(1, replays), 3), "verify_ms": round(1e3 * vsec, 3),
@@ -642,6 +646,7 @@ def run_lmx(args, wl, world, rank, local):
                        "rate": round(acc / prop, 4) if prop else None,
                        "tokens_per_step": round(toks / max(1, steps), 3)},
         "clocks": ck, "gpu_launches": int(gpu_launches),
+        "sdpa_tc_min_cache": int(lmx.lib().lmx_sdpa_tc_min_cache()),
     }
     if world == 1 and rank == 0 and not args.no_cpu and tp:
         tps = toks / max(1, steps)
@@ -954,7 +959,8 @@ def main():
     ap.add_argument("--gdn", default="", help="op-level Gated DeltaNet verify + commit B,T,Hk,Hv (configuration 4: "
                                               "4,3,16,32)")
     ap.add_argument("--sdpa-tc-min-cache", type=int, default=-1,
-                    help="with --sdpa: set lmx_set_sdpa_tc_min_cache first (0: by row count only)")
+                    help="set lmx_set_sdpa_tc_min_cache first (0: by row count only; a large value keeps "
+                         "single-token decode attention on the canonical kernel)")
     ap.add_argument("--sdpa", default="", help="one op-level attention shape B,T,Hq,Hk,cap,bits (e.g. "
                                                "16,5,64,8,8300,8 = one Llama-3-70B verify layer)")
     args = ap.parse_args()

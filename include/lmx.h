@@ -562,8 +562,9 @@ int lmx_spec_generate(void* spec, const int32_t* prompts_host, const int32_t* eo
                       lmx_cancel_fn should_cancel, void* cancel_user, lmx_token_fn on_token, void* token_user,
                       lmx_completion_info* info);
 /* Measurement hooks (no reference counterpart; used by bench.py): time one
- * piece of the step on the decoder's stream with CUDA events, `iters` launches
- * after decode.  what: 0 verify pass, 1 one draft token, 2 lm_head at
+ * piece of the step on the decoder's stream with CUDA events: the piece is
+ * captured into a CUDA graph (as the decode runs it) and replayed `iters`
+ * times, after decode.  what: 0 verify pass, 1 one draft token, 2 lm_head at
  * M = batch*(K+1), 3 lm_head at M = batch.  *bytes = algorithmic HBM bytes of
  * one launch (packed weights + scales/biases + KV rows + activations). */
 int lmx_spec_profile(void* spec, int what, int iters, double* seconds, double* bytes);
