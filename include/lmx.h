@@ -75,6 +75,14 @@ int lmx_gemv_tc_min_m(void);
  * K instead of eight warps splitting K; 0 = never.  Same math, groups summed
  * by one warp (within the same tolerance).  Process-wide; no reference
  * counterpart. */
+/* M from the tcgen05 threshold up to this bound (at most 64; default 0) run
+ * the mid-batch tensor-core GEMM (mma.sync on the exact codes, MLX's qmv math
+ * per group: s * sum q x + b * sum x) instead of the tcgen05 kernel
+ * (dequantize-then-MMA); 0 = never.  Within the same tolerance of the
+ * canonical order as the small-batch GEMV.  Process-wide; no reference
+ * counterpart. */
+int lmx_set_gemm_tcs_max_m(int m);
+int lmx_gemm_tcs_max_m(void);
 int lmx_set_gemv_tc_rows_min_tiles(int t);
 int lmx_gemv_tc_rows_min_tiles(void);
 

@@ -16,6 +16,7 @@
 #include "attn.cuh"
 #include "attn_mma.cuh"
 #include "qmv_tc.cuh"
+#include "qmm_tcs.cuh"
 #include "engine_kernels.cuh"
 #include "sample.cuh"
 #include "tp.cuh"
@@ -258,6 +259,9 @@ static int launch_qmv_bits(const QmmArgs& a, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 static int g_mma_min_m = 16;
 static int g_tcg_min_m = 4;
+// M in [the tcgen05 threshold, g_tcs_max_m] runs the mid-batch mma.sync
+// GEMM (qmm_tcs.cuh) instead of the tcgen05 kernel; 0 = never (default)
+static int g_tcs_max_m = 0;
 // matrices of at least this many 16-row tiles take the warp-per-tile form
 // of the small-batch GEMV (qmv_tc_rows_kernel); 0 = never
 static int g_tcg_rows_min_tiles = 1024;
@@ -485,6 +489,69 @@ static int launch_tcg_t(const QmmArgs& a, cudaStream_t st) {
   return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmv_tc_kernel<BITS, 2>, a, ks)), "qmv_tc: launch");
 }
 
+template <int BITS, int NT>
+static int launch_tcs_nt(const QmmArgs& a, cudaStream_t st) {
+  static int occ[64] = {};
+  int d = 0;
+  cudaGetDevice(&d);
+  const size_t smem = tcs_smem(NT * 8);
+  if (!occ[d & 63]) {
+    int n = 0;
+    int rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmm_tcs_kernel<BITS, NT>, 256, smem),
+                        "qmm_tcs: occupancy");
+    if (rc) return rc;
+    occ[d & 63] = n > 0 ? n : 1;
+  }
+  int tiles = 0;
+  if (a.mode == QMM_SWIGLU) {
+    tiles = (a.N + kTcsRows / 2 - 1) / (kTcsRows / 2);
+  } else {
+    int t16 = 0;
+    for (int i = 0; i < a.nmat; ++i) t16 += (a.mat[i].rows + kTcgRows - 1) / kTcgRows;
+    tiles = (t16 + kTcsWarps - 1) / kTcsWarps;
+  }
+  // split K over a cluster: the factor (<= 8, >= 2 groups per CTA) with the
+  // fewest waves x groups per CTA (one CTA's time is its groups in sequence);
+  // clusters reach about 96% of the SMs
+  const int G = a.K / 64, slots = occ[d & 63] * (device_sms() * 96 / 100);
+  int ks = 1;
+  long best = -1;
+  for (int k = 1; k <= kTcsMaxSplit && 2 * k <= G; ++k) {
+    const long waves = ((long)tiles * k + slots - 1) / slots, cost = waves * ((G + k - 1) / k);
+    if (best < 0 || cost < best) {
+      best = cost;
+      ks = k;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * ks);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (ks > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = ks;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cuda_check(lmx_counted(cudaLaunchKernelEx(&cfg, qmm_tcs_kernel<BITS, NT>, a, ks)), "qmm_tcs: launch");
+}
+
+template <int BITS>
+static int launch_tcs_t(const QmmArgs& a, cudaStream_t st) {
+  if (a.M <= 24) return launch_tcs_nt<BITS, 3>(a, st);
+  if (a.M <= 32) return launch_tcs_nt<BITS, 4>(a, st);
+  if (a.M <= 48) return launch_tcs_nt<BITS, 6>(a, st);
+  return launch_tcs_nt<BITS, 8>(a, st);
+}
+
 int launch_qmm(const QmmCall& c, cudaStream_t st) {
   if (c.M == 0 || c.N == 0) return LMX_OK;
   if (c.M < 0 || c.N < 0 || c.K <= 0 || c.K % 64)
@@ -519,6 +586,8 @@ int launch_qmm(const QmmCall& c, cudaStream_t st) {
   a.K = c.K;
   a.mode = c.mode;
   a.err = device_error_word();
+  if (!c.norm_w && qmm_uses_mma(c.M) && c.M <= g_tcs_max_m && c.M <= 64)
+    return c.bits == 4 ? launch_tcs_t<4>(a, st) : launch_tcs_t<8>(a, st);
   if (!c.norm_w && qmm_uses_mma(c.M)) return c.bits == 4 ? launch_mma_t<4>(a, st) : launch_mma_t<8>(a, st);
   if (qmm_uses_tcg(c.M)) return c.bits == 4 ? launch_tcg_t<4>(a, st) : launch_tcg_t<8>(a, st);
   return c.bits == 4 ? launch_qmv_bits<4>(a, st) : launch_qmv_bits<8>(a, st);
@@ -592,6 +661,14 @@ extern "C" int lmx_set_gemv_tc_min_m(int m) {
 }
 
 extern "C" int lmx_gemv_tc_min_m(void) { return g_tcg_min_m; }
+
+extern "C" int lmx_set_gemm_tcs_max_m(int m) {
+  if (m < 0 || m > 64) return set_error(LMX_ERR_INVALID, "gemm_tcs_max_m %d (0 = off, at most 64)", m);
+  g_tcs_max_m = m;
+  return LMX_OK;
+}
+
+extern "C" int lmx_gemm_tcs_max_m(void) { return g_tcs_max_m; }
 
 extern "C" int lmx_set_gemv_tc_rows_min_tiles(int t) {
   if (t < 0) return set_error(LMX_ERR_INVALID, "gemv_tc_rows_min_tiles %d", t);

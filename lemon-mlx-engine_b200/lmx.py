@@ -35,6 +35,8 @@ SIGNATURES = {
     "lmx_mma_min_m": (I, []),
     "lmx_set_gemv_tc_min_m": (I, [I]),
     "lmx_gemv_tc_min_m": (I, []),
+    "lmx_set_gemm_tcs_max_m": (I, [I]),
+    "lmx_gemm_tcs_max_m": (I, []),
     "lmx_set_gemv_tc_rows_min_tiles": (I, [I]),
     "lmx_gemv_tc_rows_min_tiles": (I, []),
     "lmx_set_fused_decode": (I, [I]),

@@ -313,6 +313,14 @@ static void qmm_block8(const float* xf, const float* xsum, int M, int K, const u
 static int g_mma_min_m = 16;
 extern "C" void orc_set_mma_min_m(int m) { g_mma_min_m = m < 0 ? 0 : m; }
 extern "C" int orc_mma_min_m(void) { return g_mma_min_m; }
+// The device's mid-batch tensor-core GEMM (M from the threshold up to this
+// bound, default 64) keeps MLX's qmv form, s * sum q x + b * sum x per group,
+// like its GEMV: the oracle then takes its canonical GEMV for those M, and the
+// dequantize-then-dot form above the bound.  0 (default, as the device) = the
+// dequantize form for every M at or above the threshold.
+static int g_tcs_max_m = 0;
+extern "C" void orc_set_tcs_max_m(int m) { g_tcs_max_m = m < 0 ? 0 : m; }
+extern "C" int orc_tcs_max_m(void) { return g_tcs_max_m; }
 
 static void qmm_dequant_rows(const float* xf, int M, int K, const uint32_t* wq, const uint16_t* sc,
                              const uint16_t* bi, int n0, int nr, int N, int bits, uint16_t* y) {
@@ -339,7 +347,7 @@ extern "C" int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* sc
                        int bits) {
   if (group != 64 || (bits != 4 && bits != 8) || K % 64 || M < 0 || N < 0) return 1;
   if (M == 0 || N == 0) return 0;
-  if (g_mma_min_m > 0 && M >= g_mma_min_m) {
+  if (g_mma_min_m > 0 && M >= g_mma_min_m && M > g_tcs_max_m) {
     std::vector<float> xf((size_t)M * K);
     for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf2f(x[i]);
     const int nblk = (N + 7) / 8;

@@ -70,6 +70,10 @@ int orc_qmm(const uint16_t* x, const uint32_t* wq, const uint16_t* scales,
 /* M >= threshold: dequantize-then-dot (the tensor-core path); 0 = never */
 void orc_set_mma_min_m(int m);
 int orc_mma_min_m(void);
+/* M in [the threshold, this bound] (default 0 = none) use the canonical GEMV form
+ * (the device's mid-batch tensor-core GEMM keeps MLX's qmv math). */
+void orc_set_tcs_max_m(int m);
+int orc_tcs_max_m(void);
 void orc_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int dim,
                   float eps);
 void orc_rope_table(int max_pos, int dims, float base, float* cos_t, float* sin_t);

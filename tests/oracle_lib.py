@@ -73,6 +73,8 @@ def _declare(L):
         "orc_qmm": (I, [P, P, P, P, P, I, I, I, I, I]),
         "orc_set_mma_min_m": (None, [I]),
         "orc_mma_min_m": (I, []),
+        "orc_set_tcs_max_m": (None, [I]),
+        "orc_tcs_max_m": (I, []),
         "orc_rms_norm": (None, [P, P, P, I, I, F]),
         "orc_rope_table": (None, [I, I, F, P, P]),
         "orc_rope_table_scaled": (None, [I, I, F, F, F, F, F, P, P]),

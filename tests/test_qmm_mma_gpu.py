@@ -16,6 +16,17 @@ from test_qmm_gpu import run_qmm
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def tcgen05_for_every_m(lmx):
+    # the mid-batch mma.sync GEMM (test_qmm_tcs_gpu) off on both sides: every
+    # M at or above the threshold takes tcgen05
+    lmx.call("lmx_set_gemm_tcs_max_m", 0)
+    O.lib().orc_set_tcs_max_m(0)
+    yield
+    lmx.call("lmx_set_gemm_tcs_max_m", 0)
+    O.lib().orc_set_tcs_max_m(0)
+
+
 def dequant_f32(wq, s, b, N, K, bits):
     return O.bf16_to_f32(O.dequantize(wq, s, b, K, 64, bits)).reshape(N, K).astype(np.float64)
 
