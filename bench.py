@@ -510,6 +510,8 @@ def run_lmx(args, wl, world, rank, local):
     lmx.call("lmx_set_device", local)
     if args.sdpa_tc_min_cache >= 0:
         lmx.call("lmx_set_sdpa_tc_min_cache", args.sdpa_tc_min_cache)
+    if args.gemm_tcs_max_m >= 0:
+        lmx.call("lmx_set_gemm_tcs_max_m", args.gemm_tcs_max_m)
     arch = getattr(lmx, wl["arch"])
     if args.layers:
         arch = dict(arch, layers=args.layers)
@@ -647,6 +649,7 @@ def run_lmx(args, wl, world, rank, local):
                        "tokens_per_step": round(toks / max(1, steps), 3)},
         "clocks": ck, "gpu_launches": int(gpu_launches),
         "sdpa_tc_min_cache": int(lmx.lib().lmx_sdpa_tc_min_cache()),
+        "gemm_tcs_max_m": int(lmx.lib().lmx_gemm_tcs_max_m()),
     }
     if world == 1 and rank == 0 and not args.no_cpu and tp:
         tps = toks / max(1, steps)
@@ -677,6 +680,8 @@ QMM_MS = [1, 2, 4, 5, 8, 12, 16, 32]
 def qmm_path(lmx, M):
     """Which K1 kernel takes M rows under the library's current thresholds."""
     mma, tcg = lmx.lib().lmx_mma_min_m(), lmx.lib().lmx_gemv_tc_min_m()
+    if mma > 0 and M >= mma and M <= min(64, lmx.lib().lmx_gemm_tcs_max_m()):
+        return "mma.sync gemm"
     if mma > 0 and M >= mma:
         return "tcgen05"
     if mma > 0 and tcg > 0 and tcg <= M <= 16:
@@ -913,6 +918,8 @@ def gdn_time(lmx, B, T, Hk, Hv, seed=2026):
 def run_qmm(args):
     lmx = _load("lmx", os.path.join(ROOT, "lemon-mlx-engine_b200", "lmx.py"))
     lmx.call("lmx_set_device", 0)
+    if args.gemm_tcs_max_m >= 0:
+        lmx.call("lmx_set_gemm_tcs_max_m", args.gemm_tcs_max_m)
     peak, kind = peaks()
     if args.qmm:
         N, K, M, bits = [int(v) for v in args.qmm.split(",")]
@@ -958,6 +965,9 @@ def main():
                                               "12,2048,512,512,10,4)")
     ap.add_argument("--gdn", default="", help="op-level Gated DeltaNet verify + commit B,T,Hk,Hv (configuration 4: "
                                               "4,3,16,32)")
+    ap.add_argument("--gemm-tcs-max-m", type=int, default=-1,
+                    help="set lmx_set_gemm_tcs_max_m first: M up to this bound on the mid-batch mma.sync GEMM "
+                         "(0: tcgen05 for every M at or above the threshold)")
     ap.add_argument("--sdpa-tc-min-cache", type=int, default=-1,
                     help="set lmx_set_sdpa_tc_min_cache first (0: by row count only; a large value keeps "
                          "single-token decode attention on the canonical kernel)")

@@ -494,11 +494,15 @@ static int launch_tcs_nt(const QmmArgs& a, cudaStream_t st) {
   static int occ[64] = {};
   int d = 0;
   cudaGetDevice(&d);
-  const size_t smem = tcs_smem(NT * 8);
+  const size_t smem = tcs_smem(NT * 8, BITS);
   if (!occ[d & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(qmm_tcs_kernel<BITS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem),
+                        "qmm_tcs: set smem");
+    if (rc) return rc;
     int n = 0;
-    int rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmm_tcs_kernel<BITS, NT>, 256, smem),
-                        "qmm_tcs: occupancy");
+    rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmm_tcs_kernel<BITS, NT>, 256, smem),
+                    "qmm_tcs: occupancy");
     if (rc) return rc;
     occ[d & 63] = n > 0 ? n : 1;
   }

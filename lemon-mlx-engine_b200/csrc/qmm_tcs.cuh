@@ -16,14 +16,17 @@
 // groups.  A cluster of `ks` CTAs splits K; the partial tiles [128 rows][M]
 // are summed in rank order through distributed shared memory.
 //
-// Activations: per block of 2 groups (128 k) every thread loads its 16-byte
-// chunks of x [M][128] into registers one block ahead, then stores them into
-// a double-buffered shared tile (16-byte chunks XOR-swizzled by row % 8) and
-// forms the per-(token, group) sums with 8-lane shuffles; one __syncthreads
-// per block.  For 4-bit weights each 8-value chunk is stored in the order
-// (k0,k4,k1,k5,k2,k6,k3,k7), the order in which a word's nibble pairs come
-// out, so that lane (q, c) loads its 16 k of a token as two 16-byte words and
-// uses them as mma B fragments unchanged; 8-bit chunks stay in k order.
+// Memory pipeline, per block of 2 groups (128 k): the CTA's packed weight
+// rows and the activations x [M][128] stream into a kTcsStages-deep ring in
+// shared memory by cp.async (16-byte copies, no multicast), kTcsStages - 1
+// blocks ahead; scales and biases come through registers one block ahead.
+// Per block one pass moves the activations from the ring into a
+// double-buffered compute tile (16-byte chunks XOR-swizzled by row % 8) and
+// forms the per-(token, group) sums with 8-lane shuffles; for 4-bit weights
+// each 8-value chunk is stored in the order (k0,k4,k1,k5,k2,k6,k3,k7), the
+// order in which a word's nibble pairs come out, so that lane (q, c) loads its
+// 16 k of a token as two 16-byte words and uses them as mma B fragments
+// unchanged (8-bit chunks stay in k order).  Two barriers per block.
 //
 // Numerics: fp32 tensor-core products of exact codes, per group the term
 // s * dot + b * xsum added into the row's accumulator in ascending group
@@ -34,20 +37,43 @@
 
 #include "qmv_tc.cuh"
 
+
 namespace lmx {
 
 static constexpr int kTcsWarps = 8;
 static constexpr int kTcsRows = 16 * kTcsWarps;  // weight rows per CTA
 static constexpr int kTcsMaxSplit = 8;
+static constexpr int kTcsStages = 4;             // ring depth (blocks of 2 groups)
 
-// Dynamic shared memory: two activation blocks [2 groups][R rows][128 B]
-// (the [128][R + 1] fp32 partial tile reuses them after the main loop), then
-// two group-sum blocks [2 groups][R] floats.
-__host__ __device__ constexpr size_t tcs_tile_bytes(int R) {
-  return (size_t)2 * 2 * R * 128 > (size_t)kTcsRows * (R + 1) * 4 ? (size_t)2 * 2 * R * 128
-                                                                   : (size_t)kTcsRows * (R + 1) * 4;
+LMX_DEV void tcs_cp16(uint32_t dst, const void* src, uint32_t bytes) {
+  // bytes 0: the 16 bytes are zero-filled and nothing is read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
-__host__ __device__ constexpr size_t tcs_smem(int R) { return tcs_tile_bytes(R) + (size_t)2 * 2 * R * 4; }
+LMX_DEV void tcs_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LMX_DEV void tcs_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared-memory layout (bytes) for R token rows and BITS-bit weights:
+//   ring[kTcsStages]: weights [8 tiles][2 groups][16 rows][8 BITS bytes],
+//                     activations [2 groups][R rows][128 B]
+//   compute tile [2][2 groups][R rows][128 B]  (the [128][R + 1] fp32 partial
+//                     tile reuses ring + compute tile after the main loop)
+//   group sums [2][2 groups][R] fp32, scales / biases [kTcsStages][8][2][16] u32
+__host__ __device__ constexpr size_t tcs_w_stage(int bits) { return (size_t)kTcsRows * 2 * 8 * bits; }
+__host__ __device__ constexpr size_t tcs_x_stage(int R) { return (size_t)2 * R * 128; }
+__host__ __device__ constexpr size_t tcs_ring_bytes(int R, int bits) {
+  return (size_t)kTcsStages * (tcs_w_stage(bits) + tcs_x_stage(R));
+}
+__host__ __device__ constexpr size_t tcs_main_bytes(int R, int bits) {
+  return tcs_ring_bytes(R, bits) + (size_t)2 * tcs_x_stage(R);
+}
+__host__ __device__ constexpr size_t tcs_smem(int R, int bits) {
+  return (tcs_main_bytes(R, bits) > (size_t)kTcsRows * (R + 1) * 4 ? tcs_main_bytes(R, bits)
+                                                                  : (size_t)kTcsRows * (R + 1) * 4) +
+         (size_t)2 * 2 * R * 4 + (size_t)kTcsStages * kTcsRows * 2 * 4;
+}
 
 template <int BITS, int NT>
 __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
@@ -56,83 +82,131 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
   constexpr int WPG = 2 * BITS;  // words per group and weight row
   constexpr int LW = BITS / 2;   // words per group, row and lane
   constexpr int RS = R + 1;      // padded token stride of the partial tile
+  constexpr size_t WST = tcs_w_stage(BITS), XST = tcs_x_stage(R);
+  constexpr size_t MAINB = tcs_main_bytes(R, BITS);
+  constexpr size_t TAIL = MAINB > (size_t)kTcsRows * RS * 4 ? MAINB : (size_t)kTcsRows * RS * 4;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* xs_tile = smem;                                              // [2][2][R][128 B]
-  float* red = reinterpret_cast<float*>(smem);                         // [128][RS] after the loop
-  float* xsum = reinterpret_cast<float*>(smem + tcs_tile_bytes(R));    // [2][2][R]
+  uint8_t* wring = smem;                                       // [S][WST]
+  uint8_t* xring = smem + kTcsStages * WST;                    // [S][XST]
+  uint8_t* xtile = smem + tcs_ring_bytes(R, BITS);             // [2][XST]
+  float* red = reinterpret_cast<float*>(smem);                 // [128][RS] after the loop
+  float* xsum = reinterpret_cast<float*>(smem + TAIL);         // [2][2][R]
+  uint32_t* sbring = reinterpret_cast<uint32_t*>(xsum + 2 * 2 * R);  // [S][8 tiles][2][16]
   __shared__ int tile_mi[kTcsWarps], tile_row0[kTcsWarps];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, q = lane >> 2, c = lane & 3;
   const int rank = ks > 1 ? (int)(blockIdx.x % ks) : 0, ctile = (int)blockIdx.x / ks;
   const bool sw = a.mode == QMM_SWIGLU;
-  int mi = 0, row0 = 0;
-  bool have;
-  if (sw) {
-    mi = warp >> 2;
-    row0 = ctile * (kTcsRows / 2) + 16 * (warp & 3);
-    have = row0 < a.N;
-  } else {
-    have = tcg_tile(a, ctile * kTcsWarps + warp, mi, row0);
+  if (tid < kTcsWarps) {
+    int mi = 0, row0 = 0;
+    bool have;
+    if (sw) {
+      mi = tid >> 2;
+      row0 = ctile * (kTcsRows / 2) + 16 * (tid & 3);
+      have = row0 < a.N;
+    } else {
+      have = tcg_tile(a, ctile * kTcsWarps + tid, mi, row0);
+    }
+    tile_mi[tid] = have ? mi : -1;
+    tile_row0[tid] = row0;
   }
-  if (lane == 0) {
-    tile_mi[warp] = have ? mi : -1;
-    tile_row0[warp] = row0;
-  }
-  const QmmMat& W = mi == 0 ? a.mat[0] : (mi == 1 ? a.mat[1] : a.mat[2]);
-  const int G = a.K / 64, rows = sw ? a.N : W.rows;
+  __syncthreads();
+  const int G = a.K / 64;
   const int g0 = rank * G / ks, g1 = (rank + 1) * G / ks;
   const int nblk = (g1 - g0 + 1) / 2;
-  const int ra = row0 + q, rb = row0 + q + 8;
-  const bool va = have && ra < rows, vb = have && rb < rows;
-  const uint32_t* wa = W.w + (size_t)(va ? ra : 0) * G * WPG + LW * c;
-  const uint32_t* wb = W.w + (size_t)(vb ? rb : 0) * G * WPG + LW * c;
-  const bf16_t* sa_p = W.s + (size_t)(va ? ra : 0) * G;
-  const bf16_t* ba_p = W.b + (size_t)(va ? ra : 0) * G;
-  const bf16_t* sb_p = W.s + (size_t)(vb ? rb : 0) * G;
-  const bf16_t* bb_p = W.b + (size_t)(vb ? rb : 0) * G;
+  const bool have = tile_mi[warp] >= 0;
+  auto mat_of = [&](int mi) -> const QmmMat& { return mi == 0 ? a.mat[0] : (mi == 1 ? a.mat[1] : a.mat[2]); };
+  auto rows_of = [&](int mi) { return sw ? a.N : mat_of(mi).rows; };
 
-  // weights of a block (2 groups) for rows q, q+8, double-buffered by block
-  uint32_t WA[2][2][LW], WB[2][2][LW], SBa[2][2], SBb[2][2];
-  auto load_w = [&](int blk, int u) {
+  // ---- staging of block blk into ring stage st ----
+  // Each thread's copies are fixed for the whole K range: its weight chunks
+  // (tile, group, row, 16-byte part) and activation chunks (group, token,
+  // 16-byte part) differ between blocks only by the group offset, so the row
+  // addresses and validity are formed once here.
+  constexpr int CH16 = WPG * 4 / 16;  // 16-byte chunks per weight row and group
+  constexpr int WITEM = kTcsWarps * 2 * 16 * CH16;
+  constexpr int XITEM = 2 * R * 8;
+  constexpr int NWI = (WITEM + 255) / 256, NXI = (XITEM + 255) / 256;
+  const uint32_t* wsrc[NWI];  // row start + the chunk's word offset, nullptr when invalid
+  uint32_t wdst[NWI];
+  int wgg[NWI];
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-      const int g = g0 + 2 * blk + gg;
-      const bool ua = va && blk < nblk && g < g1, ub = vb && blk < nblk && g < g1;
-      if constexpr (BITS == 4) {
-        const uint2 x0 = ua ? *reinterpret_cast<const uint2*>(wa + (size_t)g * WPG) : make_uint2(0, 0);
-        const uint2 x1 = ub ? *reinterpret_cast<const uint2*>(wb + (size_t)g * WPG) : make_uint2(0, 0);
-        WA[u][gg][0] = x0.x, WA[u][gg][1] = x0.y, WB[u][gg][0] = x1.x, WB[u][gg][1] = x1.y;
-      } else {
-        const uint4 x0 = ua ? *reinterpret_cast<const uint4*>(wa + (size_t)g * WPG) : make_uint4(0, 0, 0, 0);
-        const uint4 x1 = ub ? *reinterpret_cast<const uint4*>(wb + (size_t)g * WPG) : make_uint4(0, 0, 0, 0);
-        WA[u][gg][0] = x0.x, WA[u][gg][1] = x0.y, WA[u][gg][2] = x0.z, WA[u][gg][3] = x0.w;
-        WB[u][gg][0] = x1.x, WB[u][gg][1] = x1.y, WB[u][gg][2] = x1.z, WB[u][gg][3] = x1.w;
-      }
-      SBa[u][gg] = ua ? ((uint32_t)sa_p[g] | ((uint32_t)ba_p[g] << 16)) : 0u;
-      SBb[u][gg] = ub ? ((uint32_t)sb_p[g] | ((uint32_t)bb_p[g] << 16)) : 0u;
+  for (int i = 0; i < NWI; ++i) {
+    const int e = tid + 256 * i;
+    const int h = e % CH16, r = (e / CH16) & 15, gg = (e / (CH16 * 16)) & 1, w = e / (CH16 * 32);
+    wsrc[i] = nullptr;
+    wdst[i] = (uint32_t)((((w * 2 + gg) * 16 + r) * WPG * 4) + 16 * h);
+    wgg[i] = gg;
+    if (e < WITEM) {
+      const int mi = tile_mi[w], row = tile_row0[w] + r;
+      if (mi >= 0 && row < rows_of(mi)) wsrc[i] = mat_of(mi).w + (size_t)row * G * WPG + 4 * h;
+    } else {
+      wdst[i] = 0xFFFFFFFFu;
+    }
+  }
+  const bf16_t* xsrc[NXI];  // token row + the chunk's offset, nullptr when the token is padding
+  uint32_t xdst[NXI];
+  int xgg[NXI];
+#pragma unroll
+  for (int i = 0; i < NXI; ++i) {
+    const int e = tid + 256 * i, gg = e / (R * 8), n = (e >> 3) % R, j = e & 7;
+    xsrc[i] = (e < XITEM && n < a.M) ? a.x + (size_t)n * a.ldx + 8 * j : nullptr;
+    xdst[i] = e < XITEM ? (uint32_t)((gg * R + n) * 128 + 16 * j) : 0xFFFFFFFFu;
+    xgg[i] = gg;
+  }
+  auto issue_w = [&](int blk, int st) {
+    const uint32_t base = smem_u32(wring + (size_t)st * WST);
+#pragma unroll
+    for (int i = 0; i < NWI; ++i) {
+      if (wdst[i] == 0xFFFFFFFFu) continue;
+      const int g = g0 + 2 * blk + wgg[i];
+      const bool v = wsrc[i] != nullptr && g < g1;
+      tcs_cp16(base + wdst[i], v ? wsrc[i] + (size_t)g * WPG : a.mat[0].w, v ? 16u : 0u);
     }
   };
-
-  // activations: item e = (group gg, token row n, 16-byte chunk j) of a block
-  constexpr int NITEM = 2 * R * 8;
-  constexpr int NI = (NITEM + 255) / 256;
-  uint4 XR[NI];
-  auto load_x = [&](int blk) {
+  auto issue_x = [&](int blk, int st) {
+    const uint32_t base = smem_u32(xring + (size_t)st * XST);
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      const int e = tid + 256 * i, gg = e / (R * 8), n = (e >> 3) % R, j = e & 7;
-      const int g = g0 + 2 * blk + gg;
-      XR[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (e < NITEM && blk < nblk && g < g1 && n < a.M)
-        XR[i] = __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)n * a.ldx + (size_t)g * 64 + 8 * j));
+    for (int i = 0; i < NXI; ++i) {
+      if (xdst[i] == 0xFFFFFFFFu) continue;
+      const int g = g0 + 2 * blk + xgg[i];
+      const bool v = xsrc[i] != nullptr && g < g1;
+      tcs_cp16(base + xdst[i], v ? xsrc[i] + (size_t)g * 64 : a.x, v ? 16u : 0u);
     }
   };
-  // store block `u` (swizzled, 4-bit: nibble-pair order) and its group sums
-  auto store_x = [&](int u) {
+  auto issue = [&](int blk, int st) {
+    if (blk < nblk) {  // past the CTA's range: an empty group keeps the count
+      issue_w(blk, st);
+      issue_x(blk, st);
+    }
+    tcs_commit();
+  };
+  // scale | bias << 16 of one (tile, group, row) per thread
+  const bf16_t *sbs = nullptr, *sbb = nullptr;
+  {
+    const int w = tid >> 5, r = tid & 15, mi = tile_mi[w], row = tile_row0[w] + r;
+    if (mi >= 0 && row < rows_of(mi)) {
+      sbs = mat_of(mi).s + (size_t)row * G;
+      sbb = mat_of(mi).b + (size_t)row * G;
+    }
+  }
+  const int sbgg = (tid >> 4) & 1;
+  auto load_sb = [&](int blk) -> uint32_t {
+    const int g = g0 + 2 * blk + sbgg;
+    if (!sbs || g >= g1 || blk >= nblk) return 0u;
+    return (uint32_t)sbs[g] | ((uint32_t)sbb[g] << 16);
+  };
+  auto store_sb = [&](int st, uint32_t v) { sbring[(st * kTcsWarps + (tid >> 5)) * 32 + (tid & 31)] = v; };
+
+  // ring stage st -> compute tile u (swizzled, 4-bit: nibble-pair order) and
+  // the per-(group, token) sums of x
+  auto stage_x = [&](int st, int u) {
+    const uint8_t* xr = xring + (size_t)st * XST;
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
+    for (int i = 0; i < (XITEM + 255) / 256; ++i) {
       const int e = tid + 256 * i, gg = e / (R * 8), n = (e >> 3) % R, j = e & 7;
-      const uint4 v = XR[i];
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (e < XITEM) v = *reinterpret_cast<const uint4*>(xr + (gg * R + n) * 128 + 16 * j);
       float sum = 0.0f;
       sum = __fadd_rn(sum, lo_bf(v.x)), sum = __fadd_rn(sum, hi_bf(v.x));
       sum = __fadd_rn(sum, lo_bf(v.y)), sum = __fadd_rn(sum, hi_bf(v.y));
@@ -142,7 +216,7 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
-      if (e < NITEM) {
+      if (e < XITEM) {
         uint4 o = v;
         if constexpr (BITS == 4) {
           o.x = __byte_perm(v.x, v.z, 0x5410);  // (k0, k4)
@@ -150,7 +224,7 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
           o.z = __byte_perm(v.y, v.w, 0x5410);  // (k2, k6)
           o.w = __byte_perm(v.y, v.w, 0x7632);  // (k3, k7)
         }
-        *reinterpret_cast<uint4*>(xs_tile + ((size_t)(u * 2 + gg) * R + n) * 128 + ((j ^ (n & 7)) << 4)) = o;
+        *reinterpret_cast<uint4*>(xtile + (size_t)u * XST + (gg * R + n) * 128 + ((j ^ (n & 7)) << 4)) = o;
         if (j == 0) xsum[(u * 2 + gg) * R + n] = sum;
       }
     }
@@ -163,8 +237,8 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
     for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
   const uint32_t one2 = 0x3F803F80u, m128 = 0xC300C300u;
 
-  // one group: codes -> exact bf16 A fragments, products per token tile,
-  // then acc += s * dot + b * xsum for rows q (e = 0, 1) and q + 8 (e = 2, 3)
+  // one group of this warp's tile: codes -> exact bf16 A fragments, products
+  // per token tile, acc += s * dot + b * xsum (rows q: e = 0, 1; q+8: e = 2, 3)
   auto group = [&](const uint8_t* xt, const float* xsm, const uint32_t (&A)[LW], const uint32_t (&B)[LW],
                    uint32_t pa, uint32_t pb) {
     uint32_t af[4][4];
@@ -201,36 +275,58 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
       acc[t][3] = __fmaf_rn(sb, dot[3], __fmaf_rn(bb, xs.y, acc[t][3]));
     }
   };
-
-  // block blk from buffer u (a literal at each call): stage it, one barrier,
-  // prefetch the next block's activations and weights, run its groups
-  auto step = [&](const int blk, const int u) {
-    store_x(u);
-    __syncthreads();
-    if (blk + 1 < nblk) {
-      load_x(blk + 1);
-      load_w(blk + 1, u ^ 1);
-    }
-    if (have) {
+  auto compute = [&](int blk, int u, int st) {
 #pragma unroll
-      for (int gg = 0; gg < 2; ++gg)
-        if (g0 + 2 * blk + gg < g1)
-          group(xs_tile + (size_t)(u * 2 + gg) * R * 128, xsum + (u * 2 + gg) * R, WA[u][gg], WB[u][gg], SBa[u][gg],
-                SBb[u][gg]);
+    for (int gg = 0; gg < 2; ++gg) {
+      if (g0 + 2 * blk + gg >= g1) break;
+      const uint8_t* wr = wring + (size_t)st * WST + (size_t)(warp * 2 + gg) * 16 * WPG * 4 + 4 * LW * c;
+      uint32_t A[LW], B[LW];
+      if constexpr (BITS == 4) {
+        const uint2 x0 = *reinterpret_cast<const uint2*>(wr + q * WPG * 4);
+        const uint2 x1 = *reinterpret_cast<const uint2*>(wr + (q + 8) * WPG * 4);
+        A[0] = x0.x, A[1] = x0.y, B[0] = x1.x, B[1] = x1.y;
+      } else {
+        const uint4 x0 = *reinterpret_cast<const uint4*>(wr + q * WPG * 4);
+        const uint4 x1 = *reinterpret_cast<const uint4*>(wr + (q + 8) * WPG * 4);
+        A[0] = x0.x, A[1] = x0.y, A[2] = x0.z, A[3] = x0.w;
+        B[0] = x1.x, B[1] = x1.y, B[2] = x1.z, B[3] = x1.w;
+      }
+      const uint32_t* sbp = sbring + (st * kTcsWarps + warp) * 32 + gg * 16;
+      group(xtile + (size_t)u * XST + (size_t)gg * R * 128, xsum + (u * 2 + gg) * R, A, B, sbp[q], sbp[q + 8]);
     }
   };
 
-  load_w(0, 0);  // weights do not depend on the previous kernel
+  // prologue: the first blocks' weights and scales do not depend on the
+  // previous kernel and are requested before waiting for it
+  uint32_t sb0[kTcsStages - 1];
+#pragma unroll
+  for (int b = 0; b < kTcsStages - 1; ++b) {
+    if (b < nblk) issue_w(b, b);
+    sb0[b] = load_sb(b);
+  }
   grid_wait();
   grid_launch_dependents();
-  load_x(0);
-  for (int blk = 0; blk < nblk; blk += 2) {
-    step(blk, 0);
-    if (blk + 1 < nblk) step(blk + 1, 1);
+#pragma unroll
+  for (int b = 0; b < kTcsStages - 1; ++b) {
+    if (b < nblk) issue_x(b, b);
+    tcs_commit();
+    store_sb(b, sb0[b]);
   }
+  uint32_t sbv = 0u;
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int st = blk % kTcsStages, u = blk & 1;
+    tcs_wait<kTcsStages - 2>();  // this thread's copies of block blk have landed
+    __syncthreads();             // everyone's have; every warp is done with block blk - 1
+    if (blk > 0) store_sb((blk + kTcsStages - 2) % kTcsStages, sbv);
+    sbv = load_sb(blk + kTcsStages - 1);
+    issue(blk + kTcsStages - 1, (blk + kTcsStages - 1) % kTcsStages);
+    stage_x(st, u);
+    __syncthreads();
+    if (have) compute(blk, u, st);
+  }
+  tcs_wait<0>();  // no copy may land on the partial tile below
 
-  // partial tile [128 rows][R tokens] over the activation blocks (every warp
-  // is past its last read of them after this barrier)
+  // partial tile [128 rows][R tokens] over the shared memory used above
   __syncthreads();
   if (have) {
 #pragma unroll
@@ -255,7 +351,7 @@ __global__ void __launch_bounds__(256) qmm_tcs_kernel(QmmArgs a, int ks) {
     const int w = r >> 4, wm = tile_mi[w];
     if (wm < 0) continue;
     const int row = tile_row0[w] + (r & 15);
-    if (row >= (sw ? a.N : (wm == 0 ? a.mat[0].rows : (wm == 1 ? a.mat[1].rows : a.mat[2].rows)))) continue;
+    if (row >= rows_of(wm)) continue;
     float s0 = 0.0f, s1 = 0.0f;
     for (int k = 0; k < ks; ++k) {
       const float* rr = ks > 1 ? cluster.map_shared_rank(red, k) : red;
