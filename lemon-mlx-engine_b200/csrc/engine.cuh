@@ -1048,7 +1048,7 @@ static int spec_step(Spec& sp) {
     if (stoch) {
       rc = forward(*sp.dm, *sp.dc, sp.dl, tok, ld, off, B, T, sp.ws, sp.s.qlog + (size_t)i * V, true, st, K * V);
       if (!rc)
-        rc = cuda_check(samp_launch(draft_sample_kernel, B, st,
+        rc = cuda_check(samp_launch(draft_sample_kernel, B, V, 1, st,
                                    (const bf16_t*)sp.s.qlog, V, sp.s, stoch_params(sp), i, T),
                         "draft_sample");
     } else {
@@ -1059,7 +1059,7 @@ static int spec_step(Spec& sp) {
   if (!rc) rc = forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
   if (stoch) {
     if (!rc)
-      rc = cuda_check(samp_launch(accept_stochastic_kernel, B, st,
+      rc = cuda_check(samp_launch(accept_stochastic_kernel, B, V, 2, st,
                                  (const bf16_t*)sp.ws.logits, V, sp.s, stoch_params(sp)),
                       "accept_stochastic");
   } else {
@@ -1219,7 +1219,7 @@ static int spec_prefill(Spec& sp, const int32_t* prompts_host) {
   if (!rc) rc = cache_fill_synthetic(dpre, ctx, sp.cfg.context_seed, kCtxTidDraft, st);
   if (!rc) rc = forward_chunked(*sp.tm, tpre, sp.tm->n_layers, sp.prompts, P, P, B, sp.ws, sp.ws.logits, st);
   if (!rc && sp.cfg.temperature > 0.0f)
-    rc = cuda_check(samp_launch(sample_rows_kernel, B, st,
+    rc = cuda_check(samp_launch(sample_rows_kernel, B, sp.tm->c.vocab, 1, st,
                                (const bf16_t*)sp.ws.logits, sp.tm->c.vocab, sp.tm->c.vocab, stoch_params(sp),
                                0u, 0u, 3u, sp.yprefill),
                     "prefill sample");
@@ -1989,7 +1989,7 @@ extern "C" int lmx_sample(const void* logits, int rows, int V, float temperature
   if (!logits || !out || rows < 0 || V < 1) return set_error(LMX_ERR_INVALID, "sample: bad arguments");
   if (!(temperature > 0.0f)) return launch_argmax((const bf16_t*)logits, rows, V, out, (cudaStream_t)stream);
   if (!u24) return set_error(LMX_ERR_INVALID, "sample: uniforms required when temperature > 0");
-  return cuda_check(samp_launch(sample_u_kernel, rows, (cudaStream_t)stream,
+  return cuda_check(samp_launch(sample_u_kernel, rows, V, 1, (cudaStream_t)stream,
                                (const bf16_t*)logits, V, temperature, top_p, u24, out),
                     "sample");
 }
@@ -2003,7 +2003,7 @@ extern "C" int lmx_spec_accept(const void* target_logits, const void* draft_logi
   if (!(temperature > 0.0f))
     return set_error(LMX_ERR_INVALID, "spec_accept: greedy acceptance runs inside lmx_spec_decode");
   if (!draft_logits || !u_accept || !u_final) return set_error(LMX_ERR_INVALID, "spec_accept: null argument");
-  return cuda_check(samp_launch(accept_u_kernel, B, (cudaStream_t)stream,
+  return cuda_check(samp_launch(accept_u_kernel, B, V, 2, (cudaStream_t)stream,
                                (const bf16_t*)target_logits, (const bf16_t*)draft_logits, drafts, K, V, temperature,
                                top_p, u_accept, u_final, n_accepted, out_tokens),
                     "spec_accept");

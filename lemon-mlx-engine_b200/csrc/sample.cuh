@@ -84,8 +84,54 @@ LMX_DEV T* cl_peer(T* p, int rank) {
   return cooperative_groups::this_cluster().map_shared_rank(p, rank);
 }
 
-LMX_DEV uint64_t dist_w(const bf16_t* l, int j, float mx, float inv_t) {
-  const float v = bf2f(l[j]);
+// A row of logits as a CTA reads it: its own slice [v0, v1) staged once in
+// shared memory (every pass over the slice reads it from there), any other
+// index from global memory.
+struct Row {
+  const bf16_t* g;
+  const bf16_t* s;
+  int v0, v1;
+};
+
+LMX_DEV float row_at(const Row& r, int j) { return bf2f(j >= r.v0 && j < r.v1 ? r.s[j - r.v0] : r.g[j]); }
+
+// Bytes of shared memory for `n` staged row slices of a V-wide row.
+__host__ __device__ inline size_t samp_row_bytes(int V, int n) {
+  const size_t per = (size_t)(V + kSampCluster - 1) / kSampCluster;
+  return ((per * 2 + 15) / 16 * 16) * (size_t)n;
+}
+
+// Stage this CTA's slice of row g into s (every load of a batch in flight
+// before the stores); a barrier before (the previous row in s may still be
+// read) and after.
+LMX_DEV Row stage_row(const bf16_t* g, bf16_t* s, const Cl& c) {
+  constexpr int U = 20;
+  const int n = c.v1 - c.v0;
+  __syncthreads();
+  for (int base = 0; base < n; base += U * kSampThreads) {
+    uint16_t r[U];
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const int k = base + (int)threadIdx.x + i * kSampThreads;
+      r[i] = k < n ? reinterpret_cast<const uint16_t*>(g)[c.v0 + k] : (uint16_t)0;
+    }
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const int k = base + (int)threadIdx.x + i * kSampThreads;
+      if (k < n) reinterpret_cast<uint16_t*>(s)[k] = r[i];
+    }
+  }
+  __syncthreads();
+  Row row;
+  row.g = g;
+  row.s = s;
+  row.v0 = c.v0;
+  row.v1 = c.v1;
+  return row;
+}
+
+LMX_DEV uint64_t dist_w(const Row& l, int j, float mx, float inv_t) {
+  const float v = row_at(l, j);
   if (v != v) return 0;
   const float e = exp_c(__fmul_rn(__fsub_rn(v, mx), inv_t));
   return __float2ull_rn(__fmul_rn(e, 4294967296.0f));
@@ -239,12 +285,12 @@ LMX_DEV int cl_pick(int mine, int fall, Cl& c, SampScratch& sm) {
 }
 
 // Build the (temperature, top-p) distribution of one logits row.
-LMX_DEV void make_dist_dev(const bf16_t* l, int V, float temperature, float top_p, Dist& D, Cl& c,
+LMX_DEV void make_dist_dev(const Row& l, int V, float temperature, float top_p, Dist& D, Cl& c,
                            SampScratch& sm) {
   const int tid = threadIdx.x;
   float mx = -INFINITY;
   for (int j = c.v0 + tid; j < c.v1; j += kSampThreads) {
-    const float v = bf2f(l[j]);
+    const float v = row_at(l, j);
     if (v == v) mx = fmaxf(mx, v);
   }
   D.mx = cl_max(mx, c, sm);
@@ -344,7 +390,7 @@ LMX_DEV void chunk_of(const Cl& c, int& c0, int& c1) {
 }
 
 // Exclusive count of weight-tau ties before each thread's chunk (row order).
-LMX_DEV uint64_t tie_prefix(const bf16_t* l, const Dist& D, Cl& c, SampScratch& sm, uint64_t* buf) {
+LMX_DEV uint64_t tie_prefix(const Row& l, const Dist& D, Cl& c, SampScratch& sm, uint64_t* buf) {
   int c0, c1;
   chunk_of(c, c0, c1);
   uint64_t n = 0;
@@ -354,7 +400,7 @@ LMX_DEV uint64_t tie_prefix(const bf16_t* l, const Dist& D, Cl& c, SampScratch& 
 }
 
 // Draw by inverse CDF over kept weights in index order.
-LMX_DEV int draw_dev(const bf16_t* l, const Dist& D, uint32_t u24, Cl& c, SampScratch& sm) {
+LMX_DEV int draw_dev(const Row& l, const Dist& D, uint32_t u24, Cl& c, SampScratch& sm) {
   int c0, c1;
   chunk_of(c, c0, c1);
   uint64_t ties = tie_prefix(l, D, c, sm, sm.tscan);
@@ -394,7 +440,7 @@ LMX_DEV int draw_dev(const bf16_t* l, const Dist& D, uint32_t u24, Cl& c, SampSc
 }
 
 // Kept weight of token d (0 if outside the top-p set).
-LMX_DEV uint64_t kept_weight_of(const bf16_t* l, const Dist& D, int d, Cl& c, SampScratch& sm) {
+LMX_DEV uint64_t kept_weight_of(const Row& l, const Dist& D, int d, Cl& c, SampScratch& sm) {
   const uint64_t w = dist_w(l, d, D.mx, D.inv_t);
   if (!D.topp || w > D.tau) return w;
   if (w < D.tau) return 0;
@@ -406,7 +452,7 @@ LMX_DEV uint64_t kept_weight_of(const bf16_t* l, const Dist& D, int d, Cl& c, Sa
 
 // Residual draw r_j = max(0, p_j Zq - q_j Zp) by inverse CDF with u24;
 // returns -1 if R == 0.
-LMX_DEV int residual_draw_dev(const bf16_t* lp, const Dist& P, const bf16_t* lq, const Dist& Q, uint32_t u24,
+LMX_DEV int residual_draw_dev(const Row& lp, const Dist& P, const Row& lq, const Dist& Q, uint32_t u24,
                               Cl& c, SampScratch& sm) {
   int c0, c1;
   chunk_of(c, c0, c1);
@@ -459,11 +505,29 @@ struct StochParams {
 
 // Cluster launch of a sampling kernel over `rows` rows, with programmatic
 // dependent launch like every other kernel of the library.
+// nrow: row slices staged at once (2 for the acceptance kernels).
 template <typename Kern, typename... Args>
-static inline cudaError_t samp_launch(Kern kern, int rows, cudaStream_t st, Args... args) {
+static inline cudaError_t samp_launch(Kern kern, int rows, int V, int nrow, cudaStream_t st, Args... args) {
+  const size_t dyn = samp_row_bytes(V, nrow);
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> set;  // (kernel, device) -> bytes allowed
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    size_t& have = set[{(const void*)kern, dev}];
+    // static scratch + staged rows may exceed the 48 KB default: always
+    // raise the kernel's dynamic limit to what this launch needs
+    if (dyn > have) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+      if (e != cudaSuccess) return e;
+      have = dyn;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(rows * kSampCluster);
   cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = dyn;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -486,11 +550,12 @@ __global__ void __launch_bounds__(kSampThreads) sample_rows_kernel(const bf16_t*
                                                                    uint32_t slot, uint32_t stream,
                                                                    int32_t* out) {
   __shared__ SampScratch sm;
+  extern __shared__ __align__(128) uint8_t smem[];
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x / kSampCluster;
   Cl c = cl_make(V);
-  const bf16_t* l = logits + (size_t)b * ld;
+  const Row l = stage_row(logits + (size_t)b * ld, reinterpret_cast<bf16_t*>(smem), c);
   Dist D;
   make_dist_dev(l, V, sp.temperature, sp.top_p, D, c, sm);
   const int t = draw_dev(l, D, uniform24(sp.seed, sp.seq_base + b, step, slot, stream), c, sm);
@@ -509,11 +574,12 @@ namespace lmx {
 __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(const bf16_t* qlog, int V, SpecState s,
                                                                     StochParams sp, int i, int adv) {
   __shared__ SampScratch sm;
+  extern __shared__ __align__(128) uint8_t smem[];
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x / kSampCluster;
   Cl c = cl_make(V);
-  const bf16_t* l = qlog + ((size_t)b * s.K + i) * V;
+  const Row l = stage_row(qlog + ((size_t)b * s.K + i) * V, reinterpret_cast<bf16_t*>(smem), c);
   Dist D;
   make_dist_dev(l, V, sp.temperature, sp.top_p, D, c, sm);
   const int tok = draw_dev(l, D, uniform24(sp.seed, sp.seq_base + b, (uint32_t)s.ustep[b], i, 0), c, sm);
@@ -534,6 +600,9 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(const bf16_t
 __global__ void __launch_bounds__(kSampThreads) accept_stochastic_kernel(const bf16_t* tlog, int V, SpecState s,
                                                                          StochParams sp) {
   __shared__ SampScratch sm;
+  extern __shared__ __align__(128) uint8_t smem[];
+  bf16_t* rp_s = reinterpret_cast<bf16_t*>(smem);
+  bf16_t* rq_s = reinterpret_cast<bf16_t*>(smem + samp_row_bytes(V, 1));
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x / kSampCluster, K = s.K;
@@ -550,8 +619,8 @@ __global__ void __launch_bounds__(kSampThreads) accept_stochastic_kernel(const b
   const uint32_t uf = uniform24(sp.seed, sp.seq_base + b, step, 0, 2);
   int acc = K, next = -1;
   for (int i = 0; i < K; ++i) {
-    const bf16_t* lp = tlog + ((size_t)b * (K + 1) + i) * V;
-    const bf16_t* lq = s.qlog + ((size_t)b * K + i) * V;
+    const Row lp = stage_row(tlog + ((size_t)b * (K + 1) + i) * V, rp_s, c);
+    const Row lq = stage_row(s.qlog + ((size_t)b * K + i) * V, rq_s, c);
     Dist P, Q;
     make_dist_dev(lp, V, sp.temperature, sp.top_p, P, c, sm);
     make_dist_dev(lq, V, sp.temperature, sp.top_p, Q, c, sm);
@@ -565,7 +634,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_stochastic_kernel(const b
     break;
   }
   if (acc == K) {
-    const bf16_t* lp = tlog + ((size_t)b * (K + 1) + K) * V;
+    const Row lp = stage_row(tlog + ((size_t)b * (K + 1) + K) * V, rp_s, c);
     Dist P;
     make_dist_dev(lp, V, sp.temperature, sp.top_p, P, c, sm);
     next = draw_dev(lp, P, uf, c, sm);
@@ -582,11 +651,12 @@ namespace lmx {
 __global__ void __launch_bounds__(kSampThreads) sample_u_kernel(const bf16_t* logits, int V, float temperature,
                                                                 float top_p, const uint32_t* u24, int32_t* out) {
   __shared__ SampScratch sm;
+  extern __shared__ __align__(128) uint8_t smem[];
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x / kSampCluster;
   Cl c = cl_make(V);
-  const bf16_t* l = logits + (size_t)b * V;
+  const Row l = stage_row(logits + (size_t)b * V, reinterpret_cast<bf16_t*>(smem), c);
   Dist D;
   make_dist_dev(l, V, temperature, top_p, D, c, sm);
   const int t = draw_dev(l, D, u24[b] & 0xFFFFFFu, c, sm);
@@ -600,6 +670,9 @@ __global__ void __launch_bounds__(kSampThreads) accept_u_kernel(const bf16_t* tl
                                                                 const uint32_t* u_accept, const uint32_t* u_final,
                                                                 int32_t* n_accepted, int32_t* out_tokens) {
   __shared__ SampScratch sm;
+  extern __shared__ __align__(128) uint8_t smem[];
+  bf16_t* rp_s = reinterpret_cast<bf16_t*>(smem);
+  bf16_t* rq_s = reinterpret_cast<bf16_t*>(smem + samp_row_bytes(V, 1));
   grid_wait();
   grid_launch_dependents();
   const int b = blockIdx.x / kSampCluster;
@@ -607,8 +680,8 @@ __global__ void __launch_bounds__(kSampThreads) accept_u_kernel(const bf16_t* tl
   const uint32_t uf = u_final[b] & 0xFFFFFFu;
   int acc = K, next = -1;
   for (int i = 0; i < K; ++i) {
-    const bf16_t* lp = tlog + ((size_t)b * (K + 1) + i) * V;
-    const bf16_t* lq = qlog + ((size_t)b * K + i) * V;
+    const Row lp = stage_row(tlog + ((size_t)b * (K + 1) + i) * V, rp_s, c);
+    const Row lq = stage_row(qlog + ((size_t)b * K + i) * V, rq_s, c);
     Dist P, Q;
     make_dist_dev(lp, V, temperature, top_p, P, c, sm);
     make_dist_dev(lq, V, temperature, top_p, Q, c, sm);
@@ -625,7 +698,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_u_kernel(const bf16_t* tl
     break;
   }
   if (acc == K) {
-    const bf16_t* lp = tlog + ((size_t)b * (K + 1) + K) * V;
+    const Row lp = stage_row(tlog + ((size_t)b * (K + 1) + K) * V, rp_s, c);
     Dist P;
     make_dist_dev(lp, V, temperature, top_p, P, c, sm);
     next = draw_dev(lp, P, uf, c, sm);
