@@ -530,7 +530,10 @@ def run_lmx(args, wl, world, rank, local):
         comm = lmx.TpComm.from_process_group(max_rows=B * 32, max_hidden=arch["hidden"])
     target = lmx.Model(arch, args.seed, comm=comm)
     # separate draft model (seed + 1) or the target's first layers (self-draft)
-    draft = lmx.Model(darch, args.seed + 1) if darch else None
+    # tensor parallel: the draft is this rank's shard over the same
+    # communicator (--replicated-draft: a whole copy on every rank)
+    shard_draft = comm is not None and darch is not None and not args.replicated_draft
+    draft = lmx.Model(darch, args.seed + 1, comm=comm if shard_draft else None) if darch else None
     # one seeded prompt array for the whole job (split: this rank's slice of
     # it; tensor parallel: all of it on every rank); replicas: per-rank seeds
     replicas = not tp and world > 1 and not split
@@ -594,7 +597,7 @@ def run_lmx(args, wl, world, rank, local):
     # tensor parallel: every rank emits the same tokens
     toks_all = toks if tp else int(reduce(world, [float(toks)], "sum")[0])
     if tp:
-        par, scaling = f"tp{world} (target sharded, draft replicated)", "strong"
+        par, scaling = f"tp{world} (target sharded, draft {'sharded' if shard_draft else 'replicated'})", "strong"
     elif split:
         par, scaling = f"dp{world} ({B_all} sequences split over {world} ranks, {B} on rank {rank})", "strong"
     elif world > 1:
@@ -965,6 +968,8 @@ def main():
                                               "12,2048,512,512,10,4)")
     ap.add_argument("--gdn", default="", help="op-level Gated DeltaNet verify + commit B,T,Hk,Hv (configuration 4: "
                                               "4,3,16,32)")
+    ap.add_argument("--replicated-draft", action="store_true",
+                    help="tensor parallel: a whole copy of the draft on every rank instead of its shard")
     ap.add_argument("--gemm-tcs-max-m", type=int, default=-1,
                     help="set lmx_set_gemm_tcs_max_m first: M up to this bound on the mid-batch mma.sync GEMM "
                          "(0: tcgen05 for every M at or above the threshold)")

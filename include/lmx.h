@@ -517,7 +517,10 @@ typedef struct {
   int kv_quirk;
 } lmx_spec_config;
 
-/* draft may be NULL (self-draft: the first draft_layers of target). */
+/* draft may be NULL (self-draft: the first draft_layers of target).  With a
+ * tensor-parallel target (lmx_model_create_tp / lmx_model_load_tp) the draft
+ * is either replicated (a tp 1 model on every rank) or this rank's shard over
+ * the same communicator; both decode greedily. */
 int lmx_spec_create(void* target, void* draft, int draft_layers, const lmx_spec_config* cfg,
                     void** spec);
 int lmx_spec_prefill(void* spec, const int32_t* prompts_host /* [batch, prompt_len] */);

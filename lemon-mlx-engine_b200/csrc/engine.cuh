@@ -1053,7 +1053,15 @@ static int spec_step(Spec& sp) {
                         "draft_sample");
     } else {
       rc = forward(*sp.dm, *sp.dc, sp.dl, tok, ld, off, B, T, sp.ws, sp.ws.logits, true, st);
-      if (!rc) rc = launch_cluster_rows(draft_argmax_kernel, B, sp.ws.logits, V, sp.s, i, T, st);
+      if (sp.dm->tp > 1) {  // vocab-parallel argmax into the (free until the verify) pred rows
+        if (!rc) rc = model_argmax(*sp.dm, sp.ws.logits, B, sp.dm->vl, sp.s.pred, st);
+        if (!rc)
+          rc = cuda_check(lmx_launch(draft_commit_kernel, dim3((B + 127) / 128), dim3(128), 0, st, true, sp.s,
+                                     (const int32_t*)sp.s.pred, i, T),
+                          "draft commit");
+      } else if (!rc) {
+        rc = launch_cluster_rows(draft_argmax_kernel, B, sp.ws.logits, V, sp.s, i, T, st);
+      }
     }
   }
   if (!rc) rc = forward(*sp.tm, *sp.tc, sp.tm->n_layers, sp.s.vt, K + 1, 0, B, K + 1, sp.ws, sp.ws.logits, false, st);
@@ -1096,9 +1104,12 @@ static int spec_create(Model* tm, Model* dm, int dl, const lmx_spec_config& cfg,
   if (cfg.batch < 1 || cfg.K < 0 || cfg.max_tokens < 1 || cfg.prompt_len < 2 || cfg.seq_base < 0)
     return set_error(LMX_ERR_INVALID, "spec: bad config");
   if (dm->c.vocab != tm->c.vocab) return set_error(LMX_ERR_INVALID, "spec: draft and target must share the vocabulary");
-  if (dm->tp > 1) return set_error(LMX_ERR_UNSUPPORTED, "spec: the draft runs replicated (tp 1) on every rank");
-  if (tm->tp > 1 && cfg.temperature > 0.0f)
-    return set_error(LMX_ERR_UNSUPPORTED, "spec: a tensor-parallel target decodes greedily (temperature 0)");
+  // the draft runs replicated (tp 1) on every rank, or as this rank's shard
+  // over the target's communicator
+  if (dm->tp > 1 && (dm->tp != tm->tp || dm->comm != tm->comm))
+    return set_error(LMX_ERR_UNSUPPORTED, "spec: a tensor-parallel draft shares the target's communicator");
+  if ((tm->tp > 1 || dm->tp > 1) && cfg.temperature > 0.0f)
+    return set_error(LMX_ERR_UNSUPPORTED, "spec: tensor-parallel models decode greedily (temperature 0)");
   auto sp = std::make_unique<Spec>();
   sp->tm = tm;
   sp->dm = dm;

@@ -189,6 +189,23 @@ __global__ void __launch_bounds__(512) draft_argmax_kernel(const bf16_t* logits,
   cluster.sync();
 }
 
+// The same bookkeeping for a tensor-parallel draft, whose greedy token per
+// sequence comes from the vocab-parallel argmax (tok[b]): records d_{i+1},
+// advances the draft length and, after the last draft, assembles the verify
+// input.  One thread per sequence.
+__global__ void __launch_bounds__(128) draft_commit_kernel(SpecState s, const int32_t* tok, int i, int adv) {
+  grid_wait();
+  grid_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= s.B) return;
+  s.drafts[b * s.K + i] = tok[b];
+  if (s.emitted[b] < s.max_tokens) s.dlen[b] += adv;
+  if (i == s.K - 1) {
+    s.vt[b * (s.K + 1)] = s.tok2[2 * b + 1];
+    for (int k = 0; k < s.K; ++k) s.vt[b * (s.K + 1) + 1 + k] = s.drafts[b * s.K + k];
+  }
+}
+
 // Emit / commit / rollback shared by the greedy and stochastic acceptance:
 // emit y, d1..d_acc; next y = `next`; target length p+acc+1, draft p+acc.
 LMX_DEV void commit_step(const SpecState& s, int b, int acc, int next) {

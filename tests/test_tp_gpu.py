@@ -137,3 +137,25 @@ def test_tp2_checkpoint_shards_bit_exact(tp2_result):
         O.lib().orc_cache_free(oc)
         O.lib().orc_model_free(o)
         O.lib().orc_set_mma_min_m(16)
+
+
+def test_tp2_sharded_draft_stream_matches_oracle(tp2_result):
+    # the draft as a tensor-parallel shard too (vocab-parallel draft argmax):
+    # the oracle emulates the split in both models
+    O.lib().orc_set_mma_min_m(0)
+    to = O.lib().orc_model_create(C.byref(oracle_cfg(W.TARGET)), W.SEED)
+    do = O.lib().orc_model_create(C.byref(oracle_cfg(W.DRAFT)), W.SEED + 1)
+    assert O.lib().orc_model_set_tp(to, 2) == 0
+    assert O.lib().orc_model_set_tp(do, 2) == 0
+    p = W.prompts()
+    out = np.zeros((W.B, W.MT), np.int32)
+    st = np.zeros(5, np.int64)
+    prm = O.SpecParams(K=W.K, max_tokens=W.MT, temperature=0.0, top_p=1.0, seed=0, draft_layers=1,
+                       context_len=W.CTX, context_seed=W.CTX_SEED)
+    rc = O.lib().orc_spec_generate(to, do, O.ptr(p), W.B, W.P, prm, 8, O.ptr(out), O.ptr(st))
+    O.lib().orc_model_free(to)
+    O.lib().orc_model_free(do)
+    O.lib().orc_set_mma_min_m(16)
+    assert rc == 0
+    np.testing.assert_array_equal(tp2_result["stream_tp_draft"], out)
+    assert int(tp2_result["accepted_tp_draft"]) == st[2]

@@ -6,7 +6,8 @@ Every rank builds its shard of the same seeded models and runs
     vocabulary slice, gathered to rank 0 and concatenated), once per
     tensor-core threshold, and
   * a greedy speculative session: Llama-style target (tensor-parallel) with a
-    replicated draft, 8-bit KV, a synthetic context before the prompt;
+    replicated draft, 8-bit KV, a synthetic context before the prompt, and
+    the same session with the draft sharded over the communicator too;
   * with --ckpt, forwards of a checkpoint loaded as tensor-parallel shards;
 and rank 0 writes everything to --out (.npz) for the parent to compare with
 the oracle's tensor-parallel emulation.  Every rank must produce the same
@@ -117,6 +118,23 @@ def main():
             raise SystemExit(f"rank {r} emitted a different stream than rank 0")
     res["stream"] = out
     res["accepted"] = np.array(stats["accepted"])
+
+    # the same session with the draft sharded over the communicator too
+    tm = lmx.Model(TARGET, SEED, comm=comm)
+    dm = lmx.Model(DRAFT, SEED + 1, comm=comm)
+    sd = lmx.SpecDecoder(tm, dm, 1, B, K, MT, P, kv_bits=8, context_len=CTX, context_seed=CTX_SEED)
+    sd.prefill(prompts())
+    sd.decode()
+    out, stats = sd.result()
+    sd.close()
+    tm.close()
+    dm.close()
+    dist.all_gather_object(streams, out)
+    for r in range(1, world):
+        if not np.array_equal(streams[r], streams[0]):
+            raise SystemExit(f"rank {r} emitted a different stream than rank 0 (tp draft)")
+    res["stream_tp_draft"] = out
+    res["accepted_tp_draft"] = np.array(stats["accepted"])
     dist.barrier()
     comm.close()
     if rank == 0:
