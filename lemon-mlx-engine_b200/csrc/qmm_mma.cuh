@@ -365,12 +365,89 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
       }
     }
     const uint32_t tlane = (uint32_t)(32 * q) << 16;
-    const uint8_t* prow0 = Ps + rr * 128;
+    const uint32_t prow0 = smem_u32(Ps) + (uint32_t)rr * 128u;
     const int sw = rr & 7;
     int sp = 0;
     uint32_t pph = 0;  // parity of the pfull phase of stage sp
     int s = 0;
     uint32_t aph = 0;  // parity of the mdone phase that frees A stage s
+    if constexpr (BITS == 4) {
+      // 4-bit: a packed stage holds four chunks, i.e. exactly two steps, so
+      // a step takes at most one wait per ring, two 16-byte shared loads
+      // (16-byte units 2c+h of the row for its chunks c) and the two groups'
+      // scale / bias words, which are loaded a step ahead
+      const uint32_t pbase = smem_u32(Ps) + (uint32_t)rr * 128u;
+      const uint32_t offs[4] = {(uint32_t)((h ^ sw) << 4), (uint32_t)(((2 + h) ^ sw) << 4),
+                                (uint32_t)(((4 + h) ^ sw) << 4), (uint32_t)(((6 + h) ^ sw) << 4)};
+      const uint32_t tbase = tlane + tmem_a + (uint32_t)(16 * h);
+      const unsigned short* s16 = reinterpret_cast<const unsigned short*>(srow);
+      const unsigned short* b16 = reinterpret_cast<const unsigned short*>(brow);
+      uint32_t ns0 = 0, ns1 = 0, nb0 = 0, nb1 = 0;
+      auto load_sb = [&](int t) {
+        const int kc = kc0 + 2 * t;
+        const bool two = 2 * t + 1 < nloc;
+        ns0 = rvalid ? (uint32_t)__ldg(s16 + kc) : 0u;
+        nb0 = rvalid ? (uint32_t)__ldg(b16 + kc) : 0u;
+        ns1 = rvalid && two ? (uint32_t)__ldg(s16 + kc + 1) : 0u;
+        nb1 = rvalid && two ? (uint32_t)__ldg(b16 + kc + 1) : 0u;
+      };
+      if (nsteps > 0) load_sb(0);
+      for (int t = 0; t < nsteps; ++t) {
+        const uint32_t s20 = ns0 | (ns0 << 16), b20 = nb0 | (nb0 << 16);
+        const uint32_t s21 = ns1 | (ns1 << 16), b21 = nb1 | (nb1 << 16);
+        if (t + 1 < nsteps) load_sb(t + 1);
+        const bool two = 2 * t + 1 < nloc;
+        if (t >= NA && !warp_wait(&mdone[s], aph, a.err, 0x66u)) {
+          ok = false;
+          break;
+        }
+        const int half = t & 1;  // which two chunks of the packed stage
+        if (half == 0 && !warp_wait(&pfull[sp], pph, a.err, 0x65u)) {
+          ok = false;
+          break;
+        }
+        const uint32_t pst = pbase + (uint32_t)(sp * PBYTES);
+        const uint32_t off0 = half ? offs[2] : offs[0], off1 = half ? offs[3] : offs[1];
+        uint32_t w0[4], w1[4] = {0u, 0u, 0u, 0u};
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w0[0]), "=r"(w0[1]), "=r"(w0[2]), "=r"(w0[3])
+                     : "r"(pst + off0));
+        if (two)
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(w1[0]), "=r"(w1[1]), "=r"(w1[2]), "=r"(w1[3])
+                       : "r"(pst + off1));
+        const uint32_t ta = tbase + (uint32_t)(64 * s);
+        {
+          uint32_t o[16];
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) deq8_b4(w0[cc], s20, b20, &o[4 * cc]);
+          tmem_st16(ta, o);
+        }
+        if (two) {
+          uint32_t o[16];
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) deq8_b4(w1[cc], s21, b21, &o[4 * cc]);
+          tmem_st16(ta + 32u, o);
+        }
+        // a stage whose last words are consumed (used above) may be refilled
+        if (half == 1 || t == nsteps - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pfree[sp]);
+          if (++sp == NP) {
+            sp = 0;
+            pph ^= 1u;
+          }
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+        if (++s == NA) {
+          s = 0;
+          if (t >= NA) aph ^= 1u;
+        }
+      }
+    } else {
     // one step (kMmaStep chunks) at a time: every wait and shared-memory load
     // of the step first, then dequantization and TMEM stores chunk by chunk
     // (the loads of the second chunk overlap the first one's work)
@@ -411,15 +488,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
           continue;
         }
         // 16-byte units 2c+h (4-bit) or 4c+2h, 4c+2h+1 (8-bit) of the packed row
-        const uint8_t* pst = prow0 + sp * PBYTES;
+        const uint32_t pst = prow0 + (uint32_t)(sp * PBYTES);
 #pragma unroll
         for (int i = 0; i < BITS / 4; ++i) {
           const int un = (BITS == 4) ? (2 * c + h) : (4 * c + 2 * h + i);
-          const uint4 p = *reinterpret_cast<const uint4*>(pst + ((un ^ sw) << 4));
-          wv[u][4 * i] = p.x;
-          wv[u][4 * i + 1] = p.y;
-          wv[u][4 * i + 2] = p.z;
-          wv[u][4 * i + 3] = p.w;
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(wv[u][4 * i]), "=r"(wv[u][4 * i + 1]), "=r"(wv[u][4 * i + 2]), "=r"(wv[u][4 * i + 3])
+                       : "r"(pst + (uint32_t)((un ^ sw) << 4)));
         }
         endu[u] = c == CH - 1 || j == nloc - 1;
         if (endu[u] && ++sp == NP) {
@@ -459,6 +534,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
         s = 0;
         if (t >= NA) aph ^= 1u;
       }
+    }
     }
     // accumulator -> red[m][row] (fp32); the two warps of a lane quarter
     // take alternate 16-column blocks
