@@ -10,14 +10,16 @@
 //   warp 0      W producer: packed weight tile [128 (or 2 x 64) rows x 64 k]
 //               into a deep ring of `NP` stages (`pfull` / `pfree`); weights
 //               are constant, so it runs ahead of the programmatic-launch
-//               wait.
+//               wait, and the first NP stages are issued right after the
+//               barrier initialisation, before the TMEM allocation and the
+//               CTA-wide set-up barrier.
 //   warp 10     X producer: activation tiles [Mpad x 64 k] of a step (two
 //               chunks) into the `na`-stage ring shared with the A stages
 //               (`xfull` / `mdone`).
 //   warps 2..9  dequantizers, two threads per weight row (k halves of 32):
 //               packed words -> bf16(fma(scale, q, bias)) -> tcgen05.st into
-//               the A stage (`afull`); they free the packed stage as soon as
-//               its words are in registers.
+//               the A stage (`afull`); they free a packed stage once its
+//               last words are consumed.
 //   warp 1      allocates TMEM; one lane issues 4 x tcgen05.mma (K = 16, A
 //               from TMEM, B from shared memory) per chunk and commits each
 //               step's stage to `mdone`, the whole accumulation to `accf`.
@@ -236,6 +238,20 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
   if (swiglu) row0 = tile * (kMmaRows / 2);
   else mma_tile(a, tile, mi, row0);
 
+  // packed stage t of this CTA's k range into ring slot st (weights do not
+  // depend on earlier kernels)
+  const int nst = (nloc + CH - 1) / CH;
+  auto issue_w = [&](int t, int st) {
+    const int wx = (kc0 + t * CH) * 2 * BITS;  // word column of the stage's first chunk
+    mbar_arrive_expect_tx(&pfull[st], (uint32_t)PBYTES);
+    if (swiglu) {
+      tma_load_2d(Ps + st * PBYTES, &mp.w[0], wx, row0, &pfull[st]);
+      tma_load_2d(Ps + st * PBYTES + PBYTES / 2, &mp.w[1], wx, row0, &pfull[st]);
+    } else {
+      tma_load_2d(Ps + st * PBYTES, &mp.w[mi], wx, row0, &pfull[st]);
+    }
+  };
+  const int npre = min(NP, nst);  // stages issued before the CTA-wide set-up barrier
   if (threadIdx.x == 0) {
     for (int s = 0; s < NP; ++s) {
       mbar_init(&pfull[s], 1);
@@ -249,6 +265,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
     mbar_init(accf, 1);
     *s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the first weight stages start streaming before the TMEM allocation
+    // and the set-up barrier (thread 0 is the W producer's lane)
+    for (int t = 0; t < npre; ++t) issue_w(t, t);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -267,22 +286,14 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmm_mma_kernel(const __grid_co
   if (warp == 0) {
     // ---------------- W producer (no dependency on earlier kernels) ----------------
     if (lane == 0) {
-      const int nst = (nloc + CH - 1) / CH;
-      int s = 0;
+      int s = npre == NP ? 0 : npre;
       uint32_t ph = 0;  // parity of the pfree phase that frees stage s
-      for (int t = 0; t < nst; ++t) {
-        const int wx = (kc0 + t * CH) * 2 * BITS;  // word column of the stage's first chunk
+      for (int t = npre; t < nst; ++t) {
         if (t >= NP && !mbar_wait_bounded(&pfree[s], ph, a.err, 0x61u)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&pfull[s], (uint32_t)PBYTES);
-        if (swiglu) {
-          tma_load_2d(Ps + s * PBYTES, &mp.w[0], wx, row0, &pfull[s]);
-          tma_load_2d(Ps + s * PBYTES + PBYTES / 2, &mp.w[1], wx, row0, &pfull[s]);
-        } else {
-          tma_load_2d(Ps + s * PBYTES, &mp.w[mi], wx, row0, &pfull[s]);
-        }
+        issue_w(t, s);
         if (++s == NP) {
           s = 0;
           if (t >= NP) ph ^= 1u;
