@@ -159,8 +159,11 @@ LMX_DEV void sdpa_stage_raw(int jn, const uint8_t* raw, const uint32_t (&sb)[2 *
 // MT = m16 row tiles (rows padded to 16*MT <= 64).  a.tiles row tiles of
 // 16*MT rows, a.nsplit splits of the reached chunks; partials [b][kvh][tile][split]
 // [kAttnMmaRows][kPartStride], counters [b][kvh][tile].
+// One-tile blocks (single-token decode, short verify blocks) fit two CTAs per
+// SM (<= 64 registers, ~113 KB of shared memory for a 4-bit or bf16 cache),
+// which doubles the key splits the plan gives them (engine.cuh sdpa_mma_plan).
 template <int MT, int BITS>
-__global__ void __launch_bounds__(kAttnThreads, 1) sdpa_mma_kernel(SdpaArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, MT == 1 ? 2 : 1) sdpa_mma_kernel(SdpaArgs a) {
   constexpr int MP = 16 * MT;
   constexpr size_t RAW = sdpa_raw_stage<BITS>(), RB = (size_t)kHeadDim * BITS / 8;
   extern __shared__ __align__(128) uint8_t smem[];
