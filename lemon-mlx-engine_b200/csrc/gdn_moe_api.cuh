@@ -105,29 +105,36 @@ extern "C" int lmx_moe_route(const void* logits, int rows, int E, int k, int32_t
 }
 
 namespace lmx {
-template <int BITS>
-static int launch_moe_t(const MoeArgs& a, cudaStream_t st) {
+template <int BITS, bool EP>
+static int launch_moe_tt(const MoeArgs& a, cudaStream_t st) {
   static bool attr_set[64] = {};
   int d = 0;
   cudaGetDevice(&d);
   const size_t s1 = (size_t)a.H * 4, s2 = (size_t)a.k * a.I * 4;
   if (!attr_set[d & 63]) {
-    int rc = cuda_check(cudaFuncSetAttribute(moe_gateup_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    int rc = cuda_check(cudaFuncSetAttribute(moe_gateup_kernel<BITS, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              200 * 1024),
                         "moe: smem");
     if (!rc)
-      rc = cuda_check(cudaFuncSetAttribute(moe_down_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      rc = cuda_check(cudaFuncSetAttribute(moe_down_kernel<BITS, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            200 * 1024),
                       "moe: smem");
     if (rc) return rc;
     attr_set[d & 63] = true;
   }
-  int rc = cuda_check(lmx_launch(moe_gateup_kernel<BITS>, dim3((a.I + 63) / 64, a.M * a.k), dim3(256), s1, st, true, a),
+  int rc = cuda_check(lmx_launch(moe_gateup_kernel<BITS, EP>, dim3((a.I + 63) / 64, a.M * a.k), dim3(256), s1, st,
+                                 true, a),
                       "moe_gateup: launch");
   if (!rc)
-    rc = cuda_check(lmx_launch(moe_down_kernel<BITS>, dim3((a.H + 63) / 64, a.M), dim3(256), s2, st, true, a),
+    rc = cuda_check(lmx_launch(moe_down_kernel<BITS, EP>, dim3((a.H + 63) / 64, a.M), dim3(256), s2, st, true, a),
                     "moe_down: launch");
   return rc;
+}
+// Expert-parallel launches (slot outputs for ep_combine_kernel) take the EP
+// kernels; everything else the one-GPU kernels.
+template <int BITS>
+static int launch_moe_t(const MoeArgs& a, cudaStream_t st) {
+  return a.slot_out ? launch_moe_tt<BITS, true>(a, st) : launch_moe_tt<BITS, false>(a, st);
 }
 }  // namespace lmx
 
